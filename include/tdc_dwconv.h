@@ -1,0 +1,158 @@
+/*
+ * tdc_dwconv.h — C ABI of the sm_100a NHWC fp16 depthwise 3x3 conv2d forward.
+ *
+ * This is the drop-in boundary between any host (the `_tma_dwconv_C` PyTorch
+ * extension, ctypes, cgo, JNI …) and the hand-written Blackwell kernels in
+ * libtdc_sm100.so.  Signatures use plain pointers and 64-bit sizes only: no
+ * torch, no CUDA headers.  `stream` is a `cudaStream_t` passed as `void*`
+ * (NULL = the legacy default stream of the current device).
+ *
+ * Tensor layouts (all row-major, contiguous, fp16 = IEEE binary16):
+ *   x  [N, H, W, C]      input activations (NHWC)
+ *   w  [R, S, C]         depthwise filter, one RxS kernel per channel (R=S=3)
+ *   y  [N, P, Q, C]      output, P = H + 2*pad - 2, Q = W + 2*pad - 2
+ *
+ * Semantics (identical for every entry point):
+ *   y[n,p,q,c] = fp16_rne( sum_{r=0..2} sum_{s=0..2} fp32(x[n,p+r-pad,q+s-pad,c]) * fp32(w[r,s,c]) )
+ * accumulated in fp32 from +0 in r-major, s-minor order, with x = 0 outside the
+ * image.  Stride 1, symmetric zero padding pad >= 0.
+ *
+ * Ownership / threading: the caller allocates x, w, y (and `stall`) on the
+ * CUDA device that is current for the calling thread; the library never
+ * takes ownership and never synchronises.  Every entry point is stream-ordered
+ * and re-entrant; it may be called from any host thread.
+ *
+ * Return value: TDC_OK (0) or a negative TDC_ERR_* code.  Argument errors are
+ * detected on the host before any CUDA call is made.
+ */
+#ifndef TDC_DWCONV_H_
+#define TDC_DWCONV_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TDC_API __attribute__((visibility("default")))
+#else
+#define TDC_API
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define TDC_OK                    0
+#define TDC_ERR_NULL_POINTER     -1  /* x, w, y (or stall for the probe) is NULL          */
+#define TDC_ERR_BAD_SHAPE        -2  /* N,H,W,C < 1, or the output would be empty          */
+#define TDC_ERR_FILTER_SHAPE     -3  /* R != 3 or S != 3                                     */
+#define TDC_ERR_CHANNELS         -4  /* C not a multiple of 8 (v0) / 64 (ws)                 */
+#define TDC_ERR_PAD              -5  /* pad < 0                                             */
+#define TDC_ERR_N_STAGE          -6  /* n_stage not in {2, 3, 4}                             */
+#define TDC_ERR_ALIGNMENT        -7  /* x, w or y not 16-byte aligned                        */
+#define TDC_ERR_TOO_LARGE        -8  /* a dimension exceeds what the TMA descriptor encodes  */
+#define TDC_ERR_CUDA             -9  /* a CUDA runtime call failed (see tdc_last_cuda_error) */
+#define TDC_ERR_TMA_ENCODE      -10  /* cuTensorMapEncodeTiled rejected the descriptor       */
+#define TDC_ERR_DEVICE_TIMEOUT  -11  /* a kernel gave up waiting on a pipeline barrier       */
+#define TDC_ERR_NO_DEVICE       -12  /* no usable sm_100 device is current                   */
+
+/* Human-readable text for a status code (static storage, never NULL). */
+TDC_API const char* tdc_strerror(int code);
+
+/* cudaError_t of the most recent failing CUDA call made by this thread
+ * inside the library (0 if none). */
+TDC_API int tdc_last_cuda_error(void);
+
+/* Output spatial size for a stride-1 RxS conv with symmetric padding:
+ * P = H + 2*pad - R + 1, Q = W + 2*pad - S + 1.
+ * Replaces the P/Q computation of the reference host launchers
+ * (csrc/kernel_tma_ws.cu:382-385, csrc/kernel_v0_naive_float4.cu:96-99). */
+TDC_API int tdc_output_hw(int64_t H, int64_t W, int64_t R, int64_t S, int64_t pad,
+                          int64_t* P, int64_t* Q);
+
+/* Plain (non-TMA) kernel: direct 16-byte global loads, 8 channels per thread.
+ * Requires C % 8 == 0.
+ * Replaces tma_dwconv::dwconv_v0 (csrc/bindings.cpp:6,
+ * csrc/kernel_v0_naive_float4.cu:78-118), with y supplied by the caller. */
+TDC_API int tdc_dwconv_v0(const void* x, const void* w, void* y,
+                          int64_t N, int64_t H, int64_t W, int64_t C,
+                          int64_t R, int64_t S, int64_t pad, void* stream);
+
+/* TMA + warp-specialised kernel: one producer warp streams halo'd row tiles
+ * into an n_stage-deep shared-memory ring (mbarrier full/empty pairs); four
+ * consumer warps keep a 3-row sliding window of fp32 accumulators in
+ * registers.  Requires C % 64 == 0 and n_stage in {2, 3, 4}.
+ * Replaces tma_dwconv::dwconv_ws (csrc/bindings.cpp:7-8,
+ * csrc/kernel_tma_ws.cu:52-82), with y supplied by the caller. */
+TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y,
+                          int64_t N, int64_t H, int64_t W, int64_t C,
+                          int64_t R, int64_t S, int64_t pad, int64_t n_stage,
+                          void* stream);
+
+/* Number of rows of the stall tensor that tdc_dwconv_ws_probe writes for
+ * this problem (= number of CTAs the launch uses). */
+TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C,
+                                int64_t pad, int64_t n_stage, int64_t* num_blocks);
+
+/* Consumer warps per CTA of the ws kernel (the divisor for column 1 and 3 of
+ * the stall tensor when a per-warp figure is wanted). */
+TDC_API int tdc_ws_consumer_warps(void);
+
+/* Launch plan the ws kernel would use on a device with `sms` SMs and
+ * `ctas_per_sm` resident CTAs (pure host arithmetic, no CUDA call):
+ * plan[0..7] = {stage_rows, band_rows, bands, qstrips, cblocks, units, grid,
+ * dynamic smem bytes}.  No counterpart in the reference (whose grid is fixed
+ * at (ceil(P/8), C/64, N), csrc/kernel_tma_ws.cu:25-31); exposed so the
+ * planner can be checked without a GPU. */
+TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
+                        int64_t n_stage, int64_t sms, int64_t ctas_per_sm, int64_t* plan);
+
+/* Same computation as tdc_dwconv_ws, instrumented with clock64() around the
+ * pipeline waits.  `stall` is a caller-owned, zero-initialised device array of
+ * num_blocks*4 uint64 (num_blocks from tdc_ws_probe_blocks); cycles are
+ * atomically ADDED, per CTA row b:
+ *   stall[4b+0] producer cycles waiting on the empty barriers
+ *   stall[4b+1] consumer cycles waiting on the full barriers, summed over warps
+ *   stall[4b+2] producer lifetime (cycles)
+ *   stall[4b+3] consumer lifetime, summed over consumer warps
+ * Replaces tma_dwconv::dwconv_ws_probe (csrc/bindings.cpp:9-10,
+ * csrc/kernel_tma_ws.cu:410-452), with y and stall supplied by the caller. */
+TDC_API int tdc_dwconv_ws_probe(const void* x, const void* w, void* y,
+                                int64_t N, int64_t H, int64_t W, int64_t C,
+                                int64_t R, int64_t S, int64_t pad, int64_t n_stage,
+                                unsigned long long* stall, void* stream);
+
+/* ---- pipeline-wait failure detection ----------------------------------------
+ * Every mbarrier wait in the ws kernels is bounded.  A wait that exceeds the
+ * limit records a TDC_DEVICE_* code in a per-device status word, tells the
+ * other warps of its CTA to stop, waits (bounded) for the CTA's own TMA copies
+ * still in flight, and returns.  The CUDA context stays usable. */
+#define TDC_DEVICE_OK               0
+#define TDC_DEVICE_FULL_TIMEOUT     1  /* consumer waited too long for a filled stage */
+#define TDC_DEVICE_EMPTY_TIMEOUT    2  /* producer waited too long for a free stage   */
+#define TDC_DEVICE_DRAIN_TIMEOUT    3  /* an issued TMA copy never completed          */
+
+/* Wait limit used by subsequent launches from this process (default 2 s). */
+TDC_API int tdc_set_wait_timeout_ns(int64_t ns);
+
+/* Reads (and if clear != 0, resets) the status word of the CURRENT device.
+ * Synchronises the device.  info[0..3] (may be NULL) receives
+ * {code, block, stage, load index} of the first failure recorded. */
+TDC_API int tdc_device_status(int clear, int64_t* info);
+
+/* ws launch in which the producer withholds load number `withhold_load`
+ * (counting from 0 in the order a CTA issues them; -1 = withhold none), so
+ * the consumer's wait for that stage runs out after `timeout_ns`.  It exists
+ * to test the bounded-wait path: the kernel reports
+ * TDC_DEVICE_FULL_TIMEOUT through tdc_device_status and returns.  No GPU
+ * fault, trap or unbounded wait is involved. */
+TDC_API int tdc_dwconv_ws_withhold(const void* x, const void* w, void* y,
+                                   int64_t N, int64_t H, int64_t W, int64_t C,
+                                   int64_t pad, int64_t n_stage,
+                                   int64_t withhold_load, int64_t timeout_ns,
+                                   void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* TDC_DWCONV_H_ */

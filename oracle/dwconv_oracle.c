@@ -1,0 +1,182 @@
+/*
+ * dwconv_oracle.c — CPU oracle for the NHWC fp16 depthwise 3x3 conv2d forward.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker the parity tests, the
+ * smoke test and the CPU-baseline leg of the benchmark compare the CUDA path
+ * against; nothing in the shipped library links or calls it.
+ *
+ * It restates, on the CPU, the per-output arithmetic of the reference
+ * kernels of haowen-han/tma-depthwise-conv:
+ *   csrc/kernel_v0_naive_float4.cu:37-74   (acc[v] = 0; for r: for s:
+ *                                          acc[v] += half2float(x)*half2float(w);
+ *                                          y = __float2half(acc))
+ *   csrc/kernel_tma_ws.cuh:218-246         (same chain over the smem tile)
+ *   csrc/kernel_tma_ws.cu:382-385          (P = H + 2*pad - 3 + 1, Q likewise)
+ *   csrc/kernel_tma_ws.cuh:148-149         (taps outside the image read 0:
+ *                                          TMA out-of-bounds zero fill)
+ * i.e. an fp32 multiply-add chain from +0 in r-major, s-minor order, then one
+ * round-to-nearest-even to fp16.  Because the product of two fp16 values is
+ * exact in fp32, acc + x*w and fmaf(x, w, acc) give the same bits; the
+ * reference compiles `acc += a*b` to FFMA (nvcc --fmad=true), and this file
+ * uses fmaf.
+ *
+ * fp16 <-> fp32 conversions are written out bit by bit below (IEEE 754
+ * binary16, round-to-nearest-even, subnormals kept, overflow to infinity).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static float bits_to_f32(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+static uint32_t f32_to_bits(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
+
+/* binary16 -> binary32, exact for every input. */
+float oracle_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1fu;
+  const uint32_t m = h & 0x3ffu;
+  if (e == 0) {
+    /* zero or subnormal: m * 2^-24, exact in binary32 */
+    const float v = (float)m * 5.9604644775390625e-08f;
+    return bits_to_f32(sign | f32_to_bits(v));
+  }
+  if (e == 31) return bits_to_f32(sign | 0x7f800000u | (m << 13)); /* inf / nan */
+  return bits_to_f32(sign | ((e + 112u) << 23) | (m << 13));
+}
+
+/* binary32 -> binary16, round to nearest, ties to even. */
+uint16_t oracle_f32_to_f16(float f) {
+  const uint32_t x = f32_to_bits(f);
+  const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+  const uint32_t ax = x & 0x7fffffffu;
+  if (ax >= 0x7f800000u) /* inf, nan (quiet, top payload bits kept) */
+    return (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? (0x200u | ((ax >> 13) & 0x3ffu)) : 0u));
+  if (ax >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u); /* >= 65520 rounds to inf */
+  if (ax >= 0x38800000u) {                                   /* normal fp16 range */
+    const uint32_t mant = ax & 0x7fffffu;
+    uint32_t h = ((((ax >> 23) & 0xffu) - 112u) << 10) | (mant >> 13);
+    const uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h; /* carry into exponent is correct */
+    return (uint16_t)(sign | h);
+  }
+  if (ax <= 0x33000000u) return sign; /* <= 2^-25: rounds to (signed) zero */
+  {
+    /* subnormal result: count units of 2^-24 */
+    const uint32_t e = (ax >> 23) & 0xffu;          /* 102 .. 112 */
+    const uint32_t mfull = (ax & 0x7fffffu) | 0x800000u;
+    const uint32_t shift = 126u - e;                /* 14 .. 24 */
+    uint32_t h = mfull >> shift;
+    const uint32_t rem = mfull & ((1u << shift) - 1u);
+    const uint32_t half = 1u << (shift - 1u);
+    if (rem > half || (rem == half && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+  }
+}
+
+/* Output size of a stride-1 3x3 conv with symmetric padding
+ * (csrc/kernel_tma_ws.cu:384-385). */
+void oracle_output_hw(int64_t H, int64_t W, int64_t pad, int64_t* P, int64_t* Q) {
+  *P = H + 2 * pad - 3 + 1;
+  *Q = W + 2 * pad - 3 + 1;
+}
+
+/*
+ * y[n,p,q,c] = f16_rne( chain_{r=0..2, s=0..2} fmaf(x[n,p+r-pad,q+s-pad,c], w[r,s,c], acc) )
+ * x: [N,H,W,C] fp16 bits, w: [3,3,C] fp16 bits, y: [N,P,Q,C] fp16 bits.
+ * threads <= 0: use the OpenMP default.  Returns 0, or -1 on bad arguments /
+ * allocation failure.
+ */
+int oracle_dwconv3x3_f16(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t N,
+                         int64_t H, int64_t W, int64_t C, int64_t pad, int threads) {
+  if (!x || !w || !y || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0) return -1;
+  int64_t P, Q;
+  oracle_output_hw(H, W, pad, &P, &Q);
+  if (P < 0 || Q < 0) return -1;
+  if (N == 0 || C == 0 || P == 0 || Q == 0) return 0;
+
+  float* wf = (float*)malloc(sizeof(float) * 9 * (size_t)C);
+  if (!wf) return -1;
+  for (int64_t i = 0; i < 9 * C; ++i) wf[i] = oracle_f16_to_f32(w[i]);
+
+  /* decode table: every fp16 bit pattern -> fp32 */
+  float* lut = (float*)malloc(sizeof(float) * 65536);
+  if (!lut) { free(wf); return -1; }
+  for (uint32_t i = 0; i < 65536u; ++i) lut[i] = oracle_f16_to_f32((uint16_t)i);
+
+  const int64_t WP = W + 2 * pad; /* decoded row with zero columns either side */
+  int err = 0;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads) reduction(| : err)
+#endif
+  {
+    float* rows = (float*)calloc((size_t)(3 * WP * C + 1), sizeof(float));
+    float* zero_row = (float*)calloc((size_t)(WP * C + 1), sizeof(float));
+    float* acc = (float*)malloc(sizeof(float) * (size_t)(C + 1));
+    if (!rows || !zero_row || !acc) {
+      err = 1;
+    } else {
+      int64_t cached[3] = {-1, -1, -1}; /* global (n*H + h) index held in each slot */
+#ifdef _OPENMP
+#pragma omp for schedule(static)
+#endif
+      for (int64_t np = 0; np < N * P; ++np) {
+        const int64_t n = np / P, p = np % P;
+        const float* in[3];
+        for (int r = 0; r < 3; ++r) {
+          const int64_t h = p + r - pad;
+          if (h < 0 || h >= H) { in[r] = zero_row; continue; }
+          const int64_t key = n * H + h;
+          int slot = -1;
+          for (int k = 0; k < 3; ++k) if (cached[k] == key) slot = k;
+          if (slot < 0) {
+            /* evict a slot not used by the other taps of this output row */
+            for (int k = 0; k < 3 && slot < 0; ++k) {
+              int used = 0;
+              for (int rr = 0; rr < 3; ++rr) {
+                const int64_t hh = p + rr - pad;
+                if (hh >= 0 && hh < H && cached[k] == n * H + hh) used = 1;
+              }
+              if (!used) slot = k;
+            }
+            float* dst = rows + (int64_t)slot * WP * C + pad * C;
+            const uint16_t* src = x + key * W * C;
+            for (int64_t i = 0; i < W * C; ++i) dst[i] = lut[src[i]];
+            cached[slot] = key;
+          }
+          in[r] = rows + (int64_t)slot * WP * C;
+        }
+        uint16_t* out = y + np * Q * C;
+        for (int64_t q = 0; q < Q; ++q) {
+          for (int64_t c = 0; c < C; ++c) acc[c] = 0.0f;
+          for (int r = 0; r < 3; ++r)
+            for (int s = 0; s < 3; ++s) {
+              const float* xr = in[r] + (q + s) * C;
+              const float* wr = wf + (r * 3 + s) * C;
+              for (int64_t c = 0; c < C; ++c) acc[c] = fmaf(xr[c], wr[c], acc[c]);
+            }
+          for (int64_t c = 0; c < C; ++c) out[q * C + c] = oracle_f32_to_f16(acc[c]);
+        }
+      }
+    }
+    free(rows);
+    free(zero_row);
+    free(acc);
+  }
+  free(lut);
+  free(wf);
+  return err ? -1 : 0;
+}
+
+/* Threads an OpenMP parallel region would use by default (1 without OpenMP). */
+int oracle_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

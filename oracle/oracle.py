@@ -1,0 +1,103 @@
+"""CPU oracle for the NHWC fp16 depthwise 3x3 conv2d forward.
+
+TEST INFRASTRUCTURE ONLY: the parity tests, ``__graft_entry__.smoke()`` and the
+CPU-baseline leg of ``bench.py`` use this module as the checker.  The shipped
+library never imports it, and the product path has no CPU fallback.
+
+Two independent restatements of the reference arithmetic
+(haowen-han/tma-depthwise-conv ``csrc/kernel_v0_naive_float4.cu:37-74`` and
+``csrc/kernel_tma_ws.cuh:218-246``: fp32 multiply-add chain from +0 in
+r-major, s-minor order over the 3x3 taps, zero outside the image, one
+round-to-nearest-even to fp16):
+
+* :func:`dwconv_f16` calls the C restatement in ``dwconv_oracle.c``
+  (``liboracle_dwconv.so``, OpenMP) — the fast one, used at every size;
+* :func:`dwconv_f16_numpy` is a numpy restatement for small cases.
+
+The two must agree bit for bit; tests/test_oracle.py checks that, and checks
+both against the golden vectors recorded from the reference's own kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liboracle_dwconv.so")
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load liboracle_dwconv.so (built by ``make -C oracle``); raise if absent."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"oracle library missing: {LIB_PATH} (run `make -C oracle`)")
+        lib = ctypes.CDLL(LIB_PATH)
+        i64 = ctypes.c_int64
+        lib.oracle_dwconv3x3_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 5 + [ctypes.c_int]
+        lib.oracle_dwconv3x3_f16.restype = ctypes.c_int
+        lib.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
+        lib.oracle_f16_to_f32.restype = ctypes.c_float
+        lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
+        lib.oracle_f32_to_f16.restype = ctypes.c_uint16
+        lib.oracle_max_threads.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+def output_hw(H: int, W: int, pad: int) -> tuple[int, int]:
+    """P, Q of a stride-1 3x3 conv (reference csrc/kernel_tma_ws.cu:384-385)."""
+    return H + 2 * pad - 3 + 1, W + 2 * pad - 3 + 1
+
+
+def max_threads() -> int:
+    return int(load().oracle_max_threads())
+
+
+def dwconv_f16(x: np.ndarray, w: np.ndarray, pad: int, threads: int = 0) -> np.ndarray:
+    """C oracle.  x: [N,H,W,C] float16, w: [3,3,C] float16 -> [N,P,Q,C] float16."""
+    lib = load()
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    if x.ndim != 4 or w.shape != (3, 3, x.shape[3]):
+        raise ValueError("x must be [N,H,W,C] and w [3,3,C]")
+    N, H, W, C = x.shape
+    P, Q = output_hw(H, W, pad)
+    if P < 0 or Q < 0:
+        raise ValueError("negative output size")
+    y = np.empty((N, P, Q, C), dtype=np.float16)
+    rc = lib.oracle_dwconv3x3_f16(x.ctypes.data, w.ctypes.data, y.ctypes.data,
+                                  N, H, W, C, pad, int(threads))
+    if rc != 0:
+        raise RuntimeError("oracle_dwconv3x3_f16 failed")
+    return y
+
+
+def dwconv_f16_numpy(x: np.ndarray, w: np.ndarray, pad: int) -> np.ndarray:
+    """numpy restatement (small sizes).  Same chain, same order, same rounding.
+
+    numpy float32 ``acc + xs * ws`` rounds the product first, but the product
+    of two fp16 values is exact in float32, so each step equals fmaf.
+    """
+    x = np.asarray(x, dtype=np.float16)
+    w = np.asarray(w, dtype=np.float16)
+    N, H, W, C = x.shape
+    P, Q = output_hw(H, W, pad)
+    xp = np.zeros((N, H + 2 * pad, W + 2 * pad, C), dtype=np.float32)
+    xp[:, pad:pad + H, pad:pad + W, :] = x.astype(np.float32)
+    wf = w.astype(np.float32)
+    acc = np.zeros((N, P, Q, C), dtype=np.float32)
+    for r in range(3):
+        for s in range(3):
+            acc = acc + xp[:, r:r + P, s:s + Q, :] * wf[r, s]
+    return acc.astype(np.float16)  # numpy float32 -> float16 is round-to-nearest-even
+
+
+def f16_ulp(v: np.ndarray) -> np.ndarray:
+    """fp16 spacing at |v| (2^-24 in the subnormal range)."""
+    a = np.abs(np.asarray(v, dtype=np.float32))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -14)))
+    return np.exp2(e - 10).astype(np.float32)

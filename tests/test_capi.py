@@ -1,0 +1,161 @@
+"""C ABI of libtdc_sm100.so, checked without a GPU.
+
+* the library loads and exports every function include/tdc_dwconv.h declares;
+* argument errors come back as the documented status codes before any CUDA
+  call (the same conditions the reference's TORCH_CHECKs reject,
+  csrc/kernel_tma_ws.cu:54-65 / csrc/kernel_v0_naive_float4.cu:84-94);
+* the ws launch planner covers every output element exactly once.
+"""
+import ctypes as C
+import os
+import re
+
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(REPO, "tma-depthwise-conv_b200", "libtdc_sm100.so")
+HDR = os.path.join(REPO, "include", "tdc_dwconv.h")
+
+i64 = C.c_int64
+
+
+def _codes():
+    txt = open(HDR).read()
+    return {m.group(1): int(m.group(2)) for m in re.finditer(r"#define (TDC_\w+)\s+(-?\d+)", txt)}
+
+
+CODES = _codes()
+
+
+@pytest.fixture(scope="module")
+def lib():
+    L = C.CDLL(LIB)
+    L.tdc_strerror.restype = C.c_char_p
+    return L
+
+
+def test_exports_every_declared_symbol(lib):
+    names = re.findall(r"TDC_API\s+[\w\s\*]+?\b(tdc_\w+)\s*\(", open(HDR).read())
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in tdc_dwconv.h but not exported"
+
+
+def test_strerror_covers_all_codes(lib):
+    for name, code in CODES.items():
+        if name.startswith("TDC_ERR_") or name == "TDC_OK":
+            s = lib.tdc_strerror(code)
+            assert s and b"unknown" not in s, name
+    assert b"unknown" in lib.tdc_strerror(-999)
+
+
+def test_output_hw(lib):
+    P, Q = i64(), i64()
+    assert lib.tdc_output_hw(i64(224), i64(336), i64(3), i64(3), i64(1), C.byref(P), C.byref(Q)) == 0
+    assert (P.value, Q.value) == (224, 336)
+    assert lib.tdc_output_hw(i64(16), i64(16), i64(3), i64(3), i64(0), C.byref(P), C.byref(Q)) == 0
+    assert (P.value, Q.value) == (14, 14)
+    assert lib.tdc_output_hw(i64(16), i64(16), i64(3), i64(3), i64(-1), C.byref(P), C.byref(Q)) == CODES["TDC_ERR_PAD"]
+
+
+def _ws(lib, x=16, w=16, y=16, N=2, H=16, W=16, Cc=64, R=3, S=3, pad=1, ns=2):
+    p = lambda v: C.c_void_p(v) if v else None
+    return lib.tdc_dwconv_ws(p(x), p(w), p(y), i64(N), i64(H), i64(W), i64(Cc), i64(R), i64(S),
+                             i64(pad), i64(ns), None)
+
+
+def _v0(lib, x=16, w=16, y=16, N=2, H=16, W=16, Cc=64, R=3, S=3, pad=1):
+    p = lambda v: C.c_void_p(v) if v else None
+    return lib.tdc_dwconv_v0(p(x), p(w), p(y), i64(N), i64(H), i64(W), i64(Cc), i64(R), i64(S),
+                             i64(pad), None)
+
+
+def test_ws_argument_errors(lib):
+    assert _ws(lib, x=0) == CODES["TDC_ERR_NULL_POINTER"]
+    assert _ws(lib, y=0) == CODES["TDC_ERR_NULL_POINTER"]
+    assert _ws(lib, H=0) == CODES["TDC_ERR_BAD_SHAPE"]
+    assert _ws(lib, N=-1) == CODES["TDC_ERR_BAD_SHAPE"]
+    assert _ws(lib, R=5, S=5) == CODES["TDC_ERR_FILTER_SHAPE"]
+    assert _ws(lib, Cc=32) == CODES["TDC_ERR_CHANNELS"]
+    assert _ws(lib, pad=-1) == CODES["TDC_ERR_PAD"]
+    assert _ws(lib, ns=5) == CODES["TDC_ERR_N_STAGE"]
+    assert _ws(lib, ns=1) == CODES["TDC_ERR_N_STAGE"]
+    assert _ws(lib, x=24) == CODES["TDC_ERR_ALIGNMENT"]
+    assert _ws(lib, H=1, W=1, pad=0) == CODES["TDC_ERR_BAD_SHAPE"]      # P = -1
+    assert _ws(lib, N=1, H=1 << 20, W=1 << 20, Cc=1 << 10) == CODES["TDC_ERR_TOO_LARGE"]
+    # empty outputs are a successful no-op, before any device query
+    assert _ws(lib, N=0) == 0
+    assert _ws(lib, H=2, W=2, pad=0) == 0                               # P = Q = 0
+
+
+def test_v0_argument_errors(lib):
+    assert _v0(lib, w=0) == CODES["TDC_ERR_NULL_POINTER"]
+    assert _v0(lib, Cc=12) == CODES["TDC_ERR_CHANNELS"]
+    assert _v0(lib, R=1, S=1) == CODES["TDC_ERR_FILTER_SHAPE"]
+    assert _v0(lib, y=8) == CODES["TDC_ERR_ALIGNMENT"]
+    assert _v0(lib, N=0) == 0
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_valid_call_without_device_reports_no_device(lib):
+    assert _ws(lib) == CODES["TDC_ERR_NO_DEVICE"]
+    assert _v0(lib) == CODES["TDC_ERR_NO_DEVICE"]
+    nb = i64()
+    assert lib.tdc_ws_probe_blocks(i64(2), i64(16), i64(16), i64(64), i64(1), i64(2), C.byref(nb)) == CODES["TDC_ERR_NO_DEVICE"]
+
+
+def test_probe_and_status_argument_errors(lib):
+    p = C.c_void_p(16)
+    assert lib.tdc_dwconv_ws_probe(p, p, p, i64(2), i64(16), i64(16), i64(64), i64(3), i64(3),
+                                   i64(1), i64(2), None, None) == CODES["TDC_ERR_NULL_POINTER"]
+    assert lib.tdc_ws_probe_blocks(i64(2), i64(16), i64(16), i64(64), i64(1), i64(2), None) == CODES["TDC_ERR_NULL_POINTER"]
+    assert lib.tdc_set_wait_timeout_ns(i64(0)) != 0
+    assert lib.tdc_ws_consumer_warps() == 4
+
+
+def _plan(lib, N, H, W, Cc, pad, ns, sms=148, occ=4):
+    out = (i64 * 8)()
+    rc = lib.tdc_ws_plan(i64(N), i64(H), i64(W), i64(Cc), i64(pad), i64(ns), i64(sms), i64(occ), out)
+    assert rc == 0
+    return dict(zip(["stage_rows", "band_rows", "bands", "qstrips", "cblocks", "units", "grid", "smem"],
+                    list(out)))
+
+
+SHAPES = [(64, 224, 336, 256, 1), (32, 224, 336, 256, 1), (16, 112, 224, 128, 1), (8, 56, 56, 256, 1),
+          (2, 16, 16, 64, 1), (1, 1, 1, 64, 1), (1, 3, 3, 64, 5), (3, 7, 45, 128, 1), (5, 100, 1, 64, 1),
+          (1, 1000, 40, 64, 0), (80, 224, 336, 320, 1)]
+
+
+@pytest.mark.parametrize("N,H,W,Cc,pad", SHAPES)
+@pytest.mark.parametrize("ns", [2, 3, 4])
+def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
+    pl = _plan(lib, N, H, W, Cc, pad, ns)
+    P, Q = H + 2 * pad - 2, W + 2 * pad - 2
+    assert pl["stage_rows"] == {2: 4, 3: 3, 4: 2}[ns]
+    assert pl["cblocks"] == Cc // 64 and pl["qstrips"] == -(-Q // 32)
+    assert pl["bands"] * pl["band_rows"] >= P > (pl["bands"] - 1) * pl["band_rows"]
+    assert pl["band_rows"] == P or (pl["band_rows"] + 2) % pl["stage_rows"] == 0
+    assert pl["units"] == N * pl["cblocks"] * pl["qstrips"] * pl["bands"]
+    assert 1 <= pl["grid"] <= min(pl["units"], 148 * 4)
+    assert pl["smem"] == ns * pl["stage_rows"] * 34 * 128 + 128 <= 227 * 1024
+    # Rows: bands tile [0, P) exactly; columns: strips tile [0, Q) exactly.
+    rows = []
+    for b in range(pl["bands"]):
+        p0 = b * pl["band_rows"]
+        rows.extend(range(p0, min(p0 + pl["band_rows"], P)))
+    assert rows == list(range(P))
+    cols = [q for s in range(pl["qstrips"]) for q in range(s * 32, min(s * 32 + 32, Q))]
+    assert cols == list(range(Q))
+    # The persistent round-robin hands every unit to exactly one CTA.
+    seen = [0] * pl["units"]
+    for b in range(pl["grid"]):
+        for u in range(b, pl["units"], pl["grid"]):
+            seen[u] += 1
+    assert all(s == 1 for s in seen)
+
+
+def test_plan_balances_the_headline_shape(lib):
+    pl = _plan(lib, 64, 224, 336, 256, 1, 2)
+    waves = pl["units"] / pl["grid"]
+    assert waves >= 16 - 1e-9

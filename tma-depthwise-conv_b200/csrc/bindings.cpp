@@ -1,0 +1,180 @@
+// bindings.cpp — the `_tma_dwconv_C` PyTorch extension.
+//
+// Same module surface as the reference's csrc/bindings.cpp:13-26 (functions
+// dwconv_v0 / dwconv_ws / dwconv_ws_probe with keyword arguments
+// x, w, pad[, n_stage]) and the same TORCH_CHECK messages as its host
+// launchers (csrc/kernel_v0_naive_float4.cu:79-94, csrc/kernel_tma_ws.cu:54-65,
+// 369-380).  Output tensors are allocated here with torch's caching allocator
+// on x's device; the computation goes through the C ABI of libtdc_sm100.so
+// (include/tdc_dwconv.h) on torch's current stream.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <tuple>
+
+#include "tdc_dwconv.h"
+
+namespace tma_dwconv {
+namespace {
+
+void check_common(const torch::Tensor& x, const torch::Tensor& w) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda(), "tensors must live on CUDA");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf, "x must be fp16");
+  TORCH_CHECK(w.scalar_type() == torch::kHalf, "w must be fp16");
+  TORCH_CHECK(x.dim() == 4, "x must be [N,H,W,C]");
+  TORCH_CHECK(w.dim() == 3, "w must be [R,S,C]");
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous(), "x/w must be contiguous");
+  TORCH_CHECK(x.device() == w.device(), "x and w must be on the same device");
+}
+
+void check_status(int rc, const char* what) {
+  if (rc == TDC_OK) return;
+  if (rc == TDC_ERR_CUDA) {
+    TORCH_CHECK(false, what, ": ", tdc_strerror(rc), ": ",
+                cudaGetErrorString(static_cast<cudaError_t>(tdc_last_cuda_error())));
+  }
+  TORCH_CHECK(false, what, ": ", tdc_strerror(rc), " (status ", rc, ")");
+}
+
+void* stream_of(const torch::Tensor& x) {
+  return static_cast<void*>(at::cuda::getCurrentCUDAStream(x.device().index()).stream());
+}
+
+void check_ws_args(const torch::Tensor& x, const torch::Tensor& w, int64_t pad) {
+  check_common(x, w);
+  TORCH_CHECK(w.size(0) == 3 && w.size(1) == 3, "only 3x3 kernel supported");
+  TORCH_CHECK(w.size(2) == x.size(3), "channel mismatch");
+  TORCH_CHECK(x.size(3) % 64 == 0, "C must be a multiple of BlockC=64");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+}
+
+torch::Tensor alloc_out(const torch::Tensor& x, int64_t pad) {
+  int64_t P = 0, Q = 0;
+  check_status(tdc_output_hw(x.size(1), x.size(2), 3, 3, pad, &P, &Q), "output size");
+  TORCH_CHECK(P >= 0 && Q >= 0, "input too small for a 3x3 kernel with pad ", pad);
+  return torch::empty({x.size(0), P, Q, x.size(3)}, x.options());
+}
+
+}  // namespace
+
+torch::Tensor dwconv_v0(torch::Tensor x, torch::Tensor w, int64_t pad) {
+  check_common(x, w);
+  TORCH_CHECK(w.size(0) == 3 && w.size(1) == 3, "Only 3x3 kernel supported in v0");
+  TORCH_CHECK(x.size(3) == w.size(2), "channel mismatch between x and w");
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of VEC=8 (fp16 float4)");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = alloc_out(x, pad);
+  check_status(tdc_dwconv_v0(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.size(0), x.size(1),
+                             x.size(2), x.size(3), w.size(0), w.size(1), pad, stream_of(x)),
+               "dwconv_v0");
+  return y;
+}
+
+torch::Tensor dwconv_ws(torch::Tensor x, torch::Tensor w, int64_t pad, int64_t n_stage) {
+  check_ws_args(x, w, pad);
+  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = alloc_out(x, pad);
+  check_status(tdc_dwconv_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.size(0), x.size(1),
+                             x.size(2), x.size(3), 3, 3, pad, n_stage, stream_of(x)),
+               "dwconv_ws");
+  return y;
+}
+
+// Writes into a caller-provided y [N,P,Q,C] (no allocation on the call path).
+torch::Tensor dwconv_ws_out(torch::Tensor x, torch::Tensor w, torch::Tensor y, int64_t pad,
+                            int64_t n_stage) {
+  check_ws_args(x, w, pad);
+  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  int64_t P = 0, Q = 0;
+  check_status(tdc_output_hw(x.size(1), x.size(2), 3, 3, pad, &P, &Q), "output size");
+  TORCH_CHECK(y.is_cuda() && y.device() == x.device() && y.scalar_type() == torch::kHalf &&
+                  y.is_contiguous() && y.dim() == 4 && y.size(0) == x.size(0) &&
+                  y.size(1) == P && y.size(2) == Q && y.size(3) == x.size(3),
+              "y must be a contiguous fp16 [N,P,Q,C] tensor on x's device");
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_status(tdc_dwconv_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.size(0), x.size(1),
+                             x.size(2), x.size(3), 3, 3, pad, n_stage, stream_of(x)),
+               "dwconv_ws");
+  return y;
+}
+
+std::tuple<torch::Tensor, torch::Tensor> dwconv_ws_probe(torch::Tensor x, torch::Tensor w,
+                                                         int64_t pad, int64_t n_stage) {
+  check_ws_args(x, w, pad);
+  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = alloc_out(x, pad);
+  int64_t blocks = 0;
+  check_status(tdc_ws_probe_blocks(x.size(0), x.size(1), x.size(2), x.size(3), pad, n_stage,
+                                   &blocks),
+               "dwconv_ws_probe");
+  auto stall = torch::zeros({blocks, 4},
+                            torch::TensorOptions().dtype(torch::kInt64).device(x.device()));
+  check_status(
+      tdc_dwconv_ws_probe(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.size(0), x.size(1),
+                          x.size(2), x.size(3), 3, 3, pad, n_stage,
+                          reinterpret_cast<unsigned long long*>(stall.data_ptr<int64_t>()),
+                          stream_of(x)),
+      "dwconv_ws_probe");
+  return {y, stall};
+}
+
+torch::Tensor dwconv_ws_withhold(torch::Tensor x, torch::Tensor w, int64_t pad, int64_t n_stage,
+                                 int64_t withhold_load, int64_t timeout_ns) {
+  check_ws_args(x, w, pad);
+  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = alloc_out(x, pad);
+  check_status(tdc_dwconv_ws_withhold(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.size(0),
+                                      x.size(1), x.size(2), x.size(3), pad, n_stage,
+                                      withhold_load, timeout_ns, stream_of(x)),
+               "dwconv_ws_withhold");
+  return y;
+}
+
+// (code, block, stage, load) of the first pipeline-wait failure recorded on
+// `device` since the last clear; code 0 = none.  Synchronises the device.
+std::tuple<int64_t, int64_t, int64_t, int64_t> device_status(int64_t device, bool clear) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  int64_t info[4] = {0, 0, 0, 0};
+  const int rc = tdc_device_status(clear ? 1 : 0, info);
+  if (rc != TDC_OK && rc != TDC_ERR_DEVICE_TIMEOUT) check_status(rc, "device_status");
+  return {info[0], info[1], info[2], info[3]};
+}
+
+void set_wait_timeout_ns(int64_t ns) { check_status(tdc_set_wait_timeout_ns(ns), "set_wait_timeout_ns"); }
+
+int64_t consumer_warps() { return tdc_ws_consumer_warps(); }
+
+}  // namespace tma_dwconv
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("dwconv_v0", &tma_dwconv::dwconv_v0,
+        "Depthwise conv2d NHWC, plain direct-load kernel (v0 surface).", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("pad"));
+  m.def("dwconv_ws", &tma_dwconv::dwconv_ws,
+        "Depthwise conv2d NHWC, TMA + warp-specialised ring of n_stage stages.",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("n_stage"));
+  m.def("dwconv_ws_probe", &tma_dwconv::dwconv_ws_probe,
+        "Same as dwconv_ws, also returns a per-CTA stall-cycle tensor of shape "
+        "[num_blocks, 4] (cols: producer empty-wait, consumer full-wait summed over "
+        "consumer warps, producer lifetime, consumer lifetime summed over consumer warps).",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("n_stage"));
+  m.def("dwconv_ws_out", &tma_dwconv::dwconv_ws_out,
+        "dwconv_ws into a preallocated y [N,P,Q,C]; returns y.", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("y"), pybind11::arg("pad"), pybind11::arg("n_stage"));
+  m.def("dwconv_ws_withhold", &tma_dwconv::dwconv_ws_withhold,
+        "dwconv_ws whose producer withholds one load so the consumer's bounded wait runs out "
+        "(tests the failure path; see device_status).",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("n_stage"),
+        pybind11::arg("withhold_load"), pybind11::arg("timeout_ns"));
+  m.def("device_status", &tma_dwconv::device_status,
+        "(code, block, stage, load) of the first recorded pipeline-wait failure on a device.",
+        pybind11::arg("device"), pybind11::arg("clear") = true);
+  m.def("set_wait_timeout_ns", &tma_dwconv::set_wait_timeout_ns,
+        "Limit of every pipeline wait of later launches (default 2 s).", pybind11::arg("ns"));
+  m.def("consumer_warps", &tma_dwconv::consumer_warps, "Consumer warps per CTA of the ws kernel.");
+}

@@ -1,0 +1,388 @@
+// tdc_capi.cu — host half of libtdc_sm100.so: argument validation, launch
+// planning, TMA descriptor encoding and kernel launches behind the C ABI
+// declared in include/tdc_dwconv.h.
+//
+// The reference binds three C++ functions taking torch tensors
+// (csrc/bindings.cpp:5-11 → csrc/kernel_v0_naive_float4.cu:78-118,
+// csrc/kernel_tma_ws.cu:52-137).  Here the same three operations take raw
+// device pointers and sizes; tensor allocation stays with the caller.
+//
+// Differences from the reference launchers, by design:
+//  * validation returns a status code before any CUDA call is made;
+//  * the TMA descriptor is encoded with the driver's cuTensorMapEncodeTiled,
+//    fetched once through cudaGetDriverEntryPoint (no -lcuda, no CuTe);
+//  * the dynamic-smem attribute and occupancy are queried once per device and
+//    kernel instantiation instead of on every call (kernel_tma_ws.cu:36-38);
+//  * the grid is persistent (SMs x resident CTAs) over a strip-fastest unit
+//    order instead of one CTA per 8-row tile.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "tdc_dwconv.h"
+#include "tdc_kernels.cuh"
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+std::atomic<int64_t> g_timeout_ns{2000000000ll};
+
+int cuda_fail(cudaError_t e) {
+  t_last_cuda_error = int(e);
+  return TDC_ERR_CUDA;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::once_flag once;
+  int status = TDC_ERR_NO_DEVICE;
+  int sms = 0;
+  int ws_occupancy[3][2] = {};  // [n_stage-2][probe]
+};
+DeviceInfo g_dev[kMaxDevices];
+
+constexpr int kMaxDynSmem = 200 * 1024;
+
+template <int NS, bool PROBE>
+cudaError_t prepare_ws(int* occ) {
+  auto* k = &tdc::dwconv_ws_kernel<NS, PROBE>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e != cudaSuccess) return e;
+  // Occupancy at the largest ring any plan uses (stage_rows * NS <= 9 rows).
+  const size_t smem = size_t(9) * tdc::kRowBytes + 128;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+}
+
+// Returns TDC_OK and fills *info for the current device, or an error.
+int current_device(DeviceInfo** info, int* dev_out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver
+                                   ? TDC_ERR_NO_DEVICE
+                                   : cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return TDC_ERR_NO_DEVICE;
+  DeviceInfo& d = g_dev[dev];
+  std::call_once(d.once, [&d, dev]() {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      d.status = TDC_ERR_NO_DEVICE;
+      return;
+    }
+    if (major != 10 || minor != 0) {  // the cubin is sm_100a only
+      d.status = TDC_ERR_NO_DEVICE;
+      return;
+    }
+    d.sms = sms;
+    cudaError_t e2 = cudaSuccess;
+    if (e2 == cudaSuccess) e2 = prepare_ws<2, false>(&d.ws_occupancy[0][0]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<3, false>(&d.ws_occupancy[1][0]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<4, false>(&d.ws_occupancy[2][0]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<2, true>(&d.ws_occupancy[0][1]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<3, true>(&d.ws_occupancy[1][1]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<4, true>(&d.ws_occupancy[2][1]);
+    if (e2 != cudaSuccess) {
+      t_last_cuda_error = int(e2);
+      d.status = TDC_ERR_CUDA;
+      return;
+    }
+    d.status = TDC_OK;
+  });
+  if (d.status != TDC_OK) return d.status;
+  *info = &d;
+  if (dev_out) *dev_out = dev;
+  return TDC_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Common validation of the reference launchers (kernel_tma_ws.cu:54-65,
+// kernel_v0_naive_float4.cu:84-94), in the same order.
+int validate(const void* x, const void* w, const void* y, int64_t N, int64_t H, int64_t W,
+             int64_t C, int64_t R, int64_t S, int64_t pad, int64_t cmult, int64_t* P,
+             int64_t* Q) {
+  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
+  if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
+  if (R != 3 || S != 3) return TDC_ERR_FILTER_SHAPE;
+  if (C % cmult != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  *P = H + 2 * pad - R + 1;
+  *Q = W + 2 * pad - S + 1;
+  if (*P < 0 || *Q < 0) return TDC_ERR_BAD_SHAPE;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return TDC_ERR_ALIGNMENT;
+  return TDC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// ws launch plan
+// ---------------------------------------------------------------------------
+struct WsPlan {
+  int stage_rows, band_rows, bands, qstrips, cblocks;
+  int64_t units, grid;
+  size_t smem;
+};
+
+int stage_rows_for(int64_t n_stage) { return n_stage == 2 ? 4 : n_stage == 3 ? 3 : 2; }
+
+// Band height: enough units for ~16 waves of persistent CTAs (so the last,
+// partial wave costs little), bands no shorter than two stages, and
+// band_rows + 2 a multiple of stage_rows so no stage carries unused rows.
+WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
+                 int64_t ctas_per_sm) {
+  WsPlan pl{};
+  pl.stage_rows = stage_rows_for(n_stage);
+  pl.qstrips = int((Q + tdc::kStripQ - 1) / tdc::kStripQ);
+  pl.cblocks = int(C / tdc::kBlockC);
+  const int64_t strips = N * pl.cblocks * pl.qstrips;
+  const int64_t g0 = std::max<int64_t>(1, sms * ctas_per_sm);
+  const int64_t want_units = 16 * g0;
+  const int64_t want_bands = std::max<int64_t>(1, (want_units + strips - 1) / std::max<int64_t>(strips, 1));
+  int64_t band = (P + want_bands - 1) / want_bands;
+  band = std::max<int64_t>(band, std::max(2 * pl.stage_rows - 2, 6));
+  while ((band + 2) % pl.stage_rows != 0) ++band;
+  band = std::min<int64_t>(band, P);
+  pl.band_rows = int(std::max<int64_t>(band, 1));
+  pl.bands = int((P + pl.band_rows - 1) / pl.band_rows);
+  pl.units = strips * pl.bands;
+  pl.grid = std::max<int64_t>(1, std::min<int64_t>(pl.units, g0));
+  pl.smem = size_t(n_stage) * pl.stage_rows * tdc::kRowBytes + 128;
+  return pl;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 4-D map over x viewed as (C, W, H, N), innermost first; box
+// (64 ch, 34 cols, stage_rows rows, 1 image); out-of-bounds elements read 0.
+int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t W, int64_t C,
+                 int stage_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return TDC_ERR_TMA_ENCODE;
+  const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
+  const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(W) * C * 2, cuuint64_t(H) * W * C * 2};
+  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(tdc::kInCols),
+                             cuuint32_t(stage_rows), 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
+}
+
+// Limits of the descriptor and of the 32-bit fields the kernel keeps.
+int check_ws_limits(int64_t N, int64_t H, int64_t W, int64_t C, int64_t P, int64_t Q) {
+  const int64_t i32 = 0x7fffffffll;
+  if (N > i32 || H > i32 || W > i32 || C > i32 || P > i32 || Q > i32) return TDC_ERR_TOO_LARGE;
+  if (H * W * C * 2 >= (int64_t(1) << 40)) return TDC_ERR_TOO_LARGE;  // TMA stride limit
+  return TDC_OK;
+}
+
+template <int NS, bool PROBE>
+cudaError_t launch_ws_t(const CUtensorMap& map, const tdc::WsParams& prm, const WsPlan& pl,
+                        cudaStream_t st) {
+  tdc::dwconv_ws_kernel<NS, PROBE>
+      <<<dim3(unsigned(pl.grid)), dim3(tdc::kWsThreads), pl.smem, st>>>(map, prm);
+  return cudaGetLastError();
+}
+
+int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
+              int64_t R, int64_t S, int64_t pad, int64_t n_stage, unsigned long long* stall,
+              bool probe, int64_t withhold, int64_t timeout_ns, void* stream) {
+  int64_t P = 0, Q = 0;
+  int rc = validate(x, w, y, N, H, W, C, R, S, pad, tdc::kBlockC, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (probe && !stall) return TDC_ERR_NULL_POINTER;
+  rc = check_ws_limits(N, H, W, C, P, Q);
+  if (rc != TDC_OK) return rc;
+  if (N == 0 || C == 0 || P == 0 || Q == 0) return TDC_OK;  // empty output: nothing to do
+  DeviceInfo* dev = nullptr;
+  rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][probe ? 1 : 0]);
+  const WsPlan pl = make_plan(N, P, Q, C, n_stage, dev->sms, occ);
+  alignas(64) CUtensorMap map;
+  rc = encode_x_map(&map, x, N, H, W, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  tdc::WsParams prm{};
+  prm.w = static_cast<const __half*>(w);
+  prm.y = static_cast<__half*>(y);
+  prm.stall = stall;
+  prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
+  prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad);
+  prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.bands = pl.bands;
+  prm.band_rows = pl.band_rows; prm.stage_rows = pl.stage_rows;
+  prm.units = pl.units;
+  prm.timeout_ns = uint64_t(timeout_ns > 0 ? timeout_ns : g_timeout_ns.load());
+  prm.withhold = withhold;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (n_stage) {
+    case 2: e = probe ? launch_ws_t<2, true>(map, prm, pl, st) : launch_ws_t<2, false>(map, prm, pl, st); break;
+    case 3: e = probe ? launch_ws_t<3, true>(map, prm, pl, st) : launch_ws_t<3, false>(map, prm, pl, st); break;
+    default: e = probe ? launch_ws_t<4, true>(map, prm, pl, st) : launch_ws_t<4, false>(map, prm, pl, st); break;
+  }
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+TDC_API const char* tdc_strerror(int code) {
+  switch (code) {
+    case TDC_OK: return "success";
+    case TDC_ERR_NULL_POINTER: return "null pointer argument";
+    case TDC_ERR_BAD_SHAPE: return "bad shape: N,H,W,C must be non-negative with H,W >= 1 and a non-negative output size";
+    case TDC_ERR_FILTER_SHAPE: return "only 3x3 kernel supported";
+    case TDC_ERR_CHANNELS: return "C must be a multiple of the channel block (8 for v0, 64 for ws)";
+    case TDC_ERR_PAD: return "pad must be non-negative";
+    case TDC_ERR_N_STAGE: return "n_stage must be one of {2, 3, 4}";
+    case TDC_ERR_ALIGNMENT: return "x, w and y must be 16-byte aligned";
+    case TDC_ERR_TOO_LARGE: return "problem exceeds the TMA descriptor / 32-bit field limits";
+    case TDC_ERR_CUDA: return "a CUDA runtime call failed";
+    case TDC_ERR_TMA_ENCODE: return "cuTensorMapEncodeTiled failed";
+    case TDC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on a pipeline barrier";
+    case TDC_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    default: return "unknown tdc status code";
+  }
+}
+
+TDC_API int tdc_last_cuda_error(void) { return t_last_cuda_error; }
+
+TDC_API int tdc_output_hw(int64_t H, int64_t W, int64_t R, int64_t S, int64_t pad, int64_t* P,
+                          int64_t* Q) {
+  if (!P || !Q) return TDC_ERR_NULL_POINTER;
+  if (pad < 0) return TDC_ERR_PAD;
+  *P = H + 2 * pad - R + 1;
+  *Q = W + 2 * pad - S + 1;
+  return TDC_OK;
+}
+
+TDC_API int tdc_dwconv_v0(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
+                          int64_t C, int64_t R, int64_t S, int64_t pad, void* stream) {
+  int64_t P = 0, Q = 0;
+  int rc = validate(x, w, y, N, H, W, C, R, S, pad, 8, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (N == 0 || C == 0 || P == 0 || Q == 0) return TDC_OK;
+  DeviceInfo* dev = nullptr;
+  rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  tdc::V0Params prm{N, H, W, C, P, Q, pad, N * P * Q * (C / 8)};
+  const int threads = 256;
+  const int64_t want = (prm.total_vecs + threads - 1) / threads;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(want, int64_t(dev->sms) * 32));
+  tdc::dwconv_v0_kernel<<<dim3(unsigned(blocks)), dim3(threads), 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(x), static_cast<const uint4*>(w), static_cast<uint4*>(y), prm);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
+                          int64_t C, int64_t R, int64_t S, int64_t pad, int64_t n_stage,
+                          void* stream) {
+  return ws_common(x, w, y, N, H, W, C, R, S, pad, n_stage, nullptr, false, -1, 0, stream);
+}
+
+TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
+                                int64_t n_stage, int64_t* num_blocks) {
+  if (!num_blocks) return TDC_ERR_NULL_POINTER;
+  if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
+  if (C % tdc::kBlockC != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  const int64_t P = H + 2 * pad - 2, Q = W + 2 * pad - 2;
+  if (P < 0 || Q < 0) return TDC_ERR_BAD_SHAPE;
+  if (N == 0 || C == 0 || P == 0 || Q == 0) {
+    *num_blocks = 0;
+    return TDC_OK;
+  }
+  DeviceInfo* dev = nullptr;
+  int rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][1]);
+  *num_blocks = make_plan(N, P, Q, C, n_stage, dev->sms, occ).grid;
+  return TDC_OK;
+}
+
+TDC_API int tdc_ws_consumer_warps(void) { return tdc::kConsumerWarps; }
+
+TDC_API int tdc_dwconv_ws_probe(const void* x, const void* w, void* y, int64_t N, int64_t H,
+                                int64_t W, int64_t C, int64_t R, int64_t S, int64_t pad,
+                                int64_t n_stage, unsigned long long* stall, void* stream) {
+  return ws_common(x, w, y, N, H, W, C, R, S, pad, n_stage, stall, true, -1, 0, stream);
+}
+
+TDC_API int tdc_set_wait_timeout_ns(int64_t ns) {
+  if (ns <= 0) return TDC_ERR_BAD_SHAPE;
+  g_timeout_ns.store(ns);
+  return TDC_OK;
+}
+
+TDC_API int tdc_device_status(int clear, int64_t* info) {
+  DeviceInfo* dev = nullptr;
+  int rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e);
+  int h[4] = {0, 0, 0, 0};
+  e = cudaMemcpyFromSymbol(h, tdc::g_tdc_status, sizeof(h));
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (clear) {
+    const int z[4] = {0, 0, 0, 0};
+    e = cudaMemcpyToSymbol(tdc::g_tdc_status, z, sizeof(z));
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  if (info)
+    for (int i = 0; i < 4; ++i) info[i] = h[i];
+  return h[0] == 0 ? TDC_OK : TDC_ERR_DEVICE_TIMEOUT;
+}
+
+TDC_API int tdc_dwconv_ws_withhold(const void* x, const void* w, void* y, int64_t N, int64_t H,
+                                   int64_t W, int64_t C, int64_t pad, int64_t n_stage,
+                                   int64_t withhold_load, int64_t timeout_ns, void* stream) {
+  if (timeout_ns <= 0) return TDC_ERR_BAD_SHAPE;
+  return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, withhold_load,
+                   timeout_ns, stream);
+}
+
+TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad, int64_t n_stage,
+                        int64_t sms, int64_t ctas_per_sm, int64_t* plan) {
+  if (!plan) return TDC_ERR_NULL_POINTER;
+  if (N < 1 || H < 1 || W < 1 || C < tdc::kBlockC) return TDC_ERR_BAD_SHAPE;
+  if (C % tdc::kBlockC != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (sms < 1 || ctas_per_sm < 1) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = H + 2 * pad - 2, Q = W + 2 * pad - 2;
+  if (P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
+  const WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  plan[0] = pl.stage_rows;
+  plan[1] = pl.band_rows;
+  plan[2] = pl.bands;
+  plan[3] = pl.qstrips;
+  plan[4] = pl.cblocks;
+  plan[5] = pl.units;
+  plan[6] = pl.grid;
+  plan[7] = int64_t(pl.smem);
+  return TDC_OK;
+}
+
+}  // extern "C"

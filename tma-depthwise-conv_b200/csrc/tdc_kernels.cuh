@@ -1,0 +1,347 @@
+// tdc_kernels.cuh — sm_100a kernels for the NHWC fp16 depthwise 3x3 conv2d
+// forward (stride 1, symmetric zero padding, fp32 accumulation, fp16 out).
+//
+// Arithmetic contract (shared with the CPU oracle, bit for bit):
+//   acc = +0; for r in 0..2: for s in 0..2: acc = fma(fp32(x), fp32(w), acc)
+//   y   = fp16 round-to-nearest-even(acc)
+// with x = 0 outside the image.  This is the per-output computation of the
+// reference kernels (csrc/kernel_v0_naive_float4.cu:37-74 and
+// csrc/kernel_tma_ws.cuh:218-246: r-major, s-minor fp32 chain from 0).
+#pragma once
+
+#include "tdc_ptx.cuh"
+#include "tdc_dwconv.h"
+
+namespace tdc {
+
+// ============================================================================
+// Plain kernel (the `dwconv_v0` call): one thread per 8-channel output vector,
+// 16-byte global loads of x and w for each of the nine taps, no shared memory.
+// 64-bit index arithmetic throughout, grid-stride over all output vectors.
+// ============================================================================
+struct V0Params {
+  int64_t N, H, W, C, P, Q, pad;
+  int64_t total_vecs;  // N*P*Q*C/8
+};
+
+__global__ void __launch_bounds__(256) dwconv_v0_kernel(const uint4* __restrict__ x,
+                                                       const uint4* __restrict__ w,
+                                                       uint4* __restrict__ y, V0Params p) {
+  const int64_t cvecs = p.C / 8;
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < p.total_vecs;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r_ = t;
+    const int64_t cv = r_ % cvecs;  r_ /= cvecs;
+    const int64_t q  = r_ % p.Q;    r_ /= p.Q;
+    const int64_t pp = r_ % p.P;
+    const int64_t n  = r_ / p.P;
+    float acc[8];
+#pragma unroll
+    for (int v = 0; v < 8; ++v) acc[v] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const int64_t h = pp + r - p.pad;
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        const int64_t wi = q + s - p.pad;
+        const uint4 wv = __ldg(&w[(r * 3 + s) * cvecs + cv]);
+        uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+        if (h >= 0 && h < p.H && wi >= 0 && wi < p.W)
+          xv = __ldg(&x[((n * p.H + h) * p.W + wi) * cvecs + cv]);
+        fma2_f16f32(xv.x, wv.x, acc[0], acc[1]);
+        fma2_f16f32(xv.y, wv.y, acc[2], acc[3]);
+        fma2_f16f32(xv.z, wv.z, acc[4], acc[5]);
+        fma2_f16f32(xv.w, wv.w, acc[6], acc[7]);
+      }
+    }
+    uint4 o;
+    o.x = pack_half2_rn(acc[0], acc[1]);
+    o.y = pack_half2_rn(acc[2], acc[3]);
+    o.z = pack_half2_rn(acc[4], acc[5]);
+    o.w = pack_half2_rn(acc[6], acc[7]);
+    y[t] = o;  // t enumerates (n, p, q, cv) with cv innermost == y's layout
+  }
+}
+
+// ============================================================================
+// TMA warp-specialised kernel (the `dwconv_ws` / `dwconv_ws_probe` calls).
+//
+// Work decomposition.  The output is cut into units
+//   (image n, 64-channel block cb, band of `band_rows` output rows, strip of
+//    kStripQ = 32 output columns),
+// enumerated strip-fastest so that units running at the same moment on
+// different SMs are horizontal/vertical neighbours and share their halo
+// columns/rows through L2.  The grid is persistent: CTA b takes units
+// b, b + gridDim.x, …
+//
+// Per unit the producer (warp 0, one thread) streams the band's input rows
+// [p0 - pad, p0 - pad + rows + 2) as TMA boxes of (64 ch, 34 cols,
+// stage_rows rows, 1 image) into an NS-deep shared-memory ring; box
+// coordinates outside the image are zero-filled by the TMA unit, which
+// implements the padding.  Four consumer warps each own 8 output columns; a
+// lane owns one channel pair (a warp covers the 64 channels = 128 B of one
+// column, so every shared-memory read is conflict-free).  Each input row is
+// read from shared memory once per lane and FMA'd into three rows of
+// accumulators (the rows it is tap r = 0, 1, 2 of): a sliding window down
+// the band, so the vertical halo is never re-read.  After a row the oldest
+// accumulator row is complete; it is rounded to fp16 and stored with
+// 128-byte-per-warp coalesced stores.
+// ============================================================================
+constexpr int kBlockC = 64;                        // channels per unit (128 B)
+constexpr int kColsPerWarp = 8;                    // output columns per consumer warp
+constexpr int kConsumerWarps = 4;
+constexpr int kStripQ = kColsPerWarp * kConsumerWarps;  // 32 output columns
+constexpr int kInCols = kStripQ + 2;               // 34 input columns per row
+constexpr int kRowBytes = kInCols * kBlockC * 2;   // 4352 B per ring row
+constexpr int kWsThreads = 32 * (1 + kConsumerWarps);
+
+struct WsParams {
+  const __half* w;
+  __half* y;
+  unsigned long long* stall;  // probe only
+  int32_t H, W, C, P, Q, pad;
+  int32_t qstrips, cblocks, bands, band_rows, stage_rows;
+  int64_t units;  // N * cblocks * bands * qstrips
+  uint64_t timeout_ns;
+  int64_t withhold;  // load index the producer withholds (-1: none)
+};
+
+// Per-device failure record written by the bounded waits:
+// {code, block, stage, load index}.
+__device__ int g_tdc_status[4];
+
+__device__ __forceinline__ void record_failure(int code, int block, int stage, int64_t load) {
+  if (atomicCAS(&g_tdc_status[0], 0, code) == 0) {
+    g_tdc_status[1] = block;
+    g_tdc_status[2] = stage;
+    g_tdc_status[3] = int(load);
+  }
+}
+
+__device__ __forceinline__ void decode_unit(int64_t u, const WsParams& p, int& n, int& cb,
+                                            int& band, int& qs) {
+  qs = int(u % p.qstrips);
+  int64_t t = u / p.qstrips;
+  band = int(t % p.bands);
+  t /= p.bands;
+  cb = int(t % p.cblocks);
+  n = int(t / p.cblocks);
+}
+
+// Accumulators of one output row for one lane: kColsPerWarp columns x 2 channels.
+struct RowAcc {
+  float v[kColsPerWarp * 2];
+};
+
+// Feeds one input row (10 packed fp16 pairs of this lane) into the three
+// accumulator rows it contributes to:
+//   fin = output row completed by this input row (tap r = 2),
+//   mid = output row half way (r = 1),
+//   nw  = output row started by it (r = 0, initialised from +0 here).
+// Within a row, inputs are consumed left to right, so every output sees its
+// taps in (r, s) lexicographic order.
+__device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2],
+                                         const uint32_t (&wt)[9], RowAcc& fin, RowAcc& mid,
+                                         RowAcc& nw) {
+#pragma unroll
+  for (int j = 0; j < kColsPerWarp + 2; ++j) {
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      const int m = j - s;
+      if (m < 0 || m >= kColsPerWarp) continue;
+      if (s == 0) {
+        nw.v[2 * m] = 0.f;
+        nw.v[2 * m + 1] = 0.f;
+      }
+      fma2_f16f32(xr[j], wt[0 * 3 + s], nw.v[2 * m], nw.v[2 * m + 1]);
+      fma2_f16f32(xr[j], wt[1 * 3 + s], mid.v[2 * m], mid.v[2 * m + 1]);
+      fma2_f16f32(xr[j], wt[2 * 3 + s], fin.v[2 * m], fin.v[2 * m + 1]);
+    }
+  }
+}
+
+template <int NS, bool PROBE>
+__global__ void __launch_bounds__(kWsThreads) dwconv_ws_kernel(
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
+  __shared__ __align__(8) uint64_t full_bar[NS];
+  __shared__ __align__(8) uint64_t empty_bar[NS];
+  __shared__ volatile int abort_flag;
+  extern __shared__ uint8_t dyn_smem[];
+  // TMA destinations: 128-byte aligned ring of NS stages.
+  const uint32_t ring = (smem_addr(dyn_smem) + 127u) & ~127u;
+  const uint8_t* ring_ptr = dyn_smem + (ring - smem_addr(dyn_smem));
+  const uint32_t stage_bytes = uint32_t(p.stage_rows) * kRowBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  uint64_t t_start = 0;
+  if constexpr (PROBE) t_start = clock64();
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmap);
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane != 0) return;
+    uint64_t stall_cycles = 0;
+    uint32_t stage = 0, phase = 0;
+    uint32_t armed = 0, armed_parity = 0;  // bit s: stage s has a copy of phase bit
+    int64_t load = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      int n, cb, band, qs;
+      decode_unit(u, p, n, cb, band, qs);
+      const int p0 = band * p.band_rows;
+      const int rows_in = min(p.band_rows, p.P - p0) + 2;
+      const int nst = (rows_in + p.stage_rows - 1) / p.stage_rows;
+      const int32_t c0 = cb * kBlockC;
+      const int32_t w0 = qs * kStripQ - p.pad;
+      const int32_t h0 = p0 - p.pad;
+      for (int t = 0; t < nst; ++t) {
+        const uint32_t eb = smem_addr(&empty_bar[stage]);
+        uint64_t t0 = 0;
+        if constexpr (PROBE) t0 = clock64();
+        if (!mbar_wait_bounded(eb, phase ^ 1u, &abort_flag, true, p.timeout_ns)) {
+          if (!abort_flag) {
+            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load);
+            abort_flag = 1;
+          }
+          ok = false;
+          break;
+        }
+        if constexpr (PROBE) stall_cycles += clock64() - t0;
+        if (load != p.withhold) {
+          const uint32_t fb = smem_addr(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, stage_bytes);
+          tma_load_4d(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, n);
+          armed |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        } else {
+          armed &= ~(1u << stage);
+        }
+        ++load;
+        if (++stage == NS) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // Never leave the CTA while one of its copies may still write shared memory.
+    for (int s = 0; s < NS; ++s) {
+      if (!(armed & (1u << s))) continue;
+      if (!mbar_wait_bounded(smem_addr(&full_bar[s]), (armed_parity >> s) & 1u, &abort_flag,
+                             false, p.timeout_ns)) {
+        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load);
+      }
+    }
+    if constexpr (PROBE) {
+      unsigned long long* row = p.stall + 4ull * blockIdx.x;
+      atomicAdd(row + 0, (unsigned long long)stall_cycles);
+      atomicAdd(row + 2, (unsigned long long)(clock64() - t_start));
+    }
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  const int cw = warp - 1;
+  uint64_t stall_cycles = 0;
+  uint32_t stage = 0, phase = 0;
+  for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x) {
+    int n, cb, band, qs;
+    decode_unit(u, p, n, cb, band, qs);
+    const int p0 = band * p.band_rows;
+    const int rows_out = min(p.band_rows, p.P - p0);
+    const int rows_in = rows_out + 2;
+    const int c0 = cb * kBlockC;
+    const int q_first = qs * kStripQ + cw * kColsPerWarp;
+    const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
+    uint32_t wt[9];
+    {
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(p.w + c0) + lane;
+#pragma unroll
+      for (int k = 0; k < 9; ++k) wt[k] = __ldg(wp + int64_t(k) * (p.C / 2));
+    }
+    __half* yrow = p.y + ((int64_t(n) * p.P + p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
+    const int64_t y_row_stride = int64_t(p.Q) * p.C;
+
+    RowAcc a, b, c;
+#pragma unroll
+    for (int k = 0; k < kColsPerWarp * 2; ++k) a.v[k] = b.v[k] = c.v[k] = 0.f;
+
+    int lr = 0;  // row within the current stage
+    const uint8_t* sbuf = ring_ptr;
+    bool failed = false;
+
+    // One input row: acquire its stage, feed it, store the finished output
+    // row, release the stage after its last row.
+    auto step = [&](int i, RowAcc& fin, RowAcc& mid, RowAcc& nw) {
+      if (lr == 0) {
+        uint64_t t0 = 0;
+        if constexpr (PROBE) t0 = clock64();
+        const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, &abort_flag,
+                                           true, p.timeout_ns);
+        // Keep the warp uniform: one lane giving up makes the whole warp give up.
+        if (__any_sync(0xffffffffu, !got)) {
+          if (lane == 0 && !abort_flag) {
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1);
+            abort_flag = 1;
+          }
+          failed = true;
+          return;
+        }
+        if constexpr (PROBE) stall_cycles += clock64() - t0;
+        sbuf = ring_ptr + stage * stage_bytes;
+      }
+      if (n_valid > 0) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(
+            sbuf + lr * kRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+        uint32_t xr[kColsPerWarp + 2];
+#pragma unroll
+        for (int j = 0; j < kColsPerWarp + 2; ++j) xr[j] = src[j * (kBlockC / 2)];
+        feed_row(xr, wt, fin, mid, nw);
+        if (i >= 2) {
+          __half* dst = yrow + int64_t(i - 2) * y_row_stride;
+#pragma unroll
+          for (int m = 0; m < kColsPerWarp; ++m)
+            if (m < n_valid)
+              *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
+                  pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]);
+        }
+      }
+      if (++lr == p.stage_rows || i == rows_in - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+        lr = 0;
+        if (++stage == NS) { stage = 0; phase ^= 1u; }
+      }
+    };
+
+    // Rows rotate through the three accumulator sets; unrolled by three so
+    // the rotation is resolved at compile time.
+    for (int i = 0; i < rows_in; i += 3) {
+      step(i, a, b, c);
+      if (failed || i + 1 >= rows_in) break;
+      step(i + 1, b, c, a);
+      if (failed || i + 2 >= rows_in) break;
+      step(i + 2, c, a, b);
+      if (failed) break;
+    }
+    if (failed) break;
+  }
+  if constexpr (PROBE) {
+    if (lane == 0) {
+      unsigned long long* row = p.stall + 4ull * blockIdx.x;
+      atomicAdd(row + 1, (unsigned long long)stall_cycles);
+      atomicAdd(row + 3, (unsigned long long)(clock64() - t_start));
+    }
+  }
+}
+
+}  // namespace tdc

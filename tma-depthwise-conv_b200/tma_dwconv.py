@@ -1,0 +1,145 @@
+"""NHWC fp16 depthwise 3x3 conv2d forward on B200 (sm_100a): Python API.
+
+Drop-in for the reference module ``tma_dwconv`` (haowen-han/tma-depthwise-conv
+``tma_dwconv.py:1-110``): the same four public functions with the same
+signatures, argument checks and ``ValueError`` messages, backed by the
+``_tma_dwconv_C`` extension, which calls the C ABI of ``libtdc_sm100.so``.
+There is no CPU fallback: importing this module fails if the extension is not
+built, and every call needs CUDA tensors.
+
+Layouts: x ``[N, H, W, C]`` fp16, w ``[R, S, C]`` fp16 (R = S = 3), output
+``[N, P, Q, C]`` fp16 with P = H + 2*pad - 2, Q = W + 2*pad - 2.  Arithmetic:
+fp32 multiply-add chain over the taps in (r, s) order from +0, one
+round-to-nearest-even to fp16.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+import _tma_dwconv_C as _C  # type: ignore
+
+__all__ = ["dwconv_v0", "dwconv_ws", "dwconv_ws_probe", "ref_dwconv",
+           "dwconv_ws_out", "device_status", "set_wait_timeout_ns", "CONSUMER_WARPS"]
+
+#: Consumer warps per CTA of the ws kernel (divide stall columns 1 and 3 by it
+#: for per-warp figures, as the reference's probe report does).
+CONSUMER_WARPS: int = int(_C.consumer_warps())
+
+
+# ------------------------------ reference ----------------------------------
+
+def ref_dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, pad: int) -> torch.Tensor:
+    """Depthwise conv2d via ``torch.nn.functional.conv2d(groups=C)``.
+
+    Same contract as the reference's ``ref_dwconv`` (``tma_dwconv.py:14-34``):
+    x ``[N,H,W,C]``, w ``[R,S,C]``, symmetric padding; returns ``[N,P,Q,C]``
+    in x's dtype, computed by cuDNN on CUDA tensors or ATen on CPU.
+    """
+    if x_nhwc.dim() != 4 or w_rsc.dim() != 3:
+        raise ValueError("x must be [N,H,W,C] and w must be [R,S,C]")
+    C = x_nhwc.shape[3]
+    if C != w_rsc.shape[2]:
+        raise ValueError("channel mismatch between x and w")
+    x = x_nhwc.permute(0, 3, 1, 2).contiguous()
+    w = w_rsc.permute(2, 0, 1).unsqueeze(1).contiguous()
+    y = F.conv2d(x, w, bias=None, stride=1, padding=pad, groups=C)
+    return y.permute(0, 2, 3, 1).contiguous()
+
+
+# ------------------------------ validation ---------------------------------
+
+def _check(x: torch.Tensor, w: torch.Tensor, pad: int) -> None:
+    # Same checks and messages as the reference (tma_dwconv.py:39-53).
+    if not (x.is_cuda and w.is_cuda):
+        raise ValueError("x and w must be CUDA tensors")
+    if x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise ValueError("x and w must be fp16")
+    if x.dim() != 4:
+        raise ValueError(f"x must be [N,H,W,C], got shape {tuple(x.shape)}")
+    if w.dim() != 3:
+        raise ValueError(f"w must be [R,S,C], got shape {tuple(w.shape)}")
+    if x.shape[3] != w.shape[2]:
+        raise ValueError("x and w must agree on C")
+    if not (x.is_contiguous() and w.is_contiguous()):
+        raise ValueError("x and w must be contiguous")
+    if pad < 0:
+        raise ValueError("pad must be non-negative")
+
+
+def _check_ws(x: torch.Tensor, w: torch.Tensor, pad: int, n_stage: int, name: str) -> None:
+    _check(x, w, pad)
+    if x.shape[3] % 64 != 0:
+        raise ValueError(f"{name} requires C % 64 == 0")
+    if n_stage not in (2, 3, 4):
+        raise ValueError(f"n_stage must be one of {{2, 3, 4}}, got {n_stage}")
+
+
+# ------------------------------ public API ---------------------------------
+
+def dwconv_v0(x: torch.Tensor, w: torch.Tensor, pad: int = 1) -> torch.Tensor:
+    """Plain kernel: direct 16-byte global loads, 8 channels per thread (C % 8 == 0)."""
+    _check(x, w, pad)
+    return _C.dwconv_v0(x, w, int(pad))
+
+
+def dwconv_ws(x: torch.Tensor, w: torch.Tensor,
+              pad: int = 1, n_stage: int = 2) -> torch.Tensor:
+    """TMA + warp-specialised depthwise conv2d.
+
+    Args:
+        x: [N, H, W, C] fp16, contiguous, C % 64 == 0.
+        w: [R, S, C]    fp16, contiguous.
+        pad: zero-padding on both H and W.
+        n_stage: shared-memory ring depth (pipeline stages). Supported: 2, 3, 4.
+    """
+    _check_ws(x, w, pad, n_stage, "dwconv_ws")
+    return _C.dwconv_ws(x, w, int(pad), int(n_stage))
+
+
+def dwconv_ws_out(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
+                  pad: int = 1, n_stage: int = 2) -> torch.Tensor:
+    """``dwconv_ws`` writing into a preallocated contiguous ``y [N,P,Q,C]``."""
+    _check_ws(x, w, pad, n_stage, "dwconv_ws_out")
+    return _C.dwconv_ws_out(x, w, y, int(pad), int(n_stage))
+
+
+def dwconv_ws_probe(x: torch.Tensor, w: torch.Tensor,
+                    pad: int = 1, n_stage: int = 2):
+    """Same as ``dwconv_ws`` but instruments producer/consumer stalls.
+
+    Returns:
+        (y, stall): ``y`` is the output tensor; ``stall`` is an int64 CUDA
+        tensor of shape ``[num_blocks, 4]``, one row per CTA of the launch
+        (the ws grid is persistent, so ``num_blocks`` is the number of CTAs
+        resident across the GPU, at most the number of work units):
+
+          * col 0 — producer cycles waiting on ``empty`` barriers
+          * col 1 — consumer cycles waiting on ``full`` barriers, summed over
+                    the ``CONSUMER_WARPS`` consumer warps
+          * col 2 — producer lifetime (cycles)
+          * col 3 — consumer lifetime, summed over consumer warps
+
+        Compare ``mean(col 0)`` with ``mean(col 1)/CONSUMER_WARPS``:
+          * col0 >> col1  -> consumers are slower; the producer waits for them.
+          * col1 >> col0  -> loads are slower; consumers wait for data.
+    """
+    _check_ws(x, w, pad, n_stage, "dwconv_ws_probe")
+    return _C.dwconv_ws_probe(x, w, int(pad), int(n_stage))
+
+
+def device_status(device: int | None = None, clear: bool = True):
+    """First pipeline-wait failure recorded on ``device`` as (code, block, stage, load).
+
+    code 0 means none; 1 = a consumer gave up waiting for a filled stage,
+    2 = the producer gave up waiting for a free stage, 3 = an issued copy never
+    completed.  Synchronises the device.
+    """
+    if device is None:
+        device = torch.cuda.current_device()
+    return _C.device_status(int(device), bool(clear))
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    """Limit of every pipeline wait in later ws launches (default 2 s)."""
+    _C.set_wait_timeout_ns(int(ns))
