@@ -23,7 +23,8 @@
  * and re-entrant; it may be called from any host thread.
  *
  * Return value: TDC_OK (0) or a negative TDC_ERR_* code.  Argument errors are
- * detected on the host before any CUDA call is made.
+ * detected on the host before any CUDA call is made.  An empty output
+ * (N, C, P or Q == 0) is a successful no-op and may come with NULL pointers.
  */
 #ifndef TDC_DWCONV_H_
 #define TDC_DWCONV_H_
@@ -43,7 +44,7 @@ extern "C" {
 /* ---- status codes ------------------------------------------------------- */
 #define TDC_OK                    0
 #define TDC_ERR_NULL_POINTER     -1  /* x, w, y (or stall for the probe) is NULL          */
-#define TDC_ERR_BAD_SHAPE        -2  /* N,H,W,C < 1, or the output would be empty          */
+#define TDC_ERR_BAD_SHAPE        -2  /* N or C < 0, H or W < 1, or a negative output size  */
 #define TDC_ERR_FILTER_SHAPE     -3  /* R != 3 or S != 3                                     */
 #define TDC_ERR_CHANNELS         -4  /* C not a multiple of 8 (v0) / 64 (ws)                 */
 #define TDC_ERR_PAD              -5  /* pad < 0                                             */

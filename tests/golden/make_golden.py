@@ -28,9 +28,9 @@ CASES = [  # N, H, W, C, pad
     (2, 16, 16, 64, 2),
     (2, 16, 16, 64, 3),
     (1, 8, 8, 64, 1),
-    (3, 7, 45, 128, 1),
+    (2, 7, 45, 64, 1),
     (1, 5, 33, 64, 2),
-    (2, 9, 34, 192, 1),
+    (1, 9, 34, 128, 1),
 ]
 
 

@@ -1,0 +1,79 @@
+"""Python API argument checks, on the host (no GPU needed).
+
+The checks and ValueError messages must be those of the reference's
+tma_dwconv.py:39-53, 74-77 and 106-109, in the same order, so callers that
+match on them keep working.  Tensors that pass the CUDA check are stood in
+for by a small object exposing the attributes the checks read.
+"""
+import pytest
+import torch
+
+import tma_dwconv as T
+
+
+class FakeCuda:
+    def __init__(self, shape, dtype=torch.float16, contiguous=True):
+        self.shape = tuple(shape)
+        self.dtype = dtype
+        self.is_cuda = True
+        self._c = contiguous
+
+    def dim(self):
+        return len(self.shape)
+
+    def is_contiguous(self):
+        return self._c
+
+
+X = FakeCuda((2, 16, 16, 64))
+W = FakeCuda((3, 3, 64))
+
+
+@pytest.mark.parametrize("x,w,pad,msg", [
+    (torch.zeros(2, 16, 16, 64, dtype=torch.float16), W, 1, "x and w must be CUDA tensors"),
+    (FakeCuda((2, 16, 16, 64), torch.float32), W, 1, "x and w must be fp16"),
+    (X, FakeCuda((3, 3, 64), torch.bfloat16), 1, "x and w must be fp16"),
+    (FakeCuda((16, 16, 64)), W, 1, r"x must be \[N,H,W,C\], got shape \(16, 16, 64\)"),
+    (X, FakeCuda((9, 64)), 1, r"w must be \[R,S,C\], got shape \(9, 64\)"),
+    (X, FakeCuda((3, 3, 32)), 1, "x and w must agree on C"),
+    (FakeCuda((2, 16, 16, 64), contiguous=False), W, 1, "x and w must be contiguous"),
+    (X, W, -1, "pad must be non-negative"),
+])
+def test_check_messages(x, w, pad, msg):
+    for fn in (T.dwconv_v0, T.dwconv_ws, T.dwconv_ws_probe):
+        with pytest.raises(ValueError, match=msg):
+            fn(x, w, pad)
+
+
+def test_ws_specific_checks():
+    x, w = FakeCuda((2, 16, 16, 96)), FakeCuda((3, 3, 96))
+    with pytest.raises(ValueError, match=r"dwconv_ws requires C % 64 == 0"):
+        T.dwconv_ws(x, w, 1)
+    with pytest.raises(ValueError, match=r"dwconv_ws_probe requires C % 64 == 0"):
+        T.dwconv_ws_probe(x, w, 1)
+    for bad in (1, 5, 0):
+        with pytest.raises(ValueError, match=r"n_stage must be one of \{2, 3, 4\}, got %d" % bad):
+            T.dwconv_ws(X, W, 1, bad)
+
+
+def test_ref_dwconv_on_cpu_matches_layout_contract():
+    torch.manual_seed(0)
+    x = torch.randn(2, 9, 11, 64)
+    w = torch.randn(3, 3, 64)
+    y = T.ref_dwconv(x, w, 1)
+    assert y.shape == (2, 9, 11, 64) and y.is_contiguous()
+    ref = torch.nn.functional.conv2d(x.permute(0, 3, 1, 2), w.permute(2, 0, 1).unsqueeze(1), padding=1,
+                                     groups=64).permute(0, 2, 3, 1)
+    torch.testing.assert_close(y, ref)
+    with pytest.raises(ValueError, match="channel mismatch"):
+        T.ref_dwconv(x, torch.randn(3, 3, 32), 1)
+    with pytest.raises(ValueError, match=r"x must be \[N,H,W,C\] and w must be \[R,S,C\]"):
+        T.ref_dwconv(x[0], w, 1)
+
+
+def test_extension_surface():
+    for name in ("dwconv_v0", "dwconv_ws", "dwconv_ws_probe", "dwconv_ws_out", "device_status",
+                 "set_wait_timeout_ns", "consumer_warps", "dwconv_ws_withhold"):
+        assert hasattr(T._C, name), name
+    assert T.CONSUMER_WARPS == 4
+    assert "libtdc_sm100" not in T._C.__file__ and T._C.__file__.startswith(T.__file__.rsplit("/", 1)[0])

@@ -1,0 +1,121 @@
+"""The CPU oracle, pinned before it is trusted (no GPU needed).
+
+* its fp16 codec: decode exact for all 65536 bit patterns, encode equal to
+  IEEE round-to-nearest-even (numpy) on dense samples around every boundary;
+* the C restatement and the numpy restatement agree bit for bit;
+* both reproduce the golden vectors recorded from the reference's own
+  dwconv_ws and dwconv_v0 kernels on a B200 (tests/golden/ref_kernels.npz,
+  made by tests/golden/make_golden.py) bit for bit;
+* against float32 torch conv2d(groups=C) the error is within one fp16 ulp
+  plus 1e-3.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ref_kernels.npz")
+
+
+def test_decode_all_bit_patterns():
+    lib = oracle.load()
+    h = np.arange(65536, dtype=np.uint16)
+    ref = h.view(np.float16).astype(np.float32)
+    got = np.array([lib.oracle_f16_to_f32(int(v)) for v in h], dtype=np.float32)
+    same = (got.view(np.uint32) == ref.view(np.uint32)) | (np.isnan(got) & np.isnan(ref))
+    assert same.all()
+
+
+def test_encode_round_to_nearest_even():
+    lib = oracle.load()
+    rng = np.random.default_rng(1)
+    parts = [rng.standard_normal(4000).astype(np.float32) * s
+             for s in (1e-9, 3e-8, 6e-8, 1e-7, 1e-6, 6e-5, 1e-3, 1.0, 300.0, 6e4)]
+    # every fp16 value, the midpoints between neighbours and their fp32 neighbours
+    f16 = np.arange(0, 0x7c00, dtype=np.uint16).view(np.float16).astype(np.float64)
+    mids = ((f16[:-1] + f16[1:]) / 2).astype(np.float32)
+    parts += [f16.astype(np.float32)[::3], mids[::5], np.nextafter(mids[::7], np.float32(np.inf)),
+              np.nextafter(mids[::7], np.float32(0)),
+              np.array([65504, 65519, 65519.996, 65520, 65536, 1e30, np.inf, -np.inf, 0.0, -0.0,
+                        2.0 ** -25, 2.0 ** -24, 3 * 2.0 ** -26, 2.0 ** -14], np.float32)]
+    f = np.concatenate(parts)
+    f = np.concatenate([f, -f])
+    got = np.array([lib.oracle_f32_to_f16(float(v)) for v in f], dtype=np.uint16)
+    with np.errstate(over="ignore"):
+        exp = f.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, exp), f[got != exp][:10]
+
+
+@pytest.mark.parametrize("shape,pad", [((2, 16, 16, 64), 1), ((1, 7, 45, 128), 0), ((3, 5, 33, 8), 2),
+                                       ((1, 1, 1, 64), 1), ((2, 3, 3, 16), 5), ((1, 30, 2, 24), 3)])
+def test_c_and_numpy_restatements_agree(shape, pad):
+    rng = np.random.default_rng(sum(shape) + pad)
+    x = rng.standard_normal(shape).astype(np.float16)
+    w = (rng.standard_normal((3, 3, shape[3])) / 3).astype(np.float16)
+    a = oracle.dwconv_f16(x, w, pad)
+    b = oracle.dwconv_f16_numpy(x, w, pad)
+    assert a.shape == (shape[0], shape[1] + 2 * pad - 2, shape[2] + 2 * pad - 2, shape[3])
+    assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+    assert np.array_equal(a.view(np.uint16), oracle.dwconv_f16(x, w, pad, threads=1).view(np.uint16))
+
+
+def test_special_values_propagate():
+    x = np.zeros((1, 4, 4, 8), np.float16)
+    x[0, 1, 1, 0] = np.inf
+    x[0, 2, 2, 1] = np.nan
+    x[0, 0, 0, 2] = 60000
+    x[0, 0, 1, 2] = 60000  # the fp32 sum overflows fp16 -> inf
+    w = np.ones((3, 3, 8), np.float16)
+    w[..., 3] = np.inf  # padding taps multiply 0 * inf = nan
+    a, b = oracle.dwconv_f16(x, w, 1), oracle.dwconv_f16_numpy(x, w, 1)
+    assert np.array_equal(np.isnan(a), np.isnan(b))
+    m = ~np.isnan(a)
+    assert np.array_equal(a[m].view(np.uint16), b[m].view(np.uint16))
+    assert np.isinf(a[0, 0, 0, 0]) and np.isnan(a[0, 1, 1, 1]) and np.isinf(a[0, 0, 0, 2])
+    assert np.isnan(a[..., 3]).all()
+
+
+def test_empty_and_invalid():
+    x = np.zeros((2, 2, 2, 64), np.float16)
+    w = np.zeros((3, 3, 64), np.float16)
+    assert oracle.dwconv_f16(x, w, 0).shape == (2, 0, 0, 64)
+    with pytest.raises(ValueError):
+        oracle.dwconv_f16(np.zeros((1, 1, 1, 8), np.float16), np.zeros((3, 3, 8), np.float16), 0)
+    with pytest.raises(ValueError):
+        oracle.dwconv_f16(x, np.zeros((3, 3, 32), np.float16), 1)
+
+
+@pytest.mark.parametrize("shape,pad", [((2, 16, 16, 64), 1), ((1, 56, 56, 256), 1), ((2, 9, 37, 128), 2)])
+def test_within_ulp_of_fp32_conv(shape, pad):
+    torch.manual_seed(0)
+    x = torch.randn(shape).half()
+    w = (torch.randn(3, 3, shape[3]) / 3).half()
+    ref = torch.nn.functional.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(2, 0, 1).unsqueeze(1),
+                                     padding=pad, groups=shape[3]).permute(0, 2, 3, 1).numpy()
+    y = oracle.dwconv_f16(x.numpy(), w.numpy(), pad).astype(np.float32)
+    assert (np.abs(y - ref) <= oracle.f16_ulp(ref) + 1e-3).all()
+
+
+def _golden_cases():
+    if not os.path.exists(GOLDEN):
+        return []
+    z = np.load(GOLDEN)
+    return sorted({k.split("_")[0] for k in z.files})
+
+
+@pytest.mark.parametrize("case", _golden_cases() or ["missing"])
+def test_matches_reference_golden_vectors(case):
+    if case == "missing":
+        pytest.fail(f"golden vectors missing: {GOLDEN}")
+    z = np.load(GOLDEN)
+    N, H, W, C, pad = (int(v) for v in z[f"{case}_shape"])
+    x = z[f"{case}_x"].view(np.float16)
+    w = z[f"{case}_w"].view(np.float16)
+    assert x.shape == (N, H, W, C)
+    got = oracle.dwconv_f16(x, w, pad).view(np.uint16)
+    assert np.array_equal(got, z[f"{case}_ws"]), "oracle != reference dwconv_ws"
+    assert np.array_equal(got, z[f"{case}_v0"]), "oracle != reference dwconv_v0"
+    assert np.array_equal(oracle.dwconv_f16_numpy(x, w, pad).view(np.uint16), z[f"{case}_ws"])

@@ -49,13 +49,15 @@ DeviceInfo g_dev[kMaxDevices];
 
 constexpr int kMaxDynSmem = 200 * 1024;
 
+int stage_rows_for(int64_t n_stage);
+
 template <int NS, bool PROBE>
 cudaError_t prepare_ws(int* occ) {
   auto* k = &tdc::dwconv_ws_kernel<NS, PROBE>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   if (e != cudaSuccess) return e;
-  // Occupancy at the largest ring any plan uses (stage_rows * NS <= 9 rows).
-  const size_t smem = size_t(9) * tdc::kRowBytes + 128;
+  // Occupancy at the ring this instantiation uses.
+  const size_t smem = size_t(NS) * stage_rows_for(NS) * tdc::kRowBytes + 128;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
 }
 
@@ -105,10 +107,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Common validation of the reference launchers (kernel_tma_ws.cu:54-65,
 // kernel_v0_naive_float4.cu:84-94), in the same order.
+// An empty output (N, C, P or Q zero) is valid and needs no pointers: torch
+// hands out null data pointers for zero-element tensors.
 int validate(const void* x, const void* w, const void* y, int64_t N, int64_t H, int64_t W,
              int64_t C, int64_t R, int64_t S, int64_t pad, int64_t cmult, int64_t* P,
-             int64_t* Q) {
-  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
+             int64_t* Q, bool* empty) {
   if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
   if (R != 3 || S != 3) return TDC_ERR_FILTER_SHAPE;
   if (C % cmult != 0) return TDC_ERR_CHANNELS;
@@ -117,6 +120,9 @@ int validate(const void* x, const void* w, const void* y, int64_t N, int64_t H, 
   *P = H + 2 * pad - R + 1;
   *Q = W + 2 * pad - S + 1;
   if (*P < 0 || *Q < 0) return TDC_ERR_BAD_SHAPE;
+  *empty = N == 0 || C == 0 || *P == 0 || *Q == 0;
+  if (*empty) return TDC_OK;
+  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return TDC_ERR_ALIGNMENT;
   return TDC_OK;
 }
@@ -130,7 +136,16 @@ struct WsPlan {
   size_t smem;
 };
 
-int stage_rows_for(int64_t n_stage) { return n_stage == 2 ? 4 : n_stage == 3 ? 3 : 2; }
+// Ring capacity in input rows per CTA, split evenly over the n_stage stages,
+// and the number of waves of units the planner aims for.
+#ifndef TDC_RING_ROWS
+#define TDC_RING_ROWS 8
+#endif
+#ifndef TDC_WAVES
+#define TDC_WAVES 16
+#endif
+
+int stage_rows_for(int64_t n_stage) { return std::max<int>(1, TDC_RING_ROWS / int(n_stage)); }
 
 // Band height: enough units for ~16 waves of persistent CTAs (so the last,
 // partial wave costs little), bands no shorter than two stages, and
@@ -143,7 +158,7 @@ WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, in
   pl.cblocks = int(C / tdc::kBlockC);
   const int64_t strips = N * pl.cblocks * pl.qstrips;
   const int64_t g0 = std::max<int64_t>(1, sms * ctas_per_sm);
-  const int64_t want_units = 16 * g0;
+  const int64_t want_units = int64_t(TDC_WAVES) * g0;
   const int64_t want_bands = std::max<int64_t>(1, (want_units + strips - 1) / std::max<int64_t>(strips, 1));
   int64_t band = (P + want_bands - 1) / want_bands;
   band = std::max<int64_t>(band, std::max(2 * pl.stage_rows - 2, 6));
@@ -206,13 +221,14 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
               int64_t R, int64_t S, int64_t pad, int64_t n_stage, unsigned long long* stall,
               bool probe, int64_t withhold, int64_t timeout_ns, void* stream) {
   int64_t P = 0, Q = 0;
-  int rc = validate(x, w, y, N, H, W, C, R, S, pad, tdc::kBlockC, &P, &Q);
+  bool empty = false;
+  int rc = validate(x, w, y, N, H, W, C, R, S, pad, tdc::kBlockC, &P, &Q, &empty);
   if (rc != TDC_OK) return rc;
   if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
-  if (probe && !stall) return TDC_ERR_NULL_POINTER;
   rc = check_ws_limits(N, H, W, C, P, Q);
   if (rc != TDC_OK) return rc;
-  if (N == 0 || C == 0 || P == 0 || Q == 0) return TDC_OK;  // empty output: nothing to do
+  if (empty) return TDC_OK;  // nothing to do
+  if (probe && !stall) return TDC_ERR_NULL_POINTER;
   DeviceInfo* dev = nullptr;
   rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;
@@ -279,9 +295,10 @@ TDC_API int tdc_output_hw(int64_t H, int64_t W, int64_t R, int64_t S, int64_t pa
 TDC_API int tdc_dwconv_v0(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
                           int64_t C, int64_t R, int64_t S, int64_t pad, void* stream) {
   int64_t P = 0, Q = 0;
-  int rc = validate(x, w, y, N, H, W, C, R, S, pad, 8, &P, &Q);
+  bool empty = false;
+  int rc = validate(x, w, y, N, H, W, C, R, S, pad, 8, &P, &Q, &empty);
   if (rc != TDC_OK) return rc;
-  if (N == 0 || C == 0 || P == 0 || Q == 0) return TDC_OK;
+  if (empty) return TDC_OK;
   DeviceInfo* dev = nullptr;
   rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;

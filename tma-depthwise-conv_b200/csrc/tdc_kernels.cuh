@@ -128,40 +128,99 @@ __device__ __forceinline__ void decode_unit(int64_t u, const WsParams& p, int& n
   n = int(t / p.cblocks);
 }
 
+// Output stores: the result is written once and never read back by the
+// kernel, so it may be marked streaming (evict-first).
+#ifndef TDC_STORE_MODE
+#define TDC_STORE_MODE 0
+#endif
+__device__ __forceinline__ void store_out(__half* dst, uint32_t v) {
+#if TDC_STORE_MODE == 1
+  asm volatile("st.global.cs.b32 [%0], %1;" ::"l"(dst), "r"(v) : "memory");
+#else
+  *reinterpret_cast<uint32_t*>(dst) = v;
+#endif
+}
+
+// Consumer arithmetic.  TDC_MATH selects how the fp16 x fp16 -> fp32 FMAs are
+// issued; every variant performs the same IEEE operations in the same order.
+//   0: fma.rn.f32.f16 per channel (operands stay fp16)
+//   1: one cvt per input element, packed fp32 FMA (fma.rn.f32x2) per channel pair
+//   2: one cvt per input element, scalar fp32 FMA per channel
+#ifndef TDC_MATH
+#define TDC_MATH 1
+#endif
+
 // Accumulators of one output row for one lane: kColsPerWarp columns x 2 channels.
 struct RowAcc {
   float v[kColsPerWarp * 2];
 };
 
-// Feeds one input row (10 packed fp16 pairs of this lane) into the three
-// accumulator rows it contributes to:
+#if TDC_MATH == 0
+using Taps = uint32_t[9];  // packed fp16 pair per tap
+__device__ __forceinline__ void load_taps(const uint32_t* wp, int64_t stride, Taps& t) {
+#pragma unroll
+  for (int k = 0; k < 9; ++k) t[k] = __ldg(wp + k * stride);
+}
+#else
+using Taps = float[18];  // fp32 pair per tap
+__device__ __forceinline__ void load_taps(const uint32_t* wp, int64_t stride, Taps& t) {
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    const float2 f = unpack_half2(__ldg(wp + k * stride));
+    t[2 * k] = f.x;
+    t[2 * k + 1] = f.y;
+  }
+}
+#endif
+
+// acc(pair) = x(pair) * w(tap) + acc(pair), or x * w + 0 when `first`.
+__device__ __forceinline__ void tap_fma(uint32_t xh, float x0, float x1, const Taps& t, int k,
+                                        float& a0, float& a1, bool first) {
+  if (first) { a0 = 0.f; a1 = 0.f; }
+#if TDC_MATH == 0
+  fma2_f16f32(xh, t[k], a0, a1);
+#elif TDC_MATH == 1
+  ffma2(x0, x1, t[2 * k], t[2 * k + 1], a0, a1);
+#else
+  a0 = __fmaf_rn(x0, t[2 * k], a0);
+  a1 = __fmaf_rn(x1, t[2 * k + 1], a1);
+#endif
+}
+
+// Feeds one input row (kColsPerWarp + 2 packed fp16 pairs of this lane) into
+// the three accumulator rows it contributes to:
 //   fin = output row completed by this input row (tap r = 2),
 //   mid = output row half way (r = 1),
 //   nw  = output row started by it (r = 0, initialised from +0 here).
 // Within a row, inputs are consumed left to right, so every output sees its
 // taps in (r, s) lexicographic order.
-__device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2],
-                                         const uint32_t (&wt)[9], RowAcc& fin, RowAcc& mid,
-                                         RowAcc& nw) {
+__device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2], const Taps& wt,
+                                         RowAcc& fin, RowAcc& mid, RowAcc& nw) {
 #pragma unroll
   for (int j = 0; j < kColsPerWarp + 2; ++j) {
+    float x0 = 0.f, x1 = 0.f;
+#if TDC_MATH != 0
+    const float2 xf = unpack_half2(xr[j]);
+    x0 = xf.x;
+    x1 = xf.y;
+#endif
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
       const int m = j - s;
       if (m < 0 || m >= kColsPerWarp) continue;
-      if (s == 0) {
-        nw.v[2 * m] = 0.f;
-        nw.v[2 * m + 1] = 0.f;
-      }
-      fma2_f16f32(xr[j], wt[0 * 3 + s], nw.v[2 * m], nw.v[2 * m + 1]);
-      fma2_f16f32(xr[j], wt[1 * 3 + s], mid.v[2 * m], mid.v[2 * m + 1]);
-      fma2_f16f32(xr[j], wt[2 * 3 + s], fin.v[2 * m], fin.v[2 * m + 1]);
+      tap_fma(xr[j], x0, x1, wt, 0 * 3 + s, nw.v[2 * m], nw.v[2 * m + 1], s == 0);
+      tap_fma(xr[j], x0, x1, wt, 1 * 3 + s, mid.v[2 * m], mid.v[2 * m + 1], false);
+      tap_fma(xr[j], x0, x1, wt, 2 * 3 + s, fin.v[2 * m], fin.v[2 * m + 1], false);
     }
   }
 }
 
+#ifndef TDC_MIN_BLOCKS
+#define TDC_MIN_BLOCKS 1
+#endif
+
 template <int NS, bool PROBE>
-__global__ void __launch_bounds__(kWsThreads) dwconv_ws_kernel(
+__global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
   __shared__ __align__(8) uint64_t full_bar[NS];
   __shared__ __align__(8) uint64_t empty_bar[NS];
@@ -262,12 +321,8 @@ __global__ void __launch_bounds__(kWsThreads) dwconv_ws_kernel(
     const int c0 = cb * kBlockC;
     const int q_first = qs * kStripQ + cw * kColsPerWarp;
     const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
-    uint32_t wt[9];
-    {
-      const uint32_t* wp = reinterpret_cast<const uint32_t*>(p.w + c0) + lane;
-#pragma unroll
-      for (int k = 0; k < 9; ++k) wt[k] = __ldg(wp + int64_t(k) * (p.C / 2));
-    }
+    Taps wt;
+    load_taps(reinterpret_cast<const uint32_t*>(p.w + c0) + lane, p.C / 2, wt);
     __half* yrow = p.y + ((int64_t(n) * p.P + p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
     const int64_t y_row_stride = int64_t(p.Q) * p.C;
 
@@ -311,8 +366,7 @@ __global__ void __launch_bounds__(kWsThreads) dwconv_ws_kernel(
 #pragma unroll
           for (int m = 0; m < kColsPerWarp; ++m)
             if (m < n_valid)
-              *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
-                  pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]);
+              store_out(dst + int64_t(m) * p.C, pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]));
         }
       }
       if (++lr == p.stage_rows || i == rows_in - 1) {
