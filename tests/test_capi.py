@@ -135,7 +135,6 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
     assert pl["stage_rows"] >= 1
     assert pl["cblocks"] == Cc // 64 and pl["qstrips"] == -(-Q // 32)
     assert pl["bands"] * pl["band_rows"] >= P > (pl["bands"] - 1) * pl["band_rows"]
-    assert pl["band_rows"] == P or (pl["band_rows"] + 2) % pl["stage_rows"] == 0
     assert pl["units"] == N * pl["cblocks"] * pl["qstrips"] * pl["bands"]
     assert 1 <= pl["grid"] <= min(pl["units"], 148 * 4)
     assert pl["smem"] == ns * pl["stage_rows"] * 34 * 128 + 128 <= 227 * 1024
@@ -156,6 +155,9 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
 
 
 def test_plan_balances_the_headline_shape(lib):
-    pl = _plan(lib, 64, 224, 336, 256, 1, 2)
-    waves = pl["units"] / pl["grid"]
-    assert waves >= 16 - 1e-9
+    # makespan (units per CTA x rows a unit streams) within 6% of a perfect split
+    for occ in (3, 4):
+        pl = _plan(lib, 64, 224, 336, 256, 1, 2, occ=occ)
+        per_cta = -(-pl["units"] // pl["grid"])
+        ideal = 64 * 4 * 11 * 224 / pl["grid"]
+        assert per_cta * pl["band_rows"] <= 1.06 * ideal

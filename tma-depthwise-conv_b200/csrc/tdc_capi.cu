@@ -139,7 +139,7 @@ struct WsPlan {
 // Ring capacity in input rows per CTA, split evenly over the n_stage stages,
 // and the number of waves of units the planner aims for.
 #ifndef TDC_RING_ROWS
-#define TDC_RING_ROWS 8
+#define TDC_RING_ROWS 12
 #endif
 #ifndef TDC_WAVES
 #define TDC_WAVES 16
@@ -147,9 +147,20 @@ struct WsPlan {
 
 int stage_rows_for(int64_t n_stage) { return std::max<int>(1, TDC_RING_ROWS / int(n_stage)); }
 
-// Band height: enough units for ~16 waves of persistent CTAs (so the last,
-// partial wave costs little), bands no shorter than two stages, and
-// band_rows + 2 a multiple of stage_rows so no stage carries unused rows.
+#ifndef TDC_PLAN
+#define TDC_PLAN 1
+#endif
+// Relative cost of a streamed row that produces no output row of its own
+// (halo rows mostly come from L2, not HBM).
+#ifndef TDC_HALO_W
+#define TDC_HALO_W 0.5
+#endif
+
+// Band height.  Every CTA of the persistent grid takes every grid-th unit, so
+// the kernel lasts ceil(units / grid) units; each unit streams its band plus a
+// 2-row halo, rounded up to whole stages.  The planner picks the band count
+// that minimises (units per CTA) x (rows a unit streams), i.e. it trades the
+// last partial wave against the halo rows of shorter bands.
 WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
                  int64_t ctas_per_sm) {
   WsPlan pl{};
@@ -158,12 +169,31 @@ WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, in
   pl.cblocks = int(C / tdc::kBlockC);
   const int64_t strips = N * pl.cblocks * pl.qstrips;
   const int64_t g0 = std::max<int64_t>(1, sms * ctas_per_sm);
+  const int64_t sr = pl.stage_rows;
+#if TDC_PLAN == 0
   const int64_t want_units = int64_t(TDC_WAVES) * g0;
   const int64_t want_bands = std::max<int64_t>(1, (want_units + strips - 1) / std::max<int64_t>(strips, 1));
   int64_t band = (P + want_bands - 1) / want_bands;
-  band = std::max<int64_t>(band, std::max(2 * pl.stage_rows - 2, 6));
-  while ((band + 2) % pl.stage_rows != 0) ++band;
+  band = std::max<int64_t>(band, std::max<int64_t>(2 * sr - 2, 6));
+  while ((band + 2) % sr != 0) ++band;
   band = std::min<int64_t>(band, P);
+#else
+  int64_t band = P;
+  double best = -1.0;
+  const int64_t max_bands = std::min<int64_t>(P, 64);
+  for (int64_t b = 1; b <= max_bands; ++b) {
+    const int64_t rows = (P + b - 1) / b;
+    if (b > 1 && (P + rows - 1) / rows != b) continue;  // same band height as a smaller b
+    const int64_t units = strips * b;
+    const int64_t per_cta = (units + g0 - 1) / g0;
+    const int64_t streamed = ((rows + 2 + sr - 1) / sr) * sr;
+    const double cost = double(per_cta) * (double(rows) + TDC_HALO_W * double(streamed - rows));
+    if (best < 0 || cost < best) {
+      best = cost;
+      band = rows;
+    }
+  }
+#endif
   pl.band_rows = int(std::max<int64_t>(band, 1));
   pl.bands = int((P + pl.band_rows - 1) / pl.band_rows);
   pl.units = strips * pl.bands;
@@ -184,6 +214,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+#ifndef TDC_L2_PROMO
+#define TDC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
+
 // 4-D map over x viewed as (C, W, H, N), innermost first; box
 // (64 ch, 34 cols, stage_rows rows, 1 image); out-of-bounds elements read 0.
 int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t W, int64_t C,
@@ -197,7 +231,7 @@ int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t 
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  TDC_L2_PROMO, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
 }
 

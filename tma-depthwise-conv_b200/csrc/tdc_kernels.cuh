@@ -118,14 +118,28 @@ __device__ __forceinline__ void record_failure(int code, int block, int stage, i
   }
 }
 
+#ifndef TDC_ORDER
+#define TDC_ORDER 1
+#endif
 __device__ __forceinline__ void decode_unit(int64_t u, const WsParams& p, int& n, int& cb,
                                             int& band, int& qs) {
+#if TDC_ORDER == 0
+  // (n, cb, band, qs), strip fastest
   qs = int(u % p.qstrips);
   int64_t t = u / p.qstrips;
   band = int(t % p.bands);
   t /= p.bands;
   cb = int(t % p.cblocks);
   n = int(t / p.cblocks);
+#else
+  // (n, band, qs, cb), channel block fastest
+  cb = int(u % p.cblocks);
+  int64_t t = u / p.cblocks;
+  qs = int(t % p.qstrips);
+  t /= p.qstrips;
+  band = int(t % p.bands);
+  n = int(t / p.bands);
+#endif
 }
 
 // Output stores: the result is written once and never read back by the
@@ -133,9 +147,14 @@ __device__ __forceinline__ void decode_unit(int64_t u, const WsParams& p, int& n
 #ifndef TDC_STORE_MODE
 #define TDC_STORE_MODE 0
 #endif
-__device__ __forceinline__ void store_out(__half* dst, uint32_t v) {
+#ifndef TDC_LOAD_POLICY
+#define TDC_LOAD_POLICY 0
+#endif
+__device__ __forceinline__ void store_out(__half* dst, uint32_t v, uint64_t policy) {
 #if TDC_STORE_MODE == 1
   asm volatile("st.global.cs.b32 [%0], %1;" ::"l"(dst), "r"(v) : "memory");
+#elif TDC_STORE_MODE == 2
+  st_global_hint(dst, v, policy);
 #else
   *reinterpret_cast<uint32_t*>(dst) = v;
 #endif
@@ -147,7 +166,7 @@ __device__ __forceinline__ void store_out(__half* dst, uint32_t v) {
 //   1: one cvt per input element, packed fp32 FMA (fma.rn.f32x2) per channel pair
 //   2: one cvt per input element, scalar fp32 FMA per channel
 #ifndef TDC_MATH
-#define TDC_MATH 1
+#define TDC_MATH 0
 #endif
 
 // Accumulators of one output row for one lane: kColsPerWarp columns x 2 channels.
@@ -253,6 +272,9 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
     uint64_t stall_cycles = 0;
+#if TDC_LOAD_POLICY == 1
+    const uint64_t load_policy = policy_evict_last();
+#endif
     uint32_t stage = 0, phase = 0;
     uint32_t armed = 0, armed_parity = 0;  // bit s: stage s has a copy of phase bit
     int64_t load = 0;
@@ -282,7 +304,12 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
         if (load != p.withhold) {
           const uint32_t fb = smem_addr(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, stage_bytes);
+#if TDC_LOAD_POLICY == 1
+          tma_load_4d_hint(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, n,
+                           load_policy);
+#else
           tma_load_4d(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, n);
+#endif
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
         } else {
@@ -310,6 +337,11 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
 
   // ------------------------------ consumers ------------------------------
   const int cw = warp - 1;
+#if TDC_STORE_MODE == 2
+  const uint64_t store_policy = policy_evict_first();
+#else
+  const uint64_t store_policy = 0;
+#endif
   uint64_t stall_cycles = 0;
   uint32_t stage = 0, phase = 0;
   for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x) {
@@ -366,7 +398,8 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
 #pragma unroll
           for (int m = 0; m < kColsPerWarp; ++m)
             if (m < n_valid)
-              store_out(dst + int64_t(m) * p.C, pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]));
+              store_out(dst + int64_t(m) * p.C, pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]),
+                        store_policy);
         }
       }
       if (++lr == p.stage_rows || i == rows_in - 1) {
