@@ -118,8 +118,24 @@ def _plan(lib, N, H, W, Cc, pad, ns, sms=148, occ=4):
     out = (i64 * 8)()
     rc = lib.tdc_ws_plan(i64(N), i64(H), i64(W), i64(Cc), i64(pad), i64(ns), i64(sms), i64(occ), out)
     assert rc == 0
-    return dict(zip(["stage_rows", "band_rows", "bands", "qstrips", "cblocks", "units", "grid", "smem"],
-                    list(out)))
+    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_rows", "grid",
+                     "smem"], list(out)))
+
+
+def segments(pl, P, g):
+    """The segments CTA g processes, restating the kernel's SegmentIter."""
+    out = []
+    for s in range(g, pl["full_units"], pl["grid"]):
+        out.append((s, 0, P))
+    lo = g * pl["tail_rows"] // pl["grid"]
+    hi = (g + 1) * pl["tail_rows"] // pl["grid"]
+    cur = lo
+    while cur < hi:
+        strip = pl["full_units"] + cur // P
+        end = min(hi, (cur // P + 1) * P)
+        out.append((strip, cur % P, cur % P + end - cur))
+        cur = end
+    return out
 
 
 SHAPES = [(64, 224, 336, 256, 1), (32, 224, 336, 256, 1), (16, 112, 224, 128, 1), (8, 56, 56, 256, 1),
@@ -134,30 +150,36 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
     P, Q = H + 2 * pad - 2, W + 2 * pad - 2
     assert pl["stage_rows"] >= 1
     assert pl["cblocks"] == Cc // 64 and pl["qstrips"] == -(-Q // 32)
-    assert pl["bands"] * pl["band_rows"] >= P > (pl["bands"] - 1) * pl["band_rows"]
-    assert pl["units"] == N * pl["cblocks"] * pl["qstrips"] * pl["bands"]
-    assert 1 <= pl["grid"] <= min(pl["units"], 148 * 4)
+    assert pl["strips"] == N * pl["qstrips"] * pl["cblocks"]
+    assert pl["full_units"] % pl["grid"] == 0 and 0 <= pl["full_units"] < pl["strips"]
+    assert pl["tail_rows"] == (pl["strips"] - pl["full_units"]) * P
+    assert 1 <= pl["grid"] <= 148 * 4
     assert pl["smem"] == ns * pl["stage_rows"] * 34 * 128 + 128 <= 227 * 1024
-    # Rows: bands tile [0, P) exactly; columns: strips tile [0, Q) exactly.
-    rows = []
-    for b in range(pl["bands"]):
-        p0 = b * pl["band_rows"]
-        rows.extend(range(p0, min(p0 + pl["band_rows"], P)))
-    assert rows == list(range(P))
     cols = [q for s in range(pl["qstrips"]) for q in range(s * 32, min(s * 32 + 32, Q))]
     assert cols == list(range(Q))
-    # The persistent round-robin hands every unit to exactly one CTA.
-    seen = [0] * pl["units"]
-    for b in range(pl["grid"]):
-        for u in range(b, pl["units"], pl["grid"]):
-            seen[u] += 1
-    assert all(s == 1 for s in seen)
+    # every (strip, row) is produced by exactly one CTA, and CTAs differ by <= 1 row
+    seen = {}
+    rows_per_cta = []
+    for g in range(pl["grid"]):
+        n_rows = 0
+        for strip, a, b in segments(pl, P, g):
+            assert 0 <= a < b <= P
+            n_rows += b - a
+            for r in range(a, b):
+                key = (strip, r)
+                assert key not in seen
+                seen[key] = g
+        rows_per_cta.append(n_rows)
+    assert len(seen) == pl["strips"] * P
+    assert max(rows_per_cta) - min(rows_per_cta) <= P if pl["full_units"] else True
+    whole = pl["full_units"] // pl["grid"] * P
+    tail = [r - whole for r in rows_per_cta]
+    assert max(tail) - min(tail) <= 1
 
 
 def test_plan_balances_the_headline_shape(lib):
-    # makespan (units per CTA x rows a unit streams) within 6% of a perfect split
     for occ in (3, 4):
         pl = _plan(lib, 64, 224, 336, 256, 1, 2, occ=occ)
-        per_cta = -(-pl["units"] // pl["grid"])
-        ideal = 64 * 4 * 11 * 224 / pl["grid"]
-        assert per_cta * pl["band_rows"] <= 1.06 * ideal
+        assert pl["grid"] == 148 * occ
+        rows = [sum(b - a for _, a, b in segments(pl, 224, g)) for g in range(pl["grid"])]
+        assert max(rows) - min(rows) <= 1

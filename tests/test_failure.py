@@ -19,6 +19,8 @@ FULL_TIMEOUT = 1
 
 
 def _inputs():
+    # 16 rows split over 2 CTAs: each streams 10 input rows, i.e. at least two
+    # loads for every n_stage, so load number 1 exists in every CTA.
     torch.manual_seed(0)
     x = torch.randn(1, 16, 16, 64, device="cuda", dtype=torch.float16)
     w = torch.randn(3, 3, 64, device="cuda", dtype=torch.float16) * 0.1

@@ -13,8 +13,9 @@
 //    fetched once through cudaGetDriverEntryPoint (no -lcuda, no CuTe);
 //  * the dynamic-smem attribute and occupancy are queried once per device and
 //    kernel instantiation instead of on every call (kernel_tma_ws.cu:36-38);
-//  * the grid is persistent (SMs x resident CTAs) over a strip-fastest unit
-//    order instead of one CTA per 8-row tile.
+//  * the grid is persistent (SMs x resident CTAs): whole 32-column strips
+//    round-robin, then the remaining rows split evenly, instead of one CTA
+//    per 8-row tile.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -131,73 +132,38 @@ int validate(const void* x, const void* w, const void* y, int64_t N, int64_t H, 
 // ws launch plan
 // ---------------------------------------------------------------------------
 struct WsPlan {
-  int stage_rows, band_rows, bands, qstrips, cblocks;
-  int64_t units, grid;
+  int stage_rows, qstrips, cblocks;
+  int64_t strips, full_units, tail_rows, grid;
   size_t smem;
 };
 
-// Ring capacity in input rows per CTA, split evenly over the n_stage stages,
-// and the number of waves of units the planner aims for.
-#ifndef TDC_RING_ROWS
-#define TDC_RING_ROWS 12
-#endif
-#ifndef TDC_WAVES
-#define TDC_WAVES 16
-#endif
+// Ring capacity in input rows per CTA, split evenly over the n_stage stages
+// (12 rows = 52 KB, so three 114-register CTAs fit an SM with room to spare).
+constexpr int kRingRows = 12;
+// A CTA is not given fewer output rows than this (each segment streams two
+// halo rows).
+constexpr int64_t kMinRowsPerCta = 8;
 
-int stage_rows_for(int64_t n_stage) { return std::max<int>(1, TDC_RING_ROWS / int(n_stage)); }
+int stage_rows_for(int64_t n_stage) { return std::max<int>(1, kRingRows / int(n_stage)); }
 
-#ifndef TDC_PLAN
-#define TDC_PLAN 1
-#endif
-// Relative cost of a streamed row that produces no output row of its own
-// (halo rows mostly come from L2, not HBM).
-#ifndef TDC_HALO_W
-#define TDC_HALO_W 0.5
-#endif
-
-// Band height.  Every CTA of the persistent grid takes every grid-th unit, so
-// the kernel lasts ceil(units / grid) units; each unit streams its band plus a
-// 2-row halo, rounded up to whole stages.  The planner picks the band count
-// that minimises (units per CTA) x (rows a unit streams), i.e. it trades the
-// last partial wave against the halo rows of shorter bands.
+// Persistent grid of SMs x resident CTAs.  Whole strips are dealt round-robin
+// while every CTA can take one (full_units = (ceil(strips/grid) - 1) * grid);
+// the rows of the remaining strips are split evenly over the grid, so all
+// CTAs stream the same number of rows up to one (plus 2 halo rows per
+// segment) whatever the shape.
 WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
                  int64_t ctas_per_sm) {
   WsPlan pl{};
   pl.stage_rows = stage_rows_for(n_stage);
   pl.qstrips = int((Q + tdc::kStripQ - 1) / tdc::kStripQ);
   pl.cblocks = int(C / tdc::kBlockC);
-  const int64_t strips = N * pl.cblocks * pl.qstrips;
+  pl.strips = N * pl.qstrips * pl.cblocks;
   const int64_t g0 = std::max<int64_t>(1, sms * ctas_per_sm);
-  const int64_t sr = pl.stage_rows;
-#if TDC_PLAN == 0
-  const int64_t want_units = int64_t(TDC_WAVES) * g0;
-  const int64_t want_bands = std::max<int64_t>(1, (want_units + strips - 1) / std::max<int64_t>(strips, 1));
-  int64_t band = (P + want_bands - 1) / want_bands;
-  band = std::max<int64_t>(band, std::max<int64_t>(2 * sr - 2, 6));
-  while ((band + 2) % sr != 0) ++band;
-  band = std::min<int64_t>(band, P);
-#else
-  int64_t band = P;
-  double best = -1.0;
-  const int64_t max_bands = std::min<int64_t>(P, 64);
-  for (int64_t b = 1; b <= max_bands; ++b) {
-    const int64_t rows = (P + b - 1) / b;
-    if (b > 1 && (P + rows - 1) / rows != b) continue;  // same band height as a smaller b
-    const int64_t units = strips * b;
-    const int64_t per_cta = (units + g0 - 1) / g0;
-    const int64_t streamed = ((rows + 2 + sr - 1) / sr) * sr;
-    const double cost = double(per_cta) * (double(rows) + TDC_HALO_W * double(streamed - rows));
-    if (best < 0 || cost < best) {
-      best = cost;
-      band = rows;
-    }
-  }
-#endif
-  pl.band_rows = int(std::max<int64_t>(band, 1));
-  pl.bands = int((P + pl.band_rows - 1) / pl.band_rows);
-  pl.units = strips * pl.bands;
-  pl.grid = std::max<int64_t>(1, std::min<int64_t>(pl.units, g0));
+  const int64_t total_rows = pl.strips * P;
+  pl.grid = std::max<int64_t>(1, std::min(g0, (total_rows + kMinRowsPerCta - 1) / kMinRowsPerCta));
+  const int64_t waves = (pl.strips + pl.grid - 1) / pl.grid;
+  pl.full_units = (waves - 1) * pl.grid;
+  pl.tail_rows = (pl.strips - pl.full_units) * P;
   pl.smem = size_t(n_stage) * pl.stage_rows * tdc::kRowBytes + 128;
   return pl;
 }
@@ -214,10 +180,6 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-#ifndef TDC_L2_PROMO
-#define TDC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
-#endif
-
 // 4-D map over x viewed as (C, W, H, N), innermost first; box
 // (64 ch, 34 cols, stage_rows rows, 1 image); out-of-bounds elements read 0.
 int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t W, int64_t C,
@@ -231,7 +193,7 @@ int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t 
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  TDC_L2_PROMO, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
 }
 
@@ -277,9 +239,8 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.stall = stall;
   prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
   prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad);
-  prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.bands = pl.bands;
-  prm.band_rows = pl.band_rows; prm.stage_rows = pl.stage_rows;
-  prm.units = pl.units;
+  prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
+  prm.strips = pl.strips; prm.full_units = pl.full_units; prm.tail_rows = pl.tail_rows;
   prm.timeout_ns = uint64_t(timeout_ns > 0 ? timeout_ns : g_timeout_ns.load());
   prm.withhold = withhold;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -426,11 +387,11 @@ TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
   if (P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
   const WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
   plan[0] = pl.stage_rows;
-  plan[1] = pl.band_rows;
-  plan[2] = pl.bands;
-  plan[3] = pl.qstrips;
-  plan[4] = pl.cblocks;
-  plan[5] = pl.units;
+  plan[1] = pl.qstrips;
+  plan[2] = pl.cblocks;
+  plan[3] = pl.strips;
+  plan[4] = pl.full_units;
+  plan[5] = pl.tail_rows;
   plan[6] = pl.grid;
   plan[7] = int64_t(pl.smem);
   return TDC_OK;

@@ -66,15 +66,19 @@ __global__ void __launch_bounds__(256) dwconv_v0_kernel(const uint4* __restrict_
 // ============================================================================
 // TMA warp-specialised kernel (the `dwconv_ws` / `dwconv_ws_probe` calls).
 //
-// Work decomposition.  The output is cut into units
-//   (image n, 64-channel block cb, band of `band_rows` output rows, strip of
-//    kStripQ = 32 output columns),
-// enumerated strip-fastest so that units running at the same moment on
-// different SMs are horizontal/vertical neighbours and share their halo
-// columns/rows through L2.  The grid is persistent: CTA b takes units
-// b, b + gridDim.x, …
+// Work decomposition.  A strip is (image n, 32 output columns, 64-channel
+// block cb) over all P output rows; strips are enumerated (n, column strip,
+// cb) with cb fastest, so strips running at the same moment on different
+// SMs are the channel blocks of one pixel column (the same DRAM pages) and
+// horizontal neighbours (sharing their halo columns through L2).
+// The grid is persistent.  With `full_units` = (ceil(strips/grid) - 1) * grid,
+// CTA g first takes whole strips g, g + grid, ... below full_units; the
+// remaining strips' rows are then split evenly over all CTAs (CTA g takes
+// rows [g*T/grid, (g+1)*T/grid) of the remaining row sequence, possibly
+// spanning two strips), so every CTA streams the same number of rows up to
+// one, plus a 2-row halo per segment.
 //
-// Per unit the producer (warp 0, one thread) streams the band's input rows
+// Per segment the producer (warp 0, one thread) streams input rows
 // [p0 - pad, p0 - pad + rows + 2) as TMA boxes of (64 ch, 34 cols,
 // stage_rows rows, 1 image) into an NS-deep shared-memory ring; box
 // coordinates outside the image are zero-filled by the TMA unit, which
@@ -83,11 +87,11 @@ __global__ void __launch_bounds__(256) dwconv_v0_kernel(const uint4* __restrict_
 // column, so every shared-memory read is conflict-free).  Each input row is
 // read from shared memory once per lane and FMA'd into three rows of
 // accumulators (the rows it is tap r = 0, 1, 2 of): a sliding window down
-// the band, so the vertical halo is never re-read.  After a row the oldest
-// accumulator row is complete; it is rounded to fp16 and stored with
+// the segment, so the vertical halo is never re-read.  After a row the
+// oldest accumulator row is complete; it is rounded to fp16 and stored with
 // 128-byte-per-warp coalesced stores.
 // ============================================================================
-constexpr int kBlockC = 64;                        // channels per unit (128 B)
+constexpr int kBlockC = 64;                        // channels per strip (128 B)
 constexpr int kColsPerWarp = 8;                    // output columns per consumer warp
 constexpr int kConsumerWarps = 4;
 constexpr int kStripQ = kColsPerWarp * kConsumerWarps;  // 32 output columns
@@ -100,10 +104,12 @@ struct WsParams {
   __half* y;
   unsigned long long* stall;  // probe only
   int32_t H, W, C, P, Q, pad;
-  int32_t qstrips, cblocks, bands, band_rows, stage_rows;
-  int64_t units;  // N * cblocks * bands * qstrips
+  int32_t qstrips, cblocks, stage_rows;
+  int64_t strips;      // N * qstrips * cblocks
+  int64_t full_units;  // strips handed out whole (a multiple of gridDim.x)
+  int64_t tail_rows;   // (strips - full_units) * P, split evenly over the grid
   uint64_t timeout_ns;
-  int64_t withhold;  // load index the producer withholds (-1: none)
+  int64_t withhold;    // load index the producer withholds (-1: none)
 };
 
 // Per-device failure record written by the bounded waits:
@@ -118,93 +124,61 @@ __device__ __forceinline__ void record_failure(int code, int block, int stage, i
   }
 }
 
-#ifndef TDC_ORDER
-#define TDC_ORDER 1
-#endif
-__device__ __forceinline__ void decode_unit(int64_t u, const WsParams& p, int& n, int& cb,
-                                            int& band, int& qs) {
-#if TDC_ORDER == 0
-  // (n, cb, band, qs), strip fastest
-  qs = int(u % p.qstrips);
-  int64_t t = u / p.qstrips;
-  band = int(t % p.bands);
-  t /= p.bands;
-  cb = int(t % p.cblocks);
-  n = int(t / p.cblocks);
-#else
-  // (n, band, qs, cb), channel block fastest
-  cb = int(u % p.cblocks);
-  int64_t t = u / p.cblocks;
-  qs = int(t % p.qstrips);
-  t /= p.qstrips;
-  band = int(t % p.bands);
-  n = int(t / p.bands);
-#endif
-}
+// A run of output rows [p0, p0 + rows) of one strip.
+struct Segment {
+  int n, qs, cb, p0, rows;
+};
 
-// Output stores: the result is written once and never read back by the
-// kernel, so it may be marked streaming (evict-first).
-#ifndef TDC_STORE_MODE
-#define TDC_STORE_MODE 0
-#endif
-#ifndef TDC_LOAD_POLICY
-#define TDC_LOAD_POLICY 0
-#endif
-__device__ __forceinline__ void store_out(__half* dst, uint32_t v, uint64_t policy) {
-#if TDC_STORE_MODE == 1
-  asm volatile("st.global.cs.b32 [%0], %1;" ::"l"(dst), "r"(v) : "memory");
-#elif TDC_STORE_MODE == 2
-  st_global_hint(dst, v, policy);
-#else
-  *reinterpret_cast<uint32_t*>(dst) = v;
-#endif
-}
+// Enumerates the segments of one CTA; the producer and every consumer warp
+// run their own copy and see the same sequence.
+struct SegmentIter {
+  int64_t next_whole;  // next whole strip (phase 1)
+  int64_t cur, hi;     // remaining row range of the tail (phase 2)
+  int64_t grid;
+  bool in_tail;
 
-// Consumer arithmetic.  TDC_MATH selects how the fp16 x fp16 -> fp32 FMAs are
-// issued; every variant performs the same IEEE operations in the same order.
-//   0: fma.rn.f32.f16 per channel (operands stay fp16)
-//   1: one cvt per input element, packed fp32 FMA (fma.rn.f32x2) per channel pair
-//   2: one cvt per input element, scalar fp32 FMA per channel
-#ifndef TDC_MATH
-#define TDC_MATH 0
-#endif
+  __device__ SegmentIter(const WsParams& p, int64_t g, int64_t grid_)
+      : next_whole(g), cur(0), hi(0), grid(grid_), in_tail(false) {
+    (void)p;
+  }
+
+  __device__ bool next(const WsParams& p, Segment& s) {
+    int64_t strip;
+    int first, last;
+    if (next_whole < p.full_units) {
+      strip = next_whole;
+      next_whole += grid;
+      first = 0;
+      last = p.P;
+    } else {
+      if (!in_tail) {
+        in_tail = true;
+        const int64_t g = next_whole - p.full_units;  // == blockIdx.x
+        cur = g * p.tail_rows / grid;
+        hi = (g + 1) * p.tail_rows / grid;
+      }
+      if (cur >= hi) return false;
+      strip = p.full_units + cur / p.P;
+      first = int(cur % p.P);
+      const int64_t strip_end = (cur / p.P + 1) * p.P;
+      const int64_t end = hi < strip_end ? hi : strip_end;
+      last = first + int(end - cur);
+      cur = end;
+    }
+    s.cb = int(strip % p.cblocks);
+    const int64_t t = strip / p.cblocks;
+    s.qs = int(t % p.qstrips);
+    s.n = int(t / p.qstrips);
+    s.p0 = first;
+    s.rows = last - first;
+    return true;
+  }
+};
 
 // Accumulators of one output row for one lane: kColsPerWarp columns x 2 channels.
 struct RowAcc {
   float v[kColsPerWarp * 2];
 };
-
-#if TDC_MATH == 0
-using Taps = uint32_t[9];  // packed fp16 pair per tap
-__device__ __forceinline__ void load_taps(const uint32_t* wp, int64_t stride, Taps& t) {
-#pragma unroll
-  for (int k = 0; k < 9; ++k) t[k] = __ldg(wp + k * stride);
-}
-#else
-using Taps = float[18];  // fp32 pair per tap
-__device__ __forceinline__ void load_taps(const uint32_t* wp, int64_t stride, Taps& t) {
-#pragma unroll
-  for (int k = 0; k < 9; ++k) {
-    const float2 f = unpack_half2(__ldg(wp + k * stride));
-    t[2 * k] = f.x;
-    t[2 * k + 1] = f.y;
-  }
-}
-#endif
-
-// acc(pair) = x(pair) * w(tap) + acc(pair), or x * w + 0 when `first`.
-__device__ __forceinline__ void tap_fma(uint32_t xh, float x0, float x1, const Taps& t, int k,
-                                        float& a0, float& a1, bool first) {
-  if (first) { a0 = 0.f; a1 = 0.f; }
-#if TDC_MATH == 0
-  fma2_f16f32(xh, t[k], a0, a1);
-#elif TDC_MATH == 1
-  ffma2(x0, x1, t[2 * k], t[2 * k + 1], a0, a1);
-#else
-  a0 = __fmaf_rn(x0, t[2 * k], a0);
-  a1 = __fmaf_rn(x1, t[2 * k + 1], a1);
-#endif
-}
 
 // Feeds one input row (kColsPerWarp + 2 packed fp16 pairs of this lane) into
 // the three accumulator rows it contributes to:
@@ -212,28 +186,30 @@ __device__ __forceinline__ void tap_fma(uint32_t xh, float x0, float x1, const T
 //   mid = output row half way (r = 1),
 //   nw  = output row started by it (r = 0, initialised from +0 here).
 // Within a row, inputs are consumed left to right, so every output sees its
-// taps in (r, s) lexicographic order.
-__device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2], const Taps& wt,
-                                         RowAcc& fin, RowAcc& mid, RowAcc& nw) {
+// taps in (r, s) lexicographic order.  The FMAs take the fp16 operands
+// directly (fma.rn.f32.f16), which issues on both FMA pipes of sm_100 with
+// no conversion instructions.
+__device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2],
+                                         const uint32_t (&wt)[9], RowAcc& fin, RowAcc& mid,
+                                         RowAcc& nw) {
 #pragma unroll
   for (int j = 0; j < kColsPerWarp + 2; ++j) {
-    float x0 = 0.f, x1 = 0.f;
-#if TDC_MATH != 0
-    const float2 xf = unpack_half2(xr[j]);
-    x0 = xf.x;
-    x1 = xf.y;
-#endif
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
       const int m = j - s;
       if (m < 0 || m >= kColsPerWarp) continue;
-      tap_fma(xr[j], x0, x1, wt, 0 * 3 + s, nw.v[2 * m], nw.v[2 * m + 1], s == 0);
-      tap_fma(xr[j], x0, x1, wt, 1 * 3 + s, mid.v[2 * m], mid.v[2 * m + 1], false);
-      tap_fma(xr[j], x0, x1, wt, 2 * 3 + s, fin.v[2 * m], fin.v[2 * m + 1], false);
+      if (s == 0) {
+        nw.v[2 * m] = 0.f;
+        nw.v[2 * m + 1] = 0.f;
+      }
+      fma2_f16f32(xr[j], wt[0 * 3 + s], nw.v[2 * m], nw.v[2 * m + 1]);
+      fma2_f16f32(xr[j], wt[1 * 3 + s], mid.v[2 * m], mid.v[2 * m + 1]);
+      fma2_f16f32(xr[j], wt[2 * 3 + s], fin.v[2 * m], fin.v[2 * m + 1]);
     }
   }
 }
 
+// Resident CTAs per SM the kernel is compiled for (bounds its registers).
 #ifndef TDC_MIN_BLOCKS
 #define TDC_MIN_BLOCKS 1
 #endif
@@ -272,22 +248,17 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
     uint64_t stall_cycles = 0;
-#if TDC_LOAD_POLICY == 1
-    const uint64_t load_policy = policy_evict_last();
-#endif
     uint32_t stage = 0, phase = 0;
-    uint32_t armed = 0, armed_parity = 0;  // bit s: stage s has a copy of phase bit
+    uint32_t armed = 0, armed_parity = 0;  // bit s: stage s has a copy in flight / landed
     int64_t load = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-      int n, cb, band, qs;
-      decode_unit(u, p, n, cb, band, qs);
-      const int p0 = band * p.band_rows;
-      const int rows_in = min(p.band_rows, p.P - p0) + 2;
-      const int nst = (rows_in + p.stage_rows - 1) / p.stage_rows;
-      const int32_t c0 = cb * kBlockC;
-      const int32_t w0 = qs * kStripQ - p.pad;
-      const int32_t h0 = p0 - p.pad;
+    SegmentIter it(p, blockIdx.x, gridDim.x);
+    Segment sg;
+    while (ok && it.next(p, sg)) {
+      const int nst = (sg.rows + 2 + p.stage_rows - 1) / p.stage_rows;
+      const int32_t c0 = sg.cb * kBlockC;
+      const int32_t w0 = sg.qs * kStripQ - p.pad;
+      const int32_t h0 = sg.p0 - p.pad;
       for (int t = 0; t < nst; ++t) {
         const uint32_t eb = smem_addr(&empty_bar[stage]);
         uint64_t t0 = 0;
@@ -304,12 +275,7 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
         if (load != p.withhold) {
           const uint32_t fb = smem_addr(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, stage_bytes);
-#if TDC_LOAD_POLICY == 1
-          tma_load_4d_hint(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, n,
-                           load_policy);
-#else
-          tma_load_4d(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, n);
-#endif
+          tma_load_4d(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, sg.n);
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
         } else {
@@ -337,25 +303,24 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
 
   // ------------------------------ consumers ------------------------------
   const int cw = warp - 1;
-#if TDC_STORE_MODE == 2
-  const uint64_t store_policy = policy_evict_first();
-#else
-  const uint64_t store_policy = 0;
-#endif
   uint64_t stall_cycles = 0;
   uint32_t stage = 0, phase = 0;
-  for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x) {
-    int n, cb, band, qs;
-    decode_unit(u, p, n, cb, band, qs);
-    const int p0 = band * p.band_rows;
-    const int rows_out = min(p.band_rows, p.P - p0);
-    const int rows_in = rows_out + 2;
-    const int c0 = cb * kBlockC;
-    const int q_first = qs * kStripQ + cw * kColsPerWarp;
+  SegmentIter it(p, blockIdx.x, gridDim.x);
+  Segment sg;
+  int last_cb = -1;
+  uint32_t wt[9];
+  while (it.next(p, sg)) {
+    const int rows_in = sg.rows + 2;
+    const int c0 = sg.cb * kBlockC;
+    const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
     const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
-    Taps wt;
-    load_taps(reinterpret_cast<const uint32_t*>(p.w + c0) + lane, p.C / 2, wt);
-    __half* yrow = p.y + ((int64_t(n) * p.P + p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
+    if (sg.cb != last_cb) {
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(p.w + c0) + lane;
+#pragma unroll
+      for (int k = 0; k < 9; ++k) wt[k] = __ldg(wp + int64_t(k) * (p.C / 2));
+      last_cb = sg.cb;
+    }
+    __half* yrow = p.y + ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
     const int64_t y_row_stride = int64_t(p.Q) * p.C;
 
     RowAcc a, b, c;
@@ -398,8 +363,8 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
 #pragma unroll
           for (int m = 0; m < kColsPerWarp; ++m)
             if (m < n_valid)
-              store_out(dst + int64_t(m) * p.C, pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]),
-                        store_policy);
+              *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
+                  pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]);
         }
       }
       if (++lr == p.stage_rows || i == rows_in - 1) {

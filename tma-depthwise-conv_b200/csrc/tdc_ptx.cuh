@@ -93,35 +93,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Same load with an L2 cache-eviction policy (a createpolicy descriptor).
-__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const CUtensorMap* map,
-                                                 uint32_t bar, int32_t c0, int32_t c1,
-                                                 int32_t c2, int32_t c3, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar),
-      "l"(policy)
-      : "memory");
-}
-
-__device__ __forceinline__ uint64_t policy_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
-__device__ __forceinline__ uint64_t policy_evict_first() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
-__device__ __forceinline__ void st_global_hint(void* dst, uint32_t v, uint64_t policy) {
-  asm volatile("st.global.L2::cache_hint.b32 [%0], %1, %2;" ::"l"(dst), "r"(v), "l"(policy)
-               : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -142,28 +113,9 @@ __device__ __forceinline__ void fma2_f16f32(uint32_t x2, uint32_t w2, float& acc
       : "r"(x2), "r"(w2));
 }
 
-// Packed fp32 FMA: (d.x, d.y) = (a.x*b.x + c.x, a.y*b.y + c.y), one rounding each.
-__device__ __forceinline__ void ffma2(float ax, float ay, float bx, float by, float& cx, float& cy) {
-  asm("{\n"
-      " .reg .b64 ra, rb, rc;\n"
-      " mov.b64 ra, {%2, %3};\n"
-      " mov.b64 rb, {%4, %5};\n"
-      " mov.b64 rc, {%0, %1};\n"
-      " fma.rn.f32x2 rc, ra, rb, rc;\n"
-      " mov.b64 {%0, %1}, rc;\n"
-      "}\n"
-      : "+f"(cx), "+f"(cy)
-      : "f"(ax), "f"(ay), "f"(bx), "f"(by));
-}
-
 __device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
-}
-
-__device__ __forceinline__ float2 unpack_half2(uint32_t v) {
-  __half2 h = *reinterpret_cast<__half2*>(&v);
-  return __half22float2(h);
 }
 
 }  // namespace tdc
