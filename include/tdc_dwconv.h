@@ -100,9 +100,10 @@ TDC_API int tdc_ws_consumer_warps(void);
 
 /* Launch plan the ws kernel would use on a device with `sms` SMs and
  * `ctas_per_sm` resident CTAs (pure host arithmetic, no CUDA call):
- * plan[0..7] = {stage_rows, qstrips, cblocks, strips, full_units, tail_rows,
- * grid, dynamic smem bytes}: strips below full_units are dealt whole,
- * round-robin; the tail_rows rows of the rest are split evenly over the grid.  No counterpart in the reference (whose grid is fixed
+ * plan[0..7] = {stage_rows, qstrips, cblocks, strips, full_units,
+ * tail_band_rows, grid, dynamic smem bytes}: strips below full_units are
+ * dealt whole, round-robin; the rest are cut into bands of tail_band_rows
+ * rows (the last band may be shorter) and dealt the same way, band-major.  No counterpart in the reference (whose grid is fixed
  * at (ceil(P/8), C/64, N), csrc/kernel_tma_ws.cu:25-31); exposed so the
  * planner can be checked without a GPU. */
 TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,

@@ -118,29 +118,35 @@ def _plan(lib, N, H, W, Cc, pad, ns, sms=148, occ=4):
     out = (i64 * 8)()
     rc = lib.tdc_ws_plan(i64(N), i64(H), i64(W), i64(Cc), i64(pad), i64(ns), i64(sms), i64(occ), out)
     assert rc == 0
-    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_rows", "grid",
+    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
                      "smem"], list(out)))
 
 
 def segments(pl, P, g):
-    """The segments CTA g processes, restating the kernel's SegmentIter."""
+    """(strip, first row, end row) of every segment CTA g processes, restating
+    the kernel's SegmentIter: whole strips round-robin, then the remaining
+    strips in bands, band-major, round-robin."""
     out = []
-    for s in range(g, pl["full_units"], pl["grid"]):
-        out.append((s, 0, P))
-    lo = g * pl["tail_rows"] // pl["grid"]
-    hi = (g + 1) * pl["tail_rows"] // pl["grid"]
-    cur = lo
-    while cur < hi:
-        strip = pl["full_units"] + cur // P
-        end = min(hi, (cur // P + 1) * P)
-        out.append((strip, cur % P, cur % P + end - cur))
-        cur = end
+    tail = pl["strips"] - pl["full_units"]
+    hb = pl["tail_band_rows"]
+    bands = -(-P // hb)
+    k = g
+    while True:
+        if k < pl["full_units"]:
+            out.append((k, 0, P))
+        else:
+            t = k - pl["full_units"]
+            if t >= tail * bands:
+                break
+            band = t // tail
+            out.append((pl["full_units"] + t % tail, band * hb, min(P, band * hb + hb)))
+        k += pl["grid"]
     return out
 
 
 SHAPES = [(64, 224, 336, 256, 1), (32, 224, 336, 256, 1), (16, 112, 224, 128, 1), (8, 56, 56, 256, 1),
           (2, 16, 16, 64, 1), (1, 1, 1, 64, 1), (1, 3, 3, 64, 5), (3, 7, 45, 128, 1), (5, 100, 1, 64, 1),
-          (1, 1000, 40, 64, 0), (80, 224, 336, 320, 1)]
+          (1, 1000, 40, 64, 0), (80, 224, 336, 320, 1), (8, 224, 336, 256, 1)]
 
 
 @pytest.mark.parametrize("N,H,W,Cc,pad", SHAPES)
@@ -152,34 +158,26 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
     assert pl["cblocks"] == Cc // 64 and pl["qstrips"] == -(-Q // 32)
     assert pl["strips"] == N * pl["qstrips"] * pl["cblocks"]
     assert pl["full_units"] % pl["grid"] == 0 and 0 <= pl["full_units"] < pl["strips"]
-    assert pl["tail_rows"] == (pl["strips"] - pl["full_units"]) * P
+    assert pl["strips"] - pl["full_units"] <= pl["grid"]
+    assert 1 <= pl["tail_band_rows"] <= P
     assert 1 <= pl["grid"] <= 148 * 4
     assert pl["smem"] == ns * pl["stage_rows"] * 34 * 128 + 128 <= 227 * 1024
     cols = [q for s in range(pl["qstrips"]) for q in range(s * 32, min(s * 32 + 32, Q))]
     assert cols == list(range(Q))
-    # every (strip, row) is produced by exactly one CTA, and CTAs differ by <= 1 row
-    seen = {}
-    rows_per_cta = []
+    seen = set()
     for g in range(pl["grid"]):
-        n_rows = 0
         for strip, a, b in segments(pl, P, g):
             assert 0 <= a < b <= P
-            n_rows += b - a
             for r in range(a, b):
-                key = (strip, r)
-                assert key not in seen
-                seen[key] = g
-        rows_per_cta.append(n_rows)
+                assert (strip, r) not in seen
+                seen.add((strip, r))
     assert len(seen) == pl["strips"] * P
-    assert max(rows_per_cta) - min(rows_per_cta) <= P if pl["full_units"] else True
-    whole = pl["full_units"] // pl["grid"] * P
-    tail = [r - whole for r in rows_per_cta]
-    assert max(tail) - min(tail) <= 1
 
 
 def test_plan_balances_the_headline_shape(lib):
+    # the busiest CTA streams at most 3% more rows (halo included) than a perfect split
     for occ in (3, 4):
         pl = _plan(lib, 64, 224, 336, 256, 1, 2, occ=occ)
         assert pl["grid"] == 148 * occ
-        rows = [sum(b - a for _, a, b in segments(pl, 224, g)) for g in range(pl["grid"])]
-        assert max(rows) - min(rows) <= 1
+        streamed = [sum(b - a + 2 for _, a, b in segments(pl, 224, g)) for g in range(pl["grid"])]
+        assert max(streamed) <= 1.03 * (64 * 44 * 224 / pl["grid"])

@@ -14,8 +14,8 @@
 //  * the dynamic-smem attribute and occupancy are queried once per device and
 //    kernel instantiation instead of on every call (kernel_tma_ws.cu:36-38);
 //  * the grid is persistent (SMs x resident CTAs): whole 32-column strips
-//    round-robin, then the remaining rows split evenly, instead of one CTA
-//    per 8-row tile.
+//    round-robin, then the last strips in bands, instead of one CTA per
+//    8-row tile.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -132,13 +132,14 @@ int validate(const void* x, const void* w, const void* y, int64_t N, int64_t H, 
 // ws launch plan
 // ---------------------------------------------------------------------------
 struct WsPlan {
-  int stage_rows, qstrips, cblocks;
-  int64_t strips, full_units, tail_rows, grid;
+  int stage_rows, qstrips, cblocks, tail_bands, tail_band_rows;
+  int64_t strips, full_units, tail_strips, grid;
   size_t smem;
 };
 
 // Ring capacity in input rows per CTA, split evenly over the n_stage stages
-// (12 rows = 52 KB, so three 114-register CTAs fit an SM with room to spare).
+// (12 rows = 52 KB, so three CTAs of ~120 registers fit an SM with room to
+// spare).
 constexpr int kRingRows = 12;
 // A CTA is not given fewer output rows than this (each segment streams two
 // halo rows).
@@ -146,11 +147,11 @@ constexpr int64_t kMinRowsPerCta = 8;
 
 int stage_rows_for(int64_t n_stage) { return std::max<int>(1, kRingRows / int(n_stage)); }
 
-// Persistent grid of SMs x resident CTAs.  Whole strips are dealt round-robin
-// while every CTA can take one (full_units = (ceil(strips/grid) - 1) * grid);
-// the rows of the remaining strips are split evenly over the grid, so all
-// CTAs stream the same number of rows up to one (plus 2 halo rows per
-// segment) whatever the shape.
+// Persistent grid of SMs x resident CTAs.  Whole strips are dealt
+// round-robin while every CTA can take one: full_units =
+// (ceil(strips/grid) - 1) * grid.  The remaining tail_strips strips are cut
+// into bands; the band count minimises the rows the busiest CTA streams in
+// the last wave, (tail units per CTA) x (band rows + 2 halo rows).
 WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
                  int64_t ctas_per_sm) {
   WsPlan pl{};
@@ -163,7 +164,21 @@ WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, in
   pl.grid = std::max<int64_t>(1, std::min(g0, (total_rows + kMinRowsPerCta - 1) / kMinRowsPerCta));
   const int64_t waves = (pl.strips + pl.grid - 1) / pl.grid;
   pl.full_units = (waves - 1) * pl.grid;
-  pl.tail_rows = (pl.strips - pl.full_units) * P;
+  pl.tail_strips = pl.strips - pl.full_units;
+  int64_t best_cost = -1, best_rows = P;
+  for (int64_t b = 1; b <= std::min<int64_t>(P, 256); ++b) {
+    const int64_t rows = (P + b - 1) / b;
+    const int64_t bands = (P + rows - 1) / rows;
+    if (bands != b) continue;  // same band height as a smaller band count
+    const int64_t per_cta = (pl.tail_strips * bands + pl.grid - 1) / pl.grid;
+    const int64_t cost = per_cta * (rows + 2);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_rows = rows;
+    }
+  }
+  pl.tail_band_rows = int(best_rows);
+  pl.tail_bands = int((P + best_rows - 1) / best_rows);
   pl.smem = size_t(n_stage) * pl.stage_rows * tdc::kRowBytes + 128;
   return pl;
 }
@@ -240,7 +255,8 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
   prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad);
   prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
-  prm.strips = pl.strips; prm.full_units = pl.full_units; prm.tail_rows = pl.tail_rows;
+  prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
+  prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
   prm.timeout_ns = uint64_t(timeout_ns > 0 ? timeout_ns : g_timeout_ns.load());
   prm.withhold = withhold;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -391,7 +407,7 @@ TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
   plan[2] = pl.cblocks;
   plan[3] = pl.strips;
   plan[4] = pl.full_units;
-  plan[5] = pl.tail_rows;
+  plan[5] = pl.tail_band_rows;
   plan[6] = pl.grid;
   plan[7] = int64_t(pl.smem);
   return TDC_OK;

@@ -71,13 +71,13 @@ __global__ void __launch_bounds__(256) dwconv_v0_kernel(const uint4* __restrict_
 // cb) with cb fastest, so strips running at the same moment on different
 // SMs are the channel blocks of one pixel column (the same DRAM pages) and
 // horizontal neighbours (sharing their halo columns through L2).
-// The grid is persistent.  With `full_units` = (ceil(strips/grid) - 1) * grid,
-// CTA g first takes whole strips g, g + grid, ... below full_units; the
-// remaining strips' rows are then split evenly over all CTAs (CTA g takes
-// rows [g*T/grid, (g+1)*T/grid) of the remaining row sequence, possibly
-// spanning two strips), so every CTA streams the same number of rows up to
-// one, plus a 2-row halo per segment.
-//
+// The grid is persistent.  CTA g first takes whole strips g, g + grid, ...
+// below `full_units` = (ceil(strips/grid) - 1) * grid.  The last
+// `tail_strips` strips are cut into `tail_bands` bands of `tail_band_rows`
+// rows and these tail units, ordered (band, strip), are dealt round-robin
+// the same way, so the last wave is as even as the band height allows while
+// CTAs running at the same moment still work on neighbouring strips at the
+// same rows.
 // Per segment the producer (warp 0, one thread) streams input rows
 // [p0 - pad, p0 - pad + rows + 2) as TMA boxes of (64 ch, 34 cols,
 // stage_rows rows, 1 image) into an NS-deep shared-memory ring; box
@@ -105,11 +105,11 @@ struct WsParams {
   unsigned long long* stall;  // probe only
   int32_t H, W, C, P, Q, pad;
   int32_t qstrips, cblocks, stage_rows;
-  int64_t strips;      // N * qstrips * cblocks
-  int64_t full_units;  // strips handed out whole (a multiple of gridDim.x)
-  int64_t tail_rows;   // (strips - full_units) * P, split evenly over the grid
+  int32_t tail_bands, tail_band_rows;
+  int64_t full_units;   // strips handed out whole (a multiple of gridDim.x)
+  int64_t tail_strips;  // strips handed out as bands
   uint64_t timeout_ns;
-  int64_t withhold;    // load index the producer withholds (-1: none)
+  int64_t withhold;     // load index the producer withholds (-1: none)
 };
 
 // Per-device failure record written by the bounded waits:
@@ -132,43 +132,31 @@ struct Segment {
 // Enumerates the segments of one CTA; the producer and every consumer warp
 // run their own copy and see the same sequence.
 struct SegmentIter {
-  int64_t next_whole;  // next whole strip (phase 1)
-  int64_t cur, hi;     // remaining row range of the tail (phase 2)
+  int64_t next;  // next work item: whole strips first, then tail units
   int64_t grid;
-  bool in_tail;
 
-  __device__ SegmentIter(const WsParams& p, int64_t g, int64_t grid_)
-      : next_whole(g), cur(0), hi(0), grid(grid_), in_tail(false) {
-    (void)p;
-  }
+  __device__ SegmentIter(int64_t g, int64_t grid_) : next(g), grid(grid_) {}
 
-  __device__ bool next(const WsParams& p, Segment& s) {
+  __device__ bool next_segment(const WsParams& p, Segment& s) {
     int64_t strip;
     int first, last;
-    if (next_whole < p.full_units) {
-      strip = next_whole;
-      next_whole += grid;
+    if (next < p.full_units) {
+      strip = next;
       first = 0;
       last = p.P;
     } else {
-      if (!in_tail) {
-        in_tail = true;
-        const int64_t g = next_whole - p.full_units;  // == blockIdx.x
-        cur = g * p.tail_rows / grid;
-        hi = (g + 1) * p.tail_rows / grid;
-      }
-      if (cur >= hi) return false;
-      strip = p.full_units + cur / p.P;
-      first = int(cur % p.P);
-      const int64_t strip_end = (cur / p.P + 1) * p.P;
-      const int64_t end = hi < strip_end ? hi : strip_end;
-      last = first + int(end - cur);
-      cur = end;
+      const int64_t t = next - p.full_units;
+      if (t >= p.tail_strips * p.tail_bands) return false;
+      const int band = int(t / p.tail_strips);
+      strip = p.full_units + t % p.tail_strips;
+      first = band * p.tail_band_rows;
+      last = min(p.P, first + p.tail_band_rows);
     }
+    next += grid;
     s.cb = int(strip % p.cblocks);
-    const int64_t t = strip / p.cblocks;
-    s.qs = int(t % p.qstrips);
-    s.n = int(t / p.qstrips);
+    const int64_t r = strip / p.cblocks;
+    s.qs = int(r % p.qstrips);
+    s.n = int(r / p.qstrips);
     s.p0 = first;
     s.rows = last - first;
     return true;
@@ -252,9 +240,9 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
     uint32_t armed = 0, armed_parity = 0;  // bit s: stage s has a copy in flight / landed
     int64_t load = 0;
     bool ok = true;
-    SegmentIter it(p, blockIdx.x, gridDim.x);
+    SegmentIter it(blockIdx.x, gridDim.x);
     Segment sg;
-    while (ok && it.next(p, sg)) {
+    while (ok && it.next_segment(p, sg)) {
       const int nst = (sg.rows + 2 + p.stage_rows - 1) / p.stage_rows;
       const int32_t c0 = sg.cb * kBlockC;
       const int32_t w0 = sg.qs * kStripQ - p.pad;
@@ -305,11 +293,11 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
   const int cw = warp - 1;
   uint64_t stall_cycles = 0;
   uint32_t stage = 0, phase = 0;
-  SegmentIter it(p, blockIdx.x, gridDim.x);
+  SegmentIter it(blockIdx.x, gridDim.x);
   Segment sg;
   int last_cb = -1;
   uint32_t wt[9];
-  while (it.next(p, sg)) {
+  while (it.next_segment(p, sg)) {
     const int rows_in = sg.rows + 2;
     const int c0 = sg.cb * kBlockC;
     const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
