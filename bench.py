@@ -143,24 +143,32 @@ def _cuda_time(fn, steps: int, stream) -> float:
     return start.elapsed_time(end)
 
 
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def _cpu_oracle_rate(wl, x_cpu, w_cpu, images: int, repeats: int):
     """Oracle throughput on `images` images: (seconds per image, threads)."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle  # checker/baseline only
     xs = x_cpu[:images].numpy()
     ws = w_cpu.numpy()
-    oracle.dwconv_f16(xs[:1], ws, wl.pad)  # warm-up (page in, OpenMP pool)
+    threads = _host_threads()
+    oracle.dwconv_f16(xs[:1], ws, wl.pad, threads=threads)  # warm-up (page in, OpenMP pool)
     best = float("inf")
     for _ in range(repeats):
         t0 = time.perf_counter()
-        oracle.dwconv_f16(xs, ws, wl.pad)
+        oracle.dwconv_f16(xs, ws, wl.pad, threads=threads)
         best = min(best, time.perf_counter() - t0)
-    return best / images, oracle.max_threads()
+    return best / images, threads
 
 
 def _torch_cpu_rate(wl, x_cpu, w_cpu, images: int):
     """torch CPU conv2d(groups=C) in float32 on the channels_last view: s per image."""
-    threads = os.cpu_count() or 1
+    threads = _host_threads()
     torch.set_num_threads(threads)
     xf = x_cpu[:images].float().permute(0, 3, 1, 2)  # NCHW view of NHWC memory = channels_last
     wf = w_cpu.float().permute(2, 0, 1).unsqueeze(1).contiguous()
@@ -179,14 +187,15 @@ def run_reference(args, wl) -> None:
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle
     xs, ws = x.numpy(), w.numpy()
+    # every core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    threads = _host_threads()
     for _ in range(args.warmup):
-        oracle.dwconv_f16(xs, ws, wl.pad)
+        oracle.dwconv_f16(xs, ws, wl.pad, threads=threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.dwconv_f16(xs, ws, wl.pad)
+        oracle.dwconv_f16(xs, ws, wl.pad, threads=threads)
     dt = (time.perf_counter() - t0) / args.steps
     gbs = wl.bytes_per_call(1) / dt / 1e9
-    threads = oracle.max_threads()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

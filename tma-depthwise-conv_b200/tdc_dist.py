@@ -8,8 +8,10 @@ barriers around a timed region and for reducing timings (max over ranks).
 """
 from __future__ import annotations
 
+import contextlib
 import datetime
 import os
+import sys
 
 import torch
 import torch.distributed as dist
@@ -21,8 +23,26 @@ def env_rank() -> tuple[int, int, int]:
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Send file descriptor 1 to stderr for a while (communicator set-up prints
+    a version banner on stdout, which must carry only the result line)."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def init(backend: str, timeout_s: float = 120.0) -> tuple[int, int, int]:
-    """Join the process group when WORLD_SIZE > 1 (rendezvous from MASTER_ADDR/PORT)."""
+    """Join the process group when WORLD_SIZE > 1 (rendezvous from MASTER_ADDR/PORT).
+
+    The first barrier runs here, so the communicator exists (and has printed
+    whatever it prints) before the caller writes to stdout."""
     rank, world, local = env_rank()
     if world > 1 and not dist.is_initialized():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
@@ -30,8 +50,10 @@ def init(backend: str, timeout_s: float = 120.0) -> tuple[int, int, int]:
         if backend == "nccl":
             torch.cuda.set_device(local)
             kw["device_id"] = torch.device("cuda", local)
-        dist.init_process_group(backend, rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
+        with stdout_to_stderr():
+            dist.init_process_group(backend, rank=rank, world_size=world,
+                                    timeout=datetime.timedelta(seconds=timeout_s), **kw)
+            dist.barrier()
     return rank, world, local
 
 
