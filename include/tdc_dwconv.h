@@ -46,7 +46,7 @@ extern "C" {
 #define TDC_ERR_NULL_POINTER     -1  /* x, w, y (or stall for the probe) is NULL          */
 #define TDC_ERR_BAD_SHAPE        -2  /* N or C < 0, H or W < 1, or a negative output size  */
 #define TDC_ERR_FILTER_SHAPE     -3  /* R != 3 or S != 3                                     */
-#define TDC_ERR_CHANNELS         -4  /* C not a multiple of 8 (v0) / 64 (ws)                 */
+#define TDC_ERR_CHANNELS         -4  /* C not a multiple of 8 (v0, fwd) / 64 (ws)            */
 #define TDC_ERR_PAD              -5  /* pad < 0                                             */
 #define TDC_ERR_N_STAGE          -6  /* n_stage not in {2, 3, 4}                             */
 #define TDC_ERR_ALIGNMENT        -7  /* x, w or y not 16-byte aligned                        */
@@ -55,6 +55,7 @@ extern "C" {
 #define TDC_ERR_TMA_ENCODE      -10  /* cuTensorMapEncodeTiled rejected the descriptor       */
 #define TDC_ERR_DEVICE_TIMEOUT  -11  /* a kernel gave up waiting on a pipeline barrier       */
 #define TDC_ERR_NO_DEVICE       -12  /* no usable sm_100 device is current                   */
+#define TDC_ERR_ACT             -13  /* unknown activation code (tdc_dwconv3x3_fwd)          */
 
 /* Human-readable text for a status code (static storage, never NULL). */
 TDC_API const char* tdc_strerror(int code);
@@ -88,6 +89,27 @@ TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y,
                           int64_t N, int64_t H, int64_t W, int64_t C,
                           int64_t R, int64_t S, int64_t pad, int64_t n_stage,
                           void* stream);
+
+/* ---- general forward ---------------------------------------------------------
+ * The ws kernel widened beyond the reference's surface: any C % 8 == 0 (the
+ * reference's ws requires C % 64) and an optional fused epilogue, computed
+ * per output in fp32 with one rounding to fp16 at the end:
+ *   t = sum_{r,s} x*w  (as above);  t += bias[c];  t = act(t);  t += residual[n,p,q,c]
+ *   y = fp16_rne(t)
+ * act: TDC_ACT_NONE, TDC_ACT_RELU (t < 0 ? +0 : t), TDC_ACT_RELU6
+ * (min(relu(t), 6)), TDC_ACT_SILU (t / (1 + expf(-t))).
+ * bias: fp16 [C] or NULL; residual: fp16 [N,P,Q,C] or NULL (may be y itself).
+ * No counterpart in the reference; the epilogue is what a depthwise block
+ * applies next (bias, activation, skip connection), saving a full pass over y. */
+#define TDC_ACT_NONE  0
+#define TDC_ACT_RELU  1
+#define TDC_ACT_RELU6 2
+#define TDC_ACT_SILU  3
+
+TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
+                              const void* residual, void* y,
+                              int64_t N, int64_t H, int64_t W, int64_t C,
+                              int64_t pad, int64_t act, int64_t n_stage, void* stream);
 
 /* Number of rows of the stall tensor that tdc_dwconv_ws_probe writes for
  * this problem (= number of CTAs the launch uses). */

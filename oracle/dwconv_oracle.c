@@ -84,6 +84,28 @@ void oracle_output_hw(int64_t H, int64_t W, int64_t pad, int64_t* P, int64_t* Q)
   *Q = W + 2 * pad - 3 + 1;
 }
 
+/* Activation codes of the general forward's fused epilogue. */
+enum { ORACLE_ACT_NONE = 0, ORACLE_ACT_RELU = 1, ORACLE_ACT_RELU6 = 2, ORACLE_ACT_SILU = 3 };
+
+static float oracle_act(float t, int act) {
+  if (act == ORACLE_ACT_RELU) return t < 0.0f ? 0.0f : t;
+  if (act == ORACLE_ACT_RELU6) return t < 0.0f ? 0.0f : (t > 6.0f ? 6.0f : t);
+  if (act == ORACLE_ACT_SILU) return t / (1.0f + expf(-t));
+  return t;
+}
+
+/*
+ * General forward with the fused epilogue (no counterpart in the reference):
+ *   t = chain_{r,s} fmaf(x, w, acc)            (as below)
+ *   t = t + bias[c]      if bias != NULL       (fp32)
+ *   t = act(t)                                 (fp32; relu/relu6 exact, silu via expf)
+ *   t = t + residual[n,p,q,c] if residual      (fp32)
+ *   y = f16_rne(t)
+ */
+int oracle_dwconv3x3_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                            const uint16_t* residual, uint16_t* y, int64_t N, int64_t H,
+                            int64_t W, int64_t C, int64_t pad, int act, int threads);
+
 /*
  * y[n,p,q,c] = f16_rne( chain_{r=0..2, s=0..2} fmaf(x[n,p+r-pad,q+s-pad,c], w[r,s,c], acc) )
  * x: [N,H,W,C] fp16 bits, w: [3,3,C] fp16 bits, y: [N,P,Q,C] fp16 bits.
@@ -92,6 +114,12 @@ void oracle_output_hw(int64_t H, int64_t W, int64_t pad, int64_t* P, int64_t* Q)
  */
 int oracle_dwconv3x3_f16(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t N,
                          int64_t H, int64_t W, int64_t C, int64_t pad, int threads) {
+  return oracle_dwconv3x3_ex_f16(x, w, NULL, NULL, y, N, H, W, C, pad, ORACLE_ACT_NONE, threads);
+}
+
+int oracle_dwconv3x3_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                            const uint16_t* residual, uint16_t* y, int64_t N, int64_t H,
+                            int64_t W, int64_t C, int64_t pad, int act, int threads) {
   if (!x || !w || !y || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0) return -1;
   int64_t P, Q;
   oracle_output_hw(H, W, pad, &P, &Q);
@@ -159,7 +187,14 @@ int oracle_dwconv3x3_f16(const uint16_t* x, const uint16_t* w, uint16_t* y, int6
               const float* wr = wf + (r * 3 + s) * C;
               for (int64_t c = 0; c < C; ++c) acc[c] = fmaf(xr[c], wr[c], acc[c]);
             }
-          for (int64_t c = 0; c < C; ++c) out[q * C + c] = oracle_f32_to_f16(acc[c]);
+          const uint16_t* res = residual ? residual + np * Q * C + q * C : NULL;
+          for (int64_t c = 0; c < C; ++c) {
+            float t = acc[c];
+            if (bias) t = t + lut[bias[c]];
+            t = oracle_act(t, act);
+            if (res) t = t + lut[res[c]];
+            out[q * C + c] = oracle_f32_to_f16(t);
+          }
         }
       }
     }

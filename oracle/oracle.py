@@ -39,6 +39,9 @@ def load() -> ctypes.CDLL:
         i64 = ctypes.c_int64
         lib.oracle_dwconv3x3_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 5 + [ctypes.c_int]
         lib.oracle_dwconv3x3_f16.restype = ctypes.c_int
+        lib.oracle_dwconv3x3_ex_f16.argtypes = ([ctypes.c_void_p] * 5 + [i64] * 5 +
+                                                [ctypes.c_int, ctypes.c_int])
+        lib.oracle_dwconv3x3_ex_f16.restype = ctypes.c_int
         lib.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
         lib.oracle_f16_to_f32.restype = ctypes.c_float
         lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
@@ -74,6 +77,60 @@ def dwconv_f16(x: np.ndarray, w: np.ndarray, pad: int, threads: int = 0) -> np.n
     if rc != 0:
         raise RuntimeError("oracle_dwconv3x3_f16 failed")
     return y
+
+
+ACTS = {"none": 0, "relu": 1, "relu6": 2, "silu": 3}
+
+
+def dwconv_ex_f16(x: np.ndarray, w: np.ndarray, pad: int, bias: np.ndarray | None = None,
+                  residual: np.ndarray | None = None, activation: str = "none",
+                  threads: int = 0) -> np.ndarray:
+    """C oracle of the general forward with its fused epilogue (any C; see
+    dwconv_oracle.c: t = acc + bias; t = act(t); t += residual; fp16 RNE)."""
+    lib = load()
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    N, H, W, C = x.shape
+    P, Q = output_hw(H, W, pad)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float16)
+    r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float16)
+    if b is not None and b.shape != (C,):
+        raise ValueError("bias must be [C]")
+    if r is not None and r.shape != (N, P, Q, C):
+        raise ValueError("residual must be [N,P,Q,C]")
+    y = np.empty((N, P, Q, C), dtype=np.float16)
+    rc = lib.oracle_dwconv3x3_ex_f16(x.ctypes.data, w.ctypes.data,
+                                     None if b is None else b.ctypes.data,
+                                     None if r is None else r.ctypes.data, y.ctypes.data,
+                                     N, H, W, C, pad, ACTS[activation], int(threads))
+    if rc != 0:
+        raise RuntimeError("oracle_dwconv3x3_ex_f16 failed")
+    return y
+
+
+def dwconv_ex_f16_numpy(x, w, pad, bias=None, residual=None, activation="none"):
+    """numpy restatement of the general forward (small sizes)."""
+    N, H, W, C = x.shape
+    P, Q = output_hw(H, W, pad)
+    xp = np.zeros((N, H + 2 * pad, W + 2 * pad, C), dtype=np.float32)
+    xp[:, pad:pad + H, pad:pad + W, :] = np.asarray(x, np.float16).astype(np.float32)
+    wf = np.asarray(w, np.float16).astype(np.float32)
+    t = np.zeros((N, P, Q, C), dtype=np.float32)
+    for rr in range(3):
+        for ss in range(3):
+            t = t + xp[:, rr:rr + P, ss:ss + Q, :] * wf[rr, ss]
+    if bias is not None:
+        t = t + np.asarray(bias, np.float16).astype(np.float32)
+    if activation == "relu":
+        t = np.where(t < 0, np.float32(0), t)
+    elif activation == "relu6":
+        t = np.where(t < 0, np.float32(0), np.where(t > 6, np.float32(6), t))
+    elif activation == "silu":
+        with np.errstate(over="ignore"):
+            t = (t / (np.float32(1) + np.exp(-t))).astype(np.float32)
+    if residual is not None:
+        t = t + np.asarray(residual, np.float16).astype(np.float32)
+    return t.astype(np.float16)
 
 
 def dwconv_f16_numpy(x: np.ndarray, w: np.ndarray, pad: int) -> np.ndarray:

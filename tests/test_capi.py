@@ -105,6 +105,21 @@ def test_valid_call_without_device_reports_no_device(lib):
     assert lib.tdc_ws_probe_blocks(i64(2), i64(16), i64(16), i64(64), i64(1), i64(2), C.byref(nb)) == CODES["TDC_ERR_NO_DEVICE"]
 
 
+def test_general_forward_argument_errors(lib):
+    p = C.c_void_p
+    def fwd(C_=72, act=0, bias=None, res=None, x=16, ns=2):
+        return lib.tdc_dwconv3x3_fwd(p(x), p(16), bias, res, p(16), i64(2), i64(16), i64(16),
+                                     i64(C_), i64(1), i64(act), i64(ns), None)
+    assert fwd(act=4) == CODES["TDC_ERR_ACT"]
+    assert fwd(act=-1) == CODES["TDC_ERR_ACT"]
+    assert fwd(C_=12) == CODES["TDC_ERR_CHANNELS"]
+    assert fwd(ns=5) == CODES["TDC_ERR_N_STAGE"]
+    assert fwd(bias=p(20)) == CODES["TDC_ERR_ALIGNMENT"]
+    assert fwd(res=p(24)) == CODES["TDC_ERR_ALIGNMENT"]
+    if not torch.cuda.is_available():
+        assert fwd() == CODES["TDC_ERR_NO_DEVICE"]
+
+
 def test_probe_and_status_argument_errors(lib):
     p = C.c_void_p(16)
     assert lib.tdc_dwconv_ws_probe(p, p, p, i64(2), i64(16), i64(16), i64(64), i64(3), i64(3),
@@ -146,7 +161,8 @@ def segments(pl, P, g):
 
 SHAPES = [(64, 224, 336, 256, 1), (32, 224, 336, 256, 1), (16, 112, 224, 128, 1), (8, 56, 56, 256, 1),
           (2, 16, 16, 64, 1), (1, 1, 1, 64, 1), (1, 3, 3, 64, 5), (3, 7, 45, 128, 1), (5, 100, 1, 64, 1),
-          (1, 1000, 40, 64, 0), (80, 224, 336, 320, 1), (8, 224, 336, 256, 1)]
+          (1, 1000, 40, 64, 0), (80, 224, 336, 320, 1), (8, 224, 336, 256, 1), (2, 19, 45, 72, 1),
+          (3, 9, 9, 8, 0)]
 
 
 @pytest.mark.parametrize("N,H,W,Cc,pad", SHAPES)
@@ -155,7 +171,7 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
     pl = _plan(lib, N, H, W, Cc, pad, ns)
     P, Q = H + 2 * pad - 2, W + 2 * pad - 2
     assert pl["stage_rows"] >= 1
-    assert pl["cblocks"] == Cc // 64 and pl["qstrips"] == -(-Q // 32)
+    assert pl["cblocks"] == -(-Cc // 64) and pl["qstrips"] == -(-Q // 32)
     assert pl["strips"] == N * pl["qstrips"] * pl["cblocks"]
     assert pl["full_units"] % pl["grid"] == 0 and 0 <= pl["full_units"] < pl["strips"]
     assert pl["strips"] - pl["full_units"] <= pl["grid"]

@@ -11,6 +11,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <optional>
 #include <tuple>
 
 #include "tdc_dwconv.h"
@@ -135,6 +136,41 @@ torch::Tensor dwconv_ws_withhold(torch::Tensor x, torch::Tensor w, int64_t pad, 
   return y;
 }
 
+// General forward: C % 8, optional bias [C], activation, residual [N,P,Q,C]
+
+torch::Tensor dwconv3x3(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
+                        std::optional<torch::Tensor> residual, int64_t pad, int64_t act,
+                        int64_t n_stage) {
+  check_common(x, w);
+  TORCH_CHECK(w.size(0) == 3 && w.size(1) == 3, "only 3x3 kernel supported");
+  TORCH_CHECK(w.size(2) == x.size(3), "channel mismatch");
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = alloc_out(x, pad);
+  const void* bptr = nullptr;
+  const void* rptr = nullptr;
+  if (bias.has_value()) {
+    const auto& b = *bias;
+    TORCH_CHECK(b.is_cuda() && b.device() == x.device() && b.scalar_type() == torch::kHalf &&
+                    b.is_contiguous() && b.dim() == 1 && b.size(0) == x.size(3),
+                "bias must be a contiguous fp16 [C] tensor on x's device");
+    bptr = b.data_ptr();
+  }
+  if (residual.has_value()) {
+    const auto& r = *residual;
+    TORCH_CHECK(r.is_cuda() && r.device() == x.device() && r.scalar_type() == torch::kHalf &&
+                    r.is_contiguous() && r.sizes() == y.sizes(),
+                "residual must be a contiguous fp16 [N,P,Q,C] tensor on x's device");
+    rptr = r.data_ptr();
+  }
+  check_status(tdc_dwconv3x3_fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0),
+                                 x.size(1), x.size(2), x.size(3), pad, act, n_stage, stream_of(x)),
+               "dwconv3x3");
+  return y;
+}
+
 // (code, block, stage, load) of the first pipeline-wait failure recorded on
 // `device` since the last clear; code 0 = none.  Synchronises the device.
 std::tuple<int64_t, int64_t, int64_t, int64_t> device_status(int64_t device, bool clear) {
@@ -171,6 +207,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "(tests the failure path; see device_status).",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("n_stage"),
         pybind11::arg("withhold_load"), pybind11::arg("timeout_ns"));
+  m.def("dwconv3x3", &tma_dwconv::dwconv3x3,
+        "General forward: C % 8, fused bias / activation / residual epilogue.",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("bias"), pybind11::arg("residual"),
+        pybind11::arg("pad"), pybind11::arg("act"), pybind11::arg("n_stage"));
   m.def("device_status", &tma_dwconv::device_status,
         "(code, block, stage, load) of the first recorded pipeline-wait failure on a device.",
         pybind11::arg("device"), pybind11::arg("clear") = true);

@@ -44,7 +44,7 @@ struct DeviceInfo {
   std::once_flag once;
   int status = TDC_ERR_NO_DEVICE;
   int sms = 0;
-  int ws_occupancy[3][2] = {};  // [n_stage-2][probe]
+  int ws_occupancy[3][3] = {};  // [n_stage-2][plain, probe, fused]
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -52,9 +52,9 @@ constexpr int kMaxDynSmem = 200 * 1024;
 
 int stage_rows_for(int64_t n_stage);
 
-template <int NS, bool PROBE>
+template <int NS, bool PROBE, bool FUSED = false>
 cudaError_t prepare_ws(int* occ) {
-  auto* k = &tdc::dwconv_ws_kernel<NS, PROBE>;
+  auto* k = &tdc::dwconv_ws_kernel<NS, PROBE, FUSED>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   if (e != cudaSuccess) return e;
   // Occupancy at the ring this instantiation uses.
@@ -91,6 +91,9 @@ int current_device(DeviceInfo** info, int* dev_out) {
     if (e2 == cudaSuccess) e2 = prepare_ws<2, true>(&d.ws_occupancy[0][1]);
     if (e2 == cudaSuccess) e2 = prepare_ws<3, true>(&d.ws_occupancy[1][1]);
     if (e2 == cudaSuccess) e2 = prepare_ws<4, true>(&d.ws_occupancy[2][1]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<2, false, true>(&d.ws_occupancy[0][2]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<3, false, true>(&d.ws_occupancy[1][2]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<4, false, true>(&d.ws_occupancy[2][2]);
     if (e2 != cudaSuccess) {
       t_last_cuda_error = int(e2);
       d.status = TDC_ERR_CUDA;
@@ -157,7 +160,7 @@ WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, in
   WsPlan pl{};
   pl.stage_rows = stage_rows_for(n_stage);
   pl.qstrips = int((Q + tdc::kStripQ - 1) / tdc::kStripQ);
-  pl.cblocks = int(C / tdc::kBlockC);
+  pl.cblocks = int((C + tdc::kBlockC - 1) / tdc::kBlockC);
   pl.strips = N * pl.qstrips * pl.cblocks;
   const int64_t g0 = std::max<int64_t>(1, sms * ctas_per_sm);
   const int64_t total_rows = pl.strips * P;
@@ -220,21 +223,32 @@ int check_ws_limits(int64_t N, int64_t H, int64_t W, int64_t C, int64_t P, int64
   return TDC_OK;
 }
 
-template <int NS, bool PROBE>
+template <int NS, bool PROBE, bool FUSED = false>
 cudaError_t launch_ws_t(const CUtensorMap& map, const tdc::WsParams& prm, const WsPlan& pl,
                         cudaStream_t st) {
-  tdc::dwconv_ws_kernel<NS, PROBE>
+  tdc::dwconv_ws_kernel<NS, PROBE, FUSED>
       <<<dim3(unsigned(pl.grid)), dim3(tdc::kWsThreads), pl.smem, st>>>(map, prm);
   return cudaGetLastError();
 }
 
+struct Epilogue {
+  bool fused = false;
+  const void* bias = nullptr;
+  const void* residual = nullptr;
+  int act = TDC_ACT_NONE;
+};
+
 int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
               int64_t R, int64_t S, int64_t pad, int64_t n_stage, unsigned long long* stall,
-              bool probe, int64_t withhold, int64_t timeout_ns, void* stream) {
+              bool probe, int64_t withhold, int64_t timeout_ns, void* stream,
+              const Epilogue& epi = Epilogue()) {
   int64_t P = 0, Q = 0;
   bool empty = false;
-  int rc = validate(x, w, y, N, H, W, C, R, S, pad, tdc::kBlockC, &P, &Q, &empty);
+  int rc = validate(x, w, y, N, H, W, C, R, S, pad, epi.fused ? 8 : tdc::kBlockC, &P, &Q, &empty);
   if (rc != TDC_OK) return rc;
+  if (epi.fused && !empty &&
+      ((epi.bias && !aligned16(epi.bias)) || (epi.residual && !aligned16(epi.residual))))
+    return TDC_ERR_ALIGNMENT;
   if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
   rc = check_ws_limits(N, H, W, C, P, Q);
   if (rc != TDC_OK) return rc;
@@ -243,7 +257,7 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   DeviceInfo* dev = nullptr;
   rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;
-  const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][probe ? 1 : 0]);
+  const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][epi.fused ? 2 : probe ? 1 : 0]);
   const WsPlan pl = make_plan(N, P, Q, C, n_stage, dev->sms, occ);
   alignas(64) CUtensorMap map;
   rc = encode_x_map(&map, x, N, H, W, C, pl.stage_rows);
@@ -259,8 +273,19 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
   prm.timeout_ns = uint64_t(timeout_ns > 0 ? timeout_ns : g_timeout_ns.load());
   prm.withhold = withhold;
+  prm.bias = static_cast<const __half*>(epi.bias);
+  prm.residual = static_cast<const __half*>(epi.residual);
+  prm.act = epi.act;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (epi.fused) {
+    switch (n_stage) {
+      case 2: e = launch_ws_t<2, false, true>(map, prm, pl, st); break;
+      case 3: e = launch_ws_t<3, false, true>(map, prm, pl, st); break;
+      default: e = launch_ws_t<4, false, true>(map, prm, pl, st); break;
+    }
+    return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+  }
   switch (n_stage) {
     case 2: e = probe ? launch_ws_t<2, true>(map, prm, pl, st) : launch_ws_t<2, false>(map, prm, pl, st); break;
     case 3: e = probe ? launch_ws_t<3, true>(map, prm, pl, st) : launch_ws_t<3, false>(map, prm, pl, st); break;
@@ -279,7 +304,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_NULL_POINTER: return "null pointer argument";
     case TDC_ERR_BAD_SHAPE: return "bad shape: N,H,W,C must be non-negative with H,W >= 1 and a non-negative output size";
     case TDC_ERR_FILTER_SHAPE: return "only 3x3 kernel supported";
-    case TDC_ERR_CHANNELS: return "C must be a multiple of the channel block (8 for v0, 64 for ws)";
+    case TDC_ERR_CHANNELS: return "C must be a multiple of 8 (v0, general forward) or 64 (ws)";
     case TDC_ERR_PAD: return "pad must be non-negative";
     case TDC_ERR_N_STAGE: return "n_stage must be one of {2, 3, 4}";
     case TDC_ERR_ALIGNMENT: return "x, w and y must be 16-byte aligned";
@@ -288,6 +313,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_TMA_ENCODE: return "cuTensorMapEncodeTiled failed";
     case TDC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on a pipeline barrier";
     case TDC_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case TDC_ERR_ACT: return "activation code is not one of TDC_ACT_NONE, _RELU, _RELU6, _SILU";
     default: return "unknown tdc status code";
   }
 }
@@ -327,6 +353,18 @@ TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y, int64_t N, int6
                           int64_t C, int64_t R, int64_t S, int64_t pad, int64_t n_stage,
                           void* stream) {
   return ws_common(x, w, y, N, H, W, C, R, S, pad, n_stage, nullptr, false, -1, 0, stream);
+}
+
+TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
+                              const void* residual, void* y, int64_t N, int64_t H, int64_t W,
+                              int64_t C, int64_t pad, int64_t act, int64_t n_stage, void* stream) {
+  if (act < TDC_ACT_NONE || act > TDC_ACT_SILU) return TDC_ERR_ACT;
+  Epilogue epi;
+  epi.fused = true;
+  epi.bias = bias;
+  epi.residual = residual;
+  epi.act = int(act);
+  return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, -1, 0, stream, epi);
 }
 
 TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
@@ -394,8 +432,8 @@ TDC_API int tdc_dwconv_ws_withhold(const void* x, const void* w, void* y, int64_
 TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad, int64_t n_stage,
                         int64_t sms, int64_t ctas_per_sm, int64_t* plan) {
   if (!plan) return TDC_ERR_NULL_POINTER;
-  if (N < 1 || H < 1 || W < 1 || C < tdc::kBlockC) return TDC_ERR_BAD_SHAPE;
-  if (C % tdc::kBlockC != 0) return TDC_ERR_CHANNELS;
+  if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
   if (pad < 0) return TDC_ERR_PAD;
   if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
   if (sms < 1 || ctas_per_sm < 1) return TDC_ERR_BAD_SHAPE;

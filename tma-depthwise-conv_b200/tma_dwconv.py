@@ -20,7 +20,11 @@ import torch.nn.functional as F
 import _tma_dwconv_C as _C  # type: ignore
 
 __all__ = ["dwconv_v0", "dwconv_ws", "dwconv_ws_probe", "ref_dwconv",
-           "dwconv_ws_out", "device_status", "set_wait_timeout_ns", "CONSUMER_WARPS"]
+           "dwconv_ws_out", "dwconv3x3", "device_status", "set_wait_timeout_ns",
+           "CONSUMER_WARPS", "ACTIVATIONS"]
+
+#: Activations the general forward fuses into its epilogue.
+ACTIVATIONS = {"none": 0, "relu": 1, "relu6": 2, "silu": 3}
 
 #: Consumer warps per CTA of the ws kernel (divide stall columns 1 and 3 by it
 #: for per-warp figures, as the reference's probe report does).
@@ -126,6 +130,32 @@ def dwconv_ws_probe(x: torch.Tensor, w: torch.Tensor,
     """
     _check_ws(x, w, pad, n_stage, "dwconv_ws_probe")
     return _C.dwconv_ws_probe(x, w, int(pad), int(n_stage))
+
+
+def dwconv3x3(x: torch.Tensor, w: torch.Tensor, pad: int = 1,
+              bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+              activation: str = "none", n_stage: int = 2) -> torch.Tensor:
+    """General forward beyond the reference surface (same kernel as ``dwconv_ws``).
+
+    Any C % 8 == 0 (``dwconv_ws`` keeps the reference's C % 64), and an
+    optional fused epilogue computed per output in fp32 with one rounding at
+    the end: ``t = conv + bias[c]; t = activation(t); t = t + residual``.
+
+    Args:
+        x: [N, H, W, C] fp16 CUDA, contiguous.   w: [3, 3, C] fp16.
+        bias: [C] fp16 or None.   residual: [N, P, Q, C] fp16 or None.
+        activation: "none", "relu" (t < 0 ? 0 : t), "relu6", "silu" (t / (1 + exp(-t))).
+    """
+    _check(x, w, pad)
+    if w.shape[0] != 3 or w.shape[1] != 3:
+        raise ValueError("only 3x3 kernels are supported")
+    if x.shape[3] % 8 != 0:
+        raise ValueError("dwconv3x3 requires C % 8 == 0")
+    if n_stage not in (2, 3, 4):
+        raise ValueError(f"n_stage must be one of {{2, 3, 4}}, got {n_stage}")
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
+    return _C.dwconv3x3(x, w, bias, residual, int(pad), ACTIVATIONS[activation], int(n_stage))
 
 
 def device_status(device: int | None = None, clear: bool = True):
