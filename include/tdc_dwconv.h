@@ -56,12 +56,14 @@ extern "C" {
 #define TDC_ERR_DEVICE_TIMEOUT  -11  /* a kernel gave up waiting on a pipeline barrier       */
 #define TDC_ERR_NO_DEVICE       -12  /* no usable sm_100 device is current                   */
 #define TDC_ERR_ACT             -13  /* unknown activation code (tdc_dwconv3x3_fwd)          */
+#define TDC_ERR_WORKSPACE       -14  /* workspace too small (tdc_dwconv3x3_bwd_weight)       */
 
 /* Human-readable text for a status code (static storage, never NULL). */
 TDC_API const char* tdc_strerror(int code);
 
 /* cudaError_t of the most recent failing CUDA call made by this thread
- * inside the library (0 if none). */
+ * inside the library, or the CUresult of a failed cuTensorMapEncodeTiled
+ * (0 if none). */
 TDC_API int tdc_last_cuda_error(void);
 
 /* Output spatial size for a stride-1 RxS conv with symmetric padding:
@@ -111,6 +113,34 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
                               int64_t N, int64_t H, int64_t W, int64_t C,
                               int64_t pad, int64_t act, int64_t n_stage, void* stream);
 
+/* ---- backward ------------------------------------------------------------------
+ * Data gradient of the 3x3 forward (stride 1, padding pad):
+ *   dx[n,h,w,c] = sum_{r,s} dy[n, h+pad-r, w+pad-s, c] * w[r,s,c]   (dy = 0 outside)
+ * computed by the forward kernel on dy with the taps flipped (w[2-r][2-s])
+ * and padding 2 - pad (negative = a crop), fp32 chain in flipped-tap order,
+ * fp16 RNE.  dy: [N,P,Q,C] with P = H+2*pad-2 >= 1, Q likewise; dx: [N,H,W,C];
+ * C % 8 == 0.  No counterpart in the reference (forward only). */
+TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx,
+                                   int64_t N, int64_t H, int64_t W, int64_t C,
+                                   int64_t pad, int64_t n_stage, void* stream);
+
+/* Weight gradient of the 3x3 forward (stride 1, padding pad):
+ *   dw[r,s,c] = sum_{n,p,q} x[n, p+r-pad, q+s-pad, c] * dy[n,p,q,c]   (x = 0 outside)
+ * x: [N,H,W,C] fp16, dy: [N,P,Q,C] fp16, dw: [3,3,C] fp32 (written, not
+ * accumulated).  fp16 x fp16 products accumulated in fp32: per CTA and warp
+ * in a fixed order into `workspace`, then summed over the slices in a fixed
+ * order, so the result is bit-reproducible run to run.  `workspace` is
+ * caller-owned device memory of at least the size
+ * tdc_dwconv3x3_bwd_weight_workspace reports (it depends on the device's SM
+ * count); its contents need not be initialised.  C % 8 == 0.
+ * Two launches on `stream`.  No counterpart in the reference (forward only). */
+TDC_API int tdc_dwconv3x3_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
+                                               int64_t pad, int64_t n_stage, int64_t* bytes);
+TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw,
+                                     int64_t N, int64_t H, int64_t W, int64_t C,
+                                     int64_t pad, int64_t n_stage,
+                                     void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Number of rows of the stall tensor that tdc_dwconv_ws_probe writes for
  * this problem (= number of CTAs the launch uses). */
 TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C,
@@ -119,6 +149,12 @@ TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C,
 /* Consumer warps per CTA of the ws kernel (the divisor for column 1 and 3 of
  * the stall tensor when a per-warp figure is wanted). */
 TDC_API int tdc_ws_consumer_warps(void);
+
+/* Resident CTAs per SM of a ws kernel instantiation on the current device
+ * (kind 0 = ws, 1 = ws probe, 2 = general forward without epilogue / data
+ * gradient, 3 = general forward with an epilogue) and the
+ * device's SM count: the inputs tdc_ws_plan takes. */
+TDC_API int tdc_ws_occupancy(int64_t n_stage, int64_t kind, int64_t* ctas_per_sm, int64_t* sms);
 
 /* Launch plan the ws kernel would use on a device with `sms` SMs and
  * `ctas_per_sm` resident CTAs (pure host arithmetic, no CUDA call):

@@ -35,6 +35,9 @@ void check_status(int rc, const char* what) {
     TORCH_CHECK(false, what, ": ", tdc_strerror(rc), ": ",
                 cudaGetErrorString(static_cast<cudaError_t>(tdc_last_cuda_error())));
   }
+  if (rc == TDC_ERR_TMA_ENCODE) {
+    TORCH_CHECK(false, what, ": ", tdc_strerror(rc), " (CUresult ", tdc_last_cuda_error(), ")");
+  }
   TORCH_CHECK(false, what, ": ", tdc_strerror(rc), " (status ", rc, ")");
 }
 
@@ -171,6 +174,51 @@ torch::Tensor dwconv3x3(torch::Tensor x, torch::Tensor w, std::optional<torch::T
   return y;
 }
 
+// Data gradient: dy [N,P,Q,C] -> dx [N,H,W,C] with H = P - 2*pad + 2.
+torch::Tensor dwconv3x3_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, int64_t n_stage) {
+  check_common(dy, w);
+  TORCH_CHECK(w.size(0) == 3 && w.size(1) == 3 && w.size(2) == dy.size(3), "w must be [3,3,C]");
+  TORCH_CHECK(dy.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  const int64_t H = dy.size(1) - 2 * pad + 2, W = dy.size(2) - 2 * pad + 2;
+  TORCH_CHECK(H >= 1 && W >= 1, "dy is smaller than a 3x3 kernel with pad ", pad, " can produce");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  auto dx = torch::empty({dy.size(0), H, W, dy.size(3)}, dy.options());
+  if (dx.numel() == 0 || dy.numel() == 0) return dx.zero_();
+  check_status(tdc_dwconv3x3_bwd_data(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), dy.size(0), H, W,
+                                      dy.size(3), pad, n_stage, stream_of(dy)),
+               "dwconv3x3_bwd_data");
+  return dx;
+}
+
+// Weight gradient: x [N,H,W,C], dy [N,P,Q,C] -> dw [3,3,C] fp32 (workspace from
+// torch's caching allocator).
+torch::Tensor dwconv3x3_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t pad, int64_t n_stage) {
+  TORCH_CHECK(x.is_cuda() && dy.is_cuda() && x.device() == dy.device(), "tensors must live on CUDA");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf && dy.scalar_type() == torch::kHalf,
+              "x and dy must be fp16");
+  TORCH_CHECK(x.dim() == 4 && dy.dim() == 4 && x.is_contiguous() && dy.is_contiguous(),
+              "x and dy must be contiguous [N,H,W,C] / [N,P,Q,C]");
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(dy.size(0) == x.size(0) && dy.size(3) == x.size(3) &&
+                  dy.size(1) == x.size(1) + 2 * pad - 2 && dy.size(2) == x.size(2) + 2 * pad - 2,
+              "dy must be [N, H+2*pad-2, W+2*pad-2, C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dw = torch::zeros({3, 3, x.size(3)}, x.options().dtype(torch::kFloat32));
+  if (x.numel() == 0 || dy.numel() == 0) return dw;
+  int64_t bytes = 0;
+  check_status(tdc_dwconv3x3_bwd_weight_workspace(x.size(0), x.size(1), x.size(2), x.size(3), pad,
+                                                  n_stage, &bytes),
+               "dwconv3x3_bwd_weight");
+  auto ws = torch::empty({(bytes + 3) / 4}, x.options().dtype(torch::kFloat32));
+  check_status(tdc_dwconv3x3_bwd_weight(x.data_ptr(), dy.data_ptr(), dw.data_ptr<float>(),
+                                        x.size(0), x.size(1), x.size(2), x.size(3), pad, n_stage,
+                                        ws.data_ptr(), bytes, stream_of(x)),
+               "dwconv3x3_bwd_weight");
+  return dw;
+}
+
 // (code, block, stage, load) of the first pipeline-wait failure recorded on
 // `device` since the last clear; code 0 = none.  Synchronises the device.
 std::tuple<int64_t, int64_t, int64_t, int64_t> device_status(int64_t device, bool clear) {
@@ -211,6 +259,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "General forward: C % 8, fused bias / activation / residual epilogue.",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("bias"), pybind11::arg("residual"),
         pybind11::arg("pad"), pybind11::arg("act"), pybind11::arg("n_stage"));
+  m.def("dwconv3x3_bwd_data", &tma_dwconv::dwconv3x3_bwd_data,
+        "Data gradient of the 3x3 forward: dx [N,H,W,C] from dy [N,P,Q,C].", pybind11::arg("dy"),
+        pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("n_stage") = 2);
+  m.def("dwconv3x3_bwd_weight", &tma_dwconv::dwconv3x3_bwd_weight,
+        "Weight gradient of the 3x3 forward: dw [3,3,C] fp32 (deterministic).", pybind11::arg("x"),
+        pybind11::arg("dy"), pybind11::arg("pad"), pybind11::arg("n_stage") = 2);
   m.def("device_status", &tma_dwconv::device_status,
         "(code, block, stage, load) of the first recorded pipeline-wait failure on a device.",
         pybind11::arg("device"), pybind11::arg("clear") = true);

@@ -27,6 +27,7 @@
 
 #include "tdc_dwconv.h"
 #include "tdc_kernels.cuh"
+#include "tdc_wgrad.cuh"
 
 namespace {
 
@@ -44,7 +45,8 @@ struct DeviceInfo {
   std::once_flag once;
   int status = TDC_ERR_NO_DEVICE;
   int sms = 0;
-  int ws_occupancy[3][3] = {};  // [n_stage-2][plain, probe, fused]
+  int ws_occupancy[3][4] = {};  // [n_stage-2][ws, probe, general, epilogue]
+  int wgrad_occupancy[3] = {};  // [n_stage-2]
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -52,9 +54,20 @@ constexpr int kMaxDynSmem = 200 * 1024;
 
 int stage_rows_for(int64_t n_stage);
 
-template <int NS, bool PROBE, bool FUSED = false>
+int wgrad_stage_rows(int64_t n_stage);
+
+template <int NS>
+cudaError_t prepare_wgrad(int* occ) {
+  auto* k = &tdc::dwconv_wgrad_kernel<NS>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e != cudaSuccess) return e;
+  const size_t smem = size_t(NS) * wgrad_stage_rows(NS) * (tdc::kRowBytes + tdc::kDyRowBytes) + 128;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+}
+
+template <int NS, bool PROBE, int MODE = tdc::kModeWs>
 cudaError_t prepare_ws(int* occ) {
-  auto* k = &tdc::dwconv_ws_kernel<NS, PROBE, FUSED>;
+  auto* k = &tdc::dwconv_ws_kernel<NS, PROBE, MODE>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   if (e != cudaSuccess) return e;
   // Occupancy at the ring this instantiation uses.
@@ -70,6 +83,16 @@ int current_device(DeviceInfo** info, int* dev_out) {
                                    ? TDC_ERR_NO_DEVICE
                                    : cuda_fail(e);
   if (dev < 0 || dev >= kMaxDevices) return TDC_ERR_NO_DEVICE;
+  // Make the device's primary context current on this thread.  A thread that
+  // has only selected the device (for example a framework's worker thread)
+  // may have no current context yet; kernel launches would bind it lazily,
+  // but the driver's tensor-map encoder needs it bound.
+  thread_local int bound_device = -1;
+  if (bound_device != dev) {
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    bound_device = dev;
+  }
   DeviceInfo& d = g_dev[dev];
   std::call_once(d.once, [&d, dev]() {
     int major = 0, minor = 0, sms = 0;
@@ -91,9 +114,15 @@ int current_device(DeviceInfo** info, int* dev_out) {
     if (e2 == cudaSuccess) e2 = prepare_ws<2, true>(&d.ws_occupancy[0][1]);
     if (e2 == cudaSuccess) e2 = prepare_ws<3, true>(&d.ws_occupancy[1][1]);
     if (e2 == cudaSuccess) e2 = prepare_ws<4, true>(&d.ws_occupancy[2][1]);
-    if (e2 == cudaSuccess) e2 = prepare_ws<2, false, true>(&d.ws_occupancy[0][2]);
-    if (e2 == cudaSuccess) e2 = prepare_ws<3, false, true>(&d.ws_occupancy[1][2]);
-    if (e2 == cudaSuccess) e2 = prepare_ws<4, false, true>(&d.ws_occupancy[2][2]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<2, false, tdc::kModeGeneral>(&d.ws_occupancy[0][2]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<3, false, tdc::kModeGeneral>(&d.ws_occupancy[1][2]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<4, false, tdc::kModeGeneral>(&d.ws_occupancy[2][2]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<2, false, tdc::kModeEpilogue>(&d.ws_occupancy[0][3]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<3, false, tdc::kModeEpilogue>(&d.ws_occupancy[1][3]);
+    if (e2 == cudaSuccess) e2 = prepare_ws<4, false, tdc::kModeEpilogue>(&d.ws_occupancy[2][3]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<2>(&d.wgrad_occupancy[0]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<3>(&d.wgrad_occupancy[1]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<4>(&d.wgrad_occupancy[2]);
     if (e2 != cudaSuccess) {
       t_last_cuda_error = int(e2);
       d.status = TDC_ERR_CUDA;
@@ -115,12 +144,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // hands out null data pointers for zero-element tensors.
 int validate(const void* x, const void* w, const void* y, int64_t N, int64_t H, int64_t W,
              int64_t C, int64_t R, int64_t S, int64_t pad, int64_t cmult, int64_t* P,
-             int64_t* Q, bool* empty) {
+             int64_t* Q, bool* empty, bool allow_negative_pad = false) {
   if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
   if (R != 3 || S != 3) return TDC_ERR_FILTER_SHAPE;
   if (C % cmult != 0) return TDC_ERR_CHANNELS;
-  if (pad < 0) return TDC_ERR_PAD;
-  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (pad < 0 && !allow_negative_pad) return TDC_ERR_PAD;
+  if (pad > (1 << 28) || pad < -(1 << 28)) return TDC_ERR_TOO_LARGE;
   *P = H + 2 * pad - R + 1;
   *Q = W + 2 * pad - S + 1;
   if (*P < 0 || *Q < 0) return TDC_ERR_BAD_SHAPE;
@@ -149,6 +178,10 @@ constexpr int kRingRows = 12;
 constexpr int64_t kMinRowsPerCta = 8;
 
 int stage_rows_for(int64_t n_stage) { return std::max<int>(1, kRingRows / int(n_stage)); }
+
+// The weight-gradient ring carries x and dy rows (8448 B per row): 8 rows.
+constexpr int kWgradRingRows = 8;
+int wgrad_stage_rows(int64_t n_stage) { return std::max<int>(1, kWgradRingRows / int(n_stage)); }
 
 // Persistent grid of SMs x resident CTAs.  Whole strips are dealt
 // round-robin while every CTA can take one: full_units =
@@ -212,6 +245,24 @@ int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t 
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) t_last_cuda_error = int(r);
+  return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
+}
+
+// 4-D map over dy viewed as (C, Q, P, N); box (64 ch, 32 cols, stage_rows rows, 1 image).
+int encode_dy_map(CUtensorMap* map, const void* dy, int64_t N, int64_t P, int64_t Q, int64_t C,
+                  int stage_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return TDC_ERR_TMA_ENCODE;
+  const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(Q), cuuint64_t(P), cuuint64_t(N)};
+  const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(Q) * C * 2, cuuint64_t(P) * Q * C * 2};
+  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(tdc::kStripQ),
+                             cuuint32_t(stage_rows), 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(dy), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) t_last_cuda_error = int(r);
   return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
 }
 
@@ -223,10 +274,10 @@ int check_ws_limits(int64_t N, int64_t H, int64_t W, int64_t C, int64_t P, int64
   return TDC_OK;
 }
 
-template <int NS, bool PROBE, bool FUSED = false>
+template <int NS, bool PROBE, int MODE = tdc::kModeWs>
 cudaError_t launch_ws_t(const CUtensorMap& map, const tdc::WsParams& prm, const WsPlan& pl,
                         cudaStream_t st) {
-  tdc::dwconv_ws_kernel<NS, PROBE, FUSED>
+  tdc::dwconv_ws_kernel<NS, PROBE, MODE>
       <<<dim3(unsigned(pl.grid)), dim3(tdc::kWsThreads), pl.smem, st>>>(map, prm);
   return cudaGetLastError();
 }
@@ -236,6 +287,7 @@ struct Epilogue {
   const void* bias = nullptr;
   const void* residual = nullptr;
   int act = TDC_ACT_NONE;
+  bool flip_taps = false;  // data gradient: taps w[2-r][2-s], pad may be negative
 };
 
 int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
@@ -244,7 +296,10 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
               const Epilogue& epi = Epilogue()) {
   int64_t P = 0, Q = 0;
   bool empty = false;
-  int rc = validate(x, w, y, N, H, W, C, R, S, pad, epi.fused ? 8 : tdc::kBlockC, &P, &Q, &empty);
+  // The data gradient runs the forward with pad' = 2 - pad, which is negative
+  // (a crop) when pad > 2; TMA coordinates take it as it is.
+  int rc = validate(x, w, y, N, H, W, C, R, S, pad, epi.fused ? 8 : tdc::kBlockC, &P, &Q,
+                    &empty, epi.flip_taps);
   if (rc != TDC_OK) return rc;
   if (epi.fused && !empty &&
       ((epi.bias && !aligned16(epi.bias)) || (epi.residual && !aligned16(epi.residual))))
@@ -257,7 +312,10 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   DeviceInfo* dev = nullptr;
   rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;
-  const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][epi.fused ? 2 : probe ? 1 : 0]);
+  const bool with_epilogue =
+      epi.fused && (epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE);
+  const int kind = !epi.fused ? (probe ? 1 : 0) : (with_epilogue ? 3 : 2);
+  const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][kind]);
   const WsPlan pl = make_plan(N, P, Q, C, n_stage, dev->sms, occ);
   alignas(64) CUtensorMap map;
   rc = encode_x_map(&map, x, N, H, W, C, pl.stage_rows);
@@ -276,13 +334,22 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.bias = static_cast<const __half*>(epi.bias);
   prm.residual = static_cast<const __half*>(epi.residual);
   prm.act = epi.act;
+  prm.flip_taps = epi.flip_taps ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (with_epilogue) {
+    switch (n_stage) {
+      case 2: e = launch_ws_t<2, false, tdc::kModeEpilogue>(map, prm, pl, st); break;
+      case 3: e = launch_ws_t<3, false, tdc::kModeEpilogue>(map, prm, pl, st); break;
+      default: e = launch_ws_t<4, false, tdc::kModeEpilogue>(map, prm, pl, st); break;
+    }
+    return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+  }
   if (epi.fused) {
     switch (n_stage) {
-      case 2: e = launch_ws_t<2, false, true>(map, prm, pl, st); break;
-      case 3: e = launch_ws_t<3, false, true>(map, prm, pl, st); break;
-      default: e = launch_ws_t<4, false, true>(map, prm, pl, st); break;
+      case 2: e = launch_ws_t<2, false, tdc::kModeGeneral>(map, prm, pl, st); break;
+      case 3: e = launch_ws_t<3, false, tdc::kModeGeneral>(map, prm, pl, st); break;
+      default: e = launch_ws_t<4, false, tdc::kModeGeneral>(map, prm, pl, st); break;
     }
     return e == cudaSuccess ? TDC_OK : cuda_fail(e);
   }
@@ -313,6 +380,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_TMA_ENCODE: return "cuTensorMapEncodeTiled failed";
     case TDC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on a pipeline barrier";
     case TDC_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case TDC_ERR_WORKSPACE: return "workspace smaller than tdc_dwconv3x3_bwd_weight_workspace reports";
     case TDC_ERR_ACT: return "activation code is not one of TDC_ACT_NONE, _RELU, _RELU6, _SILU";
     default: return "unknown tdc status code";
   }
@@ -367,6 +435,100 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
   return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, -1, 0, stream, epi);
 }
 
+TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
+                                   int64_t W, int64_t C, int64_t pad, int64_t n_stage,
+                                   void* stream) {
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  // dy is [N, P, Q, C]; it must not be empty in P or Q (dx would be all zero).
+  const int64_t P = H + 2 * pad - 2, Q = W + 2 * pad - 2;
+  if (H < 1 || W < 1 || P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
+  Epilogue epi;
+  epi.fused = true;
+  epi.flip_taps = true;
+  // dx[n,h,w,c] = sum_{r,s} dy[n, h+pad-r, w+pad-s, c] * w[r,s,c]
+  //            = forward(dy, w[2-r][2-s], pad' = 2 - pad)
+  return ws_common(dy, w, dx, N, P, Q, C, 3, 3, 2 - pad, n_stage, nullptr, false, -1, 0, stream,
+                   epi);
+}
+
+// Plan of the weight-gradient launch: the forward planner over dy's strips.
+int wgrad_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad, int64_t n_stage,
+               WsPlan* pl, int64_t* P, int64_t* Q) {
+  if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  *P = H + 2 * pad - 2;
+  *Q = W + 2 * pad - 2;
+  if (*P < 1 || *Q < 1) return TDC_ERR_BAD_SHAPE;
+  int rc = check_ws_limits(N, H, W, C, *P, *Q);
+  if (rc != TDC_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  *pl = make_plan(N, *P, *Q, C, n_stage, dev->sms, std::max(1, dev->wgrad_occupancy[n_stage - 2]));
+  pl->stage_rows = wgrad_stage_rows(n_stage);
+  pl->smem = size_t(n_stage) * pl->stage_rows * (tdc::kRowBytes + tdc::kDyRowBytes) + 128;
+  return TDC_OK;
+}
+
+int64_t wgrad_workspace_bytes(const WsPlan& pl, int64_t C) {
+  return pl.grid * tdc::kConsumerWarps * 9 * C * int64_t(sizeof(float));
+}
+
+TDC_API int tdc_dwconv3x3_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
+                                               int64_t pad, int64_t n_stage, int64_t* bytes) {
+  if (!bytes) return TDC_ERR_NULL_POINTER;
+  WsPlan pl;
+  int64_t P, Q;
+  const int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  *bytes = wgrad_workspace_bytes(pl, C);
+  return TDC_OK;
+}
+
+TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, int64_t N,
+                                     int64_t H, int64_t W, int64_t C, int64_t pad,
+                                     int64_t n_stage, void* workspace, int64_t workspace_bytes,
+                                     void* stream) {
+  if (!x || !dy || !dw || !workspace) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dw) || !aligned16(workspace))
+    return TDC_ERR_ALIGNMENT;
+  WsPlan pl;
+  int64_t P, Q;
+  int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (workspace_bytes < wgrad_workspace_bytes(pl, C)) return TDC_ERR_WORKSPACE;
+  alignas(64) CUtensorMap xmap, dymap;
+  rc = encode_x_map(&xmap, x, N, H, W, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  tdc::WgradParams g{};
+  g.partial = static_cast<float*>(workspace);
+  g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
+  g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
+  g.tail_bands = pl.tail_bands; g.tail_band_rows = pl.tail_band_rows;
+  g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
+  g.timeout_ns = uint64_t(g_timeout_ns.load());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(unsigned(pl.grid)), block(tdc::kWsThreads);
+  switch (n_stage) {
+    case 2: tdc::dwconv_wgrad_kernel<2><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+    case 3: tdc::dwconv_wgrad_kernel<3><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+    default: tdc::dwconv_wgrad_kernel<4><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  const int n = int(9 * C);
+  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
+      static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
 TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
                                 int64_t n_stage, int64_t* num_blocks) {
   if (!num_blocks) return TDC_ERR_NULL_POINTER;
@@ -389,6 +551,18 @@ TDC_API int tdc_ws_probe_blocks(int64_t N, int64_t H, int64_t W, int64_t C, int6
 }
 
 TDC_API int tdc_ws_consumer_warps(void) { return tdc::kConsumerWarps; }
+
+TDC_API int tdc_ws_occupancy(int64_t n_stage, int64_t kind, int64_t* ctas_per_sm, int64_t* sms) {
+  if (!ctas_per_sm || !sms) return TDC_ERR_NULL_POINTER;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (kind < 0 || kind > 3) return TDC_ERR_BAD_SHAPE;
+  DeviceInfo* dev = nullptr;
+  const int rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  *ctas_per_sm = dev->ws_occupancy[n_stage - 2][kind];
+  *sms = dev->sms;
+  return TDC_OK;
+}
 
 TDC_API int tdc_dwconv_ws_probe(const void* x, const void* w, void* y, int64_t N, int64_t H,
                                 int64_t W, int64_t C, int64_t R, int64_t S, int64_t pad,

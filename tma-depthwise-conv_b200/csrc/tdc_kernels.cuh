@@ -103,9 +103,10 @@ struct WsParams {
   const __half* w;
   __half* y;
   unsigned long long* stall;  // probe only
-  const __half* bias;         // fused path only: [C] or null
-  const __half* residual;     // fused path only: [N,P,Q,C] or null
-  int32_t act;                // fused path only: TDC_ACT_*
+  const __half* bias;         // kModeEpilogue only: [C] or null
+  const __half* residual;     // kModeEpilogue only: [N,P,Q,C] or null
+  int32_t act;                // kModeEpilogue only: TDC_ACT_*
+  int32_t flip_taps;          // kModeGeneral / kModeEpilogue: use w[2-r][2-s] (data gradient)
   int32_t H, W, C, P, Q, pad;
   int32_t qstrips, cblocks, stage_rows;
   int32_t tail_bands, tail_band_rows;
@@ -203,25 +204,33 @@ __device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2],
 // Fused epilogue of the general forward, per output (fp32 throughout, one
 // rounding to fp16 at the end):
 //   t = acc; t += bias[c]; t = act(t); t += residual[n,p,q,c]
-// relu: t < 0 ? +0 : t;  relu6: min(relu(t), 6);  silu: t / (1 + expf(-t)).
+// relu: t < 0 ? +0 : t;  relu6: min(relu(t), 6) (both exact);
+// silu: t / (1 + exp(-t)) with the fast exp and divide intrinsics (a few fp32
+// ulp, far below the fp16 rounding of the result).
 __device__ __forceinline__ float apply_act(float t, int act) {
   if (act == TDC_ACT_RELU) return t < 0.f ? 0.f : t;
   if (act == TDC_ACT_RELU6) return t < 0.f ? 0.f : (t > 6.f ? 6.f : t);
-  if (act == TDC_ACT_SILU) return t / (1.f + expf(-t));
+  if (act == TDC_ACT_SILU) return __fdividef(t, 1.f + __expf(-t));
   return t;
 }
+
+// Kernel variants.
+constexpr int kModeWs = 0;        // the reference surface: C % 64, plain output
+constexpr int kModeGeneral = 1;   // C % 8 (partial last channel block), optional flipped taps
+constexpr int kModeEpilogue = 2;  // kModeGeneral + bias / activation / residual
 
 // Resident CTAs per SM the kernel is compiled for (bounds its registers).
 #ifndef TDC_MIN_BLOCKS
 #define TDC_MIN_BLOCKS 1
 #endif
 
-// FUSED = the general forward: C % 8 (the last 64-channel block may be
-// partial: TMA zero-fills the missing channels, their lanes neither read
-// taps nor store) and the epilogue above.  FUSED = false is the ws call of
-// the reference surface (C % 64, plain output).
-template <int NS, bool PROBE, bool FUSED = false>
-__global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
+// MODE (kMode*): kModeGeneral lets the last 64-channel block be partial (TMA
+// zero-fills the missing channels; their lanes neither read taps nor store)
+// and can flip the taps (the data gradient); kModeEpilogue adds the fused
+// epilogue.  kModeWs is the ws call of the reference surface.
+template <int NS, bool PROBE, int MODE = kModeWs>
+__global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOCKS)
+    dwconv_ws_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
   __shared__ __align__(8) uint64_t full_bar[NS];
   __shared__ __align__(8) uint64_t empty_bar[NS];
@@ -321,15 +330,18 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
     const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
     const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
     // This lane's channel pair exists (always on the ws path, C % 64 == 0).
-    const bool chan_ok = !FUSED || c0 + 2 * lane < p.C;
+    const bool chan_ok = MODE == kModeWs || c0 + 2 * lane < p.C;
     if (sg.cb != last_cb) {
       const uint32_t* wp = reinterpret_cast<const uint32_t*>(p.w + c0) + lane;
 #pragma unroll
-      for (int k = 0; k < 9; ++k) wt[k] = chan_ok ? __ldg(wp + int64_t(k) * (p.C / 2)) : 0u;
+      for (int k = 0; k < 9; ++k) {
+        const int src = (MODE != kModeWs && p.flip_taps) ? 8 - k : k;
+        wt[k] = chan_ok ? __ldg(wp + int64_t(src) * (p.C / 2)) : 0u;
+      }
       last_cb = sg.cb;
     }
     float bias0 = 0.f, bias1 = 0.f;
-    if constexpr (FUSED) {
+    if constexpr (MODE == kModeEpilogue) {
       if (p.bias != nullptr && chan_ok) {
         const __half2 bh = *reinterpret_cast<const __half2*>(p.bias + c0 + 2 * lane);
         bias0 = __low2float(bh);
@@ -373,39 +385,63 @@ __global__ void __launch_bounds__(kWsThreads, TDC_MIN_BLOCKS) dwconv_ws_kernel(
         uint32_t xr[kColsPerWarp + 2];
 #pragma unroll
         for (int j = 0; j < kColsPerWarp + 2; ++j) xr[j] = src[j * (kBlockC / 2)];
-        if constexpr (FUSED) {
+        if constexpr (MODE == kModeEpilogue) {
           // Residual of the row this input row completes, fetched before the
-          // FMAs so its latency overlaps them.
-          uint32_t res[kColsPerWarp];
+          // FMAs so its latency overlaps them.  Every branch below depends on
+          // kernel parameters only (warp-uniform) and is taken once per row.
           const bool with_res = p.residual != nullptr && i >= 2 && chan_ok;
-          const int64_t row_off = (yrow - p.y) + int64_t(i - 2) * y_row_stride;
+          uint32_t res[kColsPerWarp];
+          if (with_res) {
+            const __half* rrow = p.residual + ((yrow - p.y) + int64_t(i - 2) * y_row_stride);
 #pragma unroll
-          for (int m = 0; m < kColsPerWarp; ++m)
-            res[m] = (with_res && m < n_valid)
-                         ? __ldg(reinterpret_cast<const uint32_t*>(p.residual + row_off +
-                                                                   int64_t(m) * p.C))
-                         : 0u;
+            for (int m = 0; m < kColsPerWarp; ++m)
+              res[m] = m < n_valid ? __ldg(reinterpret_cast<const uint32_t*>(rrow + int64_t(m) * p.C))
+                                   : 0u;
+          }
           feed_row(xr, wt, fin, mid, nw);
           if (i >= 2 && chan_ok) {
+            // The finished row's accumulators are dead after this store (the
+            // set is re-initialised when it starts the next row), so the
+            // epilogue works on them in place.
+            float* t = fin.v;
+            if (p.bias != nullptr) {
+#pragma unroll
+              for (int m = 0; m < kColsPerWarp; ++m) { t[2 * m] += bias0; t[2 * m + 1] += bias1; }
+            }
+            switch (p.act) {
+              case TDC_ACT_RELU:
+#pragma unroll
+                for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_RELU);
+                break;
+              case TDC_ACT_RELU6:
+#pragma unroll
+                for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_RELU6);
+                break;
+              case TDC_ACT_SILU:
+#pragma unroll
+                for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_SILU);
+                break;
+              default:
+                break;
+            }
+            if (with_res) {
+#pragma unroll
+              for (int m = 0; m < kColsPerWarp; ++m) {
+                const __half2 rh = *reinterpret_cast<const __half2*>(&res[m]);
+                t[2 * m] += __low2float(rh);
+                t[2 * m + 1] += __high2float(rh);
+              }
+            }
             __half* dst = yrow + int64_t(i - 2) * y_row_stride;
 #pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m) {
-              if (m >= n_valid) continue;
-              float t0 = fin.v[2 * m], t1 = fin.v[2 * m + 1];
-              if (p.bias != nullptr) { t0 += bias0; t1 += bias1; }
-              t0 = apply_act(t0, p.act);
-              t1 = apply_act(t1, p.act);
-              if (with_res) {
-                const __half2 rh = *reinterpret_cast<const __half2*>(&res[m]);
-                t0 += __low2float(rh);
-                t1 += __high2float(rh);
-              }
-              *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) = pack_half2_rn(t0, t1);
-            }
+            for (int m = 0; m < kColsPerWarp; ++m)
+              if (m < n_valid)
+                *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
+                    pack_half2_rn(t[2 * m], t[2 * m + 1]);
           }
         } else {
           feed_row(xr, wt, fin, mid, nw);
-          if (i >= 2) {
+          if (i >= 2 && chan_ok) {
             __half* dst = yrow + int64_t(i - 2) * y_row_stride;
 #pragma unroll
             for (int m = 0; m < kColsPerWarp; ++m)

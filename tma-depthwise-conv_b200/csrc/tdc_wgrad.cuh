@@ -1,0 +1,233 @@
+// tdc_wgrad.cuh — weight gradient of the depthwise 3x3 forward, sm_100a.
+//
+//   dw[r,s,c] = sum_{n,p,q} x[n, p+r-pad, q+s-pad, c] * dy[n,p,q,c]     (x = 0 outside)
+//
+// Same streaming structure as the forward: the persistent grid walks the
+// (image, 32-column strip, 64-channel block) strips of dy with the forward's
+// SegmentIter; a producer thread TMA-loads, per stage, `stage_rows` rows of
+// x (34 halo'd columns) and the same rows of dy (32 columns) into an
+// mbarrier ring; four consumer warps (lane = channel pair, warp = 8 columns)
+// keep the last three dy rows in registers and, for every x row, FMA
+// x[i][m+s] * dy[i-r][m] into 18 fp32 accumulators (9 taps x 2 channels) per
+// lane.  Both operands stay fp16 (fma.rn.f32.f16).
+//
+// Reduction without atomics or cross-warp barriers, deterministic: when a
+// warp moves to another channel block or finishes, it adds its accumulators
+// into its own slice of a workspace, partial[cta][warp][tap][c] (zeroed by
+// the CTA at start); a second kernel sums the slices in (cta, warp) order
+// into dw (fp32).  The workspace is grid * 4 * 9 * C floats.
+#pragma once
+
+#include "tdc_kernels.cuh"
+
+namespace tdc {
+
+constexpr int kDyRowBytes = kStripQ * kBlockC * 2;  // 4096 B: 32 columns x 64 channels
+
+struct WgradParams {
+  float* partial;        // [gridDim.x][4 consumer warps][9][C] workspace
+  int32_t C, P, Q, pad;
+  int32_t qstrips, cblocks, stage_rows;
+  int32_t tail_bands, tail_band_rows;
+  int64_t full_units, tail_strips;
+  uint64_t timeout_ns;
+};
+
+// The forward's segment enumeration over dy's [N,P,Q,C] strips.
+__device__ __forceinline__ WsParams wgrad_as_ws(const WgradParams& g) {
+  WsParams p{};
+  p.C = g.C; p.P = g.P; p.Q = g.Q; p.pad = g.pad;
+  p.qstrips = g.qstrips; p.cblocks = g.cblocks; p.stage_rows = g.stage_rows;
+  p.tail_bands = g.tail_bands; p.tail_band_rows = g.tail_band_rows;
+  p.full_units = g.full_units; p.tail_strips = g.tail_strips;
+  return p;
+}
+
+template <int NS>
+__global__ void __launch_bounds__(kWsThreads, 1) dwconv_wgrad_kernel(
+    const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
+    const __grid_constant__ WgradParams g) {
+  __shared__ __align__(8) uint64_t full_bar[NS];
+  __shared__ __align__(8) uint64_t empty_bar[NS];
+  __shared__ volatile int abort_flag;
+  extern __shared__ uint8_t dyn_smem[];
+  const uint32_t ring = (smem_addr(dyn_smem) + 127u) & ~127u;
+  const uint8_t* ring_ptr = dyn_smem + (ring - smem_addr(dyn_smem));
+  const uint32_t x_bytes = uint32_t(g.stage_rows) * kRowBytes;
+  const uint32_t stage_bytes = x_bytes + uint32_t(g.stage_rows) * kDyRowBytes;
+  const WsParams p = wgrad_as_ws(g);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // This CTA's workspace slices (one per consumer warp) start at zero.
+  float* cta_slice = g.partial + int64_t(blockIdx.x) * kConsumerWarps * 9 * g.C;
+  for (int i = threadIdx.x; i < kConsumerWarps * 9 * g.C; i += blockDim.x) cta_slice[i] = 0.f;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&xmap);
+    prefetch_tensormap(&dymap);
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane != 0) return;
+    uint32_t stage = 0, phase = 0;
+    uint32_t armed = 0, armed_parity = 0;
+    int64_t load = 0;
+    bool ok = true;
+    SegmentIter it(blockIdx.x, gridDim.x);
+    Segment sg;
+    while (ok && it.next_segment(p, sg)) {
+      const int nst = (sg.rows + 2 + g.stage_rows - 1) / g.stage_rows;
+      const int32_t c0 = sg.cb * kBlockC;
+      for (int t = 0; t < nst; ++t) {
+        if (!mbar_wait_bounded(smem_addr(&empty_bar[stage]), phase ^ 1u, &abort_flag, true,
+                               g.timeout_ns)) {
+          if (!abort_flag) {
+            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load);
+            abort_flag = 1;
+          }
+          ok = false;
+          break;
+        }
+        const uint32_t fb = smem_addr(&full_bar[stage]);
+        const uint32_t dst = ring + stage * stage_bytes;
+        const int32_t row = sg.p0 + t * g.stage_rows;
+        mbar_arrive_expect_tx(fb, stage_bytes);
+        // x rows [p0 - pad + t*sr, ...), 34 columns from q0 - pad
+        tma_load_4d(dst, &xmap, fb, c0, sg.qs * kStripQ - g.pad, row - g.pad, sg.n);
+        // dy rows [p0 + t*sr, ...), 32 columns from q0 (rows past the segment are ignored)
+        tma_load_4d(dst + x_bytes, &dymap, fb, c0, sg.qs * kStripQ, row, sg.n);
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        ++load;
+        if (++stage == NS) { stage = 0; phase ^= 1u; }
+      }
+    }
+    for (int s = 0; s < NS; ++s) {
+      if (!(armed & (1u << s))) continue;
+      if (!mbar_wait_bounded(smem_addr(&full_bar[s]), (armed_parity >> s) & 1u, &abort_flag,
+                             false, g.timeout_ns))
+        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load);
+    }
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  const int cw = warp - 1;
+  uint32_t stage = 0, phase = 0;
+  SegmentIter it(blockIdx.x, gridDim.x);
+  Segment sg;
+  float acc[18];
+#pragma unroll
+  for (int k = 0; k < 18; ++k) acc[k] = 0.f;
+  int cur_cb = -1;
+  bool failed = false;
+
+  // Adds this warp's accumulators into its slice and clears them.
+  float* slice = cta_slice + int64_t(cw) * 9 * g.C;
+  auto flush = [&](int cb) {
+    const int ch = cb * kBlockC + 2 * lane;
+    if (ch < g.C) {
+#pragma unroll
+      for (int k = 0; k < 9; ++k) {
+        float2* d = reinterpret_cast<float2*>(slice + int64_t(k) * g.C + ch);
+        float2 v = *d;
+        v.x += acc[2 * k];
+        v.y += acc[2 * k + 1];
+        *d = v;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 18; ++k) acc[k] = 0.f;
+  };
+
+  while (!failed && it.next_segment(p, sg)) {
+    if (sg.cb != cur_cb) {
+      if (cur_cb >= 0) flush(cur_cb);
+      cur_cb = sg.cb;
+    }
+    const int rows_in = sg.rows + 2;
+    const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
+    const bool active = q_first < g.Q;  // warp-uniform
+    uint32_t dyw[3][kColsPerWarp];      // dy rows i, i-1, i-2 (rotating)
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int m = 0; m < kColsPerWarp; ++m) dyw[r][m] = 0u;
+    int lr = 0;
+    const uint8_t* sbuf = ring_ptr;
+    for (int i = 0; i < rows_in; ++i) {
+      if (lr == 0) {
+        const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, &abort_flag, true,
+                                           g.timeout_ns);
+        if (__any_sync(0xffffffffu, !got)) {
+          if (lane == 0 && !abort_flag) {
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1);
+            abort_flag = 1;
+          }
+          failed = true;
+          break;
+        }
+        sbuf = ring_ptr + stage * stage_bytes;
+      }
+      if (active) {
+        // shift the dy window and bring in dy row i (zero past the segment)
+#pragma unroll
+        for (int m = 0; m < kColsPerWarp; ++m) {
+          dyw[2][m] = dyw[1][m];
+          dyw[1][m] = dyw[0][m];
+        }
+        const uint32_t* dsrc = reinterpret_cast<const uint32_t*>(
+            sbuf + x_bytes + lr * kDyRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+        const bool dy_ok = i < sg.rows;
+#pragma unroll
+        for (int m = 0; m < kColsPerWarp; ++m)
+          dyw[0][m] = (dy_ok && q_first + m < g.Q) ? dsrc[m * (kBlockC / 2)] : 0u;
+        const uint32_t* xsrc = reinterpret_cast<const uint32_t*>(
+            sbuf + lr * kRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+        uint32_t xr[kColsPerWarp + 2];
+#pragma unroll
+        for (int j = 0; j < kColsPerWarp + 2; ++j) xr[j] = xsrc[j * (kBlockC / 2)];
+        // x row i is tap r of dy row i - r
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+#pragma unroll
+          for (int m = 0; m < kColsPerWarp; ++m)
+#pragma unroll
+            for (int s = 0; s < 3; ++s)
+              fma2_f16f32(xr[m + s], dyw[r][m], acc[2 * (r * 3 + s)], acc[2 * (r * 3 + s) + 1]);
+        }
+      }
+      if (++lr == g.stage_rows || i == rows_in - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+        lr = 0;
+        if (++stage == NS) { stage = 0; phase ^= 1u; }
+      }
+    }
+  }
+  if (cur_cb >= 0 && !failed) flush(cur_cb);
+}
+
+// dw[k][c] = sum over slices (cta-major, then warp, in order) of partial[slice][k][c].
+__global__ void __launch_bounds__(256) dwconv_wgrad_reduce_kernel(const float* __restrict__ partial,
+                                                                  float* __restrict__ dw,
+                                                                  int32_t slices, int32_t n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = 0.f;
+  for (int b = 0; b < slices; ++b) s += partial[int64_t(b) * n + i];
+  dw[i] = s;
+}
+
+}  // namespace tdc
