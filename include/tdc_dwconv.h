@@ -57,6 +57,7 @@ extern "C" {
 #define TDC_ERR_NO_DEVICE       -12  /* no usable sm_100 device is current                   */
 #define TDC_ERR_ACT             -13  /* unknown activation code (tdc_dwconv3x3_fwd)          */
 #define TDC_ERR_WORKSPACE       -14  /* workspace too small (tdc_dwconv3x3_bwd_weight)       */
+#define TDC_ERR_SCRATCH_LIMIT   -15  /* C beyond the static scratch (..._bwd_weight_noalloc) */
 
 /* Human-readable text for a status code (static storage, never NULL). */
 TDC_API const char* tdc_strerror(int code);
@@ -140,6 +141,28 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw,
                                      int64_t N, int64_t H, int64_t W, int64_t C,
                                      int64_t pad, int64_t n_stage,
                                      void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Weight gradient for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Same result as tdc_dwconv3x3_bwd_weight (up
+ * to the summation order when the grid differs), but the workspace is a
+ * 16 MiB array inside the library instead of caller memory, so the call
+ * allocates nothing: no cudaMalloc, no cudaFree, no allocating library call.
+ * It is meant for runtimes that fix their device budget at start-up and
+ * forbid later allocation, plug-ins whose host framework owns all device
+ * memory, and paths where an allocation could synchronise or fail.
+ *   - Every GPU that loads the library holds the 16 MiB until the process exits.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls on a device share the array and it keeps the last call's
+ *     contents (each call clears the part it uses); calls that overlap on the
+ *     GPU, e.g. on two streams, race and give wrong results.
+ *   - Limit: each CTA needs 144*C bytes of it, so the launch uses at most
+ *     16 MiB / (144*C) CTAs (fewer than the device could run once C > 256 on
+ *     a 148-SM part, which is slower, not wrong); C > 116508 is rejected with
+ *     TDC_ERR_SCRATCH_LIMIT. */
+TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, float* dw,
+                                             int64_t N, int64_t H, int64_t W, int64_t C,
+                                             int64_t pad, int64_t n_stage, void* stream);
 
 /* Number of rows of the stall tensor that tdc_dwconv_ws_probe writes for
  * this problem (= number of CTAs the launch uses). */

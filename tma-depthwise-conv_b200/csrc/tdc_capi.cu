@@ -381,6 +381,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on a pipeline barrier";
     case TDC_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
     case TDC_ERR_WORKSPACE: return "workspace smaller than tdc_dwconv3x3_bwd_weight_workspace reports";
+    case TDC_ERR_SCRATCH_LIMIT: return "C too large for the 16 MiB static scratch of tdc_dwconv3x3_bwd_weight_noalloc (C <= 116508)";
     case TDC_ERR_ACT: return "activation code is not one of TDC_ACT_NONE, _RELU, _RELU6, _SILU";
     default: return "unknown tdc status code";
   }
@@ -525,6 +526,95 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, i
   const int n = int(9 * C);
   tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
       static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+// ---------------------------------------------------------------------------
+// Weight gradient without allocation.
+//
+// Some callers cannot allocate device memory at the time they need the
+// weight gradient: runtimes that reserve a fixed device budget at start-up
+// and forbid later allocation, plug-ins whose host framework owns all device
+// memory without exposing its allocator, and latency-critical paths where
+// cudaMalloc may synchronise the device or fail at an arbitrary moment.  For
+// them the workspace of tdc_dwconv3x3_bwd_weight lives in a file-scope
+// device array instead.  The array's name is only a host-side stand-in in
+// host code; its device address is looked up once per device with
+// cudaGetSymbolAddress and passed to the kernels.
+// ---------------------------------------------------------------------------
+constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // per device, held until exit
+static __device__ __align__(256) float g_tdc_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+struct NoAllocScratch {
+  std::once_flag once;
+  float* ptr = nullptr;
+  int status = TDC_ERR_CUDA;
+};
+NoAllocScratch g_noalloc[kMaxDevices];
+
+TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, float* dw, int64_t N,
+                                             int64_t H, int64_t W, int64_t C, int64_t pad,
+                                             int64_t n_stage, void* stream) {
+  if (!x || !dy || !dw) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dw)) return TDC_ERR_ALIGNMENT;
+  WsPlan pl;
+  int64_t P, Q;
+  int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q);  // also makes the device current
+  if (rc != TDC_OK) return rc;
+  // Each CTA needs 4 warps x 9 taps x C floats of the scratch: fewer CTAs
+  // than the occupancy allows when C is large; none at all beyond the limit.
+  const int64_t per_cta = tdc::kConsumerWarps * 9 * C * int64_t(sizeof(float));
+  const int64_t max_grid = kNoAllocScratchBytes / per_cta;
+  if (max_grid < 1) return TDC_ERR_SCRATCH_LIMIT;
+  if (pl.grid > max_grid) {
+    const int stage_rows = pl.stage_rows;
+    const size_t smem = pl.smem;
+    pl = make_plan(N, P, Q, C, n_stage, max_grid, 1);
+    pl.stage_rows = stage_rows;
+    pl.smem = smem;
+  }
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  NoAllocScratch& sc = g_noalloc[dev];
+  std::call_once(sc.once, [&sc]() {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_tdc_noalloc_scratch);
+    if (err == cudaSuccess && p != nullptr) {
+      sc.ptr = static_cast<float*>(p);
+      sc.status = TDC_OK;
+    } else {
+      t_last_cuda_error = int(err);
+      sc.status = TDC_ERR_CUDA;
+    }
+  });
+  if (sc.status != TDC_OK) return sc.status;
+
+  alignas(64) CUtensorMap xmap, dymap;
+  rc = encode_x_map(&xmap, x, N, H, W, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  tdc::WgradParams g{};
+  g.partial = sc.ptr;  // every CTA zeroes its own part before accumulating
+  g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
+  g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
+  g.tail_bands = pl.tail_bands; g.tail_band_rows = pl.tail_band_rows;
+  g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
+  g.timeout_ns = uint64_t(g_timeout_ns.load());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(unsigned(pl.grid)), block(tdc::kWsThreads);
+  switch (n_stage) {
+    case 2: tdc::dwconv_wgrad_kernel<2><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+    case 3: tdc::dwconv_wgrad_kernel<3><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+    default: tdc::dwconv_wgrad_kernel<4><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  const int n = int(9 * C);
+  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
+      sc.ptr, dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
   e = cudaGetLastError();
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
