@@ -58,6 +58,7 @@ extern "C" {
 #define TDC_ERR_ACT             -13  /* unknown activation code (tdc_dwconv3x3_fwd)          */
 #define TDC_ERR_WORKSPACE       -14  /* workspace too small (tdc_dwconv3x3_bwd_weight)       */
 #define TDC_ERR_SCRATCH_LIMIT   -15  /* C beyond the static scratch (..._bwd_weight_noalloc) */
+#define TDC_ERR_STRIDE          -16  /* stride not 1 or 2 (tdc_dwconv_fwd)                  */
 
 /* Human-readable text for a status code (static storage, never NULL). */
 TDC_API const char* tdc_strerror(int code);
@@ -113,6 +114,27 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
                               const void* residual, void* y,
                               int64_t N, int64_t H, int64_t W, int64_t C,
                               int64_t pad, int64_t act, int64_t n_stage, void* stream);
+
+/* General K x K depthwise forward, K in {3, 5, 7}, stride 1 or 2, symmetric
+ * padding, with the same optional epilogue as tdc_dwconv3x3_fwd:
+ *   y[n,p,q,c] = fp16_rne(epilogue( chain_{r<K, s<K} x[n, S*p+r-pad, S*q+s-pad, c] * w[r,s,c] ))
+ * fp32 chain from +0 in (r, s) lexicographic order.  w: [K, K, C] fp16;
+ * P = (H + 2*pad - K) / S + 1, Q likewise; C % 8 == 0.  (K, stride) = (3, 1)
+ * is tdc_dwconv3x3_fwd.  No counterpart in the reference (3x3, stride 1 only). */
+TDC_API int tdc_dwconv_fwd(const void* x, const void* w, const void* bias,
+                           const void* residual, void* y,
+                           int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                           int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
+                           void* stream);
+
+/* Launch plan tdc_dwconv_fwd would use (same layout as tdc_ws_plan's
+ * plan[0..7]; pure host arithmetic).  For K >= 5 at stride 1 and 7x7 at
+ * stride 2 the kernel holds the K input rows of one output row at once, and
+ * stage_rows satisfies (n_stage - 1) * stage_rows >= K - 1.  The strip is
+ * stride*31 + K input columns wide.  No counterpart in the reference. */
+TDC_API int tdc_dwconv_fwd_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                int64_t stride, int64_t pad, int64_t n_stage, int64_t sms,
+                                int64_t ctas_per_sm, int64_t* plan);
 
 /* ---- backward ------------------------------------------------------------------
  * Data gradient of the 3x3 forward (stride 1, padding pad):

@@ -208,6 +208,84 @@ int oracle_dwconv3x3_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t
 }
 
 /*
+ * K x K depthwise forward with stride and the fused epilogue (no counterpart
+ * in the reference, which is 3x3 stride 1; its ConvParams carries a stride,
+ * csrc/common.cuh:38-40):
+ *   t = chain_{r<K, s<K} fmaf(x[n, S*p+r-pad, S*q+s-pad, c], w[r,s,c], acc), acc from +0
+ *   then bias / act / residual as oracle_dwconv3x3_ex_f16, y = f16_rne(t)
+ * w: [K,K,C]; P = (H+2*pad-K)/S + 1, Q likewise.
+ */
+int oracle_dwconv_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                         const uint16_t* residual, uint16_t* y, int64_t N, int64_t H, int64_t W,
+                         int64_t C, int64_t K, int64_t S, int64_t pad, int act, int threads) {
+  if (!x || !w || !y || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0 || K < 1 || S < 1) return -1;
+  if (H + 2 * pad < K || W + 2 * pad < K) return -1;
+  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  if (N == 0 || C == 0) return 0;
+
+  float* wf = (float*)malloc(sizeof(float) * (size_t)(K * K * C));
+  float* lut = (float*)malloc(sizeof(float) * 65536);
+  if (!wf || !lut) { free(wf); free(lut); return -1; }
+  for (uint32_t i = 0; i < 65536u; ++i) lut[i] = oracle_f16_to_f32((uint16_t)i);
+  for (int64_t i = 0; i < K * K * C; ++i) wf[i] = lut[w[i]];
+
+  const int64_t WP = W + 2 * pad;
+  int err = 0;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads) reduction(| : err)
+#endif
+  {
+    /* K decoded input rows, each with pad zero columns either side */
+    float* rows = (float*)calloc((size_t)(K * WP * C + 1), sizeof(float));
+    float* acc = (float*)malloc(sizeof(float) * (size_t)(C + 1));
+    if (!rows || !acc) {
+      err = 1;
+    } else {
+#ifdef _OPENMP
+#pragma omp for schedule(static)
+#endif
+      for (int64_t np = 0; np < N * P; ++np) {
+        const int64_t n = np / P, p = np % P;
+        for (int64_t r = 0; r < K; ++r) {
+          float* dst = rows + r * WP * C + pad * C;
+          const int64_t h = S * p + r - pad;
+          if (h < 0 || h >= H) {
+            for (int64_t i = 0; i < W * C; ++i) dst[i] = 0.0f;
+          } else {
+            const uint16_t* src = x + (n * H + h) * W * C;
+            for (int64_t i = 0; i < W * C; ++i) dst[i] = lut[src[i]];
+          }
+        }
+        uint16_t* out = y + np * Q * C;
+        for (int64_t q = 0; q < Q; ++q) {
+          for (int64_t c = 0; c < C; ++c) acc[c] = 0.0f;
+          for (int64_t r = 0; r < K; ++r)
+            for (int64_t s = 0; s < K; ++s) {
+              const float* xr = rows + r * WP * C + (S * q + s) * C;
+              const float* wr = wf + (r * K + s) * C;
+              for (int64_t c = 0; c < C; ++c) acc[c] = fmaf(xr[c], wr[c], acc[c]);
+            }
+          const uint16_t* res = residual ? residual + np * Q * C + q * C : NULL;
+          for (int64_t c = 0; c < C; ++c) {
+            float t = acc[c];
+            if (bias) t = t + lut[bias[c]];
+            t = oracle_act(t, act);
+            if (res) t = t + lut[res[c]];
+            out[q * C + c] = oracle_f32_to_f16(t);
+          }
+        }
+      }
+    }
+    free(rows);
+    free(acc);
+  }
+  free(lut);
+  free(wf);
+  return err ? -1 : 0;
+}
+
+/*
  * Data gradient (no counterpart in the reference):
  *   dx[n,h,w,c] = chain over (r', s') = (0..2, 0..2) of
  *                 fmaf(dy[n, h+pad-(2-r'), w+pad-(2-s'), c], w[2-r', 2-s', c], acc)

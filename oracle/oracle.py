@@ -42,6 +42,9 @@ def load() -> ctypes.CDLL:
         lib.oracle_dwconv3x3_ex_f16.argtypes = ([ctypes.c_void_p] * 5 + [i64] * 5 +
                                                 [ctypes.c_int, ctypes.c_int])
         lib.oracle_dwconv3x3_ex_f16.restype = ctypes.c_int
+        lib.oracle_dwconv_ex_f16.argtypes = ([ctypes.c_void_p] * 5 + [i64] * 7 +
+                                             [ctypes.c_int, ctypes.c_int])
+        lib.oracle_dwconv_ex_f16.restype = ctypes.c_int
         lib.oracle_dwconv3x3_bwd_data_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 5 + [ctypes.c_int]
         lib.oracle_dwconv3x3_bwd_data_f16.restype = ctypes.c_int
         lib.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
@@ -108,6 +111,60 @@ def dwconv_ex_f16(x: np.ndarray, w: np.ndarray, pad: int, bias: np.ndarray | Non
     if rc != 0:
         raise RuntimeError("oracle_dwconv3x3_ex_f16 failed")
     return y
+
+
+def output_hw_k(H: int, W: int, K: int, stride: int, pad: int) -> tuple[int, int]:
+    """P, Q of a K x K depthwise conv with a stride and symmetric padding."""
+    return (H + 2 * pad - K) // stride + 1, (W + 2 * pad - K) // stride + 1
+
+
+def dwconv_k_f16(x: np.ndarray, w: np.ndarray, pad: int, stride: int = 1,
+                 bias: np.ndarray | None = None, residual: np.ndarray | None = None,
+                 activation: str = "none", threads: int = 0) -> np.ndarray:
+    """C oracle of the K x K, strided forward with the fused epilogue.
+    x: [N,H,W,C] float16, w: [K,K,C] float16 -> [N,P,Q,C] float16."""
+    lib = load()
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    N, H, W, C = x.shape
+    K = w.shape[0]
+    if w.shape != (K, K, C):
+        raise ValueError("w must be [K,K,C]")
+    if H + 2 * pad < K or W + 2 * pad < K:
+        raise ValueError("negative output size")
+    P, Q = output_hw_k(H, W, K, stride, pad)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float16)
+    r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float16)
+    if b is not None and b.shape != (C,):
+        raise ValueError("bias must be [C]")
+    if r is not None and r.shape != (N, P, Q, C):
+        raise ValueError("residual must be [N,P,Q,C]")
+    y = np.empty((N, P, Q, C), dtype=np.float16)
+    rc = lib.oracle_dwconv_ex_f16(x.ctypes.data, w.ctypes.data,
+                                  None if b is None else b.ctypes.data,
+                                  None if r is None else r.ctypes.data, y.ctypes.data,
+                                  N, H, W, C, K, stride, pad, ACTS[activation], int(threads))
+    if rc != 0:
+        raise RuntimeError("oracle_dwconv_ex_f16 failed")
+    return y
+
+
+def dwconv_k_f16_numpy(x: np.ndarray, w: np.ndarray, pad: int, stride: int = 1) -> np.ndarray:
+    """numpy restatement of the K x K, strided forward (small sizes): the same
+    chain in (r, s) order from +0, products exact in float32, one RNE."""
+    x = np.asarray(x, dtype=np.float16)
+    w = np.asarray(w, dtype=np.float16)
+    N, H, W, C = x.shape
+    K = w.shape[0]
+    P, Q = output_hw_k(H, W, K, stride, pad)
+    xp = np.zeros((N, H + 2 * pad + stride, W + 2 * pad + stride, C), dtype=np.float32)
+    xp[:, pad:pad + H, pad:pad + W, :] = x.astype(np.float32)
+    wf = w.astype(np.float32)
+    acc = np.zeros((N, P, Q, C), dtype=np.float32)
+    for r in range(K):
+        for s in range(K):
+            acc = acc + xp[:, r:r + stride * P:stride, s:s + stride * Q:stride, :] * wf[r, s]
+    return acc.astype(np.float16)
 
 
 def dwconv_ex_f16_numpy(x, w, pad, bias=None, residual=None, activation="none"):
@@ -192,3 +249,18 @@ def f16_ulp(v: np.ndarray) -> np.ndarray:
     a = np.abs(np.asarray(v, dtype=np.float32))
     e = np.floor(np.log2(np.maximum(a, 2.0 ** -14)))
     return np.exp2(e - 10).astype(np.float32)
+
+
+def silu_tolerance(want: np.ndarray, residual: np.ndarray | None = None) -> np.ndarray:
+    """Bound on |kernel - oracle| for the fused silu epilogue.
+
+    The kernel's silu (fast exp and divide) is within a few fp32 ulp of the
+    oracle's expf-based one: a relative error of at most 2^-20 of the silu
+    term t, which can flip the final fp16 rounding by one ulp of the result.
+    When a residual r is added, |t| <= |y| + |r| can be much larger than the
+    result (cancellation), so the bound is one fp16 ulp of y plus
+    2^-20 * (|y| + |r|).
+    """
+    y = np.abs(np.asarray(want, dtype=np.float32))
+    r = 0.0 if residual is None else np.abs(np.asarray(residual, dtype=np.float32))
+    return f16_ulp(y) + np.float32(2.0 ** -20) * (y + r)

@@ -77,3 +77,47 @@ def test_extension_surface():
         assert hasattr(T._C, name), name
     assert T.CONSUMER_WARPS == 4
     assert "libtdc_sm100" not in T._C.__file__ and T._C.__file__.startswith(T.__file__.rsplit("/", 1)[0])
+
+
+def test_dwconv_kxk_checks():
+    x, w5 = FakeCuda((2, 16, 16, 64)), FakeCuda((5, 5, 64))
+    with pytest.raises(ValueError, match="stride must be 1 or 2, got 3"):
+        T.dwconv(x, w5, 2, stride=3)
+    with pytest.raises(ValueError, match=r"K in \{3, 5, 7\}"):
+        T.dwconv(x, FakeCuda((4, 4, 64)), 2)
+    with pytest.raises(ValueError, match=r"K in \{3, 5, 7\}"):
+        T.dwconv(x, FakeCuda((5, 3, 64)), 2)
+    with pytest.raises(ValueError, match=r"dwconv requires C % 8 == 0"):
+        T.dwconv(FakeCuda((2, 16, 16, 12)), FakeCuda((5, 5, 12)), 2)
+    with pytest.raises(ValueError, match="activation must be one of"):
+        T.dwconv(x, w5, 2, activation="gelu")
+    with pytest.raises(ValueError, match=r"n_stage must be one of \{2, 3, 4\}, got 5"):
+        T.dwconv(x, w5, 2, n_stage=5)
+    with pytest.raises(ValueError, match="pad must be non-negative"):
+        T.dwconv(x, w5, -1)
+    assert set(T.DWCONV_STAGES) == {(k, s) for k in (3, 5, 7) for s in (1, 2)}
+    assert hasattr(T._C, "dwconv_k")
+
+
+def test_convert_depthwise_convs_eligibility():
+    import tdc_torch
+    nn = torch.nn
+    model = nn.Sequential(
+        nn.Conv2d(64, 64, 3, padding=1, groups=64),             # trainable: converted
+        nn.Conv2d(64, 64, 7, padding=3, groups=64),             # forward-only geometry
+        nn.Conv2d(64, 64, 5, stride=2, padding=2, groups=64),   # forward-only geometry
+        nn.Sequential(nn.Conv2d(64, 64, 3, stride=2, padding=1, groups=64)),
+        nn.Conv2d(64, 64, 3, padding=1, groups=64, dilation=2),  # dilated: never
+        nn.Conv2d(64, 64, 3, padding=1, groups=32),              # not depthwise: never
+        nn.Conv2d(12, 12, 3, padding=1, groups=12),              # C % 8 != 0: never
+        nn.Conv2d(64, 64, 9, padding=4, groups=64),              # 9x9: never
+        nn.Conv2d(64, 64, (3, 5), padding=(1, 2), groups=64),    # non-square: never
+    )
+    assert tdc_torch.convert_depthwise_convs(model) == 1
+    assert isinstance(model[0], tdc_torch.DepthwiseConv3x3)
+    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 3
+    assert type(model[1]) is tdc_torch.DepthwiseConv2d and model[1].kernel_size == 7
+    assert model[2].stride == 2 and model[2].padding == 2 and model[3][0].stride == 2
+    assert all(isinstance(m, nn.Conv2d) for m in list(model)[4:])
+    with pytest.raises(ValueError, match="kernel_size must be 3, 5 or 7"):
+        tdc_torch.DepthwiseConv2d(64, 9)

@@ -120,6 +120,27 @@ def test_general_forward_argument_errors(lib):
         assert fwd() == CODES["TDC_ERR_NO_DEVICE"]
 
 
+def test_kxk_forward_argument_errors(lib):
+    p = C.c_void_p
+    def fwd(K=5, stride=2, C_=72, pad=2, H=16, act=0, ns=2, N=2, x=16):
+        return lib.tdc_dwconv_fwd(p(x), p(16), None, None, p(16), i64(N), i64(H), i64(16),
+                                  i64(C_), i64(K), i64(stride), i64(pad), i64(act), i64(ns), None)
+    assert fwd(K=4) == CODES["TDC_ERR_FILTER_SHAPE"]
+    assert fwd(K=9) == CODES["TDC_ERR_FILTER_SHAPE"]
+    assert fwd(stride=3) == CODES["TDC_ERR_STRIDE"]
+    assert fwd(stride=0) == CODES["TDC_ERR_STRIDE"]
+    assert fwd(C_=12) == CODES["TDC_ERR_CHANNELS"]
+    assert fwd(pad=-1) == CODES["TDC_ERR_PAD"]
+    assert fwd(ns=1) == CODES["TDC_ERR_N_STAGE"]
+    assert fwd(act=7) == CODES["TDC_ERR_ACT"]
+    assert fwd(K=7, H=2, pad=2) == CODES["TDC_ERR_BAD_SHAPE"]  # 2 + 4 < 7: no output row
+    assert fwd(x=24) == CODES["TDC_ERR_ALIGNMENT"]
+    assert fwd(N=0) == CODES["TDC_OK"]  # empty: nothing to launch
+    if not torch.cuda.is_available():
+        assert fwd() == CODES["TDC_ERR_NO_DEVICE"]
+        assert fwd(K=3, stride=1, pad=1) == CODES["TDC_ERR_NO_DEVICE"]
+
+
 def test_probe_and_status_argument_errors(lib):
     p = C.c_void_p(16)
     assert lib.tdc_dwconv_ws_probe(p, p, p, i64(2), i64(16), i64(16), i64(64), i64(3), i64(3),
@@ -188,6 +209,73 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
                 assert (strip, r) not in seen
                 seen.add((strip, r))
     assert len(seen) == pl["strips"] * P
+
+
+def _fwd_plan(lib, N, H, W, Cc, K, S, pad, ns, sms=148, occ=3):
+    out = (i64 * 8)()
+    rc = lib.tdc_dwconv_fwd_plan(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(S), i64(pad), i64(ns),
+                                 i64(sms), i64(occ), out)
+    assert rc == 0
+    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
+                     "smem"], list(out)))
+
+
+def direct_scheme(K, S):
+    """Restates tdc::direct_scheme: taps + accumulator sets + one input row of
+    registers above 100 -> one output row at a time from its K input rows."""
+    nacc = -(-K // S)
+    return K * K + nacc * 16 + (S * 7 + K) > 100
+
+
+def max_stages_held(rows, K, S, sr):
+    """Restates the direct scheme's consumer bookkeeping over one segment of
+    `rows` output rows: the most ring stages a warp holds at once."""
+    rows_in = S * (rows - 1) + K
+    nst = -(-rows_in // sr)
+    acquired = released = 0
+    worst = 0
+    for o in range(rows):
+        acquired = max(acquired, min(nst, (S * o + K - 1) // sr + 1))
+        worst = max(worst, acquired - released)
+        released = nst if o == rows - 1 else min(nst, S * (o + 1) // sr)
+        assert released <= acquired
+    assert acquired == released == nst
+    return worst
+
+
+@pytest.mark.parametrize("K,S", [(3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+@pytest.mark.parametrize("N,H,W,Cc,pad", [(64, 224, 336, 256, None), (2, 19, 45, 72, 0), (3, 7, 9, 8, None),
+                                          (1, 300, 40, 64, 4), (6, 96, 200, 256, None)])
+@pytest.mark.parametrize("ns", [2, 3, 4])
+def test_kxk_plan_covers_every_output_once(lib, K, S, N, H, W, Cc, pad, ns):
+    pad = K // 2 if pad is None else pad
+    pl = _fwd_plan(lib, N, H, W, Cc, K, S, pad, ns)
+    P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
+    sr = pl["stage_rows"]
+    assert 1 <= sr <= 256 and S * 31 + K <= 256  # TMA box extents
+    assert pl["smem"] == ns * sr * (S * 31 + K) * 128 + 128 <= 200 * 1024
+    assert pl["qstrips"] == -(-Q // 32) and pl["cblocks"] == -(-Cc // 64)
+    if direct_scheme(K, S):
+        assert (ns - 1) * sr >= K - 1
+    seen = set()
+    for g in range(pl["grid"]):
+        for strip, a, b in segments(pl, P, g):
+            assert 0 <= a < b <= P
+            if direct_scheme(K, S):
+                assert max_stages_held(b - a, K, S, sr) <= ns
+            for r in range(a, b):
+                assert (strip, r) not in seen
+                seen.add((strip, r))
+    assert len(seen) == pl["strips"] * P
+
+
+def test_kxk_plan_of_3x3_stride_1_is_the_ws_plan(lib):
+    for ns in (2, 3, 4):
+        assert _fwd_plan(lib, 8, 56, 56, 256, 3, 1, 1, ns, occ=4) == _plan(lib, 8, 56, 56, 256, 1, ns)
+
+
+def test_kxk_consumer_schemes():
+    assert [direct_scheme(K, S) for K in (3, 5, 7) for S in (1, 2)] == [False, False, True, False, True, True]
 
 
 def test_plan_balances_the_headline_shape(lib):

@@ -119,3 +119,37 @@ def test_matches_reference_golden_vectors(case):
     assert np.array_equal(got, z[f"{case}_ws"]), "oracle != reference dwconv_ws"
     assert np.array_equal(got, z[f"{case}_v0"]), "oracle != reference dwconv_v0"
     assert np.array_equal(oracle.dwconv_f16_numpy(x, w, pad).view(np.uint16), z[f"{case}_ws"])
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+@pytest.mark.parametrize("pad", [0, 1, 3])
+def test_kxk_restatements_agree(K, S, pad):
+    rng = np.random.default_rng(K * 10 + S + pad)
+    x = rng.standard_normal((2, 13, 19, 24)).astype(np.float16)
+    w = (rng.standard_normal((K, K, 24)) / K).astype(np.float16)
+    if 13 + 2 * pad < K:
+        with pytest.raises(ValueError):
+            oracle.dwconv_k_f16(x, w, pad, S)
+        return
+    c = oracle.dwconv_k_f16(x, w, pad, S)
+    n = oracle.dwconv_k_f16_numpy(x, w, pad, S)
+    assert c.shape[1:3] == oracle.output_hw_k(13, 19, K, S, pad)
+    assert np.array_equal(c.view(np.uint16), n.view(np.uint16))
+    ref = torch.nn.functional.conv2d(torch.from_numpy(x).float().permute(0, 3, 1, 2),
+                                     torch.from_numpy(w).float().permute(2, 0, 1).unsqueeze(1),
+                                     stride=S, padding=pad, groups=24).permute(0, 2, 3, 1).numpy()
+    assert (np.abs(c.astype(np.float32) - ref) <= oracle.f16_ulp(ref) + 1e-3).all()
+    if (K, S) == (3, 1):
+        assert np.array_equal(c.view(np.uint16), oracle.dwconv_f16(x, w, pad).view(np.uint16))
+
+
+def test_kxk_epilogue_matches_3x3_epilogue():
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((2, 9, 11, 16)).astype(np.float16)
+    w = (rng.standard_normal((3, 3, 16)) / 3).astype(np.float16)
+    b = rng.standard_normal(16).astype(np.float16)
+    r = rng.standard_normal((2, 9, 11, 16)).astype(np.float16)
+    for act in oracle.ACTS:
+        a = oracle.dwconv_k_f16(x, w, 1, 1, b, r, act)
+        e = oracle.dwconv_ex_f16(x, w, 1, b, r, act)
+        assert np.array_equal(a.view(np.uint16), e.view(np.uint16)), act

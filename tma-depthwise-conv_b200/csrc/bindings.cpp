@@ -174,6 +174,47 @@ torch::Tensor dwconv3x3(torch::Tensor x, torch::Tensor w, std::optional<torch::T
   return y;
 }
 
+// K x K (K = 3, 5, 7), stride 1 or 2, with the same optional epilogue.
+torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
+                       std::optional<torch::Tensor> residual, int64_t stride, int64_t pad,
+                       int64_t act, int64_t n_stage) {
+  check_common(x, w);
+  const int64_t K = w.size(0);
+  TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7), "w must be [K,K,C] with K in {3, 5, 7}");
+  TORCH_CHECK(w.size(2) == x.size(3), "channel mismatch");
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  TORCH_CHECK(x.size(1) + 2 * pad >= K && x.size(2) + 2 * pad >= K, "input too small for a ", K,
+              "x", K, " kernel with pad ", pad);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t P = (x.size(1) + 2 * pad - K) / stride + 1;
+  const int64_t Q = (x.size(2) + 2 * pad - K) / stride + 1;
+  auto y = torch::empty({x.size(0), P, Q, x.size(3)}, x.options());
+  const void* bptr = nullptr;
+  const void* rptr = nullptr;
+  if (bias.has_value()) {
+    const auto& b = *bias;
+    TORCH_CHECK(b.is_cuda() && b.device() == x.device() && b.scalar_type() == torch::kHalf &&
+                    b.is_contiguous() && b.dim() == 1 && b.size(0) == x.size(3),
+                "bias must be a contiguous fp16 [C] tensor on x's device");
+    bptr = b.data_ptr();
+  }
+  if (residual.has_value()) {
+    const auto& r = *residual;
+    TORCH_CHECK(r.is_cuda() && r.device() == x.device() && r.scalar_type() == torch::kHalf &&
+                    r.is_contiguous() && r.sizes() == y.sizes(),
+                "residual must be a contiguous fp16 [N,P,Q,C] tensor on x's device");
+    rptr = r.data_ptr();
+  }
+  check_status(tdc_dwconv_fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0),
+                              x.size(1), x.size(2), x.size(3), K, stride, pad, act, n_stage,
+                              stream_of(x)),
+               "dwconv");
+  return y;
+}
+
 // Data gradient: dy [N,P,Q,C] -> dx [N,H,W,C] with H = P - 2*pad + 2.
 torch::Tensor dwconv3x3_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, int64_t n_stage) {
   check_common(dy, w);
@@ -255,6 +296,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "(tests the failure path; see device_status).",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("n_stage"),
         pybind11::arg("withhold_load"), pybind11::arg("timeout_ns"));
+  m.def("dwconv_k", &tma_dwconv::dwconv_k,
+        "K x K (3, 5, 7) depthwise forward, stride 1 or 2, optional fused epilogue",
+        py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
+        py::arg("pad"), py::arg("act"), py::arg("n_stage"));
   m.def("dwconv3x3", &tma_dwconv::dwconv3x3,
         "General forward: C % 8, fused bias / activation / residual epilogue.",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("bias"), pybind11::arg("residual"),

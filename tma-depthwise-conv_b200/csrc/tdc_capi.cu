@@ -361,6 +361,151 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
+// ---------------------------------------------------------------------------
+// General forward for K x K taps (K = 3, 5, 7) and stride 1 or 2: one kernel
+// instantiation per (K, stride, mode, n_stage), looked up in a table.
+// ---------------------------------------------------------------------------
+using GeomLaunchFn = cudaError_t (*)(const CUtensorMap&, const tdc::WsParams&, int64_t, size_t,
+                                     cudaStream_t);
+using GeomOccFn = cudaError_t (*)(int*, size_t);
+
+template <int NS, int MODE, int K, int S>
+cudaError_t geom_launch_t(const CUtensorMap& map, const tdc::WsParams& prm, int64_t grid,
+                          size_t smem, cudaStream_t st) {
+  tdc::dwconv_ws_kernel<NS, false, MODE, K, S>
+      <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(map, prm);
+  return cudaGetLastError();
+}
+
+template <int NS, int MODE, int K, int S>
+cudaError_t geom_occ_t(int* occ, size_t smem) {
+  auto* k = &tdc::dwconv_ws_kernel<NS, false, MODE, K, S>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+}
+
+#define TDC_GEOM_NS(FN, MODE, K, S) {FN<2, MODE, K, S>, FN<3, MODE, K, S>, FN<4, MODE, K, S>}
+#define TDC_GEOM_MODES(FN, K, S) \
+  {TDC_GEOM_NS(FN, tdc::kModeGeneral, K, S), TDC_GEOM_NS(FN, tdc::kModeEpilogue, K, S)}
+#define TDC_GEOM_TABLE(FN)                                                     \
+  {{TDC_GEOM_MODES(FN, 3, 1), TDC_GEOM_MODES(FN, 3, 2)},                       \
+   {TDC_GEOM_MODES(FN, 5, 1), TDC_GEOM_MODES(FN, 5, 2)},                       \
+   {TDC_GEOM_MODES(FN, 7, 1), TDC_GEOM_MODES(FN, 7, 2)}}
+// [K index: 3, 5, 7][stride - 1][mode: general, epilogue][n_stage - 2]
+const GeomLaunchFn kGeomLaunch[3][2][2][3] = TDC_GEOM_TABLE(geom_launch_t);
+const GeomOccFn kGeomOcc[3][2][2][3] = TDC_GEOM_TABLE(geom_occ_t);
+#undef TDC_GEOM_TABLE
+#undef TDC_GEOM_MODES
+#undef TDC_GEOM_NS
+
+std::mutex g_geom_mutex;
+int g_geom_occ[kMaxDevices][3][2][2][3] = {};  // 0 = not queried yet
+
+int strip_in_cols(int K, int S) { return S * (tdc::kStripQ - 1) + K; }
+
+// Ring of about 52 KB (what 12 rows of the 3x3 stride-1 strip take) split
+// over n_stage stages.  The direct scheme holds the K input rows of one
+// output row at once, across at most ceil((K-1)/sr) + 1 stages, so it needs
+// (n_stage - 1) * sr >= K - 1; with 3 or 4 stages one more row per stage
+// leaves the producer room to run ahead (measured on the 7x7 and 5x5
+// kernels at 64 x 224 x 336 x 256: 3-8 % faster than the minimum).
+int geom_stage_rows(int K, int S, int64_t n_stage) {
+  const int ns = int(n_stage);
+  const int row_bytes = strip_in_cols(K, S) * tdc::kBlockC * 2;
+  const int ring_rows = std::max<int>(ns, (kRingRows * tdc::kRowBytes) / row_bytes);
+  int sr = std::max(1, ring_rows / ns);
+  if (tdc::direct_scheme(K, S))
+    sr = std::max(sr, (K - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
+  return sr;
+}
+
+WsPlan make_geom_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int S, int64_t n_stage,
+                      int64_t sms, int64_t ctas_per_sm) {
+  WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  pl.stage_rows = geom_stage_rows(K, S, n_stage);
+  pl.smem = size_t(n_stage) * pl.stage_rows * strip_in_cols(K, S) * tdc::kBlockC * 2 + 128;
+  return pl;
+}
+
+int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
+             int64_t K, int64_t S, int64_t pad, int64_t n_stage, const Epilogue& epi,
+             void* stream) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (S != 1 && S != 2) return TDC_ERR_STRIDE;
+  if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  if (N == 0 || C == 0) return TDC_OK;
+  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
+      (epi.residual && !aligned16(epi.residual)))
+    return TDC_ERR_ALIGNMENT;
+  int rc = check_ws_limits(N, H, W, C, P, Q);
+  if (rc != TDC_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  int devi = -1;
+  rc = current_device(&dev, &devi);
+  if (rc != TDC_OK) return rc;
+  const bool with_epilogue =
+      epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
+  const int ki = int(K / 2 - 1), si = int(S - 1), mi = with_epilogue ? 1 : 0, ni = int(n_stage - 2);
+  const int stage_rows = geom_stage_rows(int(K), int(S), n_stage);
+  const size_t smem = make_geom_plan(1, 1, 1, 8, int(K), int(S), n_stage, 1, 1).smem;
+  int occ;
+  {
+    std::lock_guard<std::mutex> lock(g_geom_mutex);
+    occ = g_geom_occ[devi][ki][si][mi][ni];
+    if (occ == 0) {
+      const cudaError_t e = kGeomOcc[ki][si][mi][ni](&occ, smem);
+      if (e != cudaSuccess) return cuda_fail(e);
+      occ = std::max(1, occ);
+      g_geom_occ[devi][ki][si][mi][ni] = occ;
+    }
+  }
+  const WsPlan pl = make_geom_plan(N, P, Q, C, int(K), int(S), n_stage, dev->sms, occ);
+  auto fn = get_encode_fn();
+  if (!fn) return TDC_ERR_TMA_ENCODE;
+  alignas(64) CUtensorMap map;
+  {
+    const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
+    const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(W) * C * 2,
+                                   cuuint64_t(H) * W * C * 2};
+    const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(strip_in_cols(int(K), int(S))),
+                               cuuint32_t(stage_rows), 1u};
+    const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+    const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      t_last_cuda_error = int(r);
+      return TDC_ERR_TMA_ENCODE;
+    }
+  }
+  tdc::WsParams prm{};
+  prm.w = static_cast<const __half*>(w);
+  prm.y = static_cast<__half*>(y);
+  prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
+  prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad);
+  prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
+  prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
+  prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
+  prm.timeout_ns = uint64_t(g_timeout_ns.load());
+  prm.withhold = -1;
+  prm.bias = static_cast<const __half*>(epi.bias);
+  prm.residual = static_cast<const __half*>(epi.residual);
+  prm.act = epi.act;
+  prm.flip_taps = 0;
+  const cudaError_t e =
+      kGeomLaunch[ki][si][mi][ni](map, prm, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
 }  // namespace
 
 extern "C" {
@@ -370,7 +515,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_OK: return "success";
     case TDC_ERR_NULL_POINTER: return "null pointer argument";
     case TDC_ERR_BAD_SHAPE: return "bad shape: N,H,W,C must be non-negative with H,W >= 1 and a non-negative output size";
-    case TDC_ERR_FILTER_SHAPE: return "only 3x3 kernel supported";
+    case TDC_ERR_FILTER_SHAPE: return "only 3x3 kernel supported (5x5 and 7x7 through tdc_dwconv_fwd)";
     case TDC_ERR_CHANNELS: return "C must be a multiple of 8 (v0, general forward) or 64 (ws)";
     case TDC_ERR_PAD: return "pad must be non-negative";
     case TDC_ERR_N_STAGE: return "n_stage must be one of {2, 3, 4}";
@@ -382,6 +527,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
     case TDC_ERR_WORKSPACE: return "workspace smaller than tdc_dwconv3x3_bwd_weight_workspace reports";
     case TDC_ERR_SCRATCH_LIMIT: return "C too large for the 16 MiB static scratch of tdc_dwconv3x3_bwd_weight_noalloc (C <= 116508)";
+    case TDC_ERR_STRIDE: return "stride must be 1 or 2";
     case TDC_ERR_ACT: return "activation code is not one of TDC_ACT_NONE, _RELU, _RELU6, _SILU";
     default: return "unknown tdc status code";
   }
@@ -434,6 +580,21 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
   epi.residual = residual;
   epi.act = int(act);
   return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, -1, 0, stream, epi);
+}
+
+TDC_API int tdc_dwconv_fwd(const void* x, const void* w, const void* bias, const void* residual,
+                           void* y, int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                           int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
+                           void* stream) {
+  if (act < TDC_ACT_NONE || act > TDC_ACT_SILU) return TDC_ERR_ACT;
+  if (K == 3 && stride == 1)
+    return tdc_dwconv3x3_fwd(x, w, bias, residual, y, N, H, W, C, pad, act, n_stage, stream);
+  Epilogue epi;
+  epi.fused = true;
+  epi.bias = bias;
+  epi.residual = residual;
+  epi.act = int(act);
+  return fwd_geom(x, w, y, N, H, W, C, K, stride, pad, n_stage, epi, stream);
 }
 
 TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
@@ -704,6 +865,33 @@ TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
   const int64_t P = H + 2 * pad - 2, Q = W + 2 * pad - 2;
   if (P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
   const WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  plan[0] = pl.stage_rows;
+  plan[1] = pl.qstrips;
+  plan[2] = pl.cblocks;
+  plan[3] = pl.strips;
+  plan[4] = pl.full_units;
+  plan[5] = pl.tail_band_rows;
+  plan[6] = pl.grid;
+  plan[7] = int64_t(pl.smem);
+  return TDC_OK;
+}
+
+TDC_API int tdc_dwconv_fwd_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                int64_t stride, int64_t pad, int64_t n_stage, int64_t sms,
+                                int64_t ctas_per_sm, int64_t* plan) {
+  if (!plan) return TDC_ERR_NULL_POINTER;
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (sms < 1 || ctas_per_sm < 1) return TDC_ERR_BAD_SHAPE;
+  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = (H + 2 * pad - K) / stride + 1, Q = (W + 2 * pad - K) / stride + 1;
+  const WsPlan pl = (K == 3 && stride == 1)
+                        ? make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm)
+                        : make_geom_plan(N, P, Q, C, int(K), int(stride), n_stage, sms, ctas_per_sm);
   plan[0] = pl.stage_rows;
   plan[1] = pl.qstrips;
   plan[2] = pl.cblocks;

@@ -1,18 +1,37 @@
-// tdc_kernels.cuh — sm_100a kernels for the NHWC fp16 depthwise 3x3 conv2d
-// forward (stride 1, symmetric zero padding, fp32 accumulation, fp16 out).
+// tdc_kernels.cuh — sm_100a kernels for the NHWC fp16 depthwise conv2d
+// forward: 3x3 stride 1 (the reference's surface), and K x K (K = 3, 5, 7)
+// with stride 1 or 2; symmetric zero padding, fp32 accumulation, fp16 out.
 //
 // Arithmetic contract (shared with the CPU oracle, bit for bit):
-//   acc = +0; for r in 0..2: for s in 0..2: acc = fma(fp32(x), fp32(w), acc)
+//   acc = +0; for r in 0..K-1: for s in 0..K-1: acc = fma(fp32(x), fp32(w), acc)
 //   y   = fp16 round-to-nearest-even(acc)
-// with x = 0 outside the image.  This is the per-output computation of the
-// reference kernels (csrc/kernel_v0_naive_float4.cu:37-74 and
-// csrc/kernel_tma_ws.cuh:218-246: r-major, s-minor fp32 chain from 0).
+// with x = 0 outside the image.  For K = 3, stride 1 this is the per-output
+// computation of the reference kernels (csrc/kernel_v0_naive_float4.cu:37-74
+// and csrc/kernel_tma_ws.cuh:218-246: r-major, s-minor fp32 chain from 0).
 #pragma once
+
+#include <type_traits>
 
 #include "tdc_ptx.cuh"
 #include "tdc_dwconv.h"
 
 namespace tdc {
+
+// Calls f(std::integral_constant<int, U>{}) for U = 0 .. N-1, in order.
+template <int U, int N>
+struct UnrollSteps {
+  template <class F>
+  __device__ __forceinline__ static void run(F&& f) {
+    if constexpr (U < N) {
+      f(std::integral_constant<int, U>{});
+      UnrollSteps<U + 1, N>::run(f);
+    }
+  }
+};
+template <int N, class F>
+__device__ __forceinline__ void unroll_steps(F&& f) {
+  UnrollSteps<0, N>::run(f);
+}
 
 // ============================================================================
 // Plain kernel (the `dwconv_v0` call): one thread per 8-channel output vector,
@@ -172,35 +191,6 @@ struct RowAcc {
   float v[kColsPerWarp * 2];
 };
 
-// Feeds one input row (kColsPerWarp + 2 packed fp16 pairs of this lane) into
-// the three accumulator rows it contributes to:
-//   fin = output row completed by this input row (tap r = 2),
-//   mid = output row half way (r = 1),
-//   nw  = output row started by it (r = 0, initialised from +0 here).
-// Within a row, inputs are consumed left to right, so every output sees its
-// taps in (r, s) lexicographic order.  The FMAs take the fp16 operands
-// directly (fma.rn.f32.f16), which issues on both FMA pipes of sm_100 with
-// no conversion instructions.
-__device__ __forceinline__ void feed_row(const uint32_t (&xr)[kColsPerWarp + 2],
-                                         const uint32_t (&wt)[9], RowAcc& fin, RowAcc& mid,
-                                         RowAcc& nw) {
-#pragma unroll
-  for (int j = 0; j < kColsPerWarp + 2; ++j) {
-#pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      const int m = j - s;
-      if (m < 0 || m >= kColsPerWarp) continue;
-      if (s == 0) {
-        nw.v[2 * m] = 0.f;
-        nw.v[2 * m + 1] = 0.f;
-      }
-      fma2_f16f32(xr[j], wt[0 * 3 + s], nw.v[2 * m], nw.v[2 * m + 1]);
-      fma2_f16f32(xr[j], wt[1 * 3 + s], mid.v[2 * m], mid.v[2 * m + 1]);
-      fma2_f16f32(xr[j], wt[2 * 3 + s], fin.v[2 * m], fin.v[2 * m + 1]);
-    }
-  }
-}
-
 // Fused epilogue of the general forward, per output (fp32 throughout, one
 // rounding to fp16 at the end):
 //   t = acc; t += bias[c]; t = act(t); t += residual[n,p,q,c]
@@ -219,19 +209,95 @@ constexpr int kModeWs = 0;        // the reference surface: C % 64, plain output
 constexpr int kModeGeneral = 1;   // C % 8 (partial last channel block), optional flipped taps
 constexpr int kModeEpilogue = 2;  // kModeGeneral + bias / activation / residual
 
+__host__ __device__ constexpr int pmod(int a, int b) { return ((a % b) + b) % b; }
+
+// Geometry of a K x K, stride-S depthwise kernel over one 32-column strip.
+// Output column q reads input columns S*q - pad + s (s < K); output row p
+// reads input rows S*p - pad + r (r < K).
+template <int K, int S>
+struct Geom {
+  static constexpr int kWarpIn = S * (kColsPerWarp - 1) + K;  // input columns one warp reads
+  static constexpr int kStripIn = S * (kStripQ - 1) + K;      // input columns of a strip (TMA box)
+  static constexpr int kRowB = kStripIn * kBlockC * 2;        // bytes of one ring row
+  // Output rows an input row can touch; they cycle through kNacc accumulator
+  // sets, and the row loop is unrolled by kPeriod = S * kNacc input rows so
+  // every set index is a compile-time constant.
+  static constexpr int kNacc = (K + S - 1) / S;
+  static constexpr int kPeriod = S * kNacc;
+  // Consumer scheme.  Sliding window: every input row is read from shared
+  // memory once and fed into the kNacc output rows it belongs to; the K*K
+  // packed tap pairs and kNacc accumulator sets live in registers.  When
+  // they do not fit (5x5 stride 1, 7x7) the direct scheme is used instead:
+  // one output row at a time from its K input rows (read K / S times each),
+  // one accumulator set, taps in registers.
+  static constexpr bool kDirect = K * K + kNacc * 2 * kColsPerWarp + kWarpIn > 100;
+  // Direct scheme: the ring's stage height sr must satisfy
+  // (NS - 1) * sr >= K - 1 (checked by the host planner).
+  static_assert(kStripIn <= 256, "TMA box dimension");
+};
+static_assert(Geom<3, 1>::kRowB == kRowBytes, "3x3 stride-1 ring row");
+
+// Geom<K, S>::kDirect for run-time K and S (host planner).
+__host__ __device__ constexpr bool direct_scheme(int K, int S) {
+  return K * K + ((K + S - 1) / S) * 2 * kColsPerWarp + (S * (kColsPerWarp - 1) + K) > 100;
+}
+static_assert(!direct_scheme(3, 1) && !direct_scheme(3, 2) && !direct_scheme(5, 2) &&
+                  direct_scheme(5, 1) && direct_scheme(7, 1) && direct_scheme(7, 2),
+              "consumer scheme per geometry");
+
+// Feeds input row u (mod the unroll period) — kWarpIn packed fp16 pairs of
+// this lane — into the accumulator sets of every output row it is a tap row
+// r of: the set of output o = (row - r) / S.  A set is initialised from +0
+// by the first tap (r = 0, s = 0) of each of its outputs.  Within a row,
+// inputs are consumed left to right, so every output sees its taps in (r, s)
+// lexicographic order.  The FMAs take the fp16 operands directly
+// (fma.rn.f32.f16), issuing on both FMA pipes with no conversion instruction.
+template <int K, int S, int U>
+__device__ __forceinline__ void feed_row(const uint32_t (&xr)[Geom<K, S>::kWarpIn],
+                                         const uint32_t (&wt)[K * K],
+                                         RowAcc (&acc)[Geom<K, S>::kNacc]) {
+  using G = Geom<K, S>;
+#pragma unroll
+  for (int j = 0; j < G::kWarpIn; ++j) {
+#pragma unroll
+    for (int s = 0; s < K; ++s) {
+      if ((j - s) < 0 || (j - s) % S != 0) continue;
+      const int m = (j - s) / S;
+      if (m >= kColsPerWarp) continue;
+#pragma unroll
+      for (int r = 0; r < K; ++r) {
+        if (pmod(U - r, S) != 0) continue;
+        const int set = pmod((U - r - pmod(U - r, S)) / S, G::kNacc);
+        RowAcc& a = acc[set];
+        if (r == 0 && s == 0) {
+          a.v[2 * m] = 0.f;
+          a.v[2 * m + 1] = 0.f;
+        }
+        fma2_f16f32(xr[j], wt[r * K + s], a.v[2 * m], a.v[2 * m + 1]);
+      }
+    }
+  }
+}
+
 // Resident CTAs per SM the kernel is compiled for (bounds its registers).
 #ifndef TDC_MIN_BLOCKS
 #define TDC_MIN_BLOCKS 1
 #endif
 
+template <int MODE>
+__host__ __device__ constexpr int ws_min_blocks() {
+  return MODE == kModeWs ? TDC_MIN_BLOCKS : 3;
+}
+
 // MODE (kMode*): kModeGeneral lets the last 64-channel block be partial (TMA
 // zero-fills the missing channels; their lanes neither read taps nor store)
 // and can flip the taps (the data gradient); kModeEpilogue adds the fused
-// epilogue.  kModeWs is the ws call of the reference surface.
-template <int NS, bool PROBE, int MODE = kModeWs>
-__global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOCKS)
-    dwconv_ws_kernel(
-    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
+// epilogue.  kModeWs is the ws call of the reference surface (3x3, stride 1).
+template <int NS, bool PROBE, int MODE = kModeWs, int K = 3, int S = 1>
+__global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
+    dwconv_ws_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
+  using G = Geom<K, S>;
+  static_assert(MODE != kModeWs || (K == 3 && S == 1), "the ws surface is 3x3, stride 1");
   __shared__ __align__(8) uint64_t full_bar[NS];
   __shared__ __align__(8) uint64_t empty_bar[NS];
   __shared__ volatile int abort_flag;
@@ -239,7 +305,7 @@ __global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOC
   // TMA destinations: 128-byte aligned ring of NS stages.
   const uint32_t ring = (smem_addr(dyn_smem) + 127u) & ~127u;
   const uint8_t* ring_ptr = dyn_smem + (ring - smem_addr(dyn_smem));
-  const uint32_t stage_bytes = uint32_t(p.stage_rows) * kRowBytes;
+  const uint32_t stage_bytes = uint32_t(p.stage_rows) * G::kRowB;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -270,13 +336,14 @@ __global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOC
     SegmentIter it(blockIdx.x, gridDim.x);
     Segment sg;
     while (ok && it.next_segment(p, sg)) {
-      const int nst = (sg.rows + 2 + p.stage_rows - 1) / p.stage_rows;
+      const int rows_in = S * (sg.rows - 1) + K;
+      const int nst = (rows_in + p.stage_rows - 1) / p.stage_rows;
       const int32_t c0 = sg.cb * kBlockC;
-      const int32_t w0 = sg.qs * kStripQ - p.pad;
-      const int32_t h0 = sg.p0 - p.pad;
+      const int32_t w0 = S * sg.qs * kStripQ - p.pad;
+      const int32_t h0 = S * sg.p0 - p.pad;
       for (int t = 0; t < nst; ++t) {
         const uint32_t eb = smem_addr(&empty_bar[stage]);
-        uint64_t t0 = 0;
+        [[maybe_unused]] uint64_t t0 = 0;
         if constexpr (PROBE) t0 = clock64();
         if (!mbar_wait_bounded(eb, phase ^ 1u, &abort_flag, true, p.timeout_ns)) {
           if (!abort_flag) {
@@ -323,9 +390,10 @@ __global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOC
   SegmentIter it(blockIdx.x, gridDim.x);
   Segment sg;
   int last_cb = -1;
-  uint32_t wt[9];
+  uint32_t wt[K * K];
+  uint32_t seq = 0;  // ring stages this warp has consumed (direct scheme)
   while (it.next_segment(p, sg)) {
-    const int rows_in = sg.rows + 2;
+    const int rows_in = S * (sg.rows - 1) + K;
     const int c0 = sg.cb * kBlockC;
     const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
     const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
@@ -334,8 +402,8 @@ __global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOC
     if (sg.cb != last_cb) {
       const uint32_t* wp = reinterpret_cast<const uint32_t*>(p.w + c0) + lane;
 #pragma unroll
-      for (int k = 0; k < 9; ++k) {
-        const int src = (MODE != kModeWs && p.flip_taps) ? 8 - k : k;
+      for (int k = 0; k < K * K; ++k) {
+        const int src = (MODE != kModeWs && p.flip_taps) ? K * K - 1 - k : k;
         wt[k] = chan_ok ? __ldg(wp + int64_t(src) * (p.C / 2)) : 0u;
       }
       last_cb = sg.cb;
@@ -351,125 +419,212 @@ __global__ void __launch_bounds__(kWsThreads, MODE != kModeWs ? 3 : TDC_MIN_BLOC
     __half* yrow = p.y + ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
     const int64_t y_row_stride = int64_t(p.Q) * p.C;
 
-    RowAcc a, b, c;
-#pragma unroll
-    for (int k = 0; k < kColsPerWarp * 2; ++k) a.v[k] = b.v[k] = c.v[k] = 0.f;
-
-    int lr = 0;  // row within the current stage
-    const uint8_t* sbuf = ring_ptr;
     bool failed = false;
 
-    // One input row: acquire its stage, feed it, store the finished output
-    // row, release the stage after its last row.
-    auto step = [&](int i, RowAcc& fin, RowAcc& mid, RowAcc& nw) {
-      if (lr == 0) {
-        uint64_t t0 = 0;
-        if constexpr (PROBE) t0 = clock64();
-        const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, &abort_flag,
-                                           true, p.timeout_ns);
-        // Keep the warp uniform: one lane giving up makes the whole warp give up.
-        if (__any_sync(0xffffffffu, !got)) {
-          if (lane == 0 && !abort_flag) {
-            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1);
-            abort_flag = 1;
-          }
-          failed = true;
-          return;
+    // Residual of output row o of the segment (epilogue only), fetched
+    // before the FMAs that finish the row so its latency overlaps them.
+    // The branch depends on kernel parameters only (warp-uniform).
+    auto load_res = [&](int o, uint32_t (&res)[kColsPerWarp]) {
+      if constexpr (MODE == kModeEpilogue) {
+        if (p.residual != nullptr && chan_ok) {
+          const __half* rrow = p.residual + ((yrow - p.y) + int64_t(o) * y_row_stride);
+#pragma unroll
+          for (int m = 0; m < kColsPerWarp; ++m)
+            res[m] = m < n_valid ? __ldg(reinterpret_cast<const uint32_t*>(rrow + int64_t(m) * p.C))
+                                 : 0u;
         }
-        if constexpr (PROBE) stall_cycles += clock64() - t0;
-        sbuf = ring_ptr + stage * stage_bytes;
-      }
-      if (n_valid > 0) {
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(
-            sbuf + lr * kRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
-        uint32_t xr[kColsPerWarp + 2];
-#pragma unroll
-        for (int j = 0; j < kColsPerWarp + 2; ++j) xr[j] = src[j * (kBlockC / 2)];
-        if constexpr (MODE == kModeEpilogue) {
-          // Residual of the row this input row completes, fetched before the
-          // FMAs so its latency overlaps them.  Every branch below depends on
-          // kernel parameters only (warp-uniform) and is taken once per row.
-          const bool with_res = p.residual != nullptr && i >= 2 && chan_ok;
-          uint32_t res[kColsPerWarp];
-          if (with_res) {
-            const __half* rrow = p.residual + ((yrow - p.y) + int64_t(i - 2) * y_row_stride);
-#pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m)
-              res[m] = m < n_valid ? __ldg(reinterpret_cast<const uint32_t*>(rrow + int64_t(m) * p.C))
-                                   : 0u;
-          }
-          feed_row(xr, wt, fin, mid, nw);
-          if (i >= 2 && chan_ok) {
-            // The finished row's accumulators are dead after this store (the
-            // set is re-initialised when it starts the next row), so the
-            // epilogue works on them in place.
-            float* t = fin.v;
-            if (p.bias != nullptr) {
-#pragma unroll
-              for (int m = 0; m < kColsPerWarp; ++m) { t[2 * m] += bias0; t[2 * m + 1] += bias1; }
-            }
-            switch (p.act) {
-              case TDC_ACT_RELU:
-#pragma unroll
-                for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_RELU);
-                break;
-              case TDC_ACT_RELU6:
-#pragma unroll
-                for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_RELU6);
-                break;
-              case TDC_ACT_SILU:
-#pragma unroll
-                for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_SILU);
-                break;
-              default:
-                break;
-            }
-            if (with_res) {
-#pragma unroll
-              for (int m = 0; m < kColsPerWarp; ++m) {
-                const __half2 rh = *reinterpret_cast<const __half2*>(&res[m]);
-                t[2 * m] += __low2float(rh);
-                t[2 * m + 1] += __high2float(rh);
-              }
-            }
-            __half* dst = yrow + int64_t(i - 2) * y_row_stride;
-#pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m)
-              if (m < n_valid)
-                *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
-                    pack_half2_rn(t[2 * m], t[2 * m + 1]);
-          }
-        } else {
-          feed_row(xr, wt, fin, mid, nw);
-          if (i >= 2 && chan_ok) {
-            __half* dst = yrow + int64_t(i - 2) * y_row_stride;
-#pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m)
-              if (m < n_valid)
-                *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
-                    pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]);
-          }
-        }
-      }
-      if (++lr == p.stage_rows || i == rows_in - 1) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
-        lr = 0;
-        if (++stage == NS) { stage = 0; phase ^= 1u; }
       }
     };
 
-    // Rows rotate through the three accumulator sets; unrolled by three so
-    // the rotation is resolved at compile time.
-    for (int i = 0; i < rows_in; i += 3) {
-      step(i, a, b, c);
-      if (failed || i + 1 >= rows_in) break;
-      step(i + 1, b, c, a);
-      if (failed || i + 2 >= rows_in) break;
-      step(i + 2, c, a, b);
+    // Stores output row o of the segment from accumulator set `fin`.
+    auto store_row = [&](int o, RowAcc& fin, const uint32_t (&res)[kColsPerWarp]) {
+      if constexpr (MODE == kModeEpilogue) {
+        if (!chan_ok) return;
+        float* t = fin.v;  // dead after this store: the set restarts from +0
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int m = 0; m < kColsPerWarp; ++m) { t[2 * m] += bias0; t[2 * m + 1] += bias1; }
+        }
+        switch (p.act) {
+          case TDC_ACT_RELU:
+#pragma unroll
+            for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_RELU);
+            break;
+          case TDC_ACT_RELU6:
+#pragma unroll
+            for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_RELU6);
+            break;
+          case TDC_ACT_SILU:
+#pragma unroll
+            for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_SILU);
+            break;
+          default:
+            break;
+        }
+        if (p.residual != nullptr) {
+#pragma unroll
+          for (int m = 0; m < kColsPerWarp; ++m) {
+            const __half2 rh = *reinterpret_cast<const __half2*>(&res[m]);
+            t[2 * m] += __low2float(rh);
+            t[2 * m + 1] += __high2float(rh);
+          }
+        }
+      } else {
+        (void)res;
+      }
+      if (!chan_ok) return;
+      __half* dst = yrow + int64_t(o) * y_row_stride;
+#pragma unroll
+      for (int m = 0; m < kColsPerWarp; ++m)
+        if (m < n_valid)
+          *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
+              pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]);
+    };
+
+    if constexpr (G::kDirect) {
+      // ---- direct scheme: output row o from input rows S*o .. S*o+K-1 ----
+      // Stage k of the segment holds input rows [k*sr, (k+1)*sr) in ring slot
+      // (seq + k) % NS, so input row i sits at ring row (base + i) mod
+      // (NS * sr) with base = (seq % NS) * sr.  The warp holds the stages from
+      // the first row of o to its last row; the host picks sr with
+      // (NS - 1) * sr >= K - 1 so that window always fits the ring.
+      const int sr = p.stage_rows;
+      const int ring_rows = NS * sr;
+      const int nst = (rows_in + sr - 1) / sr;
+      int acquired = 0, released = 0;
+      int rr0 = int(seq % NS) * sr;  // ring row of input row S*o
+      for (int o = 0; o < sg.rows; ++o) {
+        const int need = min(nst, (S * o + K - 1) / sr + 1);
+        for (; acquired < need; ++acquired) {
+          const uint32_t k = seq + uint32_t(acquired);
+          [[maybe_unused]] uint64_t t0 = 0;
+          if constexpr (PROBE) t0 = clock64();
+          const bool got = mbar_wait_bounded(smem_addr(&full_bar[k % NS]), (k / NS) & 1u,
+                                             &abort_flag, true, p.timeout_ns);
+          if (__any_sync(0xffffffffu, !got)) {
+            if (lane == 0 && !abort_flag) {
+              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, int(k % NS), -1);
+              abort_flag = 1;
+            }
+            failed = true;
+            break;
+          }
+          if constexpr (PROBE) stall_cycles += clock64() - t0;
+        }
+        if (failed) break;
+        if (n_valid > 0) {
+          uint32_t res[kColsPerWarp];
+          load_res(o, res);
+          RowAcc a;
+#pragma unroll
+          for (int r = 0; r < K; ++r) {
+            int rr = rr0 + r;
+            if (rr >= ring_rows) rr -= ring_rows;
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(
+                ring_ptr + rr * G::kRowB + (S * cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+            uint32_t xr[G::kWarpIn];
+#pragma unroll
+            for (int j = 0; j < G::kWarpIn; ++j) xr[j] = src[j * (kBlockC / 2)];
+#pragma unroll
+            for (int s2 = 0; s2 < K; ++s2)
+#pragma unroll
+              for (int m = 0; m < kColsPerWarp; ++m) {
+                if (r == 0 && s2 == 0) { a.v[2 * m] = 0.f; a.v[2 * m + 1] = 0.f; }
+                fma2_f16f32(xr[S * m + s2], wt[r * K + s2], a.v[2 * m], a.v[2 * m + 1]);
+              }
+          }
+          store_row(o, a, res);
+        }
+        // Release the stages below the first row of the next output.
+        const int rel_to = o == sg.rows - 1 ? nst : min(nst, (S * (o + 1)) / sr);
+        if (released < rel_to) {
+          __syncwarp();
+          if (lane == 0)
+            for (int k = released; k < rel_to; ++k)
+              mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(k)) % NS]));
+          released = rel_to;
+        }
+        rr0 += S;
+        if (rr0 >= ring_rows) rr0 -= ring_rows;
+      }
+      if (failed) break;
+      seq += uint32_t(nst);
+    } else {
+      RowAcc acc[G::kNacc];
+#pragma unroll
+      for (int a = 0; a < G::kNacc; ++a)
+#pragma unroll
+        for (int k = 0; k < kColsPerWarp * 2; ++k) acc[a].v[k] = 0.f;
+
+      int lr = 0;  // row within the current stage
+      const uint8_t* sbuf = ring_ptr;
+
+      // One input row i (= U mod the unroll period): acquire its stage, feed
+      // it, store the output row it completes, release the stage after its
+      // last row.
+      auto step = [&](int i, auto u_tag) {
+        constexpr int U = decltype(u_tag)::value;
+        if (lr == 0) {
+          [[maybe_unused]] uint64_t t0 = 0;
+          if constexpr (PROBE) t0 = clock64();
+          const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, &abort_flag,
+                                             true, p.timeout_ns);
+          // Keep the warp uniform: one lane giving up makes the whole warp give up.
+          if (__any_sync(0xffffffffu, !got)) {
+            if (lane == 0 && !abort_flag) {
+              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1);
+              abort_flag = 1;
+            }
+            failed = true;
+            return;
+          }
+          if constexpr (PROBE) stall_cycles += clock64() - t0;
+          sbuf = ring_ptr + stage * stage_bytes;
+        }
+        if (n_valid > 0) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(
+              sbuf + lr * G::kRowB + (S * cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+          uint32_t xr[G::kWarpIn];
+#pragma unroll
+          for (int j = 0; j < G::kWarpIn; ++j) xr[j] = src[j * (kBlockC / 2)];
+          // The output whose last tap row (r = K-1) this row is, if any.
+          constexpr bool kCompletes = pmod(U - (K - 1), S) == 0;
+          uint32_t res[kColsPerWarp];
+          if constexpr (kCompletes) {
+            if (i >= K - 1) load_res((i - (K - 1)) / S, res);
+          }
+          feed_row<K, S, U>(xr, wt, acc);
+          if constexpr (kCompletes) {
+            if (i >= K - 1) {
+              constexpr int kFin = pmod((U - (K - 1) - pmod(U - (K - 1), S)) / S, G::kNacc);
+              store_row((i - (K - 1)) / S, acc[kFin], res);
+            }
+          }
+        }
+        if (++lr == p.stage_rows || i == rows_in - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+          lr = 0;
+          if (++stage == NS) { stage = 0; phase ^= 1u; }
+        }
+      };
+
+      // Rows cycle through the accumulator sets; the loop is unrolled by the
+      // period so every set index is resolved at compile time.
+      for (int i0 = 0; i0 < rows_in; i0 += G::kPeriod) {
+        bool stop = false;
+        unroll_steps<G::kPeriod>([&](auto u_tag) {
+          constexpr int U = decltype(u_tag)::value;
+          if (stop) return;
+          const int i = i0 + U;
+          if (i >= rows_in) { stop = true; return; }
+          step(i, u_tag);
+          if (failed) stop = true;
+        });
+        if (stop) break;
+      }
       if (failed) break;
     }
-    if (failed) break;
   }
   if constexpr (PROBE) {
     if (lane == 0) {

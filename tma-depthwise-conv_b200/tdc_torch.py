@@ -1,18 +1,25 @@
-"""PyTorch integration of the depthwise 3x3 kernels: custom ops with autograd,
-and an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
+"""PyTorch integration of the depthwise kernels: custom ops with autograd, and
+an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
 
-* ``torch.ops.tdc.dwconv3x3(x_nhwc, w_rsc, pad)`` — forward (C % 8), with
-  ``torch.ops.tdc.dwconv3x3_bwd_data`` / ``torch.ops.tdc.dwconv3x3_bwd_weight``
-  registered as its autograd formula (data gradient: the same kernel with
-  flipped taps; weight gradient: a deterministic reduction kernel).  All three
-  have fake implementations, so they trace under ``torch.compile``.
-* ``DepthwiseConv3x3`` — a module with ``nn.Conv2d(C, C, 3, padding=p,
-  groups=C, bias=...)``'s parameters and NCHW interface.  A channels-last
-  NCHW tensor is NHWC in memory, so it runs on the kernels without a copy.
+* ``torch.ops.tdc.dwconv3x3(x_nhwc, w_rsc, pad)`` — 3x3 stride-1 forward
+  (C % 8), with ``torch.ops.tdc.dwconv3x3_bwd_data`` /
+  ``torch.ops.tdc.dwconv3x3_bwd_weight`` registered as its autograd formula
+  (data gradient: the same kernel with flipped taps; weight gradient: a
+  deterministic reduction kernel).
+* ``torch.ops.tdc.dwconv(x_nhwc, w_rsc, bias, stride, pad)`` — K x K (3, 5,
+  7), stride 1 or 2, with the bias added in the kernel's fp32 epilogue.  Its
+  autograd formula covers 3x3 stride 1 (the kernels above, plus the bias
+  gradient as a sum of dy); for the other geometries backward raises
+  ``NotImplementedError`` (they are forward-only kernels).
+  All ops have fake implementations, so they trace under ``torch.compile``.
+* ``DepthwiseConv2d`` — a module with ``nn.Conv2d(C, C, K, stride, padding,
+  groups=C, bias=...)``'s parameters and NCHW interface.  A channels-last NCHW
+  tensor is NHWC in memory, so it runs on the kernels without a copy.
+  ``DepthwiseConv3x3`` is its 3x3 stride-1 form.
 * ``convert_depthwise_convs(model)`` — swaps every eligible ``nn.Conv2d``
-  (3x3, stride 1, dilation 1, groups = in = out channels, symmetric integer
-  padding, zeros padding mode) for a ``DepthwiseConv3x3`` sharing its
-  parameters.
+  (depthwise, dilation 1, symmetric integer padding, zeros padding mode,
+  C % 8 == 0; 3x3 stride 1, or with ``forward_only=True`` also 5x5 / 7x7 and
+  stride 2) for a ``DepthwiseConv2d`` sharing its parameters.
 
 The reference (haowen-han/tma-depthwise-conv) has a forward-only Python API
 (``tma_dwconv.py``); everything here is beyond that surface and is built on
@@ -20,15 +27,24 @@ the same kernels.
 """
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 from torch import nn
 
 import _tma_dwconv_C as _C  # type: ignore
+from tma_dwconv import DWCONV_STAGES
+
+#: (K, stride) pairs the kernels implement; backward exists for TRAINABLE only.
+GEOMETRIES = tuple(DWCONV_STAGES)
+TRAINABLE = ((3, 1),)
 
 
-def _out_hw(h: int, w: int, pad: int) -> tuple[int, int]:
-    return h + 2 * pad - 2, w + 2 * pad - 2
+def _out_hw(h: int, w: int, pad: int, k: int = 3, stride: int = 1) -> tuple[int, int]:
+    return (h + 2 * pad - k) // stride + 1, (w + 2 * pad - k) // stride + 1
 
+
+# ------------------------------ 3x3, stride 1 ---------------------------------
 
 @torch.library.custom_op("tdc::dwconv3x3", mutates_args=())
 def dwconv3x3_op(x: torch.Tensor, w: torch.Tensor, pad: int) -> torch.Tensor:
@@ -89,31 +105,98 @@ def dwconv3x3(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, pad: int = 1) -> torch.
     return dwconv3x3_op(x_nhwc, w_rsc, int(pad))
 
 
-class DepthwiseConv3x3(nn.Module):
-    """``nn.Conv2d(C, C, 3, stride=1, padding=pad, groups=C, bias=bias)`` for
-    fp16 channels-last NCHW inputs (NHWC memory), on the sm_100a kernels.
+# ------------------------------ K x K, stride ---------------------------------
 
-    Parameters keep ``nn.Conv2d``'s layout (weight [C, 1, 3, 3], bias [C]), so
+@torch.library.custom_op("tdc::dwconv", mutates_args=())
+def dwconv_op(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], stride: int,
+              pad: int) -> torch.Tensor:
+    """Depthwise K x K forward with an optional fused bias: x [N,H,W,C] fp16,
+    w [K,K,C] fp16, bias [C] fp16 or None -> [N,P,Q,C]."""
+    k = int(w.shape[0])
+    b = None if bias is None else bias.contiguous()
+    return _C.dwconv_k(x.contiguous(), w.contiguous(), b, None, stride, pad, 0,
+                       DWCONV_STAGES[(k, stride)])
+
+
+@dwconv_op.register_fake
+def _(x, w, bias, stride, pad):
+    p, q = _out_hw(x.shape[1], x.shape[2], pad, w.shape[0], stride)
+    return x.new_empty((x.shape[0], p, q, x.shape[3]))
+
+
+def _setup_context_k(ctx, inputs, output):
+    x, w, bias, stride, pad = inputs
+    ctx.save_for_backward(x, w)
+    ctx.geometry = (int(w.shape[0]), int(stride))
+    ctx.pad = pad
+    ctx.bias_dtype = None if bias is None else bias.dtype
+
+
+def _backward_k(ctx, dy):
+    if ctx.geometry not in TRAINABLE:
+        k, s = ctx.geometry
+        raise NotImplementedError(
+            f"tdc::dwconv backward is implemented for 3x3 stride 1 only, not {k}x{k} stride {s}")
+    x, w = ctx.saved_tensors
+    dx = dw = db = None
+    if ctx.needs_input_grad[0]:
+        dx = dwconv3x3_bwd_data_op(dy, w, ctx.pad)
+    if ctx.needs_input_grad[1]:
+        dw = dwconv3x3_bwd_weight_op(x, dy, ctx.pad).to(w.dtype)
+    if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
+        db = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(ctx.bias_dtype)
+    return dx, dw, db, None, None
+
+
+dwconv_op.register_autograd(_backward_k, setup_context=_setup_context_k)
+
+
+def dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           stride: int = 1, pad: Optional[int] = None) -> torch.Tensor:
+    """Depthwise K x K on NHWC fp16 tensors (differentiable for 3x3 stride 1)."""
+    if pad is None:
+        pad = int(w_rsc.shape[0]) // 2
+    return dwconv_op(x_nhwc, w_rsc, bias, int(stride), int(pad))
+
+
+# ------------------------------ nn.Conv2d stand-in ---------------------------
+
+class DepthwiseConv2d(nn.Module):
+    """``nn.Conv2d(C, C, K, stride, padding, groups=C, bias=bias)`` for fp16
+    channels-last NCHW inputs (NHWC memory), on the sm_100a kernels, K in
+    {3, 5, 7}, stride 1 or 2 (trainable at 3x3 stride 1).
+
+    Parameters keep ``nn.Conv2d``'s layout (weight [C, 1, K, K], bias [C]), so
     state dicts load unchanged.  Inputs that are not fp16 CUDA tensors in
     channels-last layout are converted (one copy).
     """
 
-    def __init__(self, channels: int, padding: int = 1, bias: bool = True,
-                 device=None, dtype=torch.float16):
+    def __init__(self, channels: int, kernel_size: int = 3, stride: int = 1,
+                 padding: Optional[int] = None, bias: bool = True, device=None,
+                 dtype=torch.float16):
         super().__init__()
+        if (kernel_size, stride) not in GEOMETRIES:
+            raise ValueError(f"kernel_size must be 3, 5 or 7 and stride 1 or 2, got "
+                             f"{kernel_size}, {stride}")
         self.channels = channels
-        self.padding = int(padding)
-        self.weight = nn.Parameter(torch.empty(channels, 1, 3, 3, device=device, dtype=dtype))
+        self.kernel_size = int(kernel_size)
+        self.stride = int(stride)
+        self.padding = kernel_size // 2 if padding is None else int(padding)
+        self.weight = nn.Parameter(torch.empty(channels, 1, kernel_size, kernel_size,
+                                               device=device, dtype=dtype))
         self.bias = nn.Parameter(torch.empty(channels, device=device, dtype=dtype)) if bias else None
         nn.init.kaiming_uniform_(self.weight, a=5 ** 0.5)
         if self.bias is not None:
-            nn.init.uniform_(self.bias, -1.0 / 3.0, 1.0 / 3.0)
+            bound = 1.0 / kernel_size
+            nn.init.uniform_(self.bias, -bound, bound)
 
     @classmethod
-    def from_conv2d(cls, conv: nn.Conv2d) -> "DepthwiseConv3x3":
+    def from_conv2d(cls, conv: nn.Conv2d) -> "DepthwiseConv2d":
         m = cls.__new__(cls)
         nn.Module.__init__(m)
         m.channels = conv.in_channels
+        m.kernel_size = int(conv.kernel_size[0])
+        m.stride = int(conv.stride[0])
         m.padding = int(conv.padding[0])
         m.weight = conv.weight
         m.bias = conv.bias
@@ -121,31 +204,50 @@ class DepthwiseConv3x3(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = x.to(torch.float16).contiguous(memory_format=torch.channels_last)
-        x_nhwc = x.permute(0, 2, 3, 1)                       # contiguous view, no copy
-        w_rsc = self.weight.to(torch.float16)[:, 0].permute(1, 2, 0)  # [3,3,C]
-        y = dwconv3x3(x_nhwc, w_rsc.contiguous(), self.padding)
-        if self.bias is not None:
-            y = y + self.bias.to(torch.float16)
-        return y.permute(0, 3, 1, 2)                          # NCHW view, channels-last memory
+        x_nhwc = x.permute(0, 2, 3, 1)                                  # contiguous view, no copy
+        w_rsc = self.weight.to(torch.float16)[:, 0].permute(1, 2, 0)   # [K,K,C]
+        b = None if self.bias is None else self.bias.to(torch.float16)
+        y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
+        return y.permute(0, 3, 1, 2)                                    # NCHW view, channels-last memory
 
     def extra_repr(self) -> str:
-        return f"{self.channels}, padding={self.padding}, bias={self.bias is not None}"
+        return (f"{self.channels}, kernel_size={self.kernel_size}, stride={self.stride}, "
+                f"padding={self.padding}, bias={self.bias is not None}")
 
 
-def _eligible(m: nn.Module) -> bool:
-    return (isinstance(m, nn.Conv2d) and m.kernel_size == (3, 3) and m.stride == (1, 1)
-            and m.dilation == (1, 1) and m.groups == m.in_channels == m.out_channels
-            and m.in_channels % 8 == 0 and m.padding_mode == "zeros"
-            and isinstance(m.padding, tuple) and m.padding[0] == m.padding[1])
+class DepthwiseConv3x3(DepthwiseConv2d):
+    """``DepthwiseConv2d`` with a 3x3 kernel and stride 1."""
+
+    def __init__(self, channels: int, padding: int = 1, bias: bool = True, device=None,
+                 dtype=torch.float16):
+        super().__init__(channels, 3, 1, padding, bias, device, dtype)
 
 
-def convert_depthwise_convs(model: nn.Module) -> int:
-    """Replace eligible depthwise 3x3 ``nn.Conv2d`` children in place; returns the count."""
+def _eligible(m: nn.Module, forward_only: bool) -> bool:
+    if not (isinstance(m, nn.Conv2d) and m.dilation == (1, 1)
+            and m.groups == m.in_channels == m.out_channels and m.in_channels % 8 == 0
+            and m.padding_mode == "zeros" and isinstance(m.padding, tuple)
+            and m.padding[0] == m.padding[1]
+            and m.kernel_size[0] == m.kernel_size[1] and m.stride[0] == m.stride[1]):
+        return False
+    geometry = (m.kernel_size[0], m.stride[0])
+    return geometry in (GEOMETRIES if forward_only else TRAINABLE)
+
+
+def convert_depthwise_convs(model: nn.Module, forward_only: bool = False) -> int:
+    """Replace eligible depthwise ``nn.Conv2d`` children in place; returns the count.
+
+    By default only 3x3 stride-1 convolutions (which have a backward) are
+    converted; ``forward_only=True`` also converts 5x5 / 7x7 and stride 2,
+    whose backward raises ``NotImplementedError``.
+    """
     count = 0
     for name, child in list(model.named_children()):
-        if _eligible(child):
-            setattr(model, name, DepthwiseConv3x3.from_conv2d(child))
+        if _eligible(child, forward_only):
+            cls = DepthwiseConv3x3 if (child.kernel_size[0], child.stride[0]) == (3, 1) \
+                else DepthwiseConv2d
+            setattr(model, name, cls.from_conv2d(child))
             count += 1
         else:
-            count += convert_depthwise_convs(child)
+            count += convert_depthwise_convs(child, forward_only)
     return count

@@ -20,7 +20,7 @@ import torch.nn.functional as F
 import _tma_dwconv_C as _C  # type: ignore
 
 __all__ = ["dwconv_v0", "dwconv_ws", "dwconv_ws_probe", "ref_dwconv",
-           "dwconv_ws_out", "dwconv3x3", "device_status", "set_wait_timeout_ns",
+           "dwconv_ws_out", "dwconv3x3", "dwconv", "DWCONV_STAGES", "device_status", "set_wait_timeout_ns",
            "CONSUMER_WARPS", "ACTIVATIONS"]
 
 #: Activations the general forward fuses into its epilogue.
@@ -156,6 +156,46 @@ def dwconv3x3(x: torch.Tensor, w: torch.Tensor, pad: int = 1,
     if activation not in ACTIVATIONS:
         raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
     return _C.dwconv3x3(x, w, bias, residual, int(pad), ACTIVATIONS[activation], int(n_stage))
+
+
+#: Ring stages ``dwconv`` uses when ``n_stage`` is None, per (K, stride): the
+#: fastest of {2, 3, 4} measured on a B200 at 64 x 224 x 336 x 256, pad K // 2.
+DWCONV_STAGES = {(3, 1): 2, (3, 2): 4, (5, 1): 3, (5, 2): 2, (7, 1): 3, (7, 2): 3}
+
+
+def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int = 1,
+           bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+           activation: str = "none", n_stage: int | None = None) -> torch.Tensor:
+    """K x K depthwise forward, K in {3, 5, 7}, stride 1 or 2 (beyond the reference surface).
+
+    ``y[n,p,q,c] = round_fp16(epilogue(sum_{r,s} x[n, stride*p+r-pad, stride*q+s-pad, c] * w[r,s,c]))``,
+    fp32 sums in (r, s) order from zero, zero outside the image.  The
+    epilogue is ``dwconv3x3``'s.  ``pad`` defaults to K // 2, ``n_stage`` to
+    ``DWCONV_STAGES[(K, stride)]``.  3x3 stride 1 is ``dwconv3x3``.
+
+    Args:
+        x: [N, H, W, C] fp16 CUDA, contiguous, C % 8 == 0.   w: [K, K, C] fp16.
+        bias: [C] fp16 or None.   residual: [N, P, Q, C] fp16 or None, with
+        P = (H + 2*pad - K) // stride + 1 and Q likewise.
+    """
+    if w.dim() == 3 and pad is None:
+        pad = int(w.shape[0]) // 2
+    _check(x, w, pad)
+    K = int(w.shape[0])
+    if K not in (3, 5, 7) or w.shape[1] != K:
+        raise ValueError(f"w must be [K,K,C] with K in {{3, 5, 7}}, got shape {tuple(w.shape)}")
+    if stride not in (1, 2):
+        raise ValueError(f"stride must be 1 or 2, got {stride}")
+    if x.shape[3] % 8 != 0:
+        raise ValueError("dwconv requires C % 8 == 0")
+    if n_stage is None:
+        n_stage = DWCONV_STAGES[(K, stride)]
+    if n_stage not in (2, 3, 4):
+        raise ValueError(f"n_stage must be one of {{2, 3, 4}}, got {n_stage}")
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
+    return _C.dwconv_k(x, w, bias, residual, int(stride), int(pad), ACTIVATIONS[activation],
+                       int(n_stage))
 
 
 def device_status(device: int | None = None, clear: bool = True):
