@@ -59,6 +59,7 @@ extern "C" {
 #define TDC_ERR_WORKSPACE       -14  /* workspace too small (tdc_dwconv3x3_bwd_weight)       */
 #define TDC_ERR_SCRATCH_LIMIT   -15  /* C beyond the static scratch (..._bwd_weight_noalloc) */
 #define TDC_ERR_STRIDE          -16  /* stride not 1 or 2 (tdc_dwconv_fwd)                  */
+#define TDC_ERR_UNSUPPORTED     -17  /* geometry without that kernel (backward at stride 2)  */
 
 /* Human-readable text for a status code (static storage, never NULL). */
 TDC_API const char* tdc_strerror(int code);
@@ -185,6 +186,37 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw,
 TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, float* dw,
                                              int64_t N, int64_t H, int64_t W, int64_t C,
                                              int64_t pad, int64_t n_stage, void* stream);
+
+/* Backward of the K x K forward (K = 3, 5, 7) at stride 1; stride 2 returns
+ * TDC_ERR_UNSUPPORTED.  No counterpart in the reference (forward only).
+ *   tdc_dwconv_bwd_data: dx [N,H,W,C] fp16 from dy [N,P,Q,C] and w [K,K,C],
+ *     P = H + 2*pad - K + 1: the forward kernel with flipped taps and
+ *     pad' = K - 1 - pad, so the chain per output is (r', s') lexicographic
+ *     over w[K-1-r'][K-1-s'] from +0, one fp16 rounding.  For K > 3,
+ *     pad <= K - 1.  K = 3 is tdc_dwconv3x3_bwd_data.
+ *   tdc_dwconv_bwd_weight: dw [K,K,C] fp32 (written), deterministic like
+ *     tdc_dwconv3x3_bwd_weight, with a caller workspace of at least the size
+ *     tdc_dwconv_bwd_weight_workspace reports.  K = 3 is
+ *     tdc_dwconv3x3_bwd_weight.
+ *   tdc_dwconv_bwd_weight_plan: the K = 5, 7 weight-gradient launch plan,
+ *     pure host arithmetic: plan[0..7] as tdc_ws_plan (the ring holds
+ *     stage_rows rows of x and of dy per stage), plan[8] = launches (the
+ *     tap rows are split over them to bound the sums a lane holds),
+ *     plan[9] = tap rows of the tallest launch (its x window; the ring keeps
+ *     (n_stage - 1) * stage_rows >= plan[9] - 1). */
+TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx,
+                                int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                int64_t stride, int64_t pad, int64_t n_stage, void* stream);
+TDC_API int tdc_dwconv_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
+                                            int64_t K, int64_t stride, int64_t pad,
+                                            int64_t n_stage, int64_t* bytes);
+TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw,
+                                  int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                  int64_t stride, int64_t pad, int64_t n_stage,
+                                  void* workspace, int64_t workspace_bytes, void* stream);
+TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                       int64_t pad, int64_t n_stage, int64_t sms,
+                                       int64_t ctas_per_sm, int64_t* plan);
 
 /* Number of rows of the stall tensor that tdc_dwconv_ws_probe writes for
  * this problem (= number of CTAs the launch uses). */

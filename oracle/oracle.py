@@ -45,6 +45,8 @@ def load() -> ctypes.CDLL:
         lib.oracle_dwconv_ex_f16.argtypes = ([ctypes.c_void_p] * 5 + [i64] * 7 +
                                              [ctypes.c_int, ctypes.c_int])
         lib.oracle_dwconv_ex_f16.restype = ctypes.c_int
+        lib.oracle_dwconv_bwd_data_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 6 + [ctypes.c_int]
+        lib.oracle_dwconv_bwd_data_f16.restype = ctypes.c_int
         lib.oracle_dwconv3x3_bwd_data_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 5 + [ctypes.c_int]
         lib.oracle_dwconv3x3_bwd_data_f16.restype = ctypes.c_int
         lib.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
@@ -213,23 +215,30 @@ def dwconv_f16_numpy(x: np.ndarray, w: np.ndarray, pad: int) -> np.ndarray:
 
 
 def dwconv_bwd_data_f16(dy: np.ndarray, w: np.ndarray, pad: int, threads: int = 0) -> np.ndarray:
-    """C oracle of the data gradient: dx [N,H,W,C] fp16 from dy [N,P,Q,C] (taps
-    flipped, fp32 chain in the kernel's order, fp16 RNE)."""
+    """C oracle of the data gradient of the stride-1 forward: dx [N,H,W,C] fp16
+    from dy [N,P,Q,C] and w [K,K,C] (taps flipped, fp32 chain in the kernel's
+    order, fp16 RNE).  K = 3 runs the 3x3 restatement, other K the K x K one."""
     lib = load()
     dy = np.ascontiguousarray(dy, dtype=np.float16)
     w = np.ascontiguousarray(w, dtype=np.float16)
     N, P, Q, C = dy.shape
-    H, W = P - 2 * pad + 2, Q - 2 * pad + 2
+    K = w.shape[0]
+    H, W = P - 2 * pad + K - 1, Q - 2 * pad + K - 1
     dx = np.empty((N, H, W, C), dtype=np.float16)
-    rc = lib.oracle_dwconv3x3_bwd_data_f16(dy.ctypes.data, w.ctypes.data, dx.ctypes.data,
-                                           N, H, W, C, pad, int(threads))
+    if K == 3:
+        rc = lib.oracle_dwconv3x3_bwd_data_f16(dy.ctypes.data, w.ctypes.data, dx.ctypes.data,
+                                               N, H, W, C, pad, int(threads))
+    else:
+        rc = lib.oracle_dwconv_bwd_data_f16(dy.ctypes.data, w.ctypes.data, dx.ctypes.data,
+                                            N, H, W, C, K, pad, int(threads))
     if rc != 0:
-        raise RuntimeError("oracle_dwconv3x3_bwd_data_f16 failed")
+        raise RuntimeError("oracle data gradient failed")
     return dx
 
 
-def dwconv_bwd_weight_f64(x: np.ndarray, dy: np.ndarray, pad: int) -> np.ndarray:
-    """Weight gradient in float64 (the accuracy reference for the fp32 kernel):
+def dwconv_bwd_weight_f64(x: np.ndarray, dy: np.ndarray, pad: int, K: int = 3) -> np.ndarray:
+    """Weight gradient of the K x K stride-1 forward in float64 (the accuracy
+    reference for the fp32 kernels):
     dw[r,s,c] = sum_{n,p,q} x[n,p+r-pad,q+s-pad,c] * dy[n,p,q,c]."""
     x = np.asarray(x, np.float16).astype(np.float64)
     dy = np.asarray(dy, np.float16).astype(np.float64)
@@ -237,9 +246,9 @@ def dwconv_bwd_weight_f64(x: np.ndarray, dy: np.ndarray, pad: int) -> np.ndarray
     P, Q = dy.shape[1], dy.shape[2]
     xp = np.zeros((N, H + 2 * pad, W + 2 * pad, C))
     xp[:, pad:pad + H, pad:pad + W] = x
-    dw = np.empty((3, 3, C))
-    for r in range(3):
-        for s in range(3):
+    dw = np.empty((K, K, C))
+    for r in range(K):
+        for s in range(K):
             dw[r, s] = np.einsum("npqc,npqc->c", xp[:, r:r + P, s:s + Q], dy)
     return dw
 

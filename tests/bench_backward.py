@@ -1,15 +1,16 @@
-"""Backward of the depthwise 3x3 vs cuDNN, on one GPU.
+"""Backward of the depthwise K x K (stride 1) vs cuDNN, on one GPU.
 
-    python tests/bench_backward.py [--images 64]
+    python tests/bench_backward.py [--images 64] [--K 3] [--n-stage 2]
 
-Headline shape (N x 224 x 336 x 256 fp16, pad 1).  CUDA events, 5 warm-up +
-20 calls each:
-  dgrad      dwconv3x3_bwd_data   (reads dy, writes dx: 4 B per element)
-  wgrad      dwconv3x3_bwd_weight (reads x and dy: 4 B per element)
+Headline shape (N x 224 x 336 x 256 fp16, pad K // 2).  CUDA events, 5
+warm-up + 20 calls each:
+  dgrad      dwconv_bwd_data   (reads dy, writes dx: 4 B per element)
+  wgrad      dwconv_bwd_weight (reads x and dy: 4 B per element, once per
+             tap-row launch)
   cudnn      aten.convolution_backward on channels-last tensors, grad input
              and grad weight together (what nn.Conv2d's backward runs)
-Prints one JSON line per variant with µs and algorithmic GB/s.  A script,
-not a test.
+Prints one JSON line per variant with µs, algorithmic GB/s and the FMA rate
+(2 * N*H*W*C*K*K flop per gradient).  A script, not a test.
 """
 from __future__ import annotations
 
@@ -42,16 +43,20 @@ def bench_us(fn, warmup=5, iters=20) -> float:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--images", type=int, default=64)
+    ap.add_argument("--K", type=int, default=3)
+    ap.add_argument("--n-stage", type=int, default=2)
     args = ap.parse_args()
-    N, H, W, C, pad = args.images, 224, 336, 256, 1
+    K, ns = args.K, args.n_stage
+    N, H, W, C, pad = args.images, 224, 336, 256, K // 2
     g = torch.Generator(device="cuda").manual_seed(0)
     x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
     dy = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
-    w = ((torch.rand(3, 3, C, device="cuda", generator=g) * 2 - 1) / 3).half()
+    w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).half()
     io = 2 * N * H * W * C
+    flops = 2 * N * H * W * C * K * K
     rows = [
-        ("dgrad", lambda: T._C.dwconv3x3_bwd_data(dy, w, pad, 2), 2 * io),
-        ("wgrad", lambda: T._C.dwconv3x3_bwd_weight(x, dy, pad, 2), 2 * io),
+        ("dgrad", lambda: T._C.dwconv_bwd_data(dy, w, pad, 1, ns), 2 * io),
+        ("wgrad", lambda: T._C.dwconv_bwd_weight(x, dy, K, pad, 1, ns), 2 * io),
     ]
     xc, dyc = x.permute(0, 3, 1, 2), dy.permute(0, 3, 1, 2)  # channels-last NCHW views
     wc = w.permute(2, 0, 1).unsqueeze(1).contiguous()
@@ -65,8 +70,10 @@ def main() -> None:
     for name, fn, nbytes in rows:
         us = bench_us(fn)
         out[name] = us
-        print(json.dumps({"variant": name, "images": N, "us": round(us, 1),
-                          "algorithmic_GBps": round(nbytes / (us * 1e-6) / 1e9, 1)}), flush=True)
+        nf = 2 * flops if name.startswith("cudnn") else flops
+        print(json.dumps({"variant": name, "K": K, "n_stage": ns, "images": N, "us": round(us, 1),
+                          "algorithmic_GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
+                          "fma_TFLOPs": round(nf / (us * 1e-6) / 1e12, 2)}), flush=True)
     print(json.dumps({"ours_dgrad_plus_wgrad_us": round(out["dgrad"] + out["wgrad"], 1),
                       "speedup_vs_cudnn": round(out["cudnn dgrad+wgrad"] / (out["dgrad"] + out["wgrad"]), 2)}))
 

@@ -104,7 +104,7 @@ def test_convert_depthwise_convs_eligibility():
     nn = torch.nn
     model = nn.Sequential(
         nn.Conv2d(64, 64, 3, padding=1, groups=64),             # trainable: converted
-        nn.Conv2d(64, 64, 7, padding=3, groups=64),             # forward-only geometry
+        nn.Conv2d(64, 64, 7, padding=3, groups=64),             # trainable: converted
         nn.Conv2d(64, 64, 5, stride=2, padding=2, groups=64),   # forward-only geometry
         nn.Sequential(nn.Conv2d(64, 64, 3, stride=2, padding=1, groups=64)),
         nn.Conv2d(64, 64, 3, padding=1, groups=64, dilation=2),  # dilated: never
@@ -113,10 +113,10 @@ def test_convert_depthwise_convs_eligibility():
         nn.Conv2d(64, 64, 9, padding=4, groups=64),              # 9x9: never
         nn.Conv2d(64, 64, (3, 5), padding=(1, 2), groups=64),    # non-square: never
     )
-    assert tdc_torch.convert_depthwise_convs(model) == 1
+    assert tdc_torch.convert_depthwise_convs(model) == 2  # the stride-1 ones: 3x3 and 7x7
     assert isinstance(model[0], tdc_torch.DepthwiseConv3x3)
-    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 3
     assert type(model[1]) is tdc_torch.DepthwiseConv2d and model[1].kernel_size == 7
+    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 2  # + stride 2
     assert model[2].stride == 2 and model[2].padding == 2 and model[3][0].stride == 2
     assert all(isinstance(m, nn.Conv2d) for m in list(model)[4:])
     with pytest.raises(ValueError, match="kernel_size must be 3, 5 or 7"):

@@ -278,6 +278,64 @@ def test_kxk_consumer_schemes():
     assert [direct_scheme(K, S) for K in (3, 5, 7) for S in (1, 2)] == [False, False, True, False, True, True]
 
 
+def test_kxk_backward_argument_errors(lib):
+    p = C.c_void_p
+    def bd(K=7, S=1, pad=3, C_=64, ns=2):
+        return lib.tdc_dwconv_bwd_data(p(16), p(16), p(16), i64(2), i64(16), i64(16), i64(C_), i64(K),
+                                       i64(S), i64(pad), i64(ns), None)
+    def ws(K=7, S=1, pad=3, C_=64, ns=2):
+        b = i64()
+        return lib.tdc_dwconv_bwd_weight_workspace(i64(2), i64(16), i64(16), i64(C_), i64(K), i64(S),
+                                                   i64(pad), i64(ns), C.byref(b))
+    def bw(K=7, S=1, pad=3, C_=64, ns=2):
+        return lib.tdc_dwconv_bwd_weight(p(16), p(16), p(16), i64(2), i64(16), i64(16), i64(C_), i64(K),
+                                         i64(S), i64(pad), i64(ns), p(16), i64(1 << 30), None)
+    for f in (bd, ws, bw):
+        assert f(K=4) == CODES["TDC_ERR_FILTER_SHAPE"]
+        assert f(S=3) == CODES["TDC_ERR_STRIDE"]
+        assert f(S=2) == CODES["TDC_ERR_UNSUPPORTED"]
+        assert f(C_=12) == CODES["TDC_ERR_CHANNELS"]
+        assert f(ns=5) == CODES["TDC_ERR_N_STAGE"]
+    assert bd(pad=7) == CODES["TDC_ERR_PAD"]  # pad' = K - 1 - pad < 0
+    assert bd(pad=-1) == CODES["TDC_ERR_PAD"]
+    assert lib.tdc_dwconv_bwd_weight_workspace(i64(2), i64(16), i64(16), i64(64), i64(7), i64(1), i64(3),
+                                               i64(2), None) == CODES["TDC_ERR_NULL_POINTER"]
+    if not torch.cuda.is_available():
+        assert bd() == CODES["TDC_ERR_NO_DEVICE"]
+        assert ws() == CODES["TDC_ERR_NO_DEVICE"]
+        assert bw() == CODES["TDC_ERR_NO_DEVICE"]
+
+
+def _wgrad_plan(lib, N, H, W, Cc, K, pad, ns, sms=148, occ=3):
+    out = (i64 * 10)()
+    assert lib.tdc_dwconv_bwd_weight_plan(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(pad), i64(ns),
+                                          i64(sms), i64(occ), out) == 0
+    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
+                     "smem", "passes", "rows"], list(out)))
+
+
+@pytest.mark.parametrize("K", [5, 7])
+@pytest.mark.parametrize("N,H,W,Cc,pad", [(64, 224, 336, 256, None), (2, 19, 45, 72, 0), (3, 7, 9, 8, None),
+                                          (1, 300, 40, 64, 4)])
+@pytest.mark.parametrize("ns", [2, 3, 4])
+def test_kxk_wgrad_plan_covers_every_dy_row_once(lib, K, N, H, W, Cc, pad, ns):
+    pad = K // 2 if pad is None else pad
+    pl = _wgrad_plan(lib, N, H, W, Cc, K, pad, ns)
+    P, Q = H + 2 * pad - K + 1, W + 2 * pad - K + 1
+    sr, nr = pl["stage_rows"], pl["rows"]
+    assert pl["passes"] in (1, 2) and 1 <= nr <= K and pl["passes"] * nr >= K
+    assert (ns - 1) * sr >= nr - 1
+    assert pl["smem"] == ns * sr * ((32 + K - 1) * 128 + 4096) + 128 <= 200 * 1024
+    seen = set()
+    for g in range(pl["grid"]):
+        for strip, a, b in segments(pl, P, g):
+            assert max_stages_held(b - a, nr, 1, sr) <= ns
+            for r in range(a, b):
+                assert (strip, r) not in seen
+                seen.add((strip, r))
+    assert len(seen) == pl["strips"] * P
+
+
 def test_plan_balances_the_headline_shape(lib):
     # the busiest CTA streams at most 3% more rows (halo included) than a perfect split
     for occ in (3, 4):

@@ -260,6 +260,59 @@ torch::Tensor dwconv3x3_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t pa
   return dw;
 }
 
+// Backward of the K x K stride-1 forward (K = 3, 5, 7).
+torch::Tensor dwconv_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, int64_t stride,
+                              int64_t n_stage) {
+  check_common(dy, w);
+  const int64_t K = w.size(0);
+  TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7) && w.size(2) == dy.size(3),
+              "w must be [K,K,C] with K in {3, 5, 7}");
+  TORCH_CHECK(stride == 1, "the backward is implemented for stride 1 only, got stride ", stride);
+  TORCH_CHECK(dy.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(K == 3 || pad <= K - 1, "the ", K, "x", K, " data gradient needs pad <= ", K - 1);
+  const int64_t H = dy.size(1) - 2 * pad + K - 1, W = dy.size(2) - 2 * pad + K - 1;
+  TORCH_CHECK(H >= 1 && W >= 1, "dy is smaller than a ", K, "x", K, " kernel with pad ", pad,
+              " can produce");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  auto dx = torch::empty({dy.size(0), H, W, dy.size(3)}, dy.options());
+  if (dx.numel() == 0 || dy.numel() == 0) return dx.zero_();
+  check_status(tdc_dwconv_bwd_data(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), dy.size(0), H, W,
+                                   dy.size(3), K, stride, pad, n_stage, stream_of(dy)),
+               "dwconv_bwd_data");
+  return dx;
+}
+
+torch::Tensor dwconv_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t K, int64_t pad,
+                                int64_t stride, int64_t n_stage) {
+  TORCH_CHECK(x.is_cuda() && dy.is_cuda() && x.device() == dy.device(), "tensors must live on CUDA");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf && dy.scalar_type() == torch::kHalf,
+              "x and dy must be fp16");
+  TORCH_CHECK(x.dim() == 4 && dy.dim() == 4 && x.is_contiguous() && dy.is_contiguous(),
+              "x and dy must be contiguous [N,H,W,C] / [N,P,Q,C]");
+  TORCH_CHECK(K == 3 || K == 5 || K == 7, "K must be 3, 5 or 7, got ", K);
+  TORCH_CHECK(stride == 1, "the backward is implemented for stride 1 only, got stride ", stride);
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(dy.size(0) == x.size(0) && dy.size(3) == x.size(3) &&
+                  dy.size(1) == x.size(1) + 2 * pad - K + 1 &&
+                  dy.size(2) == x.size(2) + 2 * pad - K + 1,
+              "dy must be [N, H+2*pad-K+1, W+2*pad-K+1, C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dw = torch::zeros({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
+  if (x.numel() == 0 || dy.numel() == 0) return dw;
+  int64_t bytes = 0;
+  check_status(tdc_dwconv_bwd_weight_workspace(x.size(0), x.size(1), x.size(2), x.size(3), K,
+                                               stride, pad, n_stage, &bytes),
+               "dwconv_bwd_weight");
+  auto ws = torch::empty({(bytes + 3) / 4}, x.options().dtype(torch::kFloat32));
+  check_status(tdc_dwconv_bwd_weight(x.data_ptr(), dy.data_ptr(), dw.data_ptr<float>(), x.size(0),
+                                     x.size(1), x.size(2), x.size(3), K, stride, pad, n_stage,
+                                     ws.data_ptr(), bytes, stream_of(x)),
+               "dwconv_bwd_weight");
+  return dw;
+}
+
 // (code, block, stage, load) of the first pipeline-wait failure recorded on
 // `device` since the last clear; code 0 = none.  Synchronises the device.
 std::tuple<int64_t, int64_t, int64_t, int64_t> device_status(int64_t device, bool clear) {
@@ -310,6 +363,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dwconv3x3_bwd_weight", &tma_dwconv::dwconv3x3_bwd_weight,
         "Weight gradient of the 3x3 forward: dw [3,3,C] fp32 (deterministic).", pybind11::arg("x"),
         pybind11::arg("dy"), pybind11::arg("pad"), pybind11::arg("n_stage") = 2);
+  m.def("dwconv_bwd_data", &tma_dwconv::dwconv_bwd_data,
+        "Data gradient of the K x K stride-1 forward: dx [N,H,W,C] from dy [N,P,Q,C].",
+        pybind11::arg("dy"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("stride") = 1,
+        pybind11::arg("n_stage") = 2);
+  m.def("dwconv_bwd_weight", &tma_dwconv::dwconv_bwd_weight,
+        "Weight gradient of the K x K stride-1 forward: dw [K,K,C] fp32 (deterministic).",
+        pybind11::arg("x"), pybind11::arg("dy"), pybind11::arg("K"), pybind11::arg("pad"),
+        pybind11::arg("stride") = 1, pybind11::arg("n_stage") = 2);
   m.def("device_status", &tma_dwconv::device_status,
         "(code, block, stage, load) of the first recorded pipeline-wait failure on a device.",
         pybind11::arg("device"), pybind11::arg("clear") = true);

@@ -231,39 +231,36 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 4-D map over x viewed as (C, W, H, N), innermost first; box
-// (64 ch, 34 cols, stage_rows rows, 1 image); out-of-bounds elements read 0.
-int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t W, int64_t C,
-                 int stage_rows) {
+// 4-D map over an NHWC fp16 tensor viewed as (C, W, H, N), innermost first;
+// box (64 ch, box_cols columns, box_rows rows, 1 image); out-of-bounds
+// elements read 0.  Stores the CUresult of a failed encode for
+// tdc_last_cuda_error.
+int encode_nhwc_map(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W, int64_t C,
+                    int box_cols, int box_rows) {
   auto fn = get_encode_fn();
   if (!fn) return TDC_ERR_TMA_ENCODE;
   const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
   const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(W) * C * 2, cuuint64_t(H) * W * C * 2};
-  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(tdc::kInCols),
-                             cuuint32_t(stage_rows), 1u};
+  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(box_cols), cuuint32_t(box_rows),
+                             1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides,
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(t), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) t_last_cuda_error = int(r);
   return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
 }
 
-// 4-D map over dy viewed as (C, Q, P, N); box (64 ch, 32 cols, stage_rows rows, 1 image).
+// x of the 3x3 stride-1 kernels: 34 columns (a 32-column strip and its halo).
+int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t W, int64_t C,
+                 int stage_rows) {
+  return encode_nhwc_map(map, x, N, H, W, C, tdc::kInCols, stage_rows);
+}
+
+// dy [N,P,Q,C] of the weight gradients: 32 columns (one strip).
 int encode_dy_map(CUtensorMap* map, const void* dy, int64_t N, int64_t P, int64_t Q, int64_t C,
                   int stage_rows) {
-  auto fn = get_encode_fn();
-  if (!fn) return TDC_ERR_TMA_ENCODE;
-  const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(Q), cuuint64_t(P), cuuint64_t(N)};
-  const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(Q) * C * 2, cuuint64_t(P) * Q * C * 2};
-  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(tdc::kStripQ),
-                             cuuint32_t(stage_rows), 1u};
-  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(dy), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) t_last_cuda_error = int(r);
-  return r == CUDA_SUCCESS ? TDC_OK : TDC_ERR_TMA_ENCODE;
+  return encode_nhwc_map(map, dy, N, P, Q, C, tdc::kStripQ, stage_rows);
 }
 
 // Limits of the descriptor and of the 32-bit fields the kernel keeps.
@@ -468,25 +465,9 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
     }
   }
   const WsPlan pl = make_geom_plan(N, P, Q, C, int(K), int(S), n_stage, dev->sms, occ);
-  auto fn = get_encode_fn();
-  if (!fn) return TDC_ERR_TMA_ENCODE;
   alignas(64) CUtensorMap map;
-  {
-    const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
-    const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(W) * C * 2,
-                                   cuuint64_t(H) * W * C * 2};
-    const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(strip_in_cols(int(K), int(S))),
-                               cuuint32_t(stage_rows), 1u};
-    const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-    const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims,
-                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      t_last_cuda_error = int(r);
-      return TDC_ERR_TMA_ENCODE;
-    }
-  }
+  rc = encode_nhwc_map(&map, x, N, H, W, C, strip_in_cols(int(K), int(S)), stage_rows);
+  if (rc != TDC_OK) return rc;
   tdc::WsParams prm{};
   prm.w = static_cast<const __half*>(w);
   prm.y = static_cast<__half*>(y);
@@ -500,10 +481,147 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   prm.bias = static_cast<const __half*>(epi.bias);
   prm.residual = static_cast<const __half*>(epi.residual);
   prm.act = epi.act;
-  prm.flip_taps = 0;
+  prm.flip_taps = epi.flip_taps ? 1 : 0;
   const cudaError_t e =
       kGeomLaunch[ki][si][mi][ni](map, prm, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+// ---------------------------------------------------------------------------
+// Weight gradient of the K x K (K = 5, 7) stride-1 forward.
+// ---------------------------------------------------------------------------
+using WgradLaunchFn = cudaError_t (*)(const CUtensorMap&, const CUtensorMap&,
+                                      const tdc::WgradParams&, int64_t, size_t, cudaStream_t);
+
+// Tap-row passes of the K x K weight gradient: launch i covers rows
+// [R0_i, R0_i + NR_i).  A single 7x7 pass would hold 98 sums per lane and
+// spill at 128 registers (or drop to 1-2 CTAs per SM); two passes (rows 0-3,
+// then 4-6) read x and dy twice but ran 11 % faster than the best single
+// pass (3.54 vs 3.97 ms at 64 x 224 x 336 x 256).  5x5 runs as one pass
+// (2.04 ms; split in 3 + 2 rows: 2.20 ms).
+template <int K>
+struct WgradPasses;
+template <>
+struct WgradPasses<5> {
+  static constexpr int kCount = 1;
+  static constexpr int kR0[2] = {0, 0};
+  static constexpr int kNR[2] = {5, 0};
+};
+template <>
+struct WgradPasses<7> {
+  static constexpr int kCount = 2;
+  static constexpr int kR0[2] = {0, 4};
+  static constexpr int kNR[2] = {4, 3};
+};
+
+template <int NS, int K, int PASS>
+cudaError_t wgrad_kxk_launch_t(const CUtensorMap& xmap, const CUtensorMap& dymap,
+                               const tdc::WgradParams& g, int64_t grid, size_t smem,
+                               cudaStream_t st) {
+  using WP = WgradPasses<K>;
+  if constexpr (PASS < WP::kCount) {
+    tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS]>
+        <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(xmap, dymap, g);
+    return cudaGetLastError();
+  } else {
+    return cudaSuccess;
+  }
+}
+
+template <int NS, int K, int PASS>
+cudaError_t wgrad_kxk_occ_t(int* occ, size_t smem) {
+  using WP = WgradPasses<K>;
+  if constexpr (PASS < WP::kCount) {
+    auto* k = &tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS]>;
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+  } else {
+    *occ = 1 << 20;  // no such pass: does not limit the grid
+    return cudaSuccess;
+  }
+}
+
+#define TDC_WGRAD_NS(FN, K, PASS) {FN<2, K, PASS>, FN<3, K, PASS>, FN<4, K, PASS>}
+#define TDC_WGRAD_TABLE(FN)                                         \
+  {{TDC_WGRAD_NS(FN, 5, 0), TDC_WGRAD_NS(FN, 5, 1)},                \
+   {TDC_WGRAD_NS(FN, 7, 0), TDC_WGRAD_NS(FN, 7, 1)}}
+// [K index: 5, 7][pass][n_stage - 2]
+const WgradLaunchFn kWgradKxkLaunch[2][2][3] = TDC_WGRAD_TABLE(wgrad_kxk_launch_t);
+const GeomOccFn kWgradKxkOcc[2][2][3] = TDC_WGRAD_TABLE(wgrad_kxk_occ_t);
+#undef TDC_WGRAD_TABLE
+#undef TDC_WGRAD_NS
+int g_wgrad_kxk_occ[kMaxDevices][2][3] = {};  // min over passes; guarded by g_geom_mutex
+
+int wgrad_kxk_passes(int K) { return K == 5 ? WgradPasses<5>::kCount : WgradPasses<7>::kCount; }
+int wgrad_kxk_max_rows(int K) {  // the tallest pass's x window
+  return K == 5 ? WgradPasses<5>::kNR[0] : WgradPasses<7>::kNR[0];
+}
+
+int wgrad_kxk_row_bytes(int K) { return (tdc::kStripQ + K - 1) * tdc::kBlockC * 2 + tdc::kDyRowBytes; }
+
+// Ring of about 72 KB (3 CTAs per SM); the tallest pass's x window must fit,
+// as in the direct forward.
+int wgrad_kxk_stage_rows(int K, int64_t n_stage) {
+  const int ns = int(n_stage);
+  const int nr = wgrad_kxk_max_rows(K);
+  const int ring_rows = std::max(ns, (72 * 1024) / wgrad_kxk_row_bytes(K));
+  const int sr = std::max(1, ring_rows / ns);
+  return std::max(sr, (nr - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
+}
+
+WsPlan make_wgrad_kxk_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int64_t n_stage,
+                           int64_t sms, int64_t ctas_per_sm) {
+  WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  pl.stage_rows = wgrad_kxk_stage_rows(K, n_stage);
+  pl.smem = size_t(n_stage) * pl.stage_rows * wgrad_kxk_row_bytes(K) + 128;
+  return pl;
+}
+
+// Validates a K x K stride-1 weight-gradient call and plans its launch on the
+// current device (which it binds).
+int wgrad_kxk_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                   int64_t n_stage, WsPlan* pl, int64_t* P, int64_t* Q) {
+  if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  *P = H + 2 * pad - K + 1;
+  *Q = W + 2 * pad - K + 1;
+  if (*P < 1 || *Q < 1) return TDC_ERR_BAD_SHAPE;
+  int rc = check_ws_limits(N, H, W, C, *P, *Q);
+  if (rc != TDC_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  int devi = -1;
+  rc = current_device(&dev, &devi);
+  if (rc != TDC_OK) return rc;
+  const int ki = K == 5 ? 0 : 1, ni = int(n_stage - 2);
+  const size_t smem = make_wgrad_kxk_plan(1, 1, 1, 8, int(K), n_stage, 1, 1).smem;
+  int occ;
+  {
+    // Every pass runs on the same grid (they share the workspace slices), so
+    // the grid follows the pass with the lowest occupancy.
+    std::lock_guard<std::mutex> lock(g_geom_mutex);
+    occ = g_wgrad_kxk_occ[devi][ki][ni];
+    if (occ == 0) {
+      occ = 1 << 20;
+      for (int pass = 0; pass < 2; ++pass) {
+        int o = 0;
+        const cudaError_t e = kWgradKxkOcc[ki][pass][ni](&o, smem);
+        if (e != cudaSuccess) return cuda_fail(e);
+        occ = std::min(occ, std::max(1, o));
+      }
+      g_wgrad_kxk_occ[devi][ki][ni] = occ;
+    }
+  }
+  *pl = make_wgrad_kxk_plan(N, *P, *Q, C, int(K), n_stage, dev->sms, occ);
+  return TDC_OK;
+}
+
+int64_t wgrad_kxk_workspace_bytes(const WsPlan& pl, int64_t C, int64_t K) {
+  return pl.grid * tdc::kConsumerWarps * K * K * C * int64_t(sizeof(float));
 }
 
 }  // namespace
@@ -528,6 +646,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_WORKSPACE: return "workspace smaller than tdc_dwconv3x3_bwd_weight_workspace reports";
     case TDC_ERR_SCRATCH_LIMIT: return "C too large for the 16 MiB static scratch of tdc_dwconv3x3_bwd_weight_noalloc (C <= 116508)";
     case TDC_ERR_STRIDE: return "stride must be 1 or 2";
+    case TDC_ERR_UNSUPPORTED: return "not implemented for this geometry (the backward is stride 1 only)";
     case TDC_ERR_ACT: return "activation code is not one of TDC_ACT_NONE, _RELU, _RELU6, _SILU";
     default: return "unknown tdc status code";
   }
@@ -612,6 +731,112 @@ TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int6
   //            = forward(dy, w[2-r][2-s], pad' = 2 - pad)
   return ws_common(dy, w, dx, N, P, Q, C, 3, 3, 2 - pad, n_stage, nullptr, false, -1, 0, stream,
                    epi);
+}
+
+TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
+                                int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
+                                int64_t n_stage, void* stream) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (stride != 1) return TDC_ERR_UNSUPPORTED;
+  if (K == 3) return tdc_dwconv3x3_bwd_data(dy, w, dx, N, H, W, C, pad, n_stage, stream);
+  // pad' = K - 1 - pad must not be negative (pad above K - 1 leaves dx rows
+  // no output depends on; not supported for K > 3).
+  if (pad < 0 || pad > K - 1) return TDC_ERR_PAD;
+  const int64_t P = H + 2 * pad - K + 1, Q = W + 2 * pad - K + 1;
+  if (H < 1 || W < 1 || P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
+  Epilogue epi;
+  epi.fused = true;
+  epi.flip_taps = true;
+  // dx[n,h,w,c] = sum_{r,s} dy[n, h+pad-r, w+pad-s, c] * w[r,s,c]
+  //            = forward(dy, w[K-1-r][K-1-s], pad' = K - 1 - pad)
+  return fwd_geom(dy, w, dx, N, P, Q, C, K, 1, K - 1 - pad, n_stage, epi, stream);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                            int64_t stride, int64_t pad, int64_t n_stage,
+                                            int64_t* bytes) {
+  if (!bytes) return TDC_ERR_NULL_POINTER;
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (stride != 1) return TDC_ERR_UNSUPPORTED;
+  if (K == 3) return tdc_dwconv3x3_bwd_weight_workspace(N, H, W, C, pad, n_stage, bytes);
+  WsPlan pl;
+  int64_t P, Q;
+  const int rc = wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  *bytes = wgrad_kxk_workspace_bytes(pl, C, K);
+  return TDC_OK;
+}
+
+TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int64_t N, int64_t H,
+                                  int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
+                                  int64_t n_stage, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (stride != 1) return TDC_ERR_UNSUPPORTED;
+  if (K == 3)
+    return tdc_dwconv3x3_bwd_weight(x, dy, dw, N, H, W, C, pad, n_stage, workspace,
+                                    workspace_bytes, stream);
+  if (!x || !dy || !dw || !workspace) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dw) || !aligned16(workspace))
+    return TDC_ERR_ALIGNMENT;
+  WsPlan pl;
+  int64_t P, Q;
+  int rc = wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (workspace_bytes < wgrad_kxk_workspace_bytes(pl, C, K)) return TDC_ERR_WORKSPACE;
+  alignas(64) CUtensorMap xmap, dymap;
+  rc = encode_nhwc_map(&xmap, x, N, H, W, C, tdc::kStripQ + int(K) - 1, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  tdc::WgradParams g{};
+  g.partial = static_cast<float*>(workspace);
+  g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
+  g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
+  g.tail_bands = pl.tail_bands; g.tail_band_rows = pl.tail_band_rows;
+  g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
+  g.timeout_ns = uint64_t(g_timeout_ns.load());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int pass = 0; pass < wgrad_kxk_passes(int(K)); ++pass) {
+    const cudaError_t e =
+        kWgradKxkLaunch[K == 5 ? 0 : 1][pass][n_stage - 2](xmap, dymap, g, pl.grid, pl.smem, st);
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  cudaError_t e;
+  const int n = int(K * K * C);
+  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
+      static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                       int64_t pad, int64_t n_stage, int64_t sms,
+                                       int64_t ctas_per_sm, int64_t* plan) {
+  if (!plan) return TDC_ERR_NULL_POINTER;
+  if (K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (sms < 1 || ctas_per_sm < 1) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = H + 2 * pad - K + 1, Q = W + 2 * pad - K + 1;
+  if (P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
+  const WsPlan pl = make_wgrad_kxk_plan(N, P, Q, C, int(K), n_stage, sms, ctas_per_sm);
+  plan[0] = pl.stage_rows;
+  plan[1] = pl.qstrips;
+  plan[2] = pl.cblocks;
+  plan[3] = pl.strips;
+  plan[4] = pl.full_units;
+  plan[5] = pl.tail_band_rows;
+  plan[6] = pl.grid;
+  plan[7] = int64_t(pl.smem);
+  plan[8] = wgrad_kxk_passes(int(K));
+  plan[9] = wgrad_kxk_max_rows(int(K));
+  return TDC_OK;
 }
 
 // Plan of the weight-gradient launch: the forward planner over dy's strips.

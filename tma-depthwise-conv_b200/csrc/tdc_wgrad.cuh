@@ -1,4 +1,5 @@
-// tdc_wgrad.cuh — weight gradient of the depthwise 3x3 forward, sm_100a.
+// tdc_wgrad.cuh — weight gradient of the depthwise 3x3 forward (and of the
+// K x K stride-1 forward, below), sm_100a.
 //
 //   dw[r,s,c] = sum_{n,p,q} x[n, p+r-pad, q+s-pad, c] * dy[n,p,q,c]     (x = 0 outside)
 //
@@ -215,6 +216,213 @@ __global__ void __launch_bounds__(kWsThreads, 1) dwconv_wgrad_kernel(
         if (++stage == NS) { stage = 0; phase ^= 1u; }
       }
     }
+  }
+  if (cur_cb >= 0 && !failed) flush(cur_cb);
+}
+
+// ============================================================================
+// Weight gradient of the K x K (K = 5, 7) stride-1 forward:
+//   dw[r,s,c] = sum_{n,p,q} x[n, p+r-pad, q+s-pad, c] * dy[n,p,q,c]
+// computed for the tap rows r in [R0, R0 + NR) by one launch (the host runs
+// one or two launches to cover all K rows, so a lane never holds more than
+// NR*K*2 sums).  The same persistent walk over dy's strips and the same
+// producer, with the ring split in two: NS*sr rows of x (32 + K - 1 columns
+// each) followed by NS*sr rows of dy (32 columns); stage t of a segment
+// fills x rows [p0 - pad + R0 + t*sr, ...) and dy rows [p0 + t*sr, ...) in
+// slot (seq + t) % NS, so segment row i sits at ring row (base + i) mod
+// (NS*sr) in either half.  Consumers take one dy row o at a time with its NR
+// x rows (the direct scheme of the forward: the warp holds the stages of
+// that window, which the host keeps within the ring with
+// (NS - 1) * sr >= NR - 1) and accumulate x[o+R0+r][m+s] * dy[o][m] into
+// NR*K*2 fp32 sums per lane.  Workspace slices hold all K*K taps
+// (partial[cta][warp][K*K][C]); a launch zeroes and fills only its rows'
+// taps, and the reduction of the 3x3 kernel sums them.
+// ============================================================================
+template <int K>
+struct WgradGeom {
+  static constexpr int kXCols = kStripQ + K - 1;        // x columns of a strip
+  static constexpr int kXRowB = kXCols * kBlockC * 2;   // bytes of one x ring row
+  static constexpr int kXWarp = kColsPerWarp + K - 1;   // x columns one warp reads
+};
+
+template <int NS, int K, int R0, int NR>
+__global__ void __launch_bounds__(kWsThreads, 3)
+    dwconv_wgrad_kxk_kernel(const __grid_constant__ CUtensorMap xmap,
+                            const __grid_constant__ CUtensorMap dymap,
+                            const __grid_constant__ WgradParams g) {
+  static_assert(R0 >= 0 && NR >= 1 && R0 + NR <= K, "tap rows");
+  using G = WgradGeom<K>;
+  __shared__ __align__(8) uint64_t full_bar[NS];
+  __shared__ __align__(8) uint64_t empty_bar[NS];
+  __shared__ volatile int abort_flag;
+  extern __shared__ uint8_t dyn_smem[];
+  const uint32_t ring = (smem_addr(dyn_smem) + 127u) & ~127u;
+  const uint8_t* ring_ptr = dyn_smem + (ring - smem_addr(dyn_smem));
+  const int sr = g.stage_rows;
+  const int ring_rows = NS * sr;
+  const uint32_t x_stage_bytes = uint32_t(sr) * G::kXRowB;
+  const uint32_t dy_stage_bytes = uint32_t(sr) * kDyRowBytes;
+  const uint32_t dy_ring = ring + uint32_t(ring_rows) * G::kXRowB;  // 128-B aligned
+  const uint8_t* dy_ring_ptr = ring_ptr + int64_t(ring_rows) * G::kXRowB;
+  const WsParams p = wgrad_as_ws(g);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Zero this launch's taps (rows R0 .. R0+NR-1) of the CTA's warp slices.
+  float* cta_slice = g.partial + int64_t(blockIdx.x) * kConsumerWarps * (K * K) * g.C;
+  for (int i = threadIdx.x; i < kConsumerWarps * NR * K * g.C; i += blockDim.x) {
+    const int w4 = i / (NR * K * g.C);
+    cta_slice[int64_t(w4) * K * K * g.C + R0 * K * g.C + (i - w4 * NR * K * g.C)] = 0.f;
+  }
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), kConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&xmap);
+    prefetch_tensormap(&dymap);
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane != 0) return;
+    uint32_t stage = 0, phase = 0;
+    uint32_t armed = 0, armed_parity = 0;
+    int64_t load = 0;
+    bool ok = true;
+    SegmentIter it(blockIdx.x, gridDim.x);
+    Segment sg;
+    while (ok && it.next_segment(p, sg)) {
+      const int nst = (sg.rows + NR - 1 + sr - 1) / sr;
+      const int32_t c0 = sg.cb * kBlockC;
+      for (int t = 0; t < nst; ++t) {
+        if (!mbar_wait_bounded(smem_addr(&empty_bar[stage]), phase ^ 1u, &abort_flag, true,
+                               g.timeout_ns)) {
+          if (!abort_flag) {
+            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load);
+            abort_flag = 1;
+          }
+          ok = false;
+          break;
+        }
+        const uint32_t fb = smem_addr(&full_bar[stage]);
+        const int32_t row = sg.p0 + t * sr;
+        mbar_arrive_expect_tx(fb, x_stage_bytes + dy_stage_bytes);
+        // x rows [p0 - pad + R0 + t*sr, ...), 32 + K - 1 columns from q0 - pad
+        tma_load_4d(ring + stage * x_stage_bytes, &xmap, fb, c0, sg.qs * kStripQ - g.pad,
+                    row - g.pad + R0, sg.n);
+        // dy rows [p0 + t*sr, ...), 32 columns from q0 (rows past the segment are not read)
+        tma_load_4d(dy_ring + stage * dy_stage_bytes, &dymap, fb, c0, sg.qs * kStripQ, row, sg.n);
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        ++load;
+        if (++stage == NS) { stage = 0; phase ^= 1u; }
+      }
+    }
+    for (int s = 0; s < NS; ++s) {
+      if (!(armed & (1u << s))) continue;
+      if (!mbar_wait_bounded(smem_addr(&full_bar[s]), (armed_parity >> s) & 1u, &abort_flag,
+                             false, g.timeout_ns))
+        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load);
+    }
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  const int cw = warp - 1;
+  SegmentIter it(blockIdx.x, gridDim.x);
+  Segment sg;
+  float acc[2 * NR * K];
+#pragma unroll
+  for (int k = 0; k < 2 * NR * K; ++k) acc[k] = 0.f;
+  int cur_cb = -1;
+  bool failed = false;
+  uint32_t seq = 0;  // ring stages this warp has consumed
+
+  float* slice = cta_slice + int64_t(cw) * (K * K) * g.C + int64_t(R0) * K * g.C;
+  auto flush = [&](int cb) {
+    const int ch = cb * kBlockC + 2 * lane;
+    if (ch < g.C) {
+#pragma unroll
+      for (int k = 0; k < NR * K; ++k) {
+        float2* d = reinterpret_cast<float2*>(slice + int64_t(k) * g.C + ch);
+        float2 v = *d;
+        v.x += acc[2 * k];
+        v.y += acc[2 * k + 1];
+        *d = v;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2 * NR * K; ++k) acc[k] = 0.f;
+  };
+
+  while (!failed && it.next_segment(p, sg)) {
+    if (sg.cb != cur_cb) {
+      if (cur_cb >= 0) flush(cur_cb);
+      cur_cb = sg.cb;
+    }
+    const int rows_in = sg.rows + NR - 1;
+    const int nst = (rows_in + sr - 1) / sr;
+    const bool active = sg.qs * kStripQ + cw * kColsPerWarp < g.Q;  // warp-uniform
+    int acquired = 0, released = 0;
+    int rr0 = int(seq % NS) * sr;  // ring row of segment row o
+    for (int o = 0; o < sg.rows; ++o) {
+      const int need = min(nst, (o + NR - 1) / sr + 1);
+      for (; acquired < need; ++acquired) {
+        const uint32_t k = seq + uint32_t(acquired);
+        const bool got = mbar_wait_bounded(smem_addr(&full_bar[k % NS]), (k / NS) & 1u,
+                                           &abort_flag, true, g.timeout_ns);
+        if (__any_sync(0xffffffffu, !got)) {
+          if (lane == 0 && !abort_flag) {
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, int(k % NS), -1);
+            abort_flag = 1;
+          }
+          failed = true;
+          break;
+        }
+      }
+      if (failed) break;
+      if (active) {
+        // dy columns past Q were zero-filled by the copy.
+        const uint32_t* dsrc = reinterpret_cast<const uint32_t*>(
+            dy_ring_ptr + rr0 * kDyRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+        uint32_t dyr[kColsPerWarp];
+#pragma unroll
+        for (int m = 0; m < kColsPerWarp; ++m) dyr[m] = dsrc[m * (kBlockC / 2)];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          int rr = rr0 + r;
+          if (rr >= ring_rows) rr -= ring_rows;
+          const uint32_t* xsrc = reinterpret_cast<const uint32_t*>(
+              ring_ptr + rr * G::kXRowB + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+          uint32_t xr[G::kXWarp];
+#pragma unroll
+          for (int j = 0; j < G::kXWarp; ++j) xr[j] = xsrc[j * (kBlockC / 2)];
+#pragma unroll
+          for (int s2 = 0; s2 < K; ++s2)
+#pragma unroll
+            for (int m = 0; m < kColsPerWarp; ++m)
+              fma2_f16f32(xr[m + s2], dyr[m], acc[2 * (r * K + s2)], acc[2 * (r * K + s2) + 1]);
+        }
+      }
+      // Release the stages below the next dy row's first x row.
+      const int rel_to = o == sg.rows - 1 ? nst : min(nst, (o + 1) / sr);
+      if (released < rel_to) {
+        __syncwarp();
+        if (lane == 0)
+          for (int k = released; k < rel_to; ++k)
+            mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(k)) % NS]));
+        released = rel_to;
+      }
+      if (++rr0 == ring_rows) rr0 = 0;
+    }
+    seq += uint32_t(nst);
   }
   if (cur_cb >= 0 && !failed) flush(cur_cb);
 }
