@@ -1,6 +1,6 @@
 """K x K taps and stride 2 (`tma_dwconv.dwconv`) vs cuDNN, on one GPU.
 
-    python tests/bench_kxk.py [--images 64] [--n-stage N]   (default: tma_dwconv.DWCONV_STAGES)
+    python tests/bench_kxk.py [--images 64] [--n-stage N] [--only K,S] [--iters 20] [--no-cudnn]
 
 Input of the headline shape (N x 224 x 336 x 256 fp16), pad K // 2, for K in
 {3, 5, 7} and stride 1 and 2.  CUDA events, 5 warm-up + 20 calls each (x is
@@ -59,20 +59,25 @@ def main() -> None:
     ap.add_argument("--images", type=int, default=64)
     ap.add_argument("--n-stage", type=int, default=None)
     ap.add_argument("--no-cudnn", action="store_true")
+    ap.add_argument("--only", default=None, help="one geometry, e.g. 7,1 (K,stride)")
+    ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     N, H, W, C = args.images, 224, 336, 256
     hbm = hbm_peak_gbps()
     g = torch.Generator(device="cuda").manual_seed(0)
     x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
     xc = x.permute(0, 3, 1, 2)  # channels-last NCHW view
+    only = tuple(int(v) for v in args.only.split(",")) if args.only else None
     for K in (3, 5, 7):
         w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).half()
         wc = w.permute(2, 0, 1).unsqueeze(1).contiguous(memory_format=torch.channels_last)
         for S in (1, 2):
+            if only is not None and (K, S) != only:
+                continue
             pad = K // 2
             P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
             ns = args.n_stage or T.DWCONV_STAGES[(K, S)]
-            us = bench_us(lambda: T.dwconv(x, w, pad, stride=S, n_stage=ns))
+            us = bench_us(lambda: T.dwconv(x, w, pad, stride=S, n_stage=ns), iters=args.iters)
             nbytes = 2 * N * C * (H * W + P * Q)
             flops = 2 * N * P * Q * C * K * K
             t_hbm = nbytes / (hbm * 1e9) * 1e6

@@ -227,17 +227,23 @@ def direct_scheme(K, S):
     return K * K + nacc * 16 + (S * 7 + K) > 100
 
 
-def max_stages_held(rows, K, S, sr):
+def direct_rows(K, S):
+    """Restates direct_rows(K, S): output rows per pass of the direct scheme."""
+    return 1 if S == 2 else (3 if K <= 5 else 2)
+
+
+def max_stages_held(rows, K, S, sr, R=1):
     """Restates the direct scheme's consumer bookkeeping over one segment of
-    `rows` output rows: the most ring stages a warp holds at once."""
+    `rows` output rows, R per pass: the most ring stages a warp holds at once."""
     rows_in = S * (rows - 1) + K
     nst = -(-rows_in // sr)
     acquired = released = 0
     worst = 0
-    for o in range(rows):
-        acquired = max(acquired, min(nst, (S * o + K - 1) // sr + 1))
+    for o in range(0, rows, R):
+        nout = min(R, rows - o)
+        acquired = max(acquired, min(nst, (S * (o + nout - 1) + K - 1) // sr + 1))
         worst = max(worst, acquired - released)
-        released = nst if o == rows - 1 else min(nst, S * (o + 1) // sr)
+        released = nst if o + R >= rows else min(nst, S * (o + R) // sr)
         assert released <= acquired
     assert acquired == released == nst
     return worst
@@ -256,13 +262,13 @@ def test_kxk_plan_covers_every_output_once(lib, K, S, N, H, W, Cc, pad, ns):
     assert pl["smem"] == ns * sr * (S * 31 + K) * 128 + 128 <= 200 * 1024
     assert pl["qstrips"] == -(-Q // 32) and pl["cblocks"] == -(-Cc // 64)
     if direct_scheme(K, S):
-        assert (ns - 1) * sr >= K - 1
+        assert (ns - 1) * sr >= S * (direct_rows(K, S) - 1) + K - 1
     seen = set()
     for g in range(pl["grid"]):
         for strip, a, b in segments(pl, P, g):
             assert 0 <= a < b <= P
             if direct_scheme(K, S):
-                assert max_stages_held(b - a, K, S, sr) <= ns
+                assert max_stages_held(b - a, K, S, sr, direct_rows(K, S)) <= ns
             for r in range(a, b):
                 assert (strip, r) not in seen
                 seen.add((strip, r))

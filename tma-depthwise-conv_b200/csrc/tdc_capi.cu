@@ -402,18 +402,21 @@ int g_geom_occ[kMaxDevices][3][2][2][3] = {};  // 0 = not queried yet
 int strip_in_cols(int K, int S) { return S * (tdc::kStripQ - 1) + K; }
 
 // Ring of about 52 KB (what 12 rows of the 3x3 stride-1 strip take) split
-// over n_stage stages.  The direct scheme holds the K input rows of one
-// output row at once, across at most ceil((K-1)/sr) + 1 stages, so it needs
-// (n_stage - 1) * sr >= K - 1; with 3 or 4 stages one more row per stage
-// leaves the producer room to run ahead (measured on the 7x7 and 5x5
+// over n_stage stages.  A pass of the direct scheme holds its window of
+// input rows (direct_window: S*(R-1) + K for R output rows) at once, across
+// at most ceil((window-1)/sr) + 1 stages, so it needs
+// (n_stage - 1) * sr >= window - 1; with 3 or 4 stages one more row per
+// stage leaves the producer room to run ahead (measured on the 7x7 and 5x5
 // kernels at 64 x 224 x 336 x 256: 3-8 % faster than the minimum).
 int geom_stage_rows(int K, int S, int64_t n_stage) {
   const int ns = int(n_stage);
   const int row_bytes = strip_in_cols(K, S) * tdc::kBlockC * 2;
   const int ring_rows = std::max<int>(ns, (kRingRows * tdc::kRowBytes) / row_bytes);
   int sr = std::max(1, ring_rows / ns);
-  if (tdc::direct_scheme(K, S))
-    sr = std::max(sr, (K - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
+  if (tdc::direct_scheme(K, S)) {
+    const int win = tdc::direct_window(K, S);
+    sr = std::max(sr, (win - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
+  }
   return sr;
 }
 

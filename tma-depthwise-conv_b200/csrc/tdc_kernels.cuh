@@ -211,6 +211,14 @@ constexpr int kModeEpilogue = 2;  // kModeGeneral + bias / activation / residual
 
 __host__ __device__ constexpr int pmod(int a, int b) { return ((a % b) + b) % b; }
 
+// Output rows per pass of the direct scheme, measured at 64 x 224 x 336 x 256
+// (5x5: 1 / 3 / 4 rows = 1.96 / 1.61 / 1.57 ms; 7x7: 1 / 2 / 3 / 4 rows =
+// 3.01 / 2.71 / 2.96 / 3.80 ms).  Stride 2 keeps one: two rows need a 9-row
+// window for 7x7, whose ring then allows only one CTA per SM (1.0 -> 1.5 ms).
+__host__ __device__ constexpr int direct_rows(int K, int S) {
+  return S == 2 ? 1 : (K <= 5 ? 3 : 2);
+}
+
 // Geometry of a K x K, stride-S depthwise kernel over one 32-column strip.
 // Output column q reads input columns S*q - pad + s (s < K); output row p
 // reads input rows S*p - pad + r (r < K).
@@ -231,19 +239,28 @@ struct Geom {
   // one output row at a time from its K input rows (read K / S times each),
   // one accumulator set, taps in registers.
   static constexpr bool kDirect = K * K + kNacc * 2 * kColsPerWarp + kWarpIn > 100;
-  // Direct scheme: the ring's stage height sr must satisfy
-  // (NS - 1) * sr >= K - 1 (checked by the host planner).
+  // Direct scheme: output rows per pass, and the input rows a pass holds.
+  // The ring's stage height sr must satisfy (NS - 1) * sr >= kWindow - 1
+  // (checked by the host planner).
+  static constexpr int kRows = direct_rows(K, S);
+  static constexpr int kWindow = S * (kRows - 1) + K;
   static_assert(kStripIn <= 256, "TMA box dimension");
 };
 static_assert(Geom<3, 1>::kRowB == kRowBytes, "3x3 stride-1 ring row");
 
-// Geom<K, S>::kDirect for run-time K and S (host planner).
+// Geom<K, S>::kDirect and kWindow for run-time K and S (host planner).
 __host__ __device__ constexpr bool direct_scheme(int K, int S) {
   return K * K + ((K + S - 1) / S) * 2 * kColsPerWarp + (S * (kColsPerWarp - 1) + K) > 100;
+}
+__host__ __device__ constexpr int direct_window(int K, int S) {
+  return S * (direct_rows(K, S) - 1) + K;
 }
 static_assert(!direct_scheme(3, 1) && !direct_scheme(3, 2) && !direct_scheme(5, 2) &&
                   direct_scheme(5, 1) && direct_scheme(7, 1) && direct_scheme(7, 2),
               "consumer scheme per geometry");
+static_assert(direct_window(7, 1) == Geom<7, 1>::kWindow && direct_window(7, 2) == Geom<7, 2>::kWindow &&
+                  direct_window(5, 1) == Geom<5, 1>::kWindow,
+              "host and device windows agree");
 
 // Feeds input row u (mod the unroll period) — kWarpIn packed fp16 pairs of
 // this lane — into the accumulator sets of every output row it is a tap row
@@ -482,19 +499,24 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
     };
 
     if constexpr (G::kDirect) {
-      // ---- direct scheme: output row o from input rows S*o .. S*o+K-1 ----
-      // Stage k of the segment holds input rows [k*sr, (k+1)*sr) in ring slot
-      // (seq + k) % NS, so input row i sits at ring row (base + i) mod
-      // (NS * sr) with base = (seq % NS) * sr.  The warp holds the stages from
-      // the first row of o to its last row; the host picks sr with
-      // (NS - 1) * sr >= K - 1 so that window always fits the ring.
+      // ---- direct scheme: R output rows o .. o+R-1 per pass, from input
+      // rows S*o .. S*o + kWindow - 1 (kWindow = S*(R-1) + K) ----
+      // Each input row of the pass is read from shared memory once and fed
+      // to every output of the pass it is a tap row of.  Stage k of the
+      // segment holds input rows [k*sr, (k+1)*sr) in ring slot (seq + k) %
+      // NS, so input row i sits at ring row (base + i) mod (NS * sr) with
+      // base = (seq % NS) * sr.  The warp holds the stages from the first to
+      // the last input row of the pass; the host picks sr with
+      // (NS - 1) * sr >= kWindow - 1 so that window always fits the ring.
+      constexpr int R = G::kRows;
       const int sr = p.stage_rows;
       const int ring_rows = NS * sr;
       const int nst = (rows_in + sr - 1) / sr;
       int acquired = 0, released = 0;
       int rr0 = int(seq % NS) * sr;  // ring row of input row S*o
-      for (int o = 0; o < sg.rows; ++o) {
-        const int need = min(nst, (S * o + K - 1) / sr + 1);
+      for (int o = 0; o < sg.rows; o += R) {
+        const int nout = min(R, sg.rows - o);  // outputs of this pass
+        const int need = min(nst, (S * (o + nout - 1) + K - 1) / sr + 1);
         for (; acquired < need; ++acquired) {
           const uint32_t k = seq + uint32_t(acquired);
           [[maybe_unused]] uint64_t t0 = 0;
@@ -513,12 +535,13 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
         }
         if (failed) break;
         if (n_valid > 0) {
-          uint32_t res[kColsPerWarp];
-          load_res(o, res);
-          RowAcc a;
+          RowAcc a[R];
 #pragma unroll
-          for (int r = 0; r < K; ++r) {
-            int rr = rr0 + r;
+          for (int i = 0; i < G::kWindow; ++i) {
+            // Rows past the segment's input (a short last pass) feed only
+            // outputs that are not stored; skip them (warp-uniform).
+            if (i >= K && i >= S * (nout - 1) + K) break;
+            int rr = rr0 + i;
             if (rr >= ring_rows) rr -= ring_rows;
             const uint32_t* src = reinterpret_cast<const uint32_t*>(
                 ring_ptr + rr * G::kRowB + (S * cw * kColsPerWarp) * (kBlockC * 2)) + lane;
@@ -526,17 +549,28 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
 #pragma unroll
             for (int j = 0; j < G::kWarpIn; ++j) xr[j] = src[j * (kBlockC / 2)];
 #pragma unroll
-            for (int s2 = 0; s2 < K; ++s2)
+            for (int t = 0; t < R; ++t) {
+              const int r = i - S * t;  // tap row of input row i for output o + t
+              if (r < 0 || r >= K) continue;
 #pragma unroll
-              for (int m = 0; m < kColsPerWarp; ++m) {
-                if (r == 0 && s2 == 0) { a.v[2 * m] = 0.f; a.v[2 * m + 1] = 0.f; }
-                fma2_f16f32(xr[S * m + s2], wt[r * K + s2], a.v[2 * m], a.v[2 * m + 1]);
-              }
+              for (int s2 = 0; s2 < K; ++s2)
+#pragma unroll
+                for (int m = 0; m < kColsPerWarp; ++m) {
+                  if (r == 0 && s2 == 0) { a[t].v[2 * m] = 0.f; a[t].v[2 * m + 1] = 0.f; }
+                  fma2_f16f32(xr[S * m + s2], wt[r * K + s2], a[t].v[2 * m], a[t].v[2 * m + 1]);
+                }
+            }
           }
-          store_row(o, a, res);
+#pragma unroll
+          for (int t = 0; t < R; ++t) {
+            if (t >= nout) break;
+            uint32_t res[kColsPerWarp];
+            load_res(o + t, res);
+            store_row(o + t, a[t], res);
+          }
         }
-        // Release the stages below the first row of the next output.
-        const int rel_to = o == sg.rows - 1 ? nst : min(nst, (S * (o + 1)) / sr);
+        // Release the stages below the first input row of the next pass.
+        const int rel_to = o + R >= sg.rows ? nst : min(nst, (S * (o + R)) / sr);
         if (released < rel_to) {
           __syncwarp();
           if (lane == 0)
@@ -544,7 +578,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
               mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(k)) % NS]));
           released = rel_to;
         }
-        rr0 += S;
+        rr0 += S * R;
         if (rr0 >= ring_rows) rr0 -= ring_rows;
       }
       if (failed) break;

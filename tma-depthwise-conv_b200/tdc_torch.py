@@ -111,7 +111,8 @@ def dwconv3x3(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, pad: int = 1) -> torch.
 @torch.library.custom_op("tdc::dwconv_bwd_data", mutates_args=())
 def dwconv_bwd_data_op(dy: torch.Tensor, w: torch.Tensor, pad: int) -> torch.Tensor:
     """dx [N,H,W,C] of the K x K stride-1 forward, from dy [N,P,Q,C] and w [K,K,C]."""
-    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, 1, 2)
+    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, 1,
+                              DWCONV_STAGES[(int(w.shape[0]), 1)])
 
 
 @dwconv_bwd_data_op.register_fake
