@@ -59,7 +59,7 @@ extern "C" {
 #define TDC_ERR_WORKSPACE       -14  /* workspace too small (tdc_dwconv3x3_bwd_weight)       */
 #define TDC_ERR_SCRATCH_LIMIT   -15  /* C beyond the static scratch (..._bwd_weight_noalloc) */
 #define TDC_ERR_STRIDE          -16  /* stride not 1 or 2 (tdc_dwconv_fwd)                  */
-#define TDC_ERR_UNSUPPORTED     -17  /* geometry without that kernel (backward at stride 2)  */
+#define TDC_ERR_UNSUPPORTED     -17  /* no kernel for this request (e.g. an unknown plan kind) */
 
 /* Human-readable text for a status code (static storage, never NULL). */
 TDC_API const char* tdc_strerror(int code);
@@ -187,17 +187,26 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
                                              int64_t N, int64_t H, int64_t W, int64_t C,
                                              int64_t pad, int64_t n_stage, void* stream);
 
-/* Backward of the K x K forward (K = 3, 5, 7) at stride 1; stride 2 returns
- * TDC_ERR_UNSUPPORTED.  No counterpart in the reference (forward only).
- *   tdc_dwconv_bwd_data: dx [N,H,W,C] fp16 from dy [N,P,Q,C] and w [K,K,C],
- *     P = H + 2*pad - K + 1: the forward kernel with flipped taps and
- *     pad' = K - 1 - pad, so the chain per output is (r', s') lexicographic
- *     over w[K-1-r'][K-1-s'] from +0, one fp16 rounding.  For K > 3,
- *     pad <= K - 1.  K = 3 is tdc_dwconv3x3_bwd_data.
+/* Backward of the K x K forward (K = 3, 5, 7) at stride 1 or 2.  No
+ * counterpart in the reference (forward only).
+ *   tdc_dwconv_bwd_data: dx [N,H,W,C] fp16 from dy [N,P,Q,C] and w [K,K,C].
+ *     Stride 1: P = H + 2*pad - K + 1; the forward kernel with flipped taps
+ *     and pad' = K - 1 - pad, so the chain per output is (r', s')
+ *     lexicographic over w[K-1-r'][K-1-s'] from +0, one fp16 rounding.  For
+ *     K > 3, pad <= K - 1.  K = 3 is tdc_dwconv3x3_bwd_data.
+ *     Stride 2: P = (H + 2*pad - K)/2 + 1 (H is needed: two input heights
+ *     give the same P); any pad >= 0.  A transposed-stencil kernel:
+ *       dx[n,h,v,c] = chain over r = K-1 .. 0 with h + pad - r even, then
+ *                     s = K-1 .. 0 with v + pad - s even, of
+ *                     fma(dy[n, (h+pad-r)/2, (v+pad-s)/2, c], w[r,s,c], acc)
+ *     from +0 (dy = 0 outside [0,P) x [0,Q)), one fp16 rounding.
  *   tdc_dwconv_bwd_weight: dw [K,K,C] fp32 (written), deterministic like
  *     tdc_dwconv3x3_bwd_weight, with a caller workspace of at least the size
- *     tdc_dwconv_bwd_weight_workspace reports.  K = 3 is
- *     tdc_dwconv3x3_bwd_weight.
+ *     tdc_dwconv_bwd_weight_workspace reports (same stride argument).  At
+ *     stride 1, K = 3 is tdc_dwconv3x3_bwd_weight.  At stride 2,
+ *       dw[r,s,c] = sum_{n,p,q} x[n, 2p+r-pad, 2q+s-pad, c] * dy[n,p,q,c]
+ *     with P = (H + 2*pad - K)/2 + 1 (x rows and columns that no output
+ *     reads do not contribute).
  *   tdc_dwconv_bwd_weight_plan: the K = 5, 7 weight-gradient launch plan,
  *     pure host arithmetic: plan[0..7] as tdc_ws_plan (the ring holds
  *     stage_rows rows of x and of dy per stage), plan[8] = launches (the
@@ -217,6 +226,20 @@ TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw,
 TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
                                        int64_t pad, int64_t n_stage, int64_t sms,
                                        int64_t ctas_per_sm, int64_t* plan);
+
+/* Launch plan of the stride-2 backward (pure host arithmetic), which = 0 for
+ * the data gradient, 1 for the weight gradient; plan[0..7] as tdc_ws_plan.
+ * Data gradient: strips and bands over dx [N,H,W,C]; stage_rows counts dy
+ * rows of 16 + (K-1)/2 columns; plan[8] = 1 launch; plan[9] = (K+1)/2, the
+ * dy rows one pass of two dx rows holds (the ring keeps
+ * (n_stage - 1) * stage_rows >= plan[9] - 1).  Weight gradient: strips over
+ * dy [N,P,Q,C]; a stage holds stage_rows dy rows and 2*stage_rows x rows of
+ * 62 + K columns; plan[8] = launches, plan[9] = tap rows of the tallest
+ * launch (the ring keeps (n_stage - 1) * 2 * stage_rows >= plan[9] - 1).
+ * No counterpart in the reference. */
+TDC_API int tdc_dwconv_bwd_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                   int64_t pad, int64_t n_stage, int64_t which, int64_t sms,
+                                   int64_t ctas_per_sm, int64_t* plan);
 
 /* Number of rows of the stall tensor that tdc_dwconv_ws_probe writes for
  * this problem (= number of CTAs the launch uses). */

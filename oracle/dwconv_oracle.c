@@ -407,6 +407,76 @@ int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* 
   return err ? -1 : 0;
 }
 
+/*
+ * Data gradient of the K x K stride-2 forward (no counterpart in the
+ * reference, whose forward is 3x3 stride 1).  The forward reads
+ * x[n, 2p+r-pad, 2q+s-pad, c], so
+ *   dx[n,h,v,c] = chain over r = K-1 .. 0 with (h+pad-r) even, then over
+ *                 s = K-1 .. 0 with (v+pad-s) even, of
+ *                 fmaf(dy[n, (h+pad-r)/2, (v+pad-s)/2, c], w[r,s,c], acc)
+ * from +0 with dy = 0 outside [0,P) x [0,Q), P = (H+2*pad-K)/2 + 1; then
+ * f16 RNE.  r and s descending is the order of the stride-1 data gradient
+ * (the forward with flipped taps) restricted to the taps a stride-2 output
+ * reaches.
+ */
+int oracle_dwconv_bwd_data_s2_f16(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
+                                  int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                                  int threads) {
+  if (!dy || !w || !dx || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0 || K < 1) return -1;
+  if (H + 2 * pad < K || W + 2 * pad < K) return -1;
+  const int64_t P = (H + 2 * pad - K) / 2 + 1, Q = (W + 2 * pad - K) / 2 + 1;
+  if (N == 0 || C == 0) return 0;
+  float* wf = (float*)malloc(sizeof(float) * (size_t)(K * K * C));
+  float* lut = (float*)malloc(sizeof(float) * 65536);
+  if (!wf || !lut) { free(wf); free(lut); return -1; }
+  for (uint32_t i = 0; i < 65536u; ++i) lut[i] = oracle_f16_to_f32((uint16_t)i);
+  for (int64_t i = 0; i < K * K * C; ++i) wf[i] = lut[w[i]];
+  int err = 0;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads) reduction(| : err)
+#endif
+  {
+    float* acc = (float*)malloc(sizeof(float) * (size_t)(C + 1));
+    if (!acc) {
+      err = 1;
+    } else {
+#ifdef _OPENMP
+#pragma omp for schedule(static)
+#endif
+      for (int64_t nh = 0; nh < N * H; ++nh) {
+        const int64_t n = nh / H, h = nh % H;
+        for (int64_t v = 0; v < W; ++v) {
+          for (int64_t c = 0; c < C; ++c) acc[c] = 0.0f;
+          for (int64_t r = K - 1; r >= 0; --r) {
+            const int64_t hp = h + pad - r;
+            if (hp % 2 != 0) continue;
+            const int64_t p = hp / 2;
+            for (int64_t s = K - 1; s >= 0; --s) {
+              const int64_t vq = v + pad - s;
+              if (vq % 2 != 0) continue;
+              const int64_t q = vq / 2;
+              const float* wr = wf + (r * K + s) * C;
+              if (p < 0 || p >= P || q < 0 || q >= Q) {
+                for (int64_t c = 0; c < C; ++c) acc[c] = fmaf(0.0f, wr[c], acc[c]);
+              } else {
+                const uint16_t* src = dy + ((n * P + p) * Q + q) * C;
+                for (int64_t c = 0; c < C; ++c) acc[c] = fmaf(lut[src[c]], wr[c], acc[c]);
+              }
+            }
+          }
+          uint16_t* out = dx + ((n * H + h) * W + v) * C;
+          for (int64_t c = 0; c < C; ++c) out[c] = oracle_f32_to_f16(acc[c]);
+        }
+      }
+    }
+    free(acc);
+  }
+  free(lut);
+  free(wf);
+  return err ? -1 : 0;
+}
+
 /* Threads an OpenMP parallel region would use by default (1 without OpenMP). */
 int oracle_max_threads(void) {
 #ifdef _OPENMP

@@ -47,6 +47,9 @@ def load() -> ctypes.CDLL:
         lib.oracle_dwconv_ex_f16.restype = ctypes.c_int
         lib.oracle_dwconv_bwd_data_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 6 + [ctypes.c_int]
         lib.oracle_dwconv_bwd_data_f16.restype = ctypes.c_int
+        lib.oracle_dwconv_bwd_data_s2_f16.argtypes = ([ctypes.c_void_p] * 3 + [i64] * 6 +
+                                                     [ctypes.c_int])
+        lib.oracle_dwconv_bwd_data_s2_f16.restype = ctypes.c_int
         lib.oracle_dwconv3x3_bwd_data_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 5 + [ctypes.c_int]
         lib.oracle_dwconv3x3_bwd_data_f16.restype = ctypes.c_int
         lib.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
@@ -236,20 +239,67 @@ def dwconv_bwd_data_f16(dy: np.ndarray, w: np.ndarray, pad: int, threads: int = 
     return dx
 
 
-def dwconv_bwd_weight_f64(x: np.ndarray, dy: np.ndarray, pad: int, K: int = 3) -> np.ndarray:
-    """Weight gradient of the K x K stride-1 forward in float64 (the accuracy
-    reference for the fp32 kernels):
-    dw[r,s,c] = sum_{n,p,q} x[n,p+r-pad,q+s-pad,c] * dy[n,p,q,c]."""
+def dwconv_bwd_data_s2_f16(dy: np.ndarray, w: np.ndarray, pad: int, H: int, W: int,
+                           threads: int = 0) -> np.ndarray:
+    """C oracle of the data gradient of the stride-2 forward: dx [N,H,W,C] fp16
+    from dy [N,P,Q,C], P = (H + 2*pad - K)//2 + 1, and w [K,K,C]: per output,
+    the fp32 chain over the taps with h + pad - r and v + pad - s even, r then
+    s descending, one fp16 rounding (``oracle_dwconv_bwd_data_s2_f16``)."""
+    lib = load()
+    dy = np.ascontiguousarray(dy, dtype=np.float16)
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    N, P, Q, C = dy.shape
+    K = w.shape[0]
+    if ((H + 2 * pad - K) // 2 + 1, (W + 2 * pad - K) // 2 + 1) != (P, Q):
+        raise ValueError("dy does not match a stride-2 forward of an H x W input")
+    dx = np.empty((N, H, W, C), dtype=np.float16)
+    rc = lib.oracle_dwconv_bwd_data_s2_f16(dy.ctypes.data, w.ctypes.data, dx.ctypes.data,
+                                           N, H, W, C, K, pad, int(threads))
+    if rc != 0:
+        raise RuntimeError("oracle stride-2 data gradient failed")
+    return dx
+
+
+def dwconv_bwd_data_s2_numpy(dy: np.ndarray, w: np.ndarray, pad: int, H: int,
+                             W: int) -> np.ndarray:
+    """Numpy restatement of :func:`dwconv_bwd_data_s2_f16` for small cases: a
+    scatter of every tap's product into the zero-upsampled, padded dx grid,
+    taps visited r then s descending so each output sees its chain in the
+    same order (products of fp16 values are exact in float32)."""
+    dy = np.asarray(dy, np.float16).astype(np.float32)
+    wf = np.asarray(w, np.float16).astype(np.float32)
+    N, P, Q, C = dy.shape
+    K = wf.shape[0]
+    # acc over the padded grid [H + 2*pad (+ slack)]; dx[h] = grid[h + pad]
+    Hg = max(H + 2 * pad, 2 * (P - 1) + K) + 2
+    Wg = max(W + 2 * pad, 2 * (Q - 1) + K) + 2
+    acc = np.zeros((N, Hg, Wg, C), np.float32)
+    for r in range(K - 1, -1, -1):
+        for s in range(K - 1, -1, -1):
+            acc[:, r:r + 2 * P:2, s:s + 2 * Q:2] += dy * wf[r, s]
+    # Grid cells no tap reaches hold +0; every reached cell saw its taps in the
+    # oracle's order, except that out-of-range dy (zero products) are not
+    # added, which leaves finite sums unchanged.
+    return acc[:, pad:pad + H, pad:pad + W].astype(np.float16)
+
+
+def dwconv_bwd_weight_f64(x: np.ndarray, dy: np.ndarray, pad: int, K: int = 3,
+                          stride: int = 1) -> np.ndarray:
+    """Weight gradient of the K x K forward in float64 (the accuracy reference
+    for the fp32 kernels):
+    dw[r,s,c] = sum_{n,p,q} x[n, stride*p+r-pad, stride*q+s-pad, c] * dy[n,p,q,c]."""
     x = np.asarray(x, np.float16).astype(np.float64)
     dy = np.asarray(dy, np.float16).astype(np.float64)
     N, H, W, C = x.shape
     P, Q = dy.shape[1], dy.shape[2]
-    xp = np.zeros((N, H + 2 * pad, W + 2 * pad, C))
+    S = stride
+    xp = np.zeros((N, max(H + 2 * pad, S * (P - 1) + K), max(W + 2 * pad, S * (Q - 1) + K), C))
     xp[:, pad:pad + H, pad:pad + W] = x
     dw = np.empty((K, K, C))
     for r in range(K):
         for s in range(K):
-            dw[r, s] = np.einsum("npqc,npqc->c", xp[:, r:r + P, s:s + Q], dy)
+            dw[r, s] = np.einsum("npqc,npqc->c",
+                                 xp[:, r:r + S * (P - 1) + 1:S, s:s + S * (Q - 1) + 1:S], dy)
     return dw
 
 

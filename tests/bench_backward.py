@@ -1,16 +1,18 @@
-"""Backward of the depthwise K x K (stride 1) vs cuDNN, on one GPU.
+"""Backward of the depthwise K x K (stride 1 or 2) vs cuDNN, on one GPU.
 
-    python tests/bench_backward.py [--images 64] [--K 3] [--n-stage 2]
+    python tests/bench_backward.py [--images 64] [--K 3] [--stride 1] [--n-stage 2]
+                                   [--wgrad-n-stage S]
 
-Headline shape (N x 224 x 336 x 256 fp16, pad K // 2).  CUDA events, 5
+Headline shape (N x 224 x 336 x 256 fp16 input, pad K // 2; dy is
+N x P x Q x 256 with P = (224 + 2*pad - K) // stride + 1).  CUDA events, 5
 warm-up + 20 calls each:
-  dgrad      dwconv_bwd_data   (reads dy, writes dx: 4 B per element)
-  wgrad      dwconv_bwd_weight (reads x and dy: 4 B per element, once per
-             tap-row launch)
+  dgrad      dwconv_bwd_data   (reads dy, writes dx)
+  wgrad      dwconv_bwd_weight (reads x and dy, once per tap-row launch)
   cudnn      aten.convolution_backward on channels-last tensors, grad input
              and grad weight together (what nn.Conv2d's backward runs)
-Prints one JSON line per variant with µs, algorithmic GB/s and the FMA rate
-(2 * N*H*W*C*K*K flop per gradient).  A script, not a test.
+Prints one JSON line per variant with µs, algorithmic GB/s (x + dy bytes,
+dx counted as x) and the FMA rate (2 * N*P*Q*C*K*K flop per gradient).  A
+script, not a test.
 """
 from __future__ import annotations
 
@@ -44,34 +46,39 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--images", type=int, default=64)
     ap.add_argument("--K", type=int, default=3)
+    ap.add_argument("--stride", type=int, default=1, choices=[1, 2])
     ap.add_argument("--n-stage", type=int, default=2)
+    ap.add_argument("--wgrad-n-stage", type=int, default=0, help="default: --n-stage")
     args = ap.parse_args()
-    K, ns = args.K, args.n_stage
+    K, S, ns = args.K, args.stride, args.n_stage
+    wns = args.wgrad_n_stage or ns
     N, H, W, C, pad = args.images, 224, 336, 256, K // 2
+    P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
     g = torch.Generator(device="cuda").manual_seed(0)
     x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
-    dy = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
+    dy = (torch.rand(N, P, Q, C, device="cuda", generator=g) * 2 - 1).half()
     w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).half()
-    io = 2 * N * H * W * C
-    flops = 2 * N * H * W * C * K * K
+    xb, dyb = 2 * N * H * W * C, 2 * N * P * Q * C
+    flops = 2 * N * P * Q * C * K * K
     rows = [
-        ("dgrad", lambda: T._C.dwconv_bwd_data(dy, w, pad, 1, ns), 2 * io),
-        ("wgrad", lambda: T._C.dwconv_bwd_weight(x, dy, K, pad, 1, ns), 2 * io),
+        ("dgrad", lambda: T._C.dwconv_bwd_data(dy, w, pad, S, ns, H, W), xb + dyb),
+        ("wgrad", lambda: T._C.dwconv_bwd_weight(x, dy, K, pad, S, wns), xb + dyb),
     ]
     xc, dyc = x.permute(0, 3, 1, 2), dy.permute(0, 3, 1, 2)  # channels-last NCHW views
     wc = w.permute(2, 0, 1).unsqueeze(1).contiguous()
 
     def cudnn_bwd():
-        return torch.ops.aten.convolution_backward(dyc, xc, wc, None, [1, 1], [pad, pad], [1, 1],
+        return torch.ops.aten.convolution_backward(dyc, xc, wc, None, [S, S], [pad, pad], [1, 1],
                                                    False, [0, 0], C, [True, True, False])
 
-    rows.append(("cudnn dgrad+wgrad", cudnn_bwd, 3 * io))
+    rows.append(("cudnn dgrad+wgrad", cudnn_bwd, 2 * xb + 2 * dyb))
     out = {}
     for name, fn, nbytes in rows:
         us = bench_us(fn)
         out[name] = us
         nf = 2 * flops if name.startswith("cudnn") else flops
-        print(json.dumps({"variant": name, "K": K, "n_stage": ns, "images": N, "us": round(us, 1),
+        print(json.dumps({"variant": name, "K": K, "stride": S,
+                          "n_stage": wns if name == "wgrad" else ns, "images": N, "us": round(us, 1),
                           "algorithmic_GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
                           "fma_TFLOPs": round(nf / (us * 1e-6) / 1e12, 2)}), flush=True)
     print(json.dumps({"ours_dgrad_plus_wgrad_us": round(out["dgrad"] + out["wgrad"], 1),

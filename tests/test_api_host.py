@@ -103,21 +103,21 @@ def test_convert_depthwise_convs_eligibility():
     import tdc_torch
     nn = torch.nn
     model = nn.Sequential(
-        nn.Conv2d(64, 64, 3, padding=1, groups=64),             # trainable: converted
-        nn.Conv2d(64, 64, 7, padding=3, groups=64),             # trainable: converted
-        nn.Conv2d(64, 64, 5, stride=2, padding=2, groups=64),   # forward-only geometry
-        nn.Sequential(nn.Conv2d(64, 64, 3, stride=2, padding=1, groups=64)),
+        nn.Conv2d(64, 64, 3, padding=1, groups=64),             # converted
+        nn.Conv2d(64, 64, 7, padding=3, groups=64),             # converted
+        nn.Conv2d(64, 64, 5, stride=2, padding=2, groups=64),   # converted (stride 2)
+        nn.Sequential(nn.Conv2d(64, 64, 3, stride=2, padding=1, groups=64)),  # nested: converted
         nn.Conv2d(64, 64, 3, padding=1, groups=64, dilation=2),  # dilated: never
         nn.Conv2d(64, 64, 3, padding=1, groups=32),              # not depthwise: never
         nn.Conv2d(12, 12, 3, padding=1, groups=12),              # C % 8 != 0: never
         nn.Conv2d(64, 64, 9, padding=4, groups=64),              # 9x9: never
         nn.Conv2d(64, 64, (3, 5), padding=(1, 2), groups=64),    # non-square: never
     )
-    assert tdc_torch.convert_depthwise_convs(model) == 2  # the stride-1 ones: 3x3 and 7x7
+    assert tdc_torch.convert_depthwise_convs(model) == 4  # every geometry has a backward
     assert isinstance(model[0], tdc_torch.DepthwiseConv3x3)
     assert type(model[1]) is tdc_torch.DepthwiseConv2d and model[1].kernel_size == 7
-    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 2  # + stride 2
     assert model[2].stride == 2 and model[2].padding == 2 and model[3][0].stride == 2
+    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 0  # nothing left
     assert all(isinstance(m, nn.Conv2d) for m in list(model)[4:])
     with pytest.raises(ValueError, match="kernel_size must be 3, 5 or 7"):
         tdc_torch.DepthwiseConv2d(64, 9)

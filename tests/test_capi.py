@@ -299,17 +299,28 @@ def test_kxk_backward_argument_errors(lib):
     for f in (bd, ws, bw):
         assert f(K=4) == CODES["TDC_ERR_FILTER_SHAPE"]
         assert f(S=3) == CODES["TDC_ERR_STRIDE"]
-        assert f(S=2) == CODES["TDC_ERR_UNSUPPORTED"]
-        assert f(C_=12) == CODES["TDC_ERR_CHANNELS"]
-        assert f(ns=5) == CODES["TDC_ERR_N_STAGE"]
-    assert bd(pad=7) == CODES["TDC_ERR_PAD"]  # pad' = K - 1 - pad < 0
-    assert bd(pad=-1) == CODES["TDC_ERR_PAD"]
+        for S in (1, 2):
+            assert f(S=S, C_=12) == CODES["TDC_ERR_CHANNELS"]
+            assert f(S=S, ns=5) == CODES["TDC_ERR_N_STAGE"]
+            assert f(S=S, pad=-1) == CODES["TDC_ERR_PAD"]
+    assert bd(pad=7) == CODES["TDC_ERR_PAD"]  # stride 1: pad' = K - 1 - pad < 0
+    # stride 2: any pad >= 0; the padded input must hold one K x K window
+    assert lib.tdc_dwconv_bwd_data(p(16), p(16), p(16), i64(2), i64(2), i64(2), i64(64), i64(7), i64(2),
+                                   i64(1), i64(2), None) == CODES["TDC_ERR_BAD_SHAPE"]  # 2 + 2 < 7
+    assert lib.tdc_dwconv_bwd_data(None, p(16), p(16), i64(2), i64(16), i64(16), i64(64), i64(7),
+                                   i64(2), i64(3), i64(2), None) == CODES["TDC_ERR_NULL_POINTER"]
+    assert lib.tdc_dwconv_bwd_data(p(8), p(16), p(16), i64(2), i64(16), i64(16), i64(64), i64(7),
+                                   i64(2), i64(3), i64(2), None) == CODES["TDC_ERR_ALIGNMENT"]
+    # empty batch: a successful no-op before any CUDA call
+    assert lib.tdc_dwconv_bwd_data(None, None, None, i64(0), i64(16), i64(16), i64(64), i64(5), i64(2),
+                                   i64(2), i64(2), None) == 0
     assert lib.tdc_dwconv_bwd_weight_workspace(i64(2), i64(16), i64(16), i64(64), i64(7), i64(1), i64(3),
                                                i64(2), None) == CODES["TDC_ERR_NULL_POINTER"]
     if not torch.cuda.is_available():
-        assert bd() == CODES["TDC_ERR_NO_DEVICE"]
-        assert ws() == CODES["TDC_ERR_NO_DEVICE"]
-        assert bw() == CODES["TDC_ERR_NO_DEVICE"]
+        for S in (1, 2):
+            assert bd(S=S) == CODES["TDC_ERR_NO_DEVICE"]
+            assert ws(S=S) == CODES["TDC_ERR_NO_DEVICE"]
+            assert bw(S=S) == CODES["TDC_ERR_NO_DEVICE"]
 
 
 def _wgrad_plan(lib, N, H, W, Cc, K, pad, ns, sms=148, occ=3):
@@ -336,6 +347,113 @@ def test_kxk_wgrad_plan_covers_every_dy_row_once(lib, K, N, H, W, Cc, pad, ns):
     for g in range(pl["grid"]):
         for strip, a, b in segments(pl, P, g):
             assert max_stages_held(b - a, nr, 1, sr) <= ns
+            for r in range(a, b):
+                assert (strip, r) not in seen
+                seen.add((strip, r))
+    assert len(seen) == pl["strips"] * P
+
+
+def _s2_plan(lib, which, N, H, W, Cc, K, pad, ns, sms=148, occ=3):
+    out = (i64 * 10)()
+    assert lib.tdc_dwconv_bwd_s2_plan(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(pad), i64(ns),
+                                      i64(which), i64(sms), i64(occ), out) == 0
+    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
+                     "smem", "passes", "rows"], list(out)))
+
+
+def dgrad_s2_segment(h0, rows, pad, K, sr, ns):
+    """Restates the stride-2 data gradient's consumer over one segment of dx
+    rows [h0, h0 + rows): passes of two dx rows (h, h+1) with h + pad even,
+    each reading dy rows k .. k + (K-1)/2 of the segment's window.  Returns the
+    dx rows stored, the dy rows each stored row reads (by the kernel's tap
+    formula) and the most ring stages held at once."""
+    half = (K - 1) // 2
+    e0 = h0 + pad
+    e_first = e0 & ~1
+    passes = (rows + (e0 & 1) + 1) // 2
+    dy_row0 = (e_first >> 1) - half
+    dy_rows = passes + half
+    nst = -(-dy_rows // sr)
+    acquired = released = worst = 0
+    stored, reads = [], {}
+    for k in range(passes):
+        acquired = max(acquired, min(nst, (k + half) // sr + 1))
+        worst = max(worst, acquired - released)
+        h_even = e_first + 2 * k - pad
+        for h, taps in ((h_even, [K - 1 - 2 * t for t in range(half + 1)]),
+                        (h_even + 1, [K - 2 * t for t in range(1, half + 1)])):
+            if h0 <= h < h0 + rows:
+                stored.append(h)
+                # window row t holds dy row dy_row0 + k + t; it must be the row tap r reads
+                rows_read = [dy_row0 + k + (K - 1 - r) // 2 if (K - 1 - r) % 2 == 0
+                             else dy_row0 + k + (K - r) // 2 for r in taps]
+                reads[h] = (taps, rows_read)
+                assert all(0 <= dy_row0 + k + t - dy_row0 < dy_rows for t in range(half + 1))
+        released = nst if k == passes - 1 else min(nst, (k + 1) // sr)
+        assert released <= acquired
+    assert acquired == released == nst
+    return stored, reads, worst
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("N,H,W,Cc,pad", [(64, 224, 336, 256, None), (2, 19, 45, 72, 0), (3, 7, 9, 8, None),
+                                          (1, 301, 40, 64, 4), (4, 33, 47, 136, 1), (2, 8, 8, 64, 7)])
+@pytest.mark.parametrize("ns", [2, 3, 4])
+def test_dgrad_s2_plan_covers_every_dx_row_once(lib, K, N, H, W, Cc, pad, ns):
+    pad = K // 2 if pad is None else pad
+    pl = _s2_plan(lib, 0, N, H, W, Cc, K, pad, ns)
+    sr, half = pl["stage_rows"], (K - 1) // 2
+    assert pl["passes"] == 1 and pl["rows"] == half + 1
+    assert (ns - 1) * sr >= half and 1 <= sr <= 256
+    assert pl["smem"] == ns * sr * (16 + half) * 128 + 128 <= 200 * 1024
+    assert pl["qstrips"] == -(-W // 32) and pl["cblocks"] == -(-Cc // 64)
+    # dy columns: dx column v of strip qs reads (v + pad - s)/2, which must lie
+    # in the box [16*qs + ceil(pad/2) - half, + 16 + half) for every tap it uses
+    for qs in range(2):
+        q0 = 16 * qs + (pad + 1) // 2 - half
+        for v in range(32 * qs, 32 * qs + 32):
+            for s_ in range(K):
+                if (v + pad - s_) % 2 == 0:
+                    j = (v + pad - s_) // 2 - q0
+                    m, cw = (v - 32 * qs) % 8, (v - 32 * qs) // 8
+                    assert 0 <= j < 16 + half
+                    # the kernel's register index for (m, s)
+                    assert j == 4 * cw + (m + (pad & 1) - s_) // 2 - (pad & 1) + half
+    seen = set()
+    for g in range(pl["grid"]):
+        for strip, a, b in segments(pl, H, g):
+            stored, reads, worst = dgrad_s2_segment(a, b - a, pad, K, sr, ns)
+            assert worst <= ns
+            assert sorted(stored) == list(range(a, b))
+            for h, (taps, rows_read) in reads.items():
+                # the kernel's rows are the transposed stencil's: p = (h + pad - r) / 2
+                assert rows_read == [(h + pad - r) // 2 for r in taps]
+                assert all((h + pad - r) % 2 == 0 for r in taps)
+                assert sorted(taps, reverse=True) == taps
+                assert set(taps) == {r for r in range(K) if (h + pad - r) % 2 == 0}
+            for r in stored:
+                assert (strip, r) not in seen
+                seen.add((strip, r))
+    assert len(seen) == pl["strips"] * H
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("N,H,W,Cc,pad", [(64, 224, 336, 256, None), (2, 19, 45, 72, 0), (3, 7, 9, 8, None),
+                                          (1, 300, 40, 64, 4)])
+@pytest.mark.parametrize("ns", [2, 3, 4])
+def test_wgrad_s2_plan_covers_every_dy_row_once(lib, K, N, H, W, Cc, pad, ns):
+    pad = K // 2 if pad is None else pad
+    pl = _s2_plan(lib, 1, N, H, W, Cc, K, pad, ns)
+    P = (H + 2 * pad - K) // 2 + 1
+    sr, nr = pl["stage_rows"], pl["rows"]
+    assert pl["passes"] == (2 if K == 7 else 1) and nr == (4 if K == 7 else K)
+    assert (ns - 1) * 2 * sr >= nr - 1
+    assert pl["smem"] == ns * sr * (2 * (62 + K) * 128 + 4096) + 128 <= 200 * 1024
+    seen = set()
+    for g in range(pl["grid"]):
+        for strip, a, b in segments(pl, P, g):
+            # x rows: a stage holds 2*sr of them; dy row o needs x rows 2o .. 2o + nr - 1
+            assert max_stages_held(b - a, nr, 2, 2 * sr) <= ns
             for r in range(a, b):
                 assert (strip, r) not in seen
                 seen.add((strip, r))

@@ -153,12 +153,15 @@ def test_custom_op_backward_3x3_with_bias():
     torch.testing.assert_close(bd.grad.float(), dy.float().sum((0, 1, 2)), rtol=1e-3, atol=1e-2)
 
 
-def test_custom_op_backward_is_stride_1_only():
-    x, w, _ = _inputs(1, 12, 12, 64, 5, seed=15)
-    xd = x.cuda().requires_grad_()
-    y = torch.ops.tdc.dwconv(xd, w.cuda(), None, 2, 2)
-    with pytest.raises(NotImplementedError, match="stride 1 only"):
-        y.float().sum().backward()
+def test_custom_op_backward_at_stride_2_uses_the_stride_2_kernels():
+    x, w, _ = _inputs(1, 13, 12, 64, 5, seed=15)
+    xd, wd = x.cuda().requires_grad_(), w.cuda().requires_grad_()
+    y = torch.ops.tdc.dwconv(xd, wd, None, 2, 2)
+    dy = torch.randn(y.shape, generator=torch.Generator().manual_seed(16)).half().cuda()
+    y.backward(dy)
+    assert xd.grad.shape == xd.shape and wd.grad.shape == wd.shape
+    assert torch.equal(xd.grad, T._C.dwconv_bwd_data(dy, wd.detach(), 2, 2, 2, 13, 12))
+    assert torch.equal(wd.grad, T._C.dwconv_bwd_weight(xd.detach(), dy, 5, 2, 2, 2).half())
 
 
 def test_module_conversion_forward_only():

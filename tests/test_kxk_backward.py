@@ -104,10 +104,12 @@ def test_3x3_routes_to_the_3x3_kernels():
 
 def test_argument_errors():
     x, w, dy = _tensors(1, 12, 12, 64, 7, 3)
-    with pytest.raises(RuntimeError, match="stride 1 only"):
-        T._C.dwconv_bwd_data(dy.cuda(), w.cuda(), 3, 2)
-    with pytest.raises(RuntimeError, match="stride 1 only"):
-        T._C.dwconv_bwd_weight(x.cuda(), dy.cuda(), 7, 3, 2)
+    with pytest.raises(RuntimeError, match="stride must be 1 or 2"):
+        T._C.dwconv_bwd_data(dy.cuda(), w.cuda(), 3, 3)
+    with pytest.raises(RuntimeError, match="stride must be 1 or 2"):
+        T._C.dwconv_bwd_weight(x.cuda(), dy.cuda(), 7, 3, 3)
+    with pytest.raises(RuntimeError, match="is not the stride-2 output"):
+        T._C.dwconv_bwd_data(dy.cuda(), w.cuda(), 3, 2, 2, 12, 12)  # a stride-1 dy
     with pytest.raises(RuntimeError, match="needs pad <= 6"):
         T._C.dwconv_bwd_data(dy.cuda(), w.cuda(), 7)
     with pytest.raises(RuntimeError, match="dy must be"):

@@ -153,3 +153,50 @@ def test_kxk_epilogue_matches_3x3_epilogue():
         a = oracle.dwconv_k_f16(x, w, 1, 1, b, r, act)
         e = oracle.dwconv_ex_f16(x, w, 1, b, r, act)
         assert np.array_equal(a.view(np.uint16), e.view(np.uint16)), act
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("pad", [0, 1, 2, 3, 8])
+@pytest.mark.parametrize("H,W", [(9, 13), (10, 12), (7, 7), (17, 6)])
+def test_stride_2_data_gradient_restatements_agree(K, pad, H, W):
+    """C and numpy restatements of the stride-2 data gradient agree bit for
+    bit, and both are within fp16 rounding of float64 autograd."""
+    if H + 2 * pad < K or W + 2 * pad < K:
+        pytest.skip("input smaller than one padded window")
+    rng = np.random.default_rng(K * 100 + pad * 10 + H)
+    P, Q = (H + 2 * pad - K) // 2 + 1, (W + 2 * pad - K) // 2 + 1
+    dy = rng.standard_normal((2, P, Q, 16)).astype(np.float16)
+    w = (rng.standard_normal((K, K, 16)) / K).astype(np.float16)
+    a = oracle.dwconv_bwd_data_s2_f16(dy, w, pad, H, W)
+    b = oracle.dwconv_bwd_data_s2_numpy(dy, w, pad, H, W)
+    assert np.array_equal(a.view(np.uint16), b.view(np.uint16))
+    x = torch.zeros(2, 16, H, W, dtype=torch.float64, requires_grad=True)
+    wt = torch.from_numpy(w.astype(np.float64)).permute(2, 0, 1).unsqueeze(1)
+    y = torch.nn.functional.conv2d(x, wt, stride=2, padding=pad, groups=16)
+    assert tuple(y.shape[2:]) == (P, Q)
+    y.backward(torch.from_numpy(dy.astype(np.float64)).permute(0, 3, 1, 2))
+    ref = x.grad.permute(0, 2, 3, 1).numpy()
+    assert (np.abs(a.astype(np.float64) - ref) <= oracle.f16_ulp(ref) + 1e-3).all()
+
+
+def test_stride_2_data_gradient_rejects_a_mismatched_input_size():
+    dy = np.zeros((1, 5, 5, 8), np.float16)
+    w = np.zeros((3, 3, 8), np.float16)
+    oracle.dwconv_bwd_data_s2_f16(dy, w, 1, 10, 9)  # 9 and 10 both give 5
+    with pytest.raises(ValueError):
+        oracle.dwconv_bwd_data_s2_f16(dy, w, 1, 12, 10)
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("stride", [1, 2])
+def test_weight_gradient_f64_matches_autograd(K, stride):
+    rng = np.random.default_rng(K + stride)
+    pad = K // 2
+    x = rng.standard_normal((2, 11, 14, 8)).astype(np.float16)
+    xt = torch.from_numpy(x.astype(np.float64)).permute(0, 3, 1, 2)
+    wt = torch.zeros(8, 1, K, K, dtype=torch.float64, requires_grad=True)
+    y = torch.nn.functional.conv2d(xt, wt, stride=stride, padding=pad, groups=8)
+    dy = rng.standard_normal(tuple(y.permute(0, 2, 3, 1).shape)).astype(np.float16)
+    y.backward(torch.from_numpy(dy.astype(np.float64)).permute(0, 3, 1, 2))
+    dw = oracle.dwconv_bwd_weight_f64(x, dy, pad, K, stride=stride)
+    np.testing.assert_allclose(dw, wt.grad[:, 0].permute(1, 2, 0).numpy(), atol=1e-9)

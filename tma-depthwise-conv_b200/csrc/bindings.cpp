@@ -260,18 +260,35 @@ torch::Tensor dwconv3x3_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t pa
   return dw;
 }
 
-// Backward of the K x K stride-1 forward (K = 3, 5, 7).
+// Backward of the K x K forward (K = 3, 5, 7) at stride 1 or 2.  At stride 2
+// the input height / width are not determined by dy (two sizes give the same
+// output); input_h / input_w < 0 pick the smaller one.
 torch::Tensor dwconv_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, int64_t stride,
-                              int64_t n_stage) {
+                              int64_t n_stage, int64_t input_h, int64_t input_w) {
   check_common(dy, w);
   const int64_t K = w.size(0);
   TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7) && w.size(2) == dy.size(3),
               "w must be [K,K,C] with K in {3, 5, 7}");
-  TORCH_CHECK(stride == 1, "the backward is implemented for stride 1 only, got stride ", stride);
+  TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
   TORCH_CHECK(dy.size(3) % 8 == 0, "C must be a multiple of 8");
   TORCH_CHECK(pad >= 0, "pad must be non-negative");
-  TORCH_CHECK(K == 3 || pad <= K - 1, "the ", K, "x", K, " data gradient needs pad <= ", K - 1);
-  const int64_t H = dy.size(1) - 2 * pad + K - 1, W = dy.size(2) - 2 * pad + K - 1;
+  int64_t H, W;
+  if (stride == 1) {
+    TORCH_CHECK(K == 3 || pad <= K - 1, "the ", K, "x", K, " data gradient needs pad <= ", K - 1);
+    H = dy.size(1) - 2 * pad + K - 1;
+    W = dy.size(2) - 2 * pad + K - 1;
+    TORCH_CHECK(input_h < 0 || input_h == H, "input_h ", input_h, " does not match dy");
+    TORCH_CHECK(input_w < 0 || input_w == W, "input_w ", input_w, " does not match dy");
+  } else {
+    TORCH_CHECK(dy.size(1) >= 1 && dy.size(2) >= 1, "dy must have at least one row and column");
+    H = input_h >= 0 ? input_h : 2 * (dy.size(1) - 1) + K - 2 * pad;
+    W = input_w >= 0 ? input_w : 2 * (dy.size(2) - 1) + K - 2 * pad;
+    TORCH_CHECK(H + 2 * pad >= K && W + 2 * pad >= K &&
+                    (H + 2 * pad - K) / 2 + 1 == dy.size(1) &&
+                    (W + 2 * pad - K) / 2 + 1 == dy.size(2),
+                "dy [", dy.size(1), ", ", dy.size(2), "] is not the stride-2 output of a ", H,
+                "x", W, " input with pad ", pad);
+  }
   TORCH_CHECK(H >= 1 && W >= 1, "dy is smaller than a ", K, "x", K, " kernel with pad ", pad,
               " can produce");
   const c10::cuda::CUDAGuard guard(dy.device());
@@ -291,13 +308,15 @@ torch::Tensor dwconv_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t K, in
   TORCH_CHECK(x.dim() == 4 && dy.dim() == 4 && x.is_contiguous() && dy.is_contiguous(),
               "x and dy must be contiguous [N,H,W,C] / [N,P,Q,C]");
   TORCH_CHECK(K == 3 || K == 5 || K == 7, "K must be 3, 5 or 7, got ", K);
-  TORCH_CHECK(stride == 1, "the backward is implemented for stride 1 only, got stride ", stride);
+  TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
   TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
   TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(x.size(1) + 2 * pad >= K && x.size(2) + 2 * pad >= K,
+              "x is smaller than a ", K, "x", K, " kernel with pad ", pad, " needs");
   TORCH_CHECK(dy.size(0) == x.size(0) && dy.size(3) == x.size(3) &&
-                  dy.size(1) == x.size(1) + 2 * pad - K + 1 &&
-                  dy.size(2) == x.size(2) + 2 * pad - K + 1,
-              "dy must be [N, H+2*pad-K+1, W+2*pad-K+1, C]");
+                  dy.size(1) == (x.size(1) + 2 * pad - K) / stride + 1 &&
+                  dy.size(2) == (x.size(2) + 2 * pad - K) / stride + 1,
+              "dy must be [N, (H+2*pad-K)/stride+1, (W+2*pad-K)/stride+1, C]");
   const c10::cuda::CUDAGuard guard(x.device());
   auto dw = torch::zeros({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
   if (x.numel() == 0 || dy.numel() == 0) return dw;
@@ -364,11 +383,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Weight gradient of the 3x3 forward: dw [3,3,C] fp32 (deterministic).", pybind11::arg("x"),
         pybind11::arg("dy"), pybind11::arg("pad"), pybind11::arg("n_stage") = 2);
   m.def("dwconv_bwd_data", &tma_dwconv::dwconv_bwd_data,
-        "Data gradient of the K x K stride-1 forward: dx [N,H,W,C] from dy [N,P,Q,C].",
+        "Data gradient of the K x K forward (stride 1 or 2): dx [N,H,W,C] from dy [N,P,Q,C]; "
+        "input_h / input_w give H, W at stride 2 (default: the smaller size that fits dy).",
         pybind11::arg("dy"), pybind11::arg("w"), pybind11::arg("pad"), pybind11::arg("stride") = 1,
-        pybind11::arg("n_stage") = 2);
+        pybind11::arg("n_stage") = 2, pybind11::arg("input_h") = -1, pybind11::arg("input_w") = -1);
   m.def("dwconv_bwd_weight", &tma_dwconv::dwconv_bwd_weight,
-        "Weight gradient of the K x K stride-1 forward: dw [K,K,C] fp32 (deterministic).",
+        "Weight gradient of the K x K forward (stride 1 or 2): dw [K,K,C] fp32 (deterministic).",
         pybind11::arg("x"), pybind11::arg("dy"), pybind11::arg("K"), pybind11::arg("pad"),
         pybind11::arg("stride") = 1, pybind11::arg("n_stage") = 2);
   m.def("device_status", &tma_dwconv::device_status,

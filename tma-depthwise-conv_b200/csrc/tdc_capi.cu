@@ -28,6 +28,7 @@
 #include "tdc_dwconv.h"
 #include "tdc_kernels.cuh"
 #include "tdc_wgrad.cuh"
+#include "tdc_dgrad_s2.cuh"
 
 namespace {
 
@@ -505,6 +506,12 @@ using WgradLaunchFn = cudaError_t (*)(const CUtensorMap&, const CUtensorMap&,
 template <int K>
 struct WgradPasses;
 template <>
+struct WgradPasses<3> {  // stride 2 only (the stride-1 3x3 has its own kernel)
+  static constexpr int kCount = 1;
+  static constexpr int kR0[2] = {0, 0};
+  static constexpr int kNR[2] = {3, 0};
+};
+template <>
 struct WgradPasses<5> {
   static constexpr int kCount = 1;
   static constexpr int kR0[2] = {0, 0};
@@ -627,6 +634,261 @@ int64_t wgrad_kxk_workspace_bytes(const WsPlan& pl, int64_t C, int64_t K) {
   return pl.grid * tdc::kConsumerWarps * K * K * C * int64_t(sizeof(float));
 }
 
+// ---------------------------------------------------------------------------
+// Backward of the K x K stride-2 forward.
+//   data gradient: dwconv_dgrad_s2_kernel<NS, K, pad & 1> over dx's strips;
+//   weight gradient: dwconv_wgrad_kxk_kernel<NS, K, R0, NR, 2> over dy's
+//   strips (tap rows split as at stride 1) + the fixed-order reduction.
+// ---------------------------------------------------------------------------
+using DgradS2LaunchFn = cudaError_t (*)(const CUtensorMap&, const tdc::DgradS2Params&, int64_t,
+                                        size_t, cudaStream_t);
+
+template <int NS, int K, int PODD>
+cudaError_t dgrad_s2_launch_t(const CUtensorMap& map, const tdc::DgradS2Params& g, int64_t grid,
+                              size_t smem, cudaStream_t st) {
+  tdc::dwconv_dgrad_s2_kernel<NS, K, PODD>
+      <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(map, g);
+  return cudaGetLastError();
+}
+
+template <int NS, int K, int PODD>
+cudaError_t dgrad_s2_occ_t(int* occ, size_t smem) {
+  auto* k = &tdc::dwconv_dgrad_s2_kernel<NS, K, PODD>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+}
+
+#define TDC_DGS2_NS(FN, K, PODD) {FN<2, K, PODD>, FN<3, K, PODD>, FN<4, K, PODD>}
+#define TDC_DGS2_TABLE(FN)                                          \
+  {{TDC_DGS2_NS(FN, 3, 0), TDC_DGS2_NS(FN, 3, 1)},                  \
+   {TDC_DGS2_NS(FN, 5, 0), TDC_DGS2_NS(FN, 5, 1)},                  \
+   {TDC_DGS2_NS(FN, 7, 0), TDC_DGS2_NS(FN, 7, 1)}}
+// [K index: 3, 5, 7][pad & 1][n_stage - 2]
+const DgradS2LaunchFn kDgradS2Launch[3][2][3] = TDC_DGS2_TABLE(dgrad_s2_launch_t);
+const GeomOccFn kDgradS2Occ[3][2][3] = TDC_DGS2_TABLE(dgrad_s2_occ_t);
+#undef TDC_DGS2_TABLE
+#undef TDC_DGS2_NS
+int g_dgrad_s2_occ[kMaxDevices][3][2][3] = {};  // guarded by g_geom_mutex
+
+// dy columns of one 32-column dx strip (the TMA box width) and ring row bytes.
+constexpr int dgrad_s2_dy_cols(int K) { return tdc::kStripQ / 2 + (K - 1) / 2; }
+static_assert(dgrad_s2_dy_cols(3) == tdc::DgradS2Geom<3>::kDyCols &&
+                  dgrad_s2_dy_cols(5) == tdc::DgradS2Geom<5>::kDyCols &&
+                  dgrad_s2_dy_cols(7) == tdc::DgradS2Geom<7>::kDyCols,
+              "host and device box widths agree");
+int dgrad_s2_row_bytes(int K) { return dgrad_s2_dy_cols(K) * tdc::kBlockC * 2; }
+
+// 16 dy rows split over the stages; a pass holds kHalf + 1 consecutive rows,
+// which needs (n_stage - 1) * sr >= kHalf.
+int dgrad_s2_stage_rows(int K, int64_t n_stage) {
+  const int ns = int(n_stage);
+  const int sr = std::max(1, tdc::kDgradS2RingRows / ns);
+  return std::max(sr, ((K - 1) / 2 + ns - 2) / (ns - 1));
+}
+
+WsPlan make_dgrad_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int K, int64_t n_stage,
+                          int64_t sms, int64_t ctas_per_sm) {
+  WsPlan pl = make_plan(N, H, W, C, n_stage, sms, ctas_per_sm);
+  pl.stage_rows = dgrad_s2_stage_rows(K, n_stage);
+  pl.smem = size_t(n_stage) * pl.stage_rows * dgrad_s2_row_bytes(K) + 128;
+  return pl;
+}
+
+// Validation shared by the stride-2 backward calls: dy [N,P,Q,C] with
+// P = (H + 2*pad - K) / 2 + 1 >= 1, Q likewise.
+int bwd_s2_shape(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                 int64_t n_stage, int64_t* P, int64_t* Q) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
+  *P = (H + 2 * pad - K) / 2 + 1;
+  *Q = (W + 2 * pad - K) / 2 + 1;
+  return check_ws_limits(N, H, W, C, *P, *Q);
+}
+
+int dgrad_s2(const void* dy, const void* w, void* dx, int64_t N, int64_t H, int64_t W, int64_t C,
+             int64_t K, int64_t pad, int64_t n_stage, void* stream) {
+  int64_t P, Q;
+  int rc = bwd_s2_shape(N, H, W, C, K, pad, n_stage, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (N == 0 || C == 0) return TDC_OK;
+  if (!dy || !w || !dx) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(dy) || !aligned16(w) || !aligned16(dx)) return TDC_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  int devi = -1;
+  rc = current_device(&dev, &devi);
+  if (rc != TDC_OK) return rc;
+  const int ki = int(K / 2 - 1), pi = int(pad & 1), ni = int(n_stage - 2);
+  const size_t smem = make_dgrad_s2_plan(1, 1, 1, 8, int(K), n_stage, 1, 1).smem;
+  int occ;
+  {
+    std::lock_guard<std::mutex> lock(g_geom_mutex);
+    occ = g_dgrad_s2_occ[devi][ki][pi][ni];
+    if (occ == 0) {
+      const cudaError_t e = kDgradS2Occ[ki][pi][ni](&occ, smem);
+      if (e != cudaSuccess) return cuda_fail(e);
+      occ = std::max(1, occ);
+      g_dgrad_s2_occ[devi][ki][pi][ni] = occ;
+    }
+  }
+  const WsPlan pl = make_dgrad_s2_plan(N, H, W, C, int(K), n_stage, dev->sms, occ);
+  alignas(64) CUtensorMap map;
+  rc = encode_nhwc_map(&map, dy, N, P, Q, C, dgrad_s2_dy_cols(int(K)), pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  tdc::DgradS2Params g{};
+  g.w = static_cast<const __half*>(w);
+  g.dx = static_cast<__half*>(dx);
+  g.H = int32_t(H); g.W = int32_t(W); g.C = int32_t(C);
+  g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
+  g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
+  g.tail_bands = pl.tail_bands; g.tail_band_rows = pl.tail_band_rows;
+  g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
+  g.timeout_ns = uint64_t(g_timeout_ns.load());
+  const cudaError_t e =
+      kDgradS2Launch[ki][pi][ni](map, g, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+template <int NS, int K, int PASS>
+cudaError_t wgrad_s2_launch_t(const CUtensorMap& xmap, const CUtensorMap& dymap,
+                              const tdc::WgradParams& g, int64_t grid, size_t smem,
+                              cudaStream_t st) {
+  using WP = WgradPasses<K>;
+  if constexpr (PASS < WP::kCount) {
+    tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 2>
+        <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(xmap, dymap, g);
+    return cudaGetLastError();
+  } else {
+    return cudaSuccess;
+  }
+}
+
+template <int NS, int K, int PASS>
+cudaError_t wgrad_s2_occ_t(int* occ, size_t smem) {
+  using WP = WgradPasses<K>;
+  if constexpr (PASS < WP::kCount) {
+    auto* k = &tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 2>;
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+  } else {
+    *occ = 1 << 20;  // no such pass: does not limit the grid
+    return cudaSuccess;
+  }
+}
+
+#define TDC_WGS2_NS(FN, K, PASS) {FN<2, K, PASS>, FN<3, K, PASS>, FN<4, K, PASS>}
+#define TDC_WGS2_TABLE(FN)                                          \
+  {{TDC_WGS2_NS(FN, 3, 0), TDC_WGS2_NS(FN, 3, 1)},                  \
+   {TDC_WGS2_NS(FN, 5, 0), TDC_WGS2_NS(FN, 5, 1)},                  \
+   {TDC_WGS2_NS(FN, 7, 0), TDC_WGS2_NS(FN, 7, 1)}}
+// [K index: 3, 5, 7][pass][n_stage - 2]
+const WgradLaunchFn kWgradS2Launch[3][2][3] = TDC_WGS2_TABLE(wgrad_s2_launch_t);
+const GeomOccFn kWgradS2Occ[3][2][3] = TDC_WGS2_TABLE(wgrad_s2_occ_t);
+#undef TDC_WGS2_TABLE
+#undef TDC_WGS2_NS
+int g_wgrad_s2_occ[kMaxDevices][3][3] = {};  // min over passes; guarded by g_geom_mutex
+
+int wgrad_s2_passes(int K) {
+  return K == 3 ? WgradPasses<3>::kCount : wgrad_kxk_passes(K);
+}
+int wgrad_s2_max_rows(int K) { return K == 3 ? WgradPasses<3>::kNR[0] : wgrad_kxk_max_rows(K); }
+
+// One stage row = 2 x rows of S*31 + K = 62 + K columns and 1 dy row.
+int wgrad_s2_row_bytes(int K) { return 2 * (62 + K) * tdc::kBlockC * 2 + tdc::kDyRowBytes; }
+
+// Ring of about 72 KB; the tallest pass's x window (its tap rows) must fit:
+// (n_stage - 1) * 2 * sr >= rows - 1.
+int wgrad_s2_stage_rows(int K, int64_t n_stage) {
+  const int ns = int(n_stage);
+  const int nr = wgrad_s2_max_rows(K);
+  const int ring_rows = std::max(ns, (72 * 1024) / wgrad_s2_row_bytes(K));
+  const int sr = std::max(1, ring_rows / ns);
+  return std::max(sr, (nr - 1 + 2 * (ns - 1) - 1) / (2 * (ns - 1)));
+}
+
+WsPlan make_wgrad_s2_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int64_t n_stage,
+                          int64_t sms, int64_t ctas_per_sm) {
+  WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  pl.stage_rows = wgrad_s2_stage_rows(K, n_stage);
+  pl.smem = size_t(n_stage) * pl.stage_rows * wgrad_s2_row_bytes(K) + 128;
+  return pl;
+}
+
+// Validates a stride-2 weight-gradient call and plans its launch on the
+// current device.
+int wgrad_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                  int64_t n_stage, WsPlan* pl, int64_t* P, int64_t* Q) {
+  int rc = bwd_s2_shape(N, H, W, C, K, pad, n_stage, P, Q);
+  if (rc != TDC_OK) return rc;
+  if (N < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  DeviceInfo* dev = nullptr;
+  int devi = -1;
+  rc = current_device(&dev, &devi);
+  if (rc != TDC_OK) return rc;
+  const int ki = int(K / 2 - 1), ni = int(n_stage - 2);
+  const size_t smem = make_wgrad_s2_plan(1, 1, 1, 8, int(K), n_stage, 1, 1).smem;
+  int occ;
+  {
+    std::lock_guard<std::mutex> lock(g_geom_mutex);
+    occ = g_wgrad_s2_occ[devi][ki][ni];
+    if (occ == 0) {
+      occ = 1 << 20;
+      for (int pass = 0; pass < 2; ++pass) {
+        int o = 0;
+        const cudaError_t e = kWgradS2Occ[ki][pass][ni](&o, smem);
+        if (e != cudaSuccess) return cuda_fail(e);
+        occ = std::min(occ, std::max(1, o));
+      }
+      g_wgrad_s2_occ[devi][ki][ni] = occ;
+    }
+  }
+  *pl = make_wgrad_s2_plan(N, *P, *Q, C, int(K), n_stage, dev->sms, occ);
+  return TDC_OK;
+}
+
+int wgrad_s2(const void* x, const void* dy, float* dw, int64_t N, int64_t H, int64_t W, int64_t C,
+             int64_t K, int64_t pad, int64_t n_stage, void* workspace, int64_t workspace_bytes,
+             void* stream) {
+  if (!x || !dy || !dw || !workspace) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dw) || !aligned16(workspace))
+    return TDC_ERR_ALIGNMENT;
+  WsPlan pl;
+  int64_t P, Q;
+  int rc = wgrad_s2_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (workspace_bytes < wgrad_kxk_workspace_bytes(pl, C, K)) return TDC_ERR_WORKSPACE;
+  alignas(64) CUtensorMap xmap, dymap;
+  rc = encode_nhwc_map(&xmap, x, N, H, W, C, 62 + int(K), 2 * pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  if (rc != TDC_OK) return rc;
+  tdc::WgradParams g{};
+  g.partial = static_cast<float*>(workspace);
+  g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
+  g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
+  g.tail_bands = pl.tail_bands; g.tail_band_rows = pl.tail_band_rows;
+  g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
+  g.timeout_ns = uint64_t(g_timeout_ns.load());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int ki = int(K / 2 - 1);
+  for (int pass = 0; pass < wgrad_s2_passes(int(K)); ++pass) {
+    const cudaError_t e = kWgradS2Launch[ki][pass][n_stage - 2](xmap, dymap, g, pl.grid, pl.smem, st);
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  const int n = int(K * K * C);
+  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
+      static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
 }  // namespace
 
 extern "C" {
@@ -649,7 +911,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_WORKSPACE: return "workspace smaller than tdc_dwconv3x3_bwd_weight_workspace reports";
     case TDC_ERR_SCRATCH_LIMIT: return "C too large for the 16 MiB static scratch of tdc_dwconv3x3_bwd_weight_noalloc (C <= 116508)";
     case TDC_ERR_STRIDE: return "stride must be 1 or 2";
-    case TDC_ERR_UNSUPPORTED: return "not implemented for this geometry (the backward is stride 1 only)";
+    case TDC_ERR_UNSUPPORTED: return "not implemented for this geometry";
     case TDC_ERR_ACT: return "activation code is not one of TDC_ACT_NONE, _RELU, _RELU6, _SILU";
     default: return "unknown tdc status code";
   }
@@ -741,7 +1003,7 @@ TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx, int64_t
                                 int64_t n_stage, void* stream) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
-  if (stride != 1) return TDC_ERR_UNSUPPORTED;
+  if (stride == 2) return dgrad_s2(dy, w, dx, N, H, W, C, K, pad, n_stage, stream);
   if (K == 3) return tdc_dwconv3x3_bwd_data(dy, w, dx, N, H, W, C, pad, n_stage, stream);
   // pad' = K - 1 - pad must not be negative (pad above K - 1 leaves dx rows
   // no output depends on; not supported for K > 3).
@@ -762,11 +1024,12 @@ TDC_API int tdc_dwconv_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int
   if (!bytes) return TDC_ERR_NULL_POINTER;
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
-  if (stride != 1) return TDC_ERR_UNSUPPORTED;
-  if (K == 3) return tdc_dwconv3x3_bwd_weight_workspace(N, H, W, C, pad, n_stage, bytes);
+  if (K == 3 && stride == 1)
+    return tdc_dwconv3x3_bwd_weight_workspace(N, H, W, C, pad, n_stage, bytes);
   WsPlan pl;
   int64_t P, Q;
-  const int rc = wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  const int rc = stride == 2 ? wgrad_s2_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q)
+                             : wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
   if (rc != TDC_OK) return rc;
   *bytes = wgrad_kxk_workspace_bytes(pl, C, K);
   return TDC_OK;
@@ -778,7 +1041,8 @@ TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int6
                                   void* stream) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
-  if (stride != 1) return TDC_ERR_UNSUPPORTED;
+  if (stride == 2)
+    return wgrad_s2(x, dy, dw, N, H, W, C, K, pad, n_stage, workspace, workspace_bytes, stream);
   if (K == 3)
     return tdc_dwconv3x3_bwd_weight(x, dy, dw, N, H, W, C, pad, n_stage, workspace,
                                     workspace_bytes, stream);
@@ -839,6 +1103,31 @@ TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t 
   plan[7] = int64_t(pl.smem);
   plan[8] = wgrad_kxk_passes(int(K));
   plan[9] = wgrad_kxk_max_rows(int(K));
+  return TDC_OK;
+}
+
+TDC_API int tdc_dwconv_bwd_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                   int64_t pad, int64_t n_stage, int64_t which, int64_t sms,
+                                   int64_t ctas_per_sm, int64_t* plan) {
+  if (!plan) return TDC_ERR_NULL_POINTER;
+  if (which != 0 && which != 1) return TDC_ERR_UNSUPPORTED;
+  if (sms < 1 || ctas_per_sm < 1) return TDC_ERR_BAD_SHAPE;
+  int64_t P, Q;
+  const int rc = bwd_s2_shape(N, H, W, C, K, pad, n_stage, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (N < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
+  const WsPlan pl = which == 0 ? make_dgrad_s2_plan(N, H, W, C, int(K), n_stage, sms, ctas_per_sm)
+                               : make_wgrad_s2_plan(N, P, Q, C, int(K), n_stage, sms, ctas_per_sm);
+  plan[0] = pl.stage_rows;
+  plan[1] = pl.qstrips;
+  plan[2] = pl.cblocks;
+  plan[3] = pl.strips;
+  plan[4] = pl.full_units;
+  plan[5] = pl.tail_band_rows;
+  plan[6] = pl.grid;
+  plan[7] = int64_t(pl.smem);
+  plan[8] = which == 0 ? 1 : wgrad_s2_passes(int(K));
+  plan[9] = which == 0 ? (K - 1) / 2 + 1 : wgrad_s2_max_rows(int(K));
   return TDC_OK;
 }
 

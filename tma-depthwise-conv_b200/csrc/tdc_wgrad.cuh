@@ -1,5 +1,5 @@
 // tdc_wgrad.cuh — weight gradient of the depthwise 3x3 forward (and of the
-// K x K stride-1 forward, below), sm_100a.
+// K x K forward at stride 1 or 2, below), sm_100a.
 //
 //   dw[r,s,c] = sum_{n,p,q} x[n, p+r-pad, q+s-pad, c] * dy[n,p,q,c]     (x = 0 outside)
 //
@@ -221,49 +221,54 @@ __global__ void __launch_bounds__(kWsThreads, 1) dwconv_wgrad_kernel(
 }
 
 // ============================================================================
-// Weight gradient of the K x K (K = 5, 7) stride-1 forward:
-//   dw[r,s,c] = sum_{n,p,q} x[n, p+r-pad, q+s-pad, c] * dy[n,p,q,c]
+// Weight gradient of the K x K stride-S forward (K = 5, 7 at stride 1; K =
+// 3, 5, 7 at stride 2):
+//   dw[r,s,c] = sum_{n,p,q} x[n, S*p+r-pad, S*q+s-pad, c] * dy[n,p,q,c]
 // computed for the tap rows r in [R0, R0 + NR) by one launch (the host runs
 // one or two launches to cover all K rows, so a lane never holds more than
 // NR*K*2 sums).  The same persistent walk over dy's strips and the same
-// producer, with the ring split in two: NS*sr rows of x (32 + K - 1 columns
+// producer, with the ring split in two: NS*S*sr rows of x (S*31 + K columns
 // each) followed by NS*sr rows of dy (32 columns); stage t of a segment
-// fills x rows [p0 - pad + R0 + t*sr, ...) and dy rows [p0 + t*sr, ...) in
-// slot (seq + t) % NS, so segment row i sits at ring row (base + i) mod
-// (NS*sr) in either half.  Consumers take one dy row o at a time with its NR
-// x rows (the direct scheme of the forward: the warp holds the stages of
-// that window, which the host keeps within the ring with
-// (NS - 1) * sr >= NR - 1) and accumulate x[o+R0+r][m+s] * dy[o][m] into
-// NR*K*2 fp32 sums per lane.  Workspace slices hold all K*K taps
-// (partial[cta][warp][K*K][C]); a launch zeroes and fills only its rows'
-// taps, and the reduction of the 3x3 kernel sums them.
+// fills x rows [S*(p0 + t*sr) - pad + R0, ...) (S*sr of them) and dy rows
+// [p0 + t*sr, ...) (sr of them) in slot (seq + t) % NS, so segment x row i
+// sits at x ring row (S*sr*(seq % NS) + i) mod (NS*S*sr) and dy row o at dy
+// ring row (sr*(seq % NS) + o) mod (NS*sr).  Consumers take one dy row o at
+// a time with its NR x rows S*o .. S*o + NR - 1 (the direct scheme of the
+// forward: the warp holds the stages of that window, which the host keeps
+// within the ring with (NS - 1) * S * sr >= NR - 1) and accumulate
+// x[S*o+R0+r][S*m+s] * dy[o][m] into NR*K*2 fp32 sums per lane.  Workspace
+// slices hold all K*K taps (partial[cta][warp][K*K][C]); a launch zeroes and
+// fills only its rows' taps, and the reduction of the 3x3 kernel sums them.
 // ============================================================================
-template <int K>
+template <int K, int S = 1>
 struct WgradGeom {
-  static constexpr int kXCols = kStripQ + K - 1;        // x columns of a strip
-  static constexpr int kXRowB = kXCols * kBlockC * 2;   // bytes of one x ring row
-  static constexpr int kXWarp = kColsPerWarp + K - 1;   // x columns one warp reads
+  static constexpr int kXCols = S * (kStripQ - 1) + K;        // x columns of a strip
+  static constexpr int kXRowB = kXCols * kBlockC * 2;         // bytes of one x ring row
+  static constexpr int kXWarp = S * (kColsPerWarp - 1) + K;   // x columns one warp reads
 };
 
-template <int NS, int K, int R0, int NR>
+template <int NS, int K, int R0, int NR, int S = 1>
 __global__ void __launch_bounds__(kWsThreads, 3)
     dwconv_wgrad_kxk_kernel(const __grid_constant__ CUtensorMap xmap,
                             const __grid_constant__ CUtensorMap dymap,
                             const __grid_constant__ WgradParams g) {
   static_assert(R0 >= 0 && NR >= 1 && R0 + NR <= K, "tap rows");
-  using G = WgradGeom<K>;
+  static_assert(S == 1 || S == 2, "stride");
+  static_assert(NR >= S, "every dy row's stage is also an x stage of the segment");
+  using G = WgradGeom<K, S>;
   __shared__ __align__(8) uint64_t full_bar[NS];
   __shared__ __align__(8) uint64_t empty_bar[NS];
   __shared__ volatile int abort_flag;
   extern __shared__ uint8_t dyn_smem[];
   const uint32_t ring = (smem_addr(dyn_smem) + 127u) & ~127u;
   const uint8_t* ring_ptr = dyn_smem + (ring - smem_addr(dyn_smem));
-  const int sr = g.stage_rows;
-  const int ring_rows = NS * sr;
-  const uint32_t x_stage_bytes = uint32_t(sr) * G::kXRowB;
+  const int sr = g.stage_rows;               // dy rows per stage (S * sr x rows)
+  const int ring_rows = NS * sr;              // dy rows of the ring
+  const int x_ring_rows = S * ring_rows;      // x rows of the ring
+  const uint32_t x_stage_bytes = uint32_t(S * sr) * G::kXRowB;
   const uint32_t dy_stage_bytes = uint32_t(sr) * kDyRowBytes;
-  const uint32_t dy_ring = ring + uint32_t(ring_rows) * G::kXRowB;  // 128-B aligned
-  const uint8_t* dy_ring_ptr = ring_ptr + int64_t(ring_rows) * G::kXRowB;
+  const uint32_t dy_ring = ring + uint32_t(x_ring_rows) * G::kXRowB;  // 128-B aligned
+  const uint8_t* dy_ring_ptr = ring_ptr + int64_t(x_ring_rows) * G::kXRowB;
   const WsParams p = wgrad_as_ws(g);
 
   const int warp = threadIdx.x >> 5;
@@ -299,7 +304,7 @@ __global__ void __launch_bounds__(kWsThreads, 3)
     SegmentIter it(blockIdx.x, gridDim.x);
     Segment sg;
     while (ok && it.next_segment(p, sg)) {
-      const int nst = (sg.rows + NR - 1 + sr - 1) / sr;
+      const int nst = (S * (sg.rows - 1) + NR + S * sr - 1) / (S * sr);
       const int32_t c0 = sg.cb * kBlockC;
       for (int t = 0; t < nst; ++t) {
         if (!mbar_wait_bounded(smem_addr(&empty_bar[stage]), phase ^ 1u, &abort_flag, true,
@@ -314,9 +319,9 @@ __global__ void __launch_bounds__(kWsThreads, 3)
         const uint32_t fb = smem_addr(&full_bar[stage]);
         const int32_t row = sg.p0 + t * sr;
         mbar_arrive_expect_tx(fb, x_stage_bytes + dy_stage_bytes);
-        // x rows [p0 - pad + R0 + t*sr, ...), 32 + K - 1 columns from q0 - pad
-        tma_load_4d(ring + stage * x_stage_bytes, &xmap, fb, c0, sg.qs * kStripQ - g.pad,
-                    row - g.pad + R0, sg.n);
+        // x rows [S*(p0 + t*sr) - pad + R0, ...), S*31 + K columns from S*q0 - pad
+        tma_load_4d(ring + stage * x_stage_bytes, &xmap, fb, c0, S * sg.qs * kStripQ - g.pad,
+                    S * row - g.pad + R0, sg.n);
         // dy rows [p0 + t*sr, ...), 32 columns from q0 (rows past the segment are not read)
         tma_load_4d(dy_ring + stage * dy_stage_bytes, &dymap, fb, c0, sg.qs * kStripQ, row, sg.n);
         armed |= 1u << stage;
@@ -367,13 +372,14 @@ __global__ void __launch_bounds__(kWsThreads, 3)
       if (cur_cb >= 0) flush(cur_cb);
       cur_cb = sg.cb;
     }
-    const int rows_in = sg.rows + NR - 1;
-    const int nst = (rows_in + sr - 1) / sr;
+    const int rows_in = S * (sg.rows - 1) + NR;  // x rows of the segment
+    const int nst = (rows_in + S * sr - 1) / (S * sr);
     const bool active = sg.qs * kStripQ + cw * kColsPerWarp < g.Q;  // warp-uniform
     int acquired = 0, released = 0;
-    int rr0 = int(seq % NS) * sr;  // ring row of segment row o
+    int rr0 = int(seq % NS) * S * sr;  // x ring row of dy row o's first x row
+    int dr0 = int(seq % NS) * sr;      // dy ring row of dy row o
     for (int o = 0; o < sg.rows; ++o) {
-      const int need = min(nst, (o + NR - 1) / sr + 1);
+      const int need = min(nst, (S * o + NR - 1) / (S * sr) + 1);
       for (; acquired < need; ++acquired) {
         const uint32_t k = seq + uint32_t(acquired);
         const bool got = mbar_wait_bounded(smem_addr(&full_bar[k % NS]), (k / NS) & 1u,
@@ -391,16 +397,16 @@ __global__ void __launch_bounds__(kWsThreads, 3)
       if (active) {
         // dy columns past Q were zero-filled by the copy.
         const uint32_t* dsrc = reinterpret_cast<const uint32_t*>(
-            dy_ring_ptr + rr0 * kDyRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+            dy_ring_ptr + dr0 * kDyRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
         uint32_t dyr[kColsPerWarp];
 #pragma unroll
         for (int m = 0; m < kColsPerWarp; ++m) dyr[m] = dsrc[m * (kBlockC / 2)];
 #pragma unroll
         for (int r = 0; r < NR; ++r) {
           int rr = rr0 + r;
-          if (rr >= ring_rows) rr -= ring_rows;
+          if (rr >= x_ring_rows) rr -= x_ring_rows;
           const uint32_t* xsrc = reinterpret_cast<const uint32_t*>(
-              ring_ptr + rr * G::kXRowB + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
+              ring_ptr + rr * G::kXRowB + (S * cw * kColsPerWarp) * (kBlockC * 2)) + lane;
           uint32_t xr[G::kXWarp];
 #pragma unroll
           for (int j = 0; j < G::kXWarp; ++j) xr[j] = xsrc[j * (kBlockC / 2)];
@@ -408,10 +414,12 @@ __global__ void __launch_bounds__(kWsThreads, 3)
           for (int s2 = 0; s2 < K; ++s2)
 #pragma unroll
             for (int m = 0; m < kColsPerWarp; ++m)
-              fma2_f16f32(xr[m + s2], dyr[m], acc[2 * (r * K + s2)], acc[2 * (r * K + s2) + 1]);
+              fma2_f16f32(xr[S * m + s2], dyr[m], acc[2 * (r * K + s2)],
+                          acc[2 * (r * K + s2) + 1]);
         }
       }
-      // Release the stages below the next dy row's first x row.
+      // Release the stages below the next dy row's first x row (x row
+      // S*(o+1) is in stage (o+1)/sr, as dy row o+1 is).
       const int rel_to = o == sg.rows - 1 ? nst : min(nst, (o + 1) / sr);
       if (released < rel_to) {
         __syncwarp();
@@ -420,7 +428,9 @@ __global__ void __launch_bounds__(kWsThreads, 3)
             mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(k)) % NS]));
         released = rel_to;
       }
-      if (++rr0 == ring_rows) rr0 = 0;
+      rr0 += S;
+      if (rr0 >= x_ring_rows) rr0 -= x_ring_rows;
+      if (++dr0 == ring_rows) dr0 = 0;
     }
     seq += uint32_t(nst);
   }

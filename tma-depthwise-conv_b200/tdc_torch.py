@@ -8,10 +8,10 @@ an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
   deterministic reduction kernel).
 * ``torch.ops.tdc.dwconv(x_nhwc, w_rsc, bias, stride, pad)`` — K x K (3, 5,
   7), stride 1 or 2, with the bias added in the kernel's fp32 epilogue.  Its
-  autograd formula covers stride 1 (``tdc::dwconv_bwd_data`` /
-  ``tdc::dwconv_bwd_weight``, the 3x3 ops above at K = 3, and the bias
-  gradient as a sum of dy); at stride 2 backward raises
-  ``NotImplementedError`` (forward-only kernels).
+  autograd formula covers every geometry: ``tdc::dwconv_bwd_data`` /
+  ``tdc::dwconv_bwd_weight`` (at stride 2 the transposed-stencil data
+  gradient and the strided weight-gradient kernel; the 3x3 ops above at 3x3
+  stride 1), and the bias gradient as a sum of dy.
   All ops have fake implementations, so they trace under ``torch.compile``.
 * ``DepthwiseConv2d`` — a module with ``nn.Conv2d(C, C, K, stride, padding,
   groups=C, bias=...)``'s parameters and NCHW interface.  A channels-last NCHW
@@ -19,8 +19,8 @@ an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
   ``DepthwiseConv3x3`` is its 3x3 stride-1 form.
 * ``convert_depthwise_convs(model)`` — swaps every eligible ``nn.Conv2d``
   (depthwise, dilation 1, symmetric integer padding, zeros padding mode,
-  C % 8 == 0; 3x3 / 5x5 / 7x7 at stride 1, or with ``forward_only=True`` also
-  stride 2) for a ``DepthwiseConv2d`` sharing its parameters.
+  C % 8 == 0; 3x3 / 5x5 / 7x7 at stride 1 or 2) for a ``DepthwiseConv2d``
+  sharing its parameters.
 
 The reference (haowen-han/tma-depthwise-conv) has a forward-only Python API
 (``tma_dwconv.py``); everything here is beyond that surface and is built on
@@ -36,9 +36,13 @@ from torch import nn
 import _tma_dwconv_C as _C  # type: ignore
 from tma_dwconv import DWCONV_STAGES
 
-#: (K, stride) pairs the kernels implement; backward exists for TRAINABLE only.
+#: (K, stride) pairs the kernels implement, forward and backward.
 GEOMETRIES = tuple(DWCONV_STAGES)
-TRAINABLE = ((3, 1), (5, 1), (7, 1))
+TRAINABLE = GEOMETRIES
+
+#: n_stage of the data / weight gradient per (K, stride), measured at
+#: 64 x 224 x 336 x 256 (stride 1: the forward's table for the data gradient).
+BWD_STAGES = {g: (DWCONV_STAGES[g] if g[1] == 1 else 2, 2) for g in GEOMETRIES}
 
 
 def _out_hw(h: int, w: int, pad: int, k: int = 3, stride: int = 1) -> tuple[int, int]:
@@ -109,27 +113,30 @@ def dwconv3x3(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, pad: int = 1) -> torch.
 # ------------------------------ K x K, stride ---------------------------------
 
 @torch.library.custom_op("tdc::dwconv_bwd_data", mutates_args=())
-def dwconv_bwd_data_op(dy: torch.Tensor, w: torch.Tensor, pad: int) -> torch.Tensor:
-    """dx [N,H,W,C] of the K x K stride-1 forward, from dy [N,P,Q,C] and w [K,K,C]."""
-    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, 1,
-                              DWCONV_STAGES[(int(w.shape[0]), 1)])
+def dwconv_bwd_data_op(dy: torch.Tensor, w: torch.Tensor, pad: int, stride: int, input_h: int,
+                       input_w: int) -> torch.Tensor:
+    """dx [N,H,W,C] of the K x K forward, from dy [N,P,Q,C] and w [K,K,C]
+    (H = input_h, W = input_w: at stride 2, dy does not determine them)."""
+    k = int(w.shape[0])
+    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, stride,
+                              BWD_STAGES[(k, stride)][0], input_h, input_w)
 
 
 @dwconv_bwd_data_op.register_fake
-def _(dy, w, pad):
-    k = w.shape[0]
-    return dy.new_empty((dy.shape[0], dy.shape[1] - 2 * pad + k - 1, dy.shape[2] - 2 * pad + k - 1,
-                         dy.shape[3]))
+def _(dy, w, pad, stride, input_h, input_w):
+    return dy.new_empty((dy.shape[0], input_h, input_w, dy.shape[3]))
 
 
 @torch.library.custom_op("tdc::dwconv_bwd_weight", mutates_args=())
-def dwconv_bwd_weight_op(x: torch.Tensor, dy: torch.Tensor, k: int, pad: int) -> torch.Tensor:
-    """dw [K,K,C] (fp32) of the K x K stride-1 forward, from x and dy."""
-    return _C.dwconv_bwd_weight(x.contiguous(), dy.contiguous(), k, pad, 1, 2)
+def dwconv_bwd_weight_op(x: torch.Tensor, dy: torch.Tensor, k: int, pad: int,
+                         stride: int) -> torch.Tensor:
+    """dw [K,K,C] (fp32) of the K x K forward, from x and dy."""
+    return _C.dwconv_bwd_weight(x.contiguous(), dy.contiguous(), k, pad, stride,
+                                BWD_STAGES[(k, stride)][1])
 
 
 @dwconv_bwd_weight_op.register_fake
-def _(x, dy, k, pad):
+def _(x, dy, k, pad, stride):
     return x.new_empty((k, k, x.shape[3]), dtype=torch.float32)
 
 
@@ -160,16 +167,14 @@ def _setup_context_k(ctx, inputs, output):
 
 def _backward_k(ctx, dy):
     k, s = ctx.geometry
-    if ctx.geometry not in TRAINABLE:
-        raise NotImplementedError(
-            f"tdc::dwconv backward is implemented for stride 1 only, not {k}x{k} stride {s}")
     x, w = ctx.saved_tensors
     dx = dw = db = None
     if ctx.needs_input_grad[0]:
-        dx = dwconv3x3_bwd_data_op(dy, w, ctx.pad) if k == 3 else dwconv_bwd_data_op(dy, w, ctx.pad)
+        dx = (dwconv3x3_bwd_data_op(dy, w, ctx.pad) if (k, s) == (3, 1)
+              else dwconv_bwd_data_op(dy, w, ctx.pad, s, x.shape[1], x.shape[2]))
     if ctx.needs_input_grad[1]:
-        dw = (dwconv3x3_bwd_weight_op(x, dy, ctx.pad) if k == 3
-              else dwconv_bwd_weight_op(x, dy, k, ctx.pad)).to(w.dtype)
+        dw = (dwconv3x3_bwd_weight_op(x, dy, ctx.pad) if (k, s) == (3, 1)
+              else dwconv_bwd_weight_op(x, dy, k, ctx.pad, s)).to(w.dtype)
     if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
         db = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(ctx.bias_dtype)
     return dx, dw, db, None, None
@@ -180,7 +185,7 @@ dwconv_op.register_autograd(_backward_k, setup_context=_setup_context_k)
 
 def dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, bias: Optional[torch.Tensor] = None,
            stride: int = 1, pad: Optional[int] = None) -> torch.Tensor:
-    """Depthwise K x K on NHWC fp16 tensors (differentiable at stride 1)."""
+    """Depthwise K x K on NHWC fp16 tensors (differentiable at stride 1 and 2)."""
     if pad is None:
         pad = int(w_rsc.shape[0]) // 2
     return dwconv_op(x_nhwc, w_rsc, bias, int(stride), int(pad))
@@ -191,7 +196,7 @@ def dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, bias: Optional[torch.Tenso
 class DepthwiseConv2d(nn.Module):
     """``nn.Conv2d(C, C, K, stride, padding, groups=C, bias=bias)`` for fp16
     channels-last NCHW inputs (NHWC memory), on the sm_100a kernels, K in
-    {3, 5, 7}, stride 1 or 2 (trainable at stride 1).
+    {3, 5, 7}, stride 1 or 2 (forward and backward).
 
     Parameters keep ``nn.Conv2d``'s layout (weight [C, 1, K, K], bias [C]), so
     state dicts load unchanged.  Inputs that are not fp16 CUDA tensors in
@@ -264,9 +269,9 @@ def _eligible(m: nn.Module, forward_only: bool) -> bool:
 def convert_depthwise_convs(model: nn.Module, forward_only: bool = False) -> int:
     """Replace eligible depthwise ``nn.Conv2d`` children in place; returns the count.
 
-    By default only stride-1 convolutions (which have a backward) are
-    converted; ``forward_only=True`` also converts stride 2, whose backward
-    raises ``NotImplementedError``.
+    Every geometry the kernels implement (3x3 / 5x5 / 7x7, stride 1 or 2) has
+    a backward, so ``forward_only`` no longer changes what is converted; it is
+    kept so existing callers keep working.
     """
     count = 0
     for name, child in list(model.named_children()):
