@@ -230,9 +230,9 @@ TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t 
 /* Launch plan of the stride-2 backward (pure host arithmetic), which = 0 for
  * the data gradient, 1 for the weight gradient; plan[0..7] as tdc_ws_plan.
  * Data gradient: strips and bands over dx [N,H,W,C]; stage_rows counts dy
- * rows of 16 + (K-1)/2 columns; plan[8] = 1 launch; plan[9] = (K+1)/2, the
- * dy rows one pass of two dx rows holds (the ring keeps
- * (n_stage - 1) * stage_rows >= plan[9] - 1).  Weight gradient: strips over
+ * rows of 16 + (K-1)/2 columns; plan[8] = pairs of dx rows per pass (one
+ * launch); plan[9] = (K-1)/2 + plan[8], the dy rows one pass holds (the ring
+ * keeps (n_stage - 1) * stage_rows >= plan[9] - 1).  Weight gradient: strips over
  * dy [N,P,Q,C]; a stage holds stage_rows dy rows and 2*stage_rows x rows of
  * 62 + K columns; plan[8] = launches, plan[9] = tap rows of the tallest
  * launch (the ring keeps (n_stage - 1) * 2 * stage_rows >= plan[9] - 1).

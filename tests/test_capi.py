@@ -361,35 +361,41 @@ def _s2_plan(lib, which, N, H, W, Cc, K, pad, ns, sms=148, occ=3):
                      "smem", "passes", "rows"], list(out)))
 
 
-def dgrad_s2_segment(h0, rows, pad, K, sr, ns):
+def dgrad_s2_segment(h0, rows, pad, K, sr, ns, pairs):
     """Restates the stride-2 data gradient's consumer over one segment of dx
-    rows [h0, h0 + rows): passes of two dx rows (h, h+1) with h + pad even,
-    each reading dy rows k .. k + (K-1)/2 of the segment's window.  Returns the
-    dx rows stored, the dy rows each stored row reads (by the kernel's tap
-    formula) and the most ring stages held at once."""
+    rows [h0, h0 + rows): pairs of dx rows (h, h+1) with h + pad even, `pairs`
+    of them per pass, pass k reading window rows pairs*k .. pairs*k + half +
+    pairs - 1.  Returns the dx rows stored, the dy rows each stored row reads
+    (by the kernel's tap formula) and the most ring stages held at once."""
     half = (K - 1) // 2
+    win = half + pairs
     e0 = h0 + pad
     e_first = e0 & ~1
-    passes = (rows + (e0 & 1) + 1) // 2
+    npairs = (rows + (e0 & 1) + 1) // 2
+    passes = -(-npairs // pairs)
     dy_row0 = (e_first >> 1) - half
-    dy_rows = passes + half
+    dy_rows = passes * pairs + half
     nst = -(-dy_rows // sr)
     acquired = released = worst = 0
     stored, reads = [], {}
     for k in range(passes):
-        acquired = max(acquired, min(nst, (k + half) // sr + 1))
+        last_row = pairs * k + win - 1
+        assert last_row < dy_rows
+        while acquired < nst and acquired * sr <= last_row:
+            acquired += 1
         worst = max(worst, acquired - released)
-        h_even = e_first + 2 * k - pad
-        for h, taps in ((h_even, [K - 1 - 2 * t for t in range(half + 1)]),
-                        (h_even + 1, [K - 2 * t for t in range(1, half + 1)])):
-            if h0 <= h < h0 + rows:
-                stored.append(h)
-                # window row t holds dy row dy_row0 + k + t; it must be the row tap r reads
-                rows_read = [dy_row0 + k + (K - 1 - r) // 2 if (K - 1 - r) % 2 == 0
-                             else dy_row0 + k + (K - r) // 2 for r in taps]
-                reads[h] = (taps, rows_read)
-                assert all(0 <= dy_row0 + k + t - dy_row0 < dy_rows for t in range(half + 1))
-        released = nst if k == passes - 1 else min(nst, (k + 1) // sr)
+        for i in range(pairs):
+            h_even = e_first + 2 * (pairs * k + i) - pad
+            for h, taps in ((h_even, [K - 1 - 2 * u for u in range(half + 1)]),
+                            (h_even + 1, [K - 2 * u for u in range(1, half + 1)])):
+                if h0 <= h < h0 + rows:
+                    stored.append(h)
+                    # window row pairs*k + i + u holds dy row dy_row0 + that
+                    reads[h] = (taps, [dy_row0 + pairs * k + i + ((K - 1 - r) // 2 if (K - 1 - r) % 2 == 0
+                                                                   else (K - r) // 2) for r in taps])
+        next_first = 1 << 30 if k == passes - 1 else pairs * (k + 1)
+        while released < nst and (released + 1) * sr <= next_first:
+            released += 1
         assert released <= acquired
     assert acquired == released == nst
     return stored, reads, worst
@@ -402,9 +408,9 @@ def dgrad_s2_segment(h0, rows, pad, K, sr, ns):
 def test_dgrad_s2_plan_covers_every_dx_row_once(lib, K, N, H, W, Cc, pad, ns):
     pad = K // 2 if pad is None else pad
     pl = _s2_plan(lib, 0, N, H, W, Cc, K, pad, ns)
-    sr, half = pl["stage_rows"], (K - 1) // 2
-    assert pl["passes"] == 1 and pl["rows"] == half + 1
-    assert (ns - 1) * sr >= half and 1 <= sr <= 256
+    sr, half, pairs = pl["stage_rows"], (K - 1) // 2, pl["passes"]
+    assert 1 <= pairs <= 4 and pl["rows"] == half + pairs
+    assert (ns - 1) * sr >= pl["rows"] - 1 and 1 <= sr <= 256
     assert pl["smem"] == ns * sr * (16 + half) * 128 + 128 <= 200 * 1024
     assert pl["qstrips"] == -(-W // 32) and pl["cblocks"] == -(-Cc // 64)
     # dy columns: dx column v of strip qs reads (v + pad - s)/2, which must lie
@@ -422,7 +428,7 @@ def test_dgrad_s2_plan_covers_every_dx_row_once(lib, K, N, H, W, Cc, pad, ns):
     seen = set()
     for g in range(pl["grid"]):
         for strip, a, b in segments(pl, H, g):
-            stored, reads, worst = dgrad_s2_segment(a, b - a, pad, K, sr, ns)
+            stored, reads, worst = dgrad_s2_segment(a, b - a, pad, K, sr, ns, pairs)
             assert worst <= ns
             assert sorted(stored) == list(range(a, b))
             for h, (taps, rows_read) in reads.items():

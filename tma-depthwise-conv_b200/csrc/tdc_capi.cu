@@ -679,12 +679,18 @@ static_assert(dgrad_s2_dy_cols(3) == tdc::DgradS2Geom<3>::kDyCols &&
               "host and device box widths agree");
 int dgrad_s2_row_bytes(int K) { return dgrad_s2_dy_cols(K) * tdc::kBlockC * 2; }
 
-// 16 dy rows split over the stages; a pass holds kHalf + 1 consecutive rows,
-// which needs (n_stage - 1) * sr >= kHalf.
+// dy rows one pass holds at once: kHalf + pairs of dx rows per pass.
+int dgrad_s2_window(int K) { return (K - 1) / 2 + tdc::dgrad_s2_pairs(K); }
+static_assert(tdc::DgradS2Geom<3>::kWin == (1 + tdc::dgrad_s2_pairs(3)) &&
+                  tdc::DgradS2Geom<7>::kWin == (3 + tdc::dgrad_s2_pairs(7)),
+              "host and device windows agree");
+
+// 16 dy rows split over the stages; a pass holds its window of consecutive
+// rows, which needs (n_stage - 1) * sr >= window - 1.
 int dgrad_s2_stage_rows(int K, int64_t n_stage) {
   const int ns = int(n_stage);
   const int sr = std::max(1, tdc::kDgradS2RingRows / ns);
-  return std::max(sr, ((K - 1) / 2 + ns - 2) / (ns - 1));
+  return std::max(sr, (dgrad_s2_window(K) - 1 + ns - 2) / (ns - 1));
 }
 
 WsPlan make_dgrad_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int K, int64_t n_stage,
@@ -883,9 +889,8 @@ int wgrad_s2(const void* x, const void* dy, float* dw, int64_t N, int64_t H, int
     if (e != cudaSuccess) return cuda_fail(e);
   }
   const int n = int(K * K * C);
-  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
-      static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = tdc::launch_wgrad_reduce(static_cast<const float*>(workspace), dw,
+                                int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
@@ -1074,9 +1079,8 @@ TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int6
   }
   cudaError_t e;
   const int n = int(K * K * C);
-  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
-      static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
-  e = cudaGetLastError();
+  e = tdc::launch_wgrad_reduce(static_cast<const float*>(workspace), dw,
+                                int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
@@ -1126,8 +1130,8 @@ TDC_API int tdc_dwconv_bwd_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, i
   plan[5] = pl.tail_band_rows;
   plan[6] = pl.grid;
   plan[7] = int64_t(pl.smem);
-  plan[8] = which == 0 ? 1 : wgrad_s2_passes(int(K));
-  plan[9] = which == 0 ? (K - 1) / 2 + 1 : wgrad_s2_max_rows(int(K));
+  plan[8] = which == 0 ? tdc::dgrad_s2_pairs(int(K)) : wgrad_s2_passes(int(K));
+  plan[9] = which == 0 ? dgrad_s2_window(int(K)) : wgrad_s2_max_rows(int(K));
   return TDC_OK;
 }
 
@@ -1202,9 +1206,8 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, i
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   const int n = int(9 * C);
-  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
-      static_cast<const float*>(workspace), dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
-  e = cudaGetLastError();
+  e = tdc::launch_wgrad_reduce(static_cast<const float*>(workspace), dw,
+                                int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
@@ -1291,9 +1294,7 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   const int n = int(9 * C);
-  tdc::dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 255) / 256)), dim3(256), 0, st>>>(
-      sc.ptr, dw, int32_t(pl.grid * tdc::kConsumerWarps), n);
-  e = cudaGetLastError();
+  e = tdc::launch_wgrad_reduce(sc.ptr, dw, int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 

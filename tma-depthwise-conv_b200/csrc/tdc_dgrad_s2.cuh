@@ -13,10 +13,12 @@
 //
 // Work decomposition: the forward's persistent walk over 32-column strips,
 // here of dx ([N,H,W,C]): SegmentIter with P = H, Q = W.  A segment's dx rows
-// are taken in passes of two rows (h, h + 1) with h + pad even; both rows of
-// a pass read the same kHalf + 1 dy rows (e/2 - kHalf .. e/2, e = h + pad):
-// the even row with taps r = K-1-2t, the odd row with r = K-2t (t >= 1) for
-// window row t.  The producer streams dy rows (16 + kHalf columns of 64
+// are taken in pairs (h, h + 1) with h + pad even; both rows of a pair read
+// the same kHalf + 1 dy rows (e/2 - kHalf .. e/2, e = h + pad): the even row
+// with taps r = K-1-2t, the odd row with r = K-2t (t >= 1) for window row t.
+// A pass covers RP consecutive pairs (2*RP dx rows) from kHalf + RP dy rows,
+// each read from shared memory once and fed to every row of the pass it is a
+// tap row of.  The producer streams dy rows (16 + kHalf columns of 64
 // channels, the dy columns of the strip) into an NS-deep ring; consumer warp
 // cw owns dx columns 8cw .. 8cw+7 of the strip, which read dy columns
 // 4cw .. 4cw + 3 + kHalf of the box.  A lane owns one channel pair; the taps
@@ -27,13 +29,36 @@
 
 namespace tdc {
 
+// Pairs of dx rows per pass, measured at 64 x 224 x 336 x 256 (more pairs
+// amortise the per-pass bookkeeping and stores' addressing; 7x7 keeps one:
+// its 49 taps leave no registers for a second pair's accumulators).
+#ifndef TDC_DGS2_PAIRS3
+#define TDC_DGS2_PAIRS3 2
+#endif
+#ifndef TDC_DGS2_PAIRS5
+#define TDC_DGS2_PAIRS5 2
+#endif
+#ifndef TDC_DGS2_PAIRS7
+#define TDC_DGS2_PAIRS7 1
+#endif
+__host__ __device__ constexpr int dgrad_s2_pairs(int K) {
+  return K == 3 ? TDC_DGS2_PAIRS3 : (K == 5 ? TDC_DGS2_PAIRS5 : TDC_DGS2_PAIRS7);
+}
+
+// Resident CTAs per SM the kernel is compiled for (bounds its registers).
+#ifndef TDC_DGS2_MINB3
+#define TDC_DGS2_MINB3 3
+#endif
+__host__ __device__ constexpr int dgrad_s2_min_blocks(int K) { return K == 3 ? TDC_DGS2_MINB3 : 3; }
+
 template <int K>
 struct DgradS2Geom {
   static constexpr int kHalf = (K - 1) / 2;
   static constexpr int kDyCols = kStripQ / 2 + kHalf;        // dy columns of a strip (TMA box)
   static constexpr int kDyRowB = kDyCols * kBlockC * 2;      // bytes of one ring row
   static constexpr int kDyWarp = kColsPerWarp / 2 + kHalf;   // dy columns one warp reads
-  static constexpr int kWin = kHalf + 1;                     // dy rows of one pass
+  static constexpr int kPairs = dgrad_s2_pairs(K);           // dx row pairs per pass
+  static constexpr int kWin = kHalf + kPairs;                // dy rows of one pass
 };
 
 // Ring capacity in dy rows, split over the n_stage stages.
@@ -59,11 +84,13 @@ __device__ __forceinline__ WsParams dgrad_s2_as_ws(const DgradS2Params& g) {
   return p;
 }
 
-// Passes and dy rows of a segment of dx rows [h0, h0 + rows): the first pass
+// Passes and dy rows of a segment of dx rows [h0, h0 + rows): the first pair
 // starts at the even e = h + pad at or below h0 + pad (its even row is h0 - 1,
-// outside the segment, when h0 + pad is odd).
+// outside the segment, when h0 + pad is odd); pass k holds pairs
+// kPairs*k .. kPairs*k + kPairs - 1 and reads window rows kPairs*k ..
+// kPairs*k + kWin - 1.  Rows of pairs past the segment are computed, not stored.
 struct DgradS2Seg {
-  int e_first;   // h + pad of the even row of pass 0
+  int e_first;   // h + pad of the even row of pair 0
   int passes;
   int dy_row0;   // first dy row of the segment's window (may be negative)
   int dy_rows;   // dy rows the segment streams
@@ -71,12 +98,14 @@ struct DgradS2Seg {
 
 template <int K>
 __host__ __device__ __forceinline__ DgradS2Seg dgrad_s2_segment(int h0, int rows, int pad) {
+  using G = DgradS2Geom<K>;
   DgradS2Seg s;
   const int e0 = h0 + pad;
   s.e_first = e0 & ~1;
-  s.passes = (rows + (e0 & 1) + 1) / 2;
-  s.dy_row0 = (s.e_first >> 1) - DgradS2Geom<K>::kHalf;
-  s.dy_rows = s.passes + DgradS2Geom<K>::kHalf;
+  const int pairs = (rows + (e0 & 1) + 1) / 2;
+  s.passes = (pairs + G::kPairs - 1) / G::kPairs;
+  s.dy_row0 = (s.e_first >> 1) - G::kHalf;
+  s.dy_rows = s.passes * G::kPairs + G::kHalf;
   return s;
 }
 
@@ -84,7 +113,7 @@ __host__ __device__ __forceinline__ DgradS2Seg dgrad_s2_segment(int h0, int rows
 // fixes at compile time which taps (and which dy column of the lane's
 // registers) each of the 8 columns uses.
 template <int NS, int K, int PODD>
-__global__ void __launch_bounds__(kWsThreads, 3)
+__global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
     dwconv_dgrad_s2_kernel(const __grid_constant__ CUtensorMap dymap,
                            const __grid_constant__ DgradS2Params g) {
   using G = DgradS2Geom<K>;
@@ -165,8 +194,13 @@ __global__ void __launch_bounds__(kWsThreads, 3)
   Segment sg;
   int last_cb = -1;
   uint32_t wt[K * K];
-  uint32_t seq = 0;  // ring stages this warp has consumed
+  // Next ring stage to acquire / release, as slot and phase (no division).
+  int acq_slot = 0, rel_slot = 0;
+  uint32_t acq_phase = 0;
+  int seg_slot = 0;  // slot of the current segment's first stage
   bool failed = false;
+  const int64_t dx_col_stride = g.C;
+  const int64_t dx_row_stride = int64_t(g.W) * g.C;
   while (!failed && it.next_segment(p, sg)) {
     const DgradS2Seg d = dgrad_s2_segment<K>(sg.p0, sg.rows, g.pad);
     const int nst = (d.dy_rows + sr - 1) / sr;
@@ -181,31 +215,37 @@ __global__ void __launch_bounds__(kWsThreads, 3)
     const int v_first = sg.qs * kStripQ + cw * kColsPerWarp;
     const int n_valid = min(kColsPerWarp, g.W - v_first);  // <= 0: warp idle
     __half* dxcol = g.dx + (int64_t(sg.n) * g.H * g.W + v_first) * g.C + c0 + 2 * lane;
-    const int64_t dx_row_stride = int64_t(g.W) * g.C;
+    const int h_end = sg.p0 + sg.rows;
     int acquired = 0, released = 0;
-    int rr0 = int(seq % NS) * sr;  // ring row of window row 0 of the current pass
+    int acq_end = 0;  // window rows covered by the acquired stages (acquired * sr)
+    int rel_end = sr; // window rows up to the end of stage `released`
+    int rr0 = seg_slot * sr;  // ring row of window row 0 of the current pass
     for (int k = 0; k < d.passes; ++k) {
-      // Pass k reads dy rows k .. k + kHalf of the segment's window.
-      const int need = min(nst, (k + G::kHalf) / sr + 1);
-      for (; acquired < need; ++acquired) {
-        const uint32_t a = seq + uint32_t(acquired);
-        const bool got = mbar_wait_bounded(smem_addr(&full_bar[a % NS]), (a / NS) & 1u,
-                                           &abort_flag, true, g.timeout_ns);
+      // Pass k reads window rows kPairs*k .. kPairs*k + kWin - 1.
+      const int last_row = G::kPairs * k + G::kWin - 1;
+      while (acquired < nst && acq_end <= last_row) {
+        const bool got = mbar_wait_bounded(smem_addr(&full_bar[acq_slot]), acq_phase, &abort_flag,
+                                           true, g.timeout_ns);
         if (__any_sync(0xffffffffu, !got)) {
           if (lane == 0 && !abort_flag) {
-            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, int(a % NS), -1);
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1);
             abort_flag = 1;
           }
           failed = true;
           break;
         }
+        ++acquired;
+        acq_end += sr;
+        if (++acq_slot == NS) { acq_slot = 0; acq_phase ^= 1u; }
       }
       if (failed) break;
-      const int h_even = d.e_first + 2 * k - g.pad;  // dx row with h + pad even
+      const int h_first = d.e_first + 2 * G::kPairs * k - g.pad;  // even row of the pass's pair 0
       if (n_valid > 0) {
-        RowAcc ae, ao;  // even-e row h_even, odd-e row h_even + 1
+        RowAcc ae[G::kPairs], ao[G::kPairs];  // pair i: rows h_first + 2i (even e), + 1 (odd e)
 #pragma unroll
-        for (int i = 0; i < 2 * kColsPerWarp; ++i) { ae.v[i] = 0.f; ao.v[i] = 0.f; }
+        for (int i = 0; i < G::kPairs; ++i)
+#pragma unroll
+          for (int v = 0; v < 2 * kColsPerWarp; ++v) { ae[i].v[v] = 0.f; ao[i].v[v] = 0.f; }
 #pragma unroll
         for (int t = 0; t < G::kWin; ++t) {
           int rr = rr0 + t;
@@ -216,49 +256,60 @@ __global__ void __launch_bounds__(kWsThreads, 3)
 #pragma unroll
           for (int j = 0; j < G::kDyWarp; ++j) dr[j] = src[j * (kBlockC / 2)];
 #pragma unroll
-          for (int m = 0; m < kColsPerWarp; ++m) {
+          for (int i = 0; i < G::kPairs; ++i) {
+            const int u = t - i;  // window row of pair i
+            if (u < 0 || u > G::kHalf) continue;
 #pragma unroll
-            for (int s = K - 1; s >= 0; --s) {
-              if (((m + PODD + s) & 1) != 0) continue;  // v + pad - s must be even
-              // dy column of (m, s) relative to the warp's first one
-              const int j = (m + PODD - s) / 2 - PODD + G::kHalf;
-              fma2_f16f32(dr[j], wt[(K - 1 - 2 * t) * K + s], ae.v[2 * m], ae.v[2 * m + 1]);
-              if (t >= 1)
-                fma2_f16f32(dr[j], wt[(K - 2 * t) * K + s], ao.v[2 * m], ao.v[2 * m + 1]);
+            for (int m = 0; m < kColsPerWarp; ++m) {
+#pragma unroll
+              for (int s = K - 1; s >= 0; --s) {
+                if (((m + PODD + s) & 1) != 0) continue;  // v + pad - s must be even
+                // dy column of (m, s) relative to the warp's first one
+                const int j = (m + PODD - s) / 2 - PODD + G::kHalf;
+                fma2_f16f32(dr[j], wt[(K - 1 - 2 * u) * K + s], ae[i].v[2 * m], ae[i].v[2 * m + 1]);
+                if (u >= 1)
+                  fma2_f16f32(dr[j], wt[(K - 2 * u) * K + s], ao[i].v[2 * m], ao[i].v[2 * m + 1]);
+              }
             }
           }
         }
         if (chan_ok) {
-          if (h_even >= sg.p0) {
-            __half* dst = dxcol + int64_t(h_even) * dx_row_stride;
 #pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m)
-              if (m < n_valid)
-                *reinterpret_cast<uint32_t*>(dst + int64_t(m) * g.C) =
-                    pack_half2_rn(ae.v[2 * m], ae.v[2 * m + 1]);
-          }
-          if (h_even + 1 < sg.p0 + sg.rows) {
-            __half* dst = dxcol + int64_t(h_even + 1) * dx_row_stride;
+          for (int i = 0; i < 2 * G::kPairs; ++i) {
+            const int h = h_first + i;  // rows h_first .. h_first + 2*kPairs - 1
+            if (h < sg.p0 || h >= h_end) continue;
+            const RowAcc& a = (i & 1) ? ao[i / 2] : ae[i / 2];
+            __half* dst = dxcol + int64_t(h) * dx_row_stride;
+            if (n_valid == kColsPerWarp) {
 #pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m)
-              if (m < n_valid)
-                *reinterpret_cast<uint32_t*>(dst + int64_t(m) * g.C) =
-                    pack_half2_rn(ao.v[2 * m], ao.v[2 * m + 1]);
+              for (int m = 0; m < kColsPerWarp; ++m)
+                *reinterpret_cast<uint32_t*>(dst + m * dx_col_stride) =
+                    pack_half2_rn(a.v[2 * m], a.v[2 * m + 1]);
+            } else {
+#pragma unroll
+              for (int m = 0; m < kColsPerWarp; ++m)
+                if (m < n_valid)
+                  *reinterpret_cast<uint32_t*>(dst + m * dx_col_stride) =
+                      pack_half2_rn(a.v[2 * m], a.v[2 * m + 1]);
+            }
           }
         }
       }
-      // Release the stages below the next pass's first dy row.
-      const int rel_to = k == d.passes - 1 ? nst : min(nst, (k + 1) / sr);
-      if (released < rel_to) {
+      // Release the stages wholly below the next pass's first window row.
+      const int next_first = k == d.passes - 1 ? (1 << 30) : G::kPairs * (k + 1);
+      if (released < nst && rel_end <= next_first) {
         __syncwarp();
-        if (lane == 0)
-          for (int a = released; a < rel_to; ++a)
-            mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(a)) % NS]));
-        released = rel_to;
+        while (released < nst && rel_end <= next_first) {
+          if (lane == 0) mbar_arrive(smem_addr(&empty_bar[rel_slot]));
+          ++released;
+          rel_end += sr;
+          if (++rel_slot == NS) rel_slot = 0;
+        }
       }
-      if (++rr0 == ring_rows) rr0 = 0;
+      rr0 += G::kPairs;
+      if (rr0 >= ring_rows) rr0 -= ring_rows;
     }
-    seq += uint32_t(nst);
+    seg_slot = acq_slot;  // the next segment starts at a fresh stage
   }
 }
 

@@ -437,15 +437,41 @@ __global__ void __launch_bounds__(kWsThreads, 3)
   if (cur_cb >= 0 && !failed) flush(cur_cb);
 }
 
-// dw[k][c] = sum over slices (cta-major, then warp, in order) of partial[slice][k][c].
-__global__ void __launch_bounds__(256) dwconv_wgrad_reduce_kernel(const float* __restrict__ partial,
-                                                                  float* __restrict__ dw,
-                                                                  int32_t slices, int32_t n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+// dw[i] = sum over the slices of partial[slice][i] (i = k*C + c), in a fixed
+// order: block b owns outputs 32b .. 32b+31; warp g of the block sums slices
+// g, g + 32, g + 64, ... in ascending order for its lane's output, and the 32
+// warp sums are combined by a fixed binary tree in shared memory.  The order
+// depends only on the slice count, so results are bit-reproducible, and each
+// output's 1 + slices/32 dependent loads keep the kernel short (one thread
+// per output would chain all slices).
+constexpr int kReduceGroups = 32;
+
+__global__ void __launch_bounds__(32 * kReduceGroups) dwconv_wgrad_reduce_kernel(
+    const float* __restrict__ partial, float* __restrict__ dw, int32_t slices, int32_t n) {
+  __shared__ float part[kReduceGroups][33];
+  const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int b = 0; b < slices; ++b) s += partial[int64_t(b) * n + i];
-  dw[i] = s;
+  if (i < n) {
+#pragma unroll 4
+    for (int b = grp; b < slices; b += kReduceGroups) s += partial[int64_t(b) * n + i];
+  }
+  part[grp][lane] = s;
+  __syncthreads();
+#pragma unroll
+  for (int h = kReduceGroups / 2; h >= 1; h >>= 1) {
+    if (grp < h) part[grp][lane] += part[grp + h][lane];
+    __syncthreads();
+  }
+  if (grp == 0 && i < n) dw[i] = part[0][lane];
+}
+
+// Launch of the reduction over `slices` workspace slices of n floats.
+inline cudaError_t launch_wgrad_reduce(const float* partial, float* dw, int32_t slices, int32_t n,
+                                       cudaStream_t st) {
+  dwconv_wgrad_reduce_kernel<<<dim3(unsigned((n + 31) / 32)), dim3(32 * kReduceGroups), 0, st>>>(
+      partial, dw, slices, n);
+  return cudaGetLastError();
 }
 
 }  // namespace tdc

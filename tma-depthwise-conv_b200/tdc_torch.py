@@ -41,8 +41,13 @@ GEOMETRIES = tuple(DWCONV_STAGES)
 TRAINABLE = GEOMETRIES
 
 #: n_stage of the data / weight gradient per (K, stride), measured at
-#: 64 x 224 x 336 x 256 (stride 1: the forward's table for the data gradient).
-BWD_STAGES = {g: (DWCONV_STAGES[g] if g[1] == 1 else 2, 2) for g in GEOMETRIES}
+#: 64 x 224 x 336 x 256 (stride 1 data gradient: the forward's table; stride-2
+#: weight gradient, 2 / 3 / 4 stages: 3x3 546 / 470 / 465 us, 5x5 837 / 856 /
+#: 678 us, 7x7 1242 / 1177 / 1274 us).
+BWD_STAGES = {(3, 1): (DWCONV_STAGES[(3, 1)], 2), (5, 1): (DWCONV_STAGES[(5, 1)], 2),
+              (7, 1): (DWCONV_STAGES[(7, 1)], 2),
+              (3, 2): (2, 4), (5, 2): (2, 4), (7, 2): (2, 3)}
+assert set(BWD_STAGES) == set(GEOMETRIES)
 
 
 def _out_hw(h: int, w: int, pad: int, k: int = 3, stride: int = 1) -> tuple[int, int]:
