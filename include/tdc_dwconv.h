@@ -95,6 +95,26 @@ TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y,
                           int64_t R, int64_t S, int64_t pad, int64_t n_stage,
                           void* stream);
 
+/* tdc_dwconv_ws for inputs and outputs in HOST memory: copies w and x to the
+ * device, runs the ws kernel and copies y back, pipelined over chunks of
+ * `chunk_images` images (0 = N/16 rounded up) so that the host->device copy
+ * of one chunk, the kernel of the previous one and the device->host copy of
+ * the one before run at the same time (the two copy directions use separate
+ * copy engines).  x_host [N,H,W,C], w_host [3,3,C] and y_host [N,P,Q,C]
+ * should be page-locked (cudaHostAlloc / cudaHostRegister) for the copies to
+ * be asynchronous; x_dev, w_dev and y_dev are caller-owned device buffers of
+ * the same sizes.  The work is ordered after what is already queued on
+ * `stream`, and `stream` waits for the last copy back, so y_host holds the
+ * result once `stream` has completed.  The library runs the chunks on three
+ * streams of its own per device, created on the first call.  Same
+ * requirements and status codes as tdc_dwconv_ws (R = S = 3 implied).
+ * Replaces the caller-side sequence H2D copy -> tma_dwconv::dwconv_ws ->
+ * D2H copy around the reference's extension call (csrc/bindings.cpp:7-8). */
+TDC_API int tdc_dwconv_ws_host(const void* x_host, const void* w_host, void* y_host,
+                               int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
+                               int64_t n_stage, void* x_dev, void* w_dev, void* y_dev,
+                               int64_t chunk_images, void* stream);
+
 /* ---- general forward ---------------------------------------------------------
  * The ws kernel widened beyond the reference's surface: any C % 8 == 0 (the
  * reference's ws requires C % 64) and an optional fused epilogue, computed

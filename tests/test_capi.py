@@ -473,3 +473,21 @@ def test_plan_balances_the_headline_shape(lib):
         assert pl["grid"] == 148 * occ
         streamed = [sum(b - a + 2 for _, a, b in segments(pl, 224, g)) for g in range(pl["grid"])]
         assert max(streamed) <= 1.03 * (64 * 44 * 224 / pl["grid"])
+
+
+def test_host_pipeline_argument_errors(lib):
+    p = C.c_void_p
+    def hp(xh=16, wh=16, yh=16, xd=16, wd=16, yd=16, N=2, H=16, W=16, Cc=64, pad=1, ns=2, chunk=0):
+        q = lambda v: p(v) if v else None
+        return lib.tdc_dwconv_ws_host(q(xh), q(wh), q(yh), i64(N), i64(H), i64(W), i64(Cc), i64(pad),
+                                      i64(ns), q(xd), q(wd), q(yd), i64(chunk), None)
+    assert hp(xh=0) == CODES["TDC_ERR_NULL_POINTER"]
+    assert hp(yd=0) == CODES["TDC_ERR_NULL_POINTER"]
+    assert hp(xd=8) == CODES["TDC_ERR_ALIGNMENT"]
+    assert hp(Cc=32) == CODES["TDC_ERR_CHANNELS"]
+    assert hp(ns=5) == CODES["TDC_ERR_N_STAGE"]
+    assert hp(pad=-1) == CODES["TDC_ERR_PAD"]
+    assert hp(chunk=-1) == CODES["TDC_ERR_BAD_SHAPE"]
+    assert hp(N=0, xh=0, wh=0, yh=0, xd=0, wd=0, yd=0) == 0  # empty: no-op
+    if not torch.cuda.is_available():
+        assert hp() == CODES["TDC_ERR_NO_DEVICE"]

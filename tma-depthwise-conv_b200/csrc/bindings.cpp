@@ -332,6 +332,39 @@ torch::Tensor dwconv_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t K, in
   return dw;
 }
 
+// ws forward on host tensors, pipelined over chunks of images (see
+// tdc_dwconv_ws_host): x_host / w_host / y_host are CPU tensors (pinned for
+// overlap), x_dev / w_dev / y_dev device buffers of the same shapes on the
+// current device; returns y_host.
+torch::Tensor dwconv_ws_host(torch::Tensor x_host, torch::Tensor w_host, torch::Tensor y_host,
+                             torch::Tensor x_dev, torch::Tensor w_dev, torch::Tensor y_dev,
+                             int64_t pad, int64_t n_stage, int64_t chunk_images) {
+  TORCH_CHECK(!x_host.is_cuda() && !w_host.is_cuda() && !y_host.is_cuda(),
+              "x_host, w_host and y_host must be CPU tensors");
+  TORCH_CHECK(x_dev.is_cuda() && w_dev.is_cuda() && y_dev.is_cuda() &&
+                  x_dev.device() == w_dev.device() && x_dev.device() == y_dev.device(),
+              "x_dev, w_dev and y_dev must live on one CUDA device");
+  for (const auto* t : {&x_host, &w_host, &y_host, &x_dev, &w_dev, &y_dev})
+    TORCH_CHECK(t->scalar_type() == torch::kHalf && t->is_contiguous(),
+                "host and device tensors must be contiguous fp16");
+  TORCH_CHECK(x_host.sizes() == x_dev.sizes() && w_host.sizes() == w_dev.sizes() &&
+                  y_host.sizes() == y_dev.sizes(),
+              "host and device tensors must have the same shapes");
+  check_ws_args(x_dev, w_dev, pad);
+  int64_t P = 0, Q = 0;
+  check_status(tdc_output_hw(x_dev.size(1), x_dev.size(2), 3, 3, pad, &P, &Q), "output size");
+  TORCH_CHECK(y_dev.dim() == 4 && y_dev.size(0) == x_dev.size(0) && y_dev.size(1) == P &&
+                  y_dev.size(2) == Q && y_dev.size(3) == x_dev.size(3),
+              "y must be [N, P, Q, C]");
+  const c10::cuda::CUDAGuard guard(x_dev.device());
+  check_status(tdc_dwconv_ws_host(x_host.data_ptr(), w_host.data_ptr(), y_host.data_ptr(),
+                                  x_dev.size(0), x_dev.size(1), x_dev.size(2), x_dev.size(3), pad,
+                                  n_stage, x_dev.data_ptr(), w_dev.data_ptr(), y_dev.data_ptr(),
+                                  chunk_images, stream_of(x_dev)),
+               "dwconv_ws_host");
+  return y_host;
+}
+
 // (code, block, stage, load) of the first pipeline-wait failure recorded on
 // `device` since the last clear; code 0 = none.  Synchronises the device.
 std::tuple<int64_t, int64_t, int64_t, int64_t> device_status(int64_t device, bool clear) {
@@ -363,6 +396,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dwconv_ws_out", &tma_dwconv::dwconv_ws_out,
         "dwconv_ws into a preallocated y [N,P,Q,C]; returns y.", pybind11::arg("x"),
         pybind11::arg("w"), pybind11::arg("y"), pybind11::arg("pad"), pybind11::arg("n_stage"));
+  m.def("dwconv_ws_host", &tma_dwconv::dwconv_ws_host,
+        "dwconv_ws on host tensors: H2D copies, kernels and D2H copies pipelined over chunks "
+        "of images; returns y_host.",
+        pybind11::arg("x_host"), pybind11::arg("w_host"), pybind11::arg("y_host"),
+        pybind11::arg("x_dev"), pybind11::arg("w_dev"), pybind11::arg("y_dev"), pybind11::arg("pad"),
+        pybind11::arg("n_stage"), pybind11::arg("chunk_images") = 0);
   m.def("dwconv_ws_withhold", &tma_dwconv::dwconv_ws_withhold,
         "dwconv_ws whose producer withholds one load so the consumer's bounded wait runs out "
         "(tests the failure path; see device_status).",

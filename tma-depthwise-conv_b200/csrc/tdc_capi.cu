@@ -24,6 +24,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "tdc_dwconv.h"
 #include "tdc_kernels.cuh"
@@ -894,6 +895,47 @@ int wgrad_s2(const void* x, const void* dy, float* dw, int64_t N, int64_t H, int
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined call with host buffers (tdc_dwconv_ws_host): the batch goes in
+// chunks of images over three library-owned streams per device, one for the
+// host->device copies, one for the kernels and one for the device->host
+// copies, chained by events, so the two copy directions and the kernels
+// overlap.  The streams and events are created once per device and reused;
+// the enqueue is serialised per device, so calls from several host threads
+// do not share an event in flight.
+// ---------------------------------------------------------------------------
+struct HostPipe {
+  std::mutex m;
+  bool ready = false;
+  cudaStream_t s[3] = {nullptr, nullptr, nullptr};  // h2d, kernels, d2h
+  cudaEvent_t start = nullptr, end = nullptr;
+  std::vector<cudaEvent_t> copied, computed;        // per chunk
+};
+HostPipe g_pipe[kMaxDevices];
+
+cudaError_t pipe_events(std::vector<cudaEvent_t>& v, size_t n) {
+  while (v.size() < n) {
+    cudaEvent_t e;
+    const cudaError_t r = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    if (r != cudaSuccess) return r;
+    v.push_back(e);
+  }
+  return cudaSuccess;
+}
+
+cudaError_t pipe_ready(HostPipe& hp) {
+  if (hp.ready) return cudaSuccess;
+  for (auto& st : hp.s) {
+    if (st) continue;
+    const cudaError_t r = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (r != cudaSuccess) return r;
+  }
+  cudaError_t r = hp.start ? cudaSuccess : cudaEventCreateWithFlags(&hp.start, cudaEventDisableTiming);
+  if (r == cudaSuccess && !hp.end) r = cudaEventCreateWithFlags(&hp.end, cudaEventDisableTiming);
+  hp.ready = r == cudaSuccess;
+  return r;
+}
+
 }  // namespace
 
 extern "C" {
@@ -957,6 +999,67 @@ TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y, int64_t N, int6
                           int64_t C, int64_t R, int64_t S, int64_t pad, int64_t n_stage,
                           void* stream) {
   return ws_common(x, w, y, N, H, W, C, R, S, pad, n_stage, nullptr, false, -1, 0, stream);
+}
+
+TDC_API int tdc_dwconv_ws_host(const void* x_host, const void* w_host, void* y_host,
+                               int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
+                               int64_t n_stage, void* x_dev, void* w_dev, void* y_dev,
+                               int64_t chunk_images, void* stream) {
+  int64_t P = 0, Q = 0;
+  bool empty = false;
+  int rc = validate(x_dev, w_dev, y_dev, N, H, W, C, 3, 3, pad, tdc::kBlockC, &P, &Q, &empty);
+  if (rc != TDC_OK) return rc;
+  if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
+  if (chunk_images < 0) return TDC_ERR_BAD_SHAPE;
+  if (empty) return TDC_OK;
+  if (!x_host || !w_host || !y_host) return TDC_ERR_NULL_POINTER;
+  rc = check_ws_limits(N, H, W, C, P, Q);
+  if (rc != TDC_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  int devi = -1;
+  rc = current_device(&dev, &devi);
+  if (rc != TDC_OK) return rc;
+  const int64_t chunk = chunk_images > 0 ? std::min(chunk_images, N)
+                                         : std::max<int64_t>(1, (N + 15) / 16);
+  const int64_t chunks = (N + chunk - 1) / chunk;
+  const size_t x_img = size_t(H) * W * C * 2, y_img = size_t(P) * Q * C * 2;
+  auto* xh = static_cast<const uint8_t*>(x_host);
+  auto* xd = static_cast<uint8_t*>(x_dev);
+  auto* yh = static_cast<uint8_t*>(y_host);
+  auto* yd = static_cast<uint8_t*>(y_dev);
+  cudaStream_t caller = static_cast<cudaStream_t>(stream);
+  HostPipe& hp = g_pipe[devi];
+  std::lock_guard<std::mutex> lock(hp.m);
+  cudaError_t e = pipe_ready(hp);
+  if (e == cudaSuccess) e = pipe_events(hp.copied, size_t(chunks));
+  if (e == cudaSuccess) e = pipe_events(hp.computed, size_t(chunks));
+  if (e != cudaSuccess) return cuda_fail(e);
+  // Everything starts after the work already queued on the caller's stream.
+  e = cudaEventRecord(hp.start, caller);
+  for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(hp.s[i], hp.start, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(w_dev, w_host, size_t(9) * C * 2, cudaMemcpyHostToDevice, hp.s[0]);
+  for (int64_t i = 0; i < chunks && e == cudaSuccess; ++i) {
+    const int64_t n0 = i * chunk, n = std::min(chunk, N - n0);
+    e = cudaMemcpyAsync(xd + n0 * x_img, xh + n0 * x_img, n * x_img, cudaMemcpyHostToDevice,
+                        hp.s[0]);
+    if (e == cudaSuccess) e = cudaEventRecord(hp.copied[i], hp.s[0]);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.s[1], hp.copied[i], 0);
+    if (e != cudaSuccess) break;
+    rc = ws_common(xd + n0 * x_img, w_dev, yd + n0 * y_img, n, H, W, C, 3, 3, pad, n_stage,
+                   nullptr, false, -1, 0, hp.s[1]);
+    if (rc != TDC_OK) return rc;
+    e = cudaEventRecord(hp.computed[i], hp.s[1]);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.s[2], hp.computed[i], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(yh + n0 * y_img, yd + n0 * y_img, n * y_img, cudaMemcpyDeviceToHost,
+                          hp.s[2]);
+  }
+  // The caller's stream continues once the last result is back on the host
+  // (the d2h stream waited for every chunk's kernel, which waited for its copy).
+  if (e == cudaSuccess) e = cudaEventRecord(hp.end, hp.s[2]);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(caller, hp.end, 0);
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
 TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,

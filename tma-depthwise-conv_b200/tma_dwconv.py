@@ -20,7 +20,8 @@ import torch.nn.functional as F
 import _tma_dwconv_C as _C  # type: ignore
 
 __all__ = ["dwconv_v0", "dwconv_ws", "dwconv_ws_probe", "ref_dwconv",
-           "dwconv_ws_out", "dwconv3x3", "dwconv", "DWCONV_STAGES", "device_status", "set_wait_timeout_ns",
+           "dwconv_ws_out", "dwconv_ws_host", "dwconv3x3", "dwconv", "DWCONV_STAGES", "device_status",
+           "set_wait_timeout_ns",
            "CONSUMER_WARPS", "ACTIVATIONS"]
 
 #: Activations the general forward fuses into its epilogue.
@@ -106,6 +107,48 @@ def dwconv_ws_out(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
     """``dwconv_ws`` writing into a preallocated contiguous ``y [N,P,Q,C]``."""
     _check_ws(x, w, pad, n_stage, "dwconv_ws_out")
     return _C.dwconv_ws_out(x, w, y, int(pad), int(n_stage))
+
+
+def dwconv_ws_host(x: torch.Tensor, w: torch.Tensor, pad: int = 1, n_stage: int = 2,
+                   chunk_images: int = 0, out: torch.Tensor | None = None,
+                   device: torch.device | int | None = None, sync: bool = True) -> torch.Tensor:
+    """``dwconv_ws`` for tensors in host memory, end to end.
+
+    Copies w and x to ``device`` (default: the current CUDA device), runs the
+    ws kernel and copies y back into ``out`` (a new pinned CPU tensor when
+    None), pipelined over chunks of ``chunk_images`` images (0: N/16 rounded
+    up) so the two copy directions and the kernels overlap.  ``x`` and ``w``
+    are contiguous fp16 CPU tensors; pin ``x`` (``x.pin_memory()``) for the
+    copies to overlap.  With ``sync`` the call returns once ``out`` holds the
+    result; otherwise ``out`` is ready when the device's current stream is.
+    """
+    if x.is_cuda or w.is_cuda:
+        raise ValueError("dwconv_ws_host takes CPU tensors (use dwconv_ws for device tensors)")
+    if x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise ValueError("x and w must be fp16")
+    if x.dim() != 4 or w.dim() != 3 or x.shape[3] != w.shape[2]:
+        raise ValueError("x must be [N,H,W,C] and w [R,S,C] with the same C")
+    if x.shape[3] % 64 != 0:
+        raise ValueError("dwconv_ws_host requires C % 64 == 0")
+    if n_stage not in (2, 3, 4):
+        raise ValueError(f"n_stage must be one of {{2, 3, 4}}, got {n_stage}")
+    if pad < 0:
+        raise ValueError("pad must be non-negative")
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index))
+    N, H, W, C = x.shape
+    P, Q = H + 2 * pad - 2, W + 2 * pad - 2
+    if out is None:
+        out = torch.empty((N, P, Q, C), dtype=torch.float16, pin_memory=True)
+    x, w = x.contiguous(), w.contiguous()
+    with torch.cuda.device(dev):
+        xd = torch.empty(x.shape, dtype=torch.float16, device=dev)
+        wd = torch.empty(w.shape, dtype=torch.float16, device=dev)
+        yd = torch.empty(out.shape, dtype=torch.float16, device=dev)
+        _C.dwconv_ws_host(x, w, out, xd, wd, yd, int(pad), int(n_stage), int(chunk_images))
+        if sync:
+            torch.cuda.current_stream(dev).synchronize()
+    return out
 
 
 def dwconv_ws_probe(x: torch.Tensor, w: torch.Tensor,
