@@ -97,7 +97,7 @@ TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y,
 
 /* tdc_dwconv_ws for inputs and outputs in HOST memory: copies w and x to the
  * device, runs the ws kernel and copies y back, pipelined over chunks of
- * `chunk_images` images (0 = N/16 rounded up) so that the host->device copy
+ * `chunk_images` images (0 = N/64 rounded up) so that the host->device copy
  * of one chunk, the kernel of the previous one and the device->host copy of
  * the one before run at the same time (the two copy directions use separate
  * copy engines).  x_host [N,H,W,C], w_host [3,3,C] and y_host [N,P,Q,C]
@@ -228,11 +228,13 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
  *     with P = (H + 2*pad - K)/2 + 1 (x rows and columns that no output
  *     reads do not contribute).
  *   tdc_dwconv_bwd_weight_plan: the K = 5, 7 weight-gradient launch plan,
- *     pure host arithmetic: plan[0..7] as tdc_ws_plan (the ring holds
- *     stage_rows rows of x and of dy per stage), plan[8] = launches (the
- *     tap rows are split over them to bound the sums a lane holds),
- *     plan[9] = tap rows of the tallest launch (its x window; the ring keeps
- *     (n_stage - 1) * stage_rows >= plan[9] - 1). */
+ *     pure host arithmetic, into plan[0..10]: plan[0..7] as tdc_ws_plan (the
+ *     ring holds stage_rows rows of x and of dy per stage), plan[8] =
+ *     launches (the tap rows are split over them to bound the sums a lane
+ *     holds), plan[9] = tap rows of the tallest launch, plan[10] = dy rows a
+ *     consumer step takes (they share x rows; the step holds
+ *     plan[9] + plan[10] - 1 x rows, and the ring keeps
+ *     (n_stage - 1) * stage_rows >= plan[9] + plan[10] - 2). */
 TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx,
                                 int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
                                 int64_t stride, int64_t pad, int64_t n_stage, void* stream);
@@ -247,15 +249,18 @@ TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t 
                                        int64_t pad, int64_t n_stage, int64_t sms,
                                        int64_t ctas_per_sm, int64_t* plan);
 
-/* Launch plan of the stride-2 backward (pure host arithmetic), which = 0 for
- * the data gradient, 1 for the weight gradient; plan[0..7] as tdc_ws_plan.
+/* Launch plan of the stride-2 backward (pure host arithmetic) into
+ * plan[0..10], which = 0 for the data gradient, 1 for the weight gradient;
+ * plan[0..7] as tdc_ws_plan.
  * Data gradient: strips and bands over dx [N,H,W,C]; stage_rows counts dy
  * rows of 16 + (K-1)/2 columns; plan[8] = pairs of dx rows per pass (one
  * launch); plan[9] = (K-1)/2 + plan[8], the dy rows one pass holds (the ring
- * keeps (n_stage - 1) * stage_rows >= plan[9] - 1).  Weight gradient: strips over
- * dy [N,P,Q,C]; a stage holds stage_rows dy rows and 2*stage_rows x rows of
- * 62 + K columns; plan[8] = launches, plan[9] = tap rows of the tallest
- * launch (the ring keeps (n_stage - 1) * 2 * stage_rows >= plan[9] - 1).
+ * keeps (n_stage - 1) * stage_rows >= plan[9] - 1); plan[10] = dx rows per
+ * pass.  Weight gradient: strips over dy [N,P,Q,C]; a stage holds
+ * stage_rows dy rows and 2*stage_rows x rows of 62 + K columns; plan[8] =
+ * launches, plan[9] = tap rows of the tallest launch, plan[10] = dy rows a
+ * consumer step takes (the step holds 2*(plan[10] - 1) + plan[9] x rows, and
+ * the ring keeps (n_stage - 1) * 2 * stage_rows >= that - 1).
  * No counterpart in the reference. */
 TDC_API int tdc_dwconv_bwd_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
                                    int64_t pad, int64_t n_stage, int64_t which, int64_t sms,

@@ -324,11 +324,11 @@ def test_kxk_backward_argument_errors(lib):
 
 
 def _wgrad_plan(lib, N, H, W, Cc, K, pad, ns, sms=148, occ=3):
-    out = (i64 * 10)()
+    out = (i64 * 11)()
     assert lib.tdc_dwconv_bwd_weight_plan(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(pad), i64(ns),
                                           i64(sms), i64(occ), out) == 0
     return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
-                     "smem", "passes", "rows"], list(out)))
+                     "smem", "passes", "rows", "step"], list(out)))
 
 
 @pytest.mark.parametrize("K", [5, 7])
@@ -339,14 +339,14 @@ def test_kxk_wgrad_plan_covers_every_dy_row_once(lib, K, N, H, W, Cc, pad, ns):
     pad = K // 2 if pad is None else pad
     pl = _wgrad_plan(lib, N, H, W, Cc, K, pad, ns)
     P, Q = H + 2 * pad - K + 1, W + 2 * pad - K + 1
-    sr, nr = pl["stage_rows"], pl["rows"]
-    assert pl["passes"] in (1, 2) and 1 <= nr <= K and pl["passes"] * nr >= K
-    assert (ns - 1) * sr >= nr - 1
+    sr, nr, dr = pl["stage_rows"], pl["rows"], pl["step"]
+    assert pl["passes"] in (1, 2) and 1 <= nr <= K and pl["passes"] * nr >= K and 1 <= dr <= 4
+    assert (ns - 1) * sr >= nr + dr - 2
     assert pl["smem"] == ns * sr * ((32 + K - 1) * 128 + 4096) + 128 <= 200 * 1024
     seen = set()
     for g in range(pl["grid"]):
         for strip, a, b in segments(pl, P, g):
-            assert max_stages_held(b - a, nr, 1, sr) <= ns
+            assert max_stages_held(b - a, nr, 1, sr, dr) <= ns
             for r in range(a, b):
                 assert (strip, r) not in seen
                 seen.add((strip, r))
@@ -354,11 +354,11 @@ def test_kxk_wgrad_plan_covers_every_dy_row_once(lib, K, N, H, W, Cc, pad, ns):
 
 
 def _s2_plan(lib, which, N, H, W, Cc, K, pad, ns, sms=148, occ=3):
-    out = (i64 * 10)()
+    out = (i64 * 11)()
     assert lib.tdc_dwconv_bwd_s2_plan(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(pad), i64(ns),
                                       i64(which), i64(sms), i64(occ), out) == 0
     return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
-                     "smem", "passes", "rows"], list(out)))
+                     "smem", "passes", "rows", "step"], list(out)))
 
 
 def dgrad_s2_segment(h0, rows, pad, K, sr, ns, pairs):
@@ -409,7 +409,7 @@ def test_dgrad_s2_plan_covers_every_dx_row_once(lib, K, N, H, W, Cc, pad, ns):
     pad = K // 2 if pad is None else pad
     pl = _s2_plan(lib, 0, N, H, W, Cc, K, pad, ns)
     sr, half, pairs = pl["stage_rows"], (K - 1) // 2, pl["passes"]
-    assert 1 <= pairs <= 4 and pl["rows"] == half + pairs
+    assert 1 <= pairs <= 4 and pl["rows"] == half + pairs and pl["step"] == 2 * pairs
     assert (ns - 1) * sr >= pl["rows"] - 1 and 1 <= sr <= 256
     assert pl["smem"] == ns * sr * (16 + half) * 128 + 128 <= 200 * 1024
     assert pl["qstrips"] == -(-W // 32) and pl["cblocks"] == -(-Cc // 64)
@@ -451,15 +451,16 @@ def test_wgrad_s2_plan_covers_every_dy_row_once(lib, K, N, H, W, Cc, pad, ns):
     pad = K // 2 if pad is None else pad
     pl = _s2_plan(lib, 1, N, H, W, Cc, K, pad, ns)
     P = (H + 2 * pad - K) // 2 + 1
-    sr, nr = pl["stage_rows"], pl["rows"]
-    assert pl["passes"] == (2 if K == 7 else 1) and nr == (4 if K == 7 else K)
-    assert (ns - 1) * 2 * sr >= nr - 1
+    sr, nr, dr = pl["stage_rows"], pl["rows"], pl["step"]
+    assert pl["passes"] == (2 if K == 7 else 1) and nr == (4 if K == 7 else K) and 1 <= dr <= 4
+    assert (ns - 1) * 2 * sr >= 2 * (dr - 1) + nr - 1
     assert pl["smem"] == ns * sr * (2 * (62 + K) * 128 + 4096) + 128 <= 200 * 1024
     seen = set()
     for g in range(pl["grid"]):
         for strip, a, b in segments(pl, P, g):
-            # x rows: a stage holds 2*sr of them; dy row o needs x rows 2o .. 2o + nr - 1
-            assert max_stages_held(b - a, nr, 2, 2 * sr) <= ns
+            # x rows: a stage holds 2*sr of them; a step of dr dy rows from o
+            # needs x rows 2o .. 2(o + dr - 1) + nr - 1
+            assert max_stages_held(b - a, nr, 2, 2 * sr, dr) <= ns
             for r in range(a, b):
                 assert (strip, r) not in seen
                 seen.add((strip, r))

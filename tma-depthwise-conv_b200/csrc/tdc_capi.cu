@@ -572,14 +572,18 @@ int wgrad_kxk_max_rows(int K) {  // the tallest pass's x window
 
 int wgrad_kxk_row_bytes(int K) { return (tdc::kStripQ + K - 1) * tdc::kBlockC * 2 + tdc::kDyRowBytes; }
 
-// Ring of about 72 KB (3 CTAs per SM); the tallest pass's x window must fit,
-// as in the direct forward.
+// x rows one consumer step of the tallest pass holds: the tap rows of its dy
+// rows (tdc::wgrad_dy_rows of them, S x rows apart).
+int wgrad_window(int K, int S, int nr) { return S * (tdc::wgrad_dy_rows(K, S) - 1) + nr; }
+
+// Ring of about 72 KB (3 CTAs per SM); the tallest pass's step window must
+// fit, as in the direct forward.
 int wgrad_kxk_stage_rows(int K, int64_t n_stage) {
   const int ns = int(n_stage);
-  const int nr = wgrad_kxk_max_rows(K);
+  const int win = wgrad_window(K, 1, wgrad_kxk_max_rows(K));
   const int ring_rows = std::max(ns, (72 * 1024) / wgrad_kxk_row_bytes(K));
   const int sr = std::max(1, ring_rows / ns);
-  return std::max(sr, (nr - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
+  return std::max(sr, (win - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
 }
 
 WsPlan make_wgrad_kxk_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int64_t n_stage,
@@ -810,14 +814,14 @@ int wgrad_s2_max_rows(int K) { return K == 3 ? WgradPasses<3>::kNR[0] : wgrad_kx
 // One stage row = 2 x rows of S*31 + K = 62 + K columns and 1 dy row.
 int wgrad_s2_row_bytes(int K) { return 2 * (62 + K) * tdc::kBlockC * 2 + tdc::kDyRowBytes; }
 
-// Ring of about 72 KB; the tallest pass's x window (its tap rows) must fit:
-// (n_stage - 1) * 2 * sr >= rows - 1.
+// Ring of about 72 KB; the tallest pass's step window of x rows must fit:
+// (n_stage - 1) * 2 * sr >= window - 1.
 int wgrad_s2_stage_rows(int K, int64_t n_stage) {
   const int ns = int(n_stage);
-  const int nr = wgrad_s2_max_rows(K);
+  const int win = wgrad_window(K, 2, wgrad_s2_max_rows(K));
   const int ring_rows = std::max(ns, (72 * 1024) / wgrad_s2_row_bytes(K));
   const int sr = std::max(1, ring_rows / ns);
-  return std::max(sr, (nr - 1 + 2 * (ns - 1) - 1) / (2 * (ns - 1)));
+  return std::max(sr, (win - 1 + 2 * (ns - 1) - 1) / (2 * (ns - 1)));
 }
 
 WsPlan make_wgrad_s2_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int64_t n_stage,
@@ -1019,8 +1023,11 @@ TDC_API int tdc_dwconv_ws_host(const void* x_host, const void* w_host, void* y_h
   int devi = -1;
   rc = current_device(&dev, &devi);
   if (rc != TDC_OK) return rc;
+  // Default: N/64 images per chunk (one image at N <= 64: measured on
+  // 64 x 224 x 336 x 256, 1 / 2 / 4 / 8 / 16 images per chunk took 52.0 /
+  // 52.6 / 54.5 / 56.4 / 60.8 ms; the copies alone 44.4 ms H2D, 43.1 ms D2H).
   const int64_t chunk = chunk_images > 0 ? std::min(chunk_images, N)
-                                         : std::max<int64_t>(1, (N + 15) / 16);
+                                         : std::max<int64_t>(1, (N + 63) / 64);
   const int64_t chunks = (N + chunk - 1) / chunk;
   const size_t x_img = size_t(H) * W * C * 2, y_img = size_t(P) * Q * C * 2;
   auto* xh = static_cast<const uint8_t*>(x_host);
@@ -1210,6 +1217,7 @@ TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t 
   plan[7] = int64_t(pl.smem);
   plan[8] = wgrad_kxk_passes(int(K));
   plan[9] = wgrad_kxk_max_rows(int(K));
+  plan[10] = tdc::wgrad_dy_rows(int(K), 1);
   return TDC_OK;
 }
 
@@ -1235,6 +1243,7 @@ TDC_API int tdc_dwconv_bwd_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, i
   plan[7] = int64_t(pl.smem);
   plan[8] = which == 0 ? tdc::dgrad_s2_pairs(int(K)) : wgrad_s2_passes(int(K));
   plan[9] = which == 0 ? dgrad_s2_window(int(K)) : wgrad_s2_max_rows(int(K));
+  plan[10] = which == 0 ? 2 * tdc::dgrad_s2_pairs(int(K)) : tdc::wgrad_dy_rows(int(K), 2);
   return TDC_OK;
 }
 

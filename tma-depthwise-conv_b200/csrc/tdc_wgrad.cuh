@@ -240,6 +240,22 @@ __global__ void __launch_bounds__(kWsThreads, 1) dwconv_wgrad_kernel(
 // slices hold all K*K taps (partial[cta][warp][K*K][C]); a launch zeroes and
 // fills only its rows' taps, and the reduction of the 3x3 kernel sums them.
 // ============================================================================
+// dy rows a consumer step takes (they share the x rows of their windows, so
+// an x row is read from shared memory once per step instead of once per dy
+// row).  Measured at 64 x 224 x 336 x 256, best n_stage each (us, 1 / 2 / 3
+// rows): stride 1 5x5 1812 / 1559 / 1479, 7x7 3165 / 2938 / 2840; stride 2
+// (windows two x rows taller per extra dy row) 3x3 458 / 502 / 551, 5x5
+// 633 / 675 / 793, 7x7 1101 / 1278 / 1288.
+#ifndef TDC_WGRAD_DY_ROWS_S1
+#define TDC_WGRAD_DY_ROWS_S1 3
+#endif
+#ifndef TDC_WGRAD_DY_ROWS_S2
+#define TDC_WGRAD_DY_ROWS_S2 1
+#endif
+__host__ __device__ constexpr int wgrad_dy_rows(int K, int S) {
+  return K > 0 && S == 1 ? TDC_WGRAD_DY_ROWS_S1 : TDC_WGRAD_DY_ROWS_S2;
+}
+
 template <int K, int S = 1>
 struct WgradGeom {
   static constexpr int kXCols = S * (kStripQ - 1) + K;        // x columns of a strip
@@ -340,6 +356,8 @@ __global__ void __launch_bounds__(kWsThreads, 3)
   }
 
   // ------------------------------ consumers ------------------------------
+  constexpr int DR = wgrad_dy_rows(K, S);
+  constexpr int kWin = S * (DR - 1) + NR;  // x rows of one step
   const int cw = warp - 1;
   SegmentIter it(blockIdx.x, gridDim.x);
   Segment sg;
@@ -348,7 +366,11 @@ __global__ void __launch_bounds__(kWsThreads, 3)
   for (int k = 0; k < 2 * NR * K; ++k) acc[k] = 0.f;
   int cur_cb = -1;
   bool failed = false;
-  uint32_t seq = 0;  // ring stages this warp has consumed
+  // Next ring stage to acquire / release, as slot and phase (no division).
+  int acq_slot = 0, rel_slot = 0;
+  uint32_t acq_phase = 0;
+  int seg_slot = 0;  // slot of the current segment's first stage
+  const int xs = S * sr;  // x rows per stage
 
   float* slice = cta_slice + int64_t(cw) * (K * K) * g.C + int64_t(R0) * K * g.C;
   auto flush = [&](int cb) {
@@ -373,37 +395,49 @@ __global__ void __launch_bounds__(kWsThreads, 3)
       cur_cb = sg.cb;
     }
     const int rows_in = S * (sg.rows - 1) + NR;  // x rows of the segment
-    const int nst = (rows_in + S * sr - 1) / (S * sr);
+    const int nst = (rows_in + xs - 1) / xs;
     const bool active = sg.qs * kStripQ + cw * kColsPerWarp < g.Q;  // warp-uniform
     int acquired = 0, released = 0;
-    int rr0 = int(seq % NS) * S * sr;  // x ring row of dy row o's first x row
-    int dr0 = int(seq % NS) * sr;      // dy ring row of dy row o
-    for (int o = 0; o < sg.rows; ++o) {
-      const int need = min(nst, (S * o + NR - 1) / (S * sr) + 1);
-      for (; acquired < need; ++acquired) {
-        const uint32_t k = seq + uint32_t(acquired);
-        const bool got = mbar_wait_bounded(smem_addr(&full_bar[k % NS]), (k / NS) & 1u,
-                                           &abort_flag, true, g.timeout_ns);
+    int acq_end = 0;   // x rows covered by the acquired stages
+    int rel_end = xs;  // x rows up to the end of stage `released`
+    int rr0 = seg_slot * xs;  // x ring row of step's first dy row's first x row
+    int dr0 = seg_slot * sr;  // dy ring row of the step's first dy row
+    for (int o = 0; o < sg.rows; o += DR) {
+      const int nout = min(DR, sg.rows - o);  // dy rows of this step
+      const int last_x = S * (o + nout - 1) + NR - 1;
+      while (acquired < nst && acq_end <= last_x) {
+        const bool got = mbar_wait_bounded(smem_addr(&full_bar[acq_slot]), acq_phase, &abort_flag,
+                                           true, g.timeout_ns);
         if (__any_sync(0xffffffffu, !got)) {
           if (lane == 0 && !abort_flag) {
-            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, int(k % NS), -1);
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1);
             abort_flag = 1;
           }
           failed = true;
           break;
         }
+        ++acquired;
+        acq_end += xs;
+        if (++acq_slot == NS) { acq_slot = 0; acq_phase ^= 1u; }
       }
       if (failed) break;
       if (active) {
         // dy columns past Q were zero-filled by the copy.
-        const uint32_t* dsrc = reinterpret_cast<const uint32_t*>(
-            dy_ring_ptr + dr0 * kDyRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
-        uint32_t dyr[kColsPerWarp];
+        uint32_t dyr[DR][kColsPerWarp];
 #pragma unroll
-        for (int m = 0; m < kColsPerWarp; ++m) dyr[m] = dsrc[m * (kBlockC / 2)];
+        for (int t = 0; t < DR; ++t) {
+          int dr = dr0 + t;
+          if (dr >= ring_rows) dr -= ring_rows;
+          const uint32_t* dsrc = reinterpret_cast<const uint32_t*>(
+              dy_ring_ptr + dr * kDyRowBytes + (cw * kColsPerWarp) * (kBlockC * 2)) + lane;
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
-          int rr = rr0 + r;
+          for (int m = 0; m < kColsPerWarp; ++m) dyr[t][m] = t < nout ? dsrc[m * (kBlockC / 2)] : 0u;
+        }
+        // x row i of the step is tap row r = i - S*t of its dy row t.
+#pragma unroll
+        for (int i = 0; i < kWin; ++i) {
+          if (i > last_x - S * o) break;  // past the last valid dy row's window (warp-uniform)
+          int rr = rr0 + i;
           if (rr >= x_ring_rows) rr -= x_ring_rows;
           const uint32_t* xsrc = reinterpret_cast<const uint32_t*>(
               ring_ptr + rr * G::kXRowB + (S * cw * kColsPerWarp) * (kBlockC * 2)) + lane;
@@ -411,28 +445,35 @@ __global__ void __launch_bounds__(kWsThreads, 3)
 #pragma unroll
           for (int j = 0; j < G::kXWarp; ++j) xr[j] = xsrc[j * (kBlockC / 2)];
 #pragma unroll
-          for (int s2 = 0; s2 < K; ++s2)
+          for (int t = 0; t < DR; ++t) {
+            const int r = i - S * t;
+            if (r < 0 || r >= NR) continue;
 #pragma unroll
-            for (int m = 0; m < kColsPerWarp; ++m)
-              fma2_f16f32(xr[S * m + s2], dyr[m], acc[2 * (r * K + s2)],
-                          acc[2 * (r * K + s2) + 1]);
+            for (int s2 = 0; s2 < K; ++s2)
+#pragma unroll
+              for (int m = 0; m < kColsPerWarp; ++m)
+                fma2_f16f32(xr[S * m + s2], dyr[t][m], acc[2 * (r * K + s2)],
+                            acc[2 * (r * K + s2) + 1]);
+          }
         }
       }
-      // Release the stages below the next dy row's first x row (x row
-      // S*(o+1) is in stage (o+1)/sr, as dy row o+1 is).
-      const int rel_to = o == sg.rows - 1 ? nst : min(nst, (o + 1) / sr);
-      if (released < rel_to) {
+      // Release the stages wholly below the next step's first x row.
+      const int next_first = o + DR >= sg.rows ? (1 << 30) : S * (o + DR);
+      if (released < nst && rel_end <= next_first) {
         __syncwarp();
-        if (lane == 0)
-          for (int k = released; k < rel_to; ++k)
-            mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(k)) % NS]));
-        released = rel_to;
+        while (released < nst && rel_end <= next_first) {
+          if (lane == 0) mbar_arrive(smem_addr(&empty_bar[rel_slot]));
+          ++released;
+          rel_end += xs;
+          if (++rel_slot == NS) rel_slot = 0;
+        }
       }
-      rr0 += S;
+      rr0 += S * DR;
       if (rr0 >= x_ring_rows) rr0 -= x_ring_rows;
-      if (++dr0 == ring_rows) dr0 = 0;
+      dr0 += DR;
+      if (dr0 >= ring_rows) dr0 -= ring_rows;
     }
-    seq += uint32_t(nst);
+    seg_slot = acq_slot;  // the next segment starts at a fresh stage
   }
   if (cur_cb >= 0 && !failed) flush(cur_cb);
 }

@@ -41,11 +41,12 @@ GEOMETRIES = tuple(DWCONV_STAGES)
 TRAINABLE = GEOMETRIES
 
 #: n_stage of the data / weight gradient per (K, stride), measured at
-#: 64 x 224 x 336 x 256 (stride 1 data gradient: the forward's table; stride-2
-#: weight gradient, 2 / 3 / 4 stages: 3x3 546 / 470 / 465 us, 5x5 837 / 856 /
-#: 678 us, 7x7 1242 / 1177 / 1274 us).
-BWD_STAGES = {(3, 1): (DWCONV_STAGES[(3, 1)], 2), (5, 1): (DWCONV_STAGES[(5, 1)], 2),
-              (7, 1): (DWCONV_STAGES[(7, 1)], 2),
+#: 64 x 224 x 336 x 256 (stride 1 data gradient: the forward's table; weight
+#: gradient, 2 / 3 / 4 stages, us: 5x5 1618 / 1540 / 1479, 7x7 3218 / 2840 /
+#: 2890; stride 2: 3x3 526 / 467 / 458, 5x5 792 / 806 / 633, 7x7 1184 / 1101 /
+#: 1119).
+BWD_STAGES = {(3, 1): (DWCONV_STAGES[(3, 1)], 2), (5, 1): (DWCONV_STAGES[(5, 1)], 4),
+              (7, 1): (DWCONV_STAGES[(7, 1)], 3),
               (3, 2): (2, 4), (5, 2): (2, 4), (7, 2): (2, 3)}
 assert set(BWD_STAGES) == set(GEOMETRIES)
 

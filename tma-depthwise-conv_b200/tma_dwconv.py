@@ -116,7 +116,7 @@ def dwconv_ws_host(x: torch.Tensor, w: torch.Tensor, pad: int = 1, n_stage: int 
 
     Copies w and x to ``device`` (default: the current CUDA device), runs the
     ws kernel and copies y back into ``out`` (a new pinned CPU tensor when
-    None), pipelined over chunks of ``chunk_images`` images (0: N/16 rounded
+    None), pipelined over chunks of ``chunk_images`` images (0: N/64 rounded
     up) so the two copy directions and the kernels overlap.  ``x`` and ``w``
     are contiguous fp16 CPU tensors; pin ``x`` (``x.pin_memory()``) for the
     copies to overlap.  With ``sync`` the call returns once ``out`` holds the
