@@ -408,7 +408,10 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
   Segment sg;
   int last_cb = -1;
   uint32_t wt[K * K];
-  uint32_t seq = 0;  // ring stages this warp has consumed (direct scheme)
+  // Direct scheme: next ring stage to acquire / release, as slot and phase
+  // (running counters, no division per pass).
+  int acq_slot = 0, rel_slot = 0, seg_slot = 0;
+  uint32_t acq_phase = 0;
   while (it.next_segment(p, sg)) {
     const int rows_in = S * (sg.rows - 1) + K;
     const int c0 = sg.cb * kBlockC;
@@ -503,35 +506,39 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
       // rows S*o .. S*o + kWindow - 1 (kWindow = S*(R-1) + K) ----
       // Each input row of the pass is read from shared memory once and fed
       // to every output of the pass it is a tap row of.  Stage k of the
-      // segment holds input rows [k*sr, (k+1)*sr) in ring slot (seq + k) %
-      // NS, so input row i sits at ring row (base + i) mod (NS * sr) with
-      // base = (seq % NS) * sr.  The warp holds the stages from the first to
-      // the last input row of the pass; the host picks sr with
+      // segment holds input rows [k*sr, (k+1)*sr) in ring slot
+      // (seg_slot + k) % NS, so input row i sits at ring row
+      // (seg_slot * sr + i) mod (NS * sr).  The warp holds the stages from
+      // the first to the last input row of the pass; the host picks sr with
       // (NS - 1) * sr >= kWindow - 1 so that window always fits the ring.
       constexpr int R = G::kRows;
       const int sr = p.stage_rows;
       const int ring_rows = NS * sr;
       const int nst = (rows_in + sr - 1) / sr;
       int acquired = 0, released = 0;
-      int rr0 = int(seq % NS) * sr;  // ring row of input row S*o
+      int acq_end = 0;   // input rows covered by the acquired stages
+      int rel_end = sr;  // input rows up to the end of stage `released`
+      int rr0 = seg_slot * sr;  // ring row of input row S*o
       for (int o = 0; o < sg.rows; o += R) {
         const int nout = min(R, sg.rows - o);  // outputs of this pass
-        const int need = min(nst, (S * (o + nout - 1) + K - 1) / sr + 1);
-        for (; acquired < need; ++acquired) {
-          const uint32_t k = seq + uint32_t(acquired);
+        const int last_in = S * (o + nout - 1) + K - 1;
+        while (acquired < nst && acq_end <= last_in) {
           [[maybe_unused]] uint64_t t0 = 0;
           if constexpr (PROBE) t0 = clock64();
-          const bool got = mbar_wait_bounded(smem_addr(&full_bar[k % NS]), (k / NS) & 1u,
+          const bool got = mbar_wait_bounded(smem_addr(&full_bar[acq_slot]), acq_phase,
                                              &abort_flag, true, p.timeout_ns);
           if (__any_sync(0xffffffffu, !got)) {
             if (lane == 0 && !abort_flag) {
-              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, int(k % NS), -1);
+              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1);
               abort_flag = 1;
             }
             failed = true;
             break;
           }
           if constexpr (PROBE) stall_cycles += clock64() - t0;
+          ++acquired;
+          acq_end += sr;
+          if (++acq_slot == NS) { acq_slot = 0; acq_phase ^= 1u; }
         }
         if (failed) break;
         if (n_valid > 0) {
@@ -569,20 +576,22 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
             store_row(o + t, a[t], res);
           }
         }
-        // Release the stages below the first input row of the next pass.
-        const int rel_to = o + R >= sg.rows ? nst : min(nst, (S * (o + R)) / sr);
-        if (released < rel_to) {
+        // Release the stages wholly below the first input row of the next pass.
+        const int next_first = o + R >= sg.rows ? (1 << 30) : S * (o + R);
+        if (released < nst && rel_end <= next_first) {
           __syncwarp();
-          if (lane == 0)
-            for (int k = released; k < rel_to; ++k)
-              mbar_arrive(smem_addr(&empty_bar[(seq + uint32_t(k)) % NS]));
-          released = rel_to;
+          while (released < nst && rel_end <= next_first) {
+            if (lane == 0) mbar_arrive(smem_addr(&empty_bar[rel_slot]));
+            ++released;
+            rel_end += sr;
+            if (++rel_slot == NS) rel_slot = 0;
+          }
         }
         rr0 += S * R;
         if (rr0 >= ring_rows) rr0 -= ring_rows;
       }
       if (failed) break;
-      seq += uint32_t(nst);
+      seg_slot = acq_slot;  // the next segment starts at a fresh stage
     } else {
       RowAcc acc[G::kNacc];
 #pragma unroll

@@ -203,7 +203,7 @@ def dwconv3x3(x: torch.Tensor, w: torch.Tensor, pad: int = 1,
 
 #: Ring stages ``dwconv`` uses when ``n_stage`` is None, per (K, stride): the
 #: fastest of {2, 3, 4} measured on a B200 at 64 x 224 x 336 x 256, pad K // 2.
-DWCONV_STAGES = {(3, 1): 2, (3, 2): 4, (5, 1): 3, (5, 2): 2, (7, 1): 3, (7, 2): 3}
+DWCONV_STAGES = {(3, 1): 2, (3, 2): 4, (5, 1): 4, (5, 2): 2, (7, 1): 3, (7, 2): 4}
 
 
 def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int = 1,
