@@ -29,6 +29,8 @@ SHAPES = [  # N, H, W, C, pad (None: K // 2)
     (4, 56, 56, 256, None),
     (1, 7, 7, 64, None),
     (2, 33, 70, 64, 2),
+    (1, 1, 1, 8, None),     # one pixel: only the centre tap reaches it
+    (2, 2, 3, 16, None),
 ]
 
 
