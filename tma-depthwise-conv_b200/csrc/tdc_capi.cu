@@ -273,12 +273,32 @@ int check_ws_limits(int64_t N, int64_t H, int64_t W, int64_t C, int64_t P, int64
   return TDC_OK;
 }
 
+// Launches a forward kernel with programmatic stream serialization: its CTAs
+// may start (barrier set-up, descriptor prefetch) while the previous kernel on
+// the stream drains; the kernel waits for that kernel (griddepcontrol.wait)
+// before its first global-memory access.  Saves part of the launch latency
+// of back-to-back calls on small problems (8 x 56 x 56 x 256: 10.25 -> 8.3-8.5
+// us per call; 64 x 224 x 336 x 256 unchanged within noise).
+template <class... Args>
+cudaError_t launch_pdl(void (*kernel)(Args...), int64_t grid, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(tdc::kWsThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <int NS, bool PROBE, int MODE = tdc::kModeWs>
 cudaError_t launch_ws_t(const CUtensorMap& map, const tdc::WsParams& prm, const WsPlan& pl,
                         cudaStream_t st) {
-  tdc::dwconv_ws_kernel<NS, PROBE, MODE>
-      <<<dim3(unsigned(pl.grid)), dim3(tdc::kWsThreads), pl.smem, st>>>(map, prm);
-  return cudaGetLastError();
+  return launch_pdl(&tdc::dwconv_ws_kernel<NS, PROBE, MODE>, pl.grid, pl.smem, st, map, prm);
 }
 
 struct Epilogue {
@@ -371,9 +391,7 @@ using GeomOccFn = cudaError_t (*)(int*, size_t);
 template <int NS, int MODE, int K, int S>
 cudaError_t geom_launch_t(const CUtensorMap& map, const tdc::WsParams& prm, int64_t grid,
                           size_t smem, cudaStream_t st) {
-  tdc::dwconv_ws_kernel<NS, false, MODE, K, S>
-      <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(map, prm);
-  return cudaGetLastError();
+  return launch_pdl(&tdc::dwconv_ws_kernel<NS, false, MODE, K, S>, grid, smem, st, map, prm);
 }
 
 template <int NS, int MODE, int K, int S>

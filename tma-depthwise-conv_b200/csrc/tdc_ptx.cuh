@@ -97,6 +97,16 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- programmatic dependent launch -----------------------------------------------
+// A kernel launched with programmatic stream serialization may start while the
+// previous kernel on its stream is still finishing.  griddep_wait blocks until
+// that kernel has completed and its memory is visible (a no-op for a kernel
+// launched without the attribute); every thread calls it before its first
+// global-memory access.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- arithmetic -------------------------------------------------------------
 // acc{0,1} = fp32(x.{lo,hi}) * fp32(w.{lo,hi}) + acc{0,1}, one rounding each.
 // The product of two fp16 values is exact in fp32, so this equals
