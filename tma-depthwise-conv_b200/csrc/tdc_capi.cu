@@ -434,6 +434,10 @@ int geom_stage_rows(int K, int S, int64_t n_stage) {
   const int ring_rows = std::max<int>(ns, (kRingRows * tdc::kRowBytes) / row_bytes);
   int sr = std::max(1, ring_rows / ns);
   if (tdc::direct_scheme(K, S)) {
+    // The extra row leaves the producer a stage to fill while the window is
+    // held.  Dropping it to fit three 7x7 stride-2 CTAs per SM (n_stage 4 x 2
+    // rows = 70.6 KB instead of 4 x 3 = 106 KB) was slower, 1109 vs 870 us:
+    // the 7-row window then holds every stage and nothing is prefetched.
     const int win = tdc::direct_window(K, S);
     sr = std::max(sr, (win - 1 + ns - 2) / (ns - 1) + (ns >= 3 ? 1 : 0));
   }
