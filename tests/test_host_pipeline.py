@@ -58,3 +58,29 @@ def test_argument_errors():
     with pytest.raises(RuntimeError, match="same shapes"):
         T._C.dwconv_ws_host(x, w, torch.empty(1, 8, 8, 64).half(), x.cuda(), w.cuda(),
                             torch.empty(1, 6, 6, 64, device="cuda").half(), 1, 2, 0)
+
+
+def test_calls_from_two_host_threads():
+    # The library's per-device copy / kernel streams are shared; concurrent
+    # callers are serialised while they enqueue, and each gets its own result.
+    import threading
+    inputs = [_inputs(4, 30, 64, 64, seed=20 + i) for i in range(2)]
+    wants = [T.dwconv_ws(x.cuda(), w.cuda(), 1, 2).cpu() for x, w in inputs]
+    outs, errors = [None, None], []
+
+    def run(i):
+        try:
+            x, w = inputs[i]
+            for _ in range(5):
+                outs[i] = T.dwconv_ws_host(x.pin_memory(), w.pin_memory(), 1, 2, chunk_images=1)
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for got, want in zip(outs, wants):
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
