@@ -148,6 +148,17 @@ TDC_API int tdc_dwconv_fwd(const void* x, const void* w, const void* bias,
                            int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
                            void* stream);
 
+/* tdc_dwconv_fwd for bfloat16 tensors: x, w, bias, residual and y hold
+ * bfloat16 (1 sign, 8 exponent, 7 mantissa bits) instead of fp16.  Same
+ * geometries, epilogue and fp32 chain; each element is widened to fp32
+ * exactly and the result is rounded to nearest-even bfloat16 once.  3x3
+ * stride 1 included.  No counterpart in the reference (fp16 only). */
+TDC_API int tdc_dwconv_fwd_bf16(const void* x, const void* w, const void* bias,
+                                const void* residual, void* y,
+                                int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
+                                void* stream);
+
 /* Launch plan tdc_dwconv_fwd would use (same layout as tdc_ws_plan's
  * plan[0..7]; pure host arithmetic).  For K >= 5 at stride 1 and 7x7 at
  * stride 2 the kernel holds the K input rows of one output row at once, and
@@ -248,6 +259,24 @@ TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw,
 TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
                                        int64_t pad, int64_t n_stage, int64_t sms,
                                        int64_t ctas_per_sm, int64_t* plan);
+
+/* The backward for bfloat16 tensors (dy, w, x, dx bfloat16; dw fp32): the
+ * same kernels and results' definitions as tdc_dwconv_bwd_data /
+ * tdc_dwconv_bwd_weight(_workspace), with bfloat16 elements and bfloat16
+ * rounding of dx.  At stride 1 the data gradient needs pad <= K - 1 (also
+ * for K = 3).  The workspace size can differ from the fp16 call's: query it
+ * with tdc_dwconv_bwd_weight_workspace_bf16.  No counterpart in the
+ * reference. */
+TDC_API int tdc_dwconv_bwd_data_bf16(const void* dy, const void* w, void* dx,
+                                     int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                     int64_t stride, int64_t pad, int64_t n_stage, void* stream);
+TDC_API int tdc_dwconv_bwd_weight_workspace_bf16(int64_t N, int64_t H, int64_t W, int64_t C,
+                                                 int64_t K, int64_t stride, int64_t pad,
+                                                 int64_t n_stage, int64_t* bytes);
+TDC_API int tdc_dwconv_bwd_weight_bf16(const void* x, const void* dy, float* dw,
+                                       int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                       int64_t stride, int64_t pad, int64_t n_stage,
+                                       void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Launch plan of the stride-2 backward (pure host arithmetic) into
  * plan[0..10], which = 0 for the data gradient, 1 for the weight gradient;

@@ -77,6 +77,31 @@ uint16_t oracle_f32_to_f16(float f) {
   }
 }
 
+/* bfloat16 -> binary32: the top 16 bits of a binary32, exact. */
+float oracle_bf16_to_f32(uint16_t b) { return bits_to_f32((uint32_t)b << 16); }
+
+/* binary32 -> bfloat16, round to nearest, ties to even (infinities kept, a NaN
+ * stays a quiet NaN of the same sign). */
+uint16_t oracle_f32_to_bf16(float f) {
+  uint32_t x = f32_to_bits(f);
+  if ((x & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((x >> 16) | 0x40u);
+  x += 0x7fffu + ((x >> 16) & 1u);
+  return (uint16_t)(x >> 16);
+}
+
+/* Element codecs of the activations and filters: fp16 (the reference's) or
+ * bf16.  Arithmetic is fp32 either way; products of two elements are exact. */
+enum { CODEC_F16 = 0, CODEC_BF16 = 1 };
+
+static void codec_lut(int codec, float* lut) {
+  for (uint32_t i = 0; i < 65536u; ++i)
+    lut[i] = codec == CODEC_BF16 ? oracle_bf16_to_f32((uint16_t)i) : oracle_f16_to_f32((uint16_t)i);
+}
+
+static uint16_t codec_round(int codec, float f) {
+  return codec == CODEC_BF16 ? oracle_f32_to_bf16(f) : oracle_f32_to_f16(f);
+}
+
 /* Output size of a stride-1 3x3 conv with symmetric padding
  * (csrc/kernel_tma_ws.cu:384-385). */
 void oracle_output_hw(int64_t H, int64_t W, int64_t pad, int64_t* P, int64_t* Q) {
@@ -215,9 +240,9 @@ int oracle_dwconv3x3_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t
  *   then bias / act / residual as oracle_dwconv3x3_ex_f16, y = f16_rne(t)
  * w: [K,K,C]; P = (H+2*pad-K)/S + 1, Q likewise.
  */
-int oracle_dwconv_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
-                         const uint16_t* residual, uint16_t* y, int64_t N, int64_t H, int64_t W,
-                         int64_t C, int64_t K, int64_t S, int64_t pad, int act, int threads) {
+static int dwconv_ex(int codec, const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                     const uint16_t* residual, uint16_t* y, int64_t N, int64_t H, int64_t W,
+                     int64_t C, int64_t K, int64_t S, int64_t pad, int act, int threads) {
   if (!x || !w || !y || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0 || K < 1 || S < 1) return -1;
   if (H + 2 * pad < K || W + 2 * pad < K) return -1;
   const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
@@ -226,7 +251,7 @@ int oracle_dwconv_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* b
   float* wf = (float*)malloc(sizeof(float) * (size_t)(K * K * C));
   float* lut = (float*)malloc(sizeof(float) * 65536);
   if (!wf || !lut) { free(wf); free(lut); return -1; }
-  for (uint32_t i = 0; i < 65536u; ++i) lut[i] = oracle_f16_to_f32((uint16_t)i);
+  codec_lut(codec, lut);
   for (int64_t i = 0; i < K * K * C; ++i) wf[i] = lut[w[i]];
 
   const int64_t WP = W + 2 * pad;
@@ -272,7 +297,7 @@ int oracle_dwconv_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* b
             if (bias) t = t + lut[bias[c]];
             t = oracle_act(t, act);
             if (res) t = t + lut[res[c]];
-            out[q * C + c] = oracle_f32_to_f16(t);
+            out[q * C + c] = codec_round(codec, t);
           }
         }
       }
@@ -283,6 +308,20 @@ int oracle_dwconv_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* b
   free(lut);
   free(wf);
   return err ? -1 : 0;
+}
+
+int oracle_dwconv_ex_f16(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                         const uint16_t* residual, uint16_t* y, int64_t N, int64_t H, int64_t W,
+                         int64_t C, int64_t K, int64_t S, int64_t pad, int act, int threads) {
+  return dwconv_ex(CODEC_F16, x, w, bias, residual, y, N, H, W, C, K, S, pad, act, threads);
+}
+
+/* The same with bfloat16 elements (x, w, bias, residual, y as bf16 bits):
+ * decoded exactly to fp32, y = bf16_rne(t).  No counterpart in the reference. */
+int oracle_dwconv_ex_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* bias,
+                          const uint16_t* residual, uint16_t* y, int64_t N, int64_t H, int64_t W,
+                          int64_t C, int64_t K, int64_t S, int64_t pad, int act, int threads) {
+  return dwconv_ex(CODEC_BF16, x, w, bias, residual, y, N, H, W, C, K, S, pad, act, threads);
 }
 
 /*
@@ -353,9 +392,8 @@ int oracle_dwconv3x3_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_
  *                 fmaf(dy[n, h+pad-(K-1-r'), w+pad-(K-1-s'), c], w[K-1-r', K-1-s', c], acc)
  * with dy = 0 outside [0,P) x [0,Q), P = H+2*pad-K+1; then f16 RNE.
  */
-int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
-                               int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
-                               int threads) {
+static int bwd_data_s1(int codec, const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
+                       int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad, int threads) {
   if (!dy || !w || !dx || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0 || K < 1) return -1;
   const int64_t P = H + 2 * pad - K + 1, Q = W + 2 * pad - K + 1;
   if (P < 1 || Q < 1) return -1;
@@ -363,7 +401,7 @@ int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* 
   float* wf = (float*)malloc(sizeof(float) * (size_t)(K * K * C));
   float* lut = (float*)malloc(sizeof(float) * 65536);
   if (!wf || !lut) { free(wf); free(lut); return -1; }
-  for (uint32_t i = 0; i < 65536u; ++i) lut[i] = oracle_f16_to_f32((uint16_t)i);
+  codec_lut(codec, lut);
   for (int64_t i = 0; i < K * K * C; ++i) wf[i] = lut[w[i]];
   int err = 0;
 #ifdef _OPENMP
@@ -396,7 +434,7 @@ int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* 
             }
           }
           uint16_t* out = dx + ((n * H + h) * W + x) * C;
-          for (int64_t c = 0; c < C; ++c) out[c] = oracle_f32_to_f16(acc[c]);
+          for (int64_t c = 0; c < C; ++c) out[c] = codec_round(codec, acc[c]);
         }
       }
     }
@@ -405,6 +443,19 @@ int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* 
   free(lut);
   free(wf);
   return err ? -1 : 0;
+}
+
+int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
+                               int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                               int threads) {
+  return bwd_data_s1(CODEC_F16, dy, w, dx, N, H, W, C, K, pad, threads);
+}
+
+/* bfloat16 elements, otherwise as oracle_dwconv_bwd_data_f16. */
+int oracle_dwconv_bwd_data_bf16(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
+                                int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                                int threads) {
+  return bwd_data_s1(CODEC_BF16, dy, w, dx, N, H, W, C, K, pad, threads);
 }
 
 /*
@@ -419,9 +470,8 @@ int oracle_dwconv_bwd_data_f16(const uint16_t* dy, const uint16_t* w, uint16_t* 
  * (the forward with flipped taps) restricted to the taps a stride-2 output
  * reaches.
  */
-int oracle_dwconv_bwd_data_s2_f16(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
-                                  int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
-                                  int threads) {
+static int bwd_data_s2(int codec, const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
+                       int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad, int threads) {
   if (!dy || !w || !dx || N < 0 || H < 1 || W < 1 || C < 0 || pad < 0 || K < 1) return -1;
   if (H + 2 * pad < K || W + 2 * pad < K) return -1;
   const int64_t P = (H + 2 * pad - K) / 2 + 1, Q = (W + 2 * pad - K) / 2 + 1;
@@ -429,7 +479,7 @@ int oracle_dwconv_bwd_data_s2_f16(const uint16_t* dy, const uint16_t* w, uint16_
   float* wf = (float*)malloc(sizeof(float) * (size_t)(K * K * C));
   float* lut = (float*)malloc(sizeof(float) * 65536);
   if (!wf || !lut) { free(wf); free(lut); return -1; }
-  for (uint32_t i = 0; i < 65536u; ++i) lut[i] = oracle_f16_to_f32((uint16_t)i);
+  codec_lut(codec, lut);
   for (int64_t i = 0; i < K * K * C; ++i) wf[i] = lut[w[i]];
   int err = 0;
 #ifdef _OPENMP
@@ -466,7 +516,7 @@ int oracle_dwconv_bwd_data_s2_f16(const uint16_t* dy, const uint16_t* w, uint16_
             }
           }
           uint16_t* out = dx + ((n * H + h) * W + v) * C;
-          for (int64_t c = 0; c < C; ++c) out[c] = oracle_f32_to_f16(acc[c]);
+          for (int64_t c = 0; c < C; ++c) out[c] = codec_round(codec, acc[c]);
         }
       }
     }
@@ -475,6 +525,19 @@ int oracle_dwconv_bwd_data_s2_f16(const uint16_t* dy, const uint16_t* w, uint16_
   free(lut);
   free(wf);
   return err ? -1 : 0;
+}
+
+int oracle_dwconv_bwd_data_s2_f16(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t N,
+                                  int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
+                                  int threads) {
+  return bwd_data_s2(CODEC_F16, dy, w, dx, N, H, W, C, K, pad, threads);
+}
+
+/* bfloat16 elements, otherwise as oracle_dwconv_bwd_data_s2_f16. */
+int oracle_dwconv_bwd_data_s2_bf16(const uint16_t* dy, const uint16_t* w, uint16_t* dx,
+                                   int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                   int64_t pad, int threads) {
+  return bwd_data_s2(CODEC_BF16, dy, w, dx, N, H, W, C, K, pad, threads);
 }
 
 /* Threads an OpenMP parallel region would use by default (1 without OpenMP). */

@@ -50,6 +50,16 @@ def load() -> ctypes.CDLL:
         lib.oracle_dwconv_bwd_data_s2_f16.argtypes = ([ctypes.c_void_p] * 3 + [i64] * 6 +
                                                      [ctypes.c_int])
         lib.oracle_dwconv_bwd_data_s2_f16.restype = ctypes.c_int
+        for name in ("oracle_dwconv_bwd_data_bf16", "oracle_dwconv_bwd_data_s2_bf16"):
+            getattr(lib, name).argtypes = [ctypes.c_void_p] * 3 + [i64] * 6 + [ctypes.c_int]
+            getattr(lib, name).restype = ctypes.c_int
+        lib.oracle_dwconv_ex_bf16.argtypes = ([ctypes.c_void_p] * 5 + [i64] * 7 +
+                                              [ctypes.c_int, ctypes.c_int])
+        lib.oracle_dwconv_ex_bf16.restype = ctypes.c_int
+        lib.oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
+        lib.oracle_bf16_to_f32.restype = ctypes.c_float
+        lib.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
+        lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
         lib.oracle_dwconv3x3_bwd_data_f16.argtypes = [ctypes.c_void_p] * 3 + [i64] * 5 + [ctypes.c_int]
         lib.oracle_dwconv3x3_bwd_data_f16.restype = ctypes.c_int
         lib.oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
@@ -152,6 +162,78 @@ def dwconv_k_f16(x: np.ndarray, w: np.ndarray, pad: int, stride: int = 1,
     if rc != 0:
         raise RuntimeError("oracle_dwconv_ex_f16 failed")
     return y
+
+
+def _bits(a: np.ndarray, shape=None) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    if a.dtype not in (np.uint16, np.int16):
+        raise ValueError("bfloat16 data is passed as its 16-bit patterns (uint16 / int16)")
+    a = a.view(np.uint16)
+    if shape is not None and a.shape != shape:
+        raise ValueError(f"expected shape {shape}, got {a.shape}")
+    return a
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    """bfloat16 bit patterns -> float32 values (exact)."""
+    return (_bits(bits).astype(np.uint32) << 16).view(np.float32)
+
+
+def dwconv_k_bf16(x: np.ndarray, w: np.ndarray, pad: int, stride: int = 1,
+                  bias: np.ndarray | None = None, residual: np.ndarray | None = None,
+                  activation: str = "none", threads: int = 0) -> np.ndarray:
+    """C oracle of the K x K, strided forward with bfloat16 elements: the same
+    fp32 chain and epilogue as :func:`dwconv_k_f16`, one round-to-nearest-even
+    to bfloat16 (``oracle_dwconv_ex_bf16``).  x [N,H,W,C], w [K,K,C], bias
+    [C], residual [N,P,Q,C] and the result are bfloat16 bit patterns
+    (uint16)."""
+    lib = load()
+    x = _bits(x)
+    N, H, W, C = x.shape
+    w = _bits(w)
+    K = w.shape[0]
+    if w.shape != (K, K, C):
+        raise ValueError("w must be [K,K,C]")
+    if H + 2 * pad < K or W + 2 * pad < K:
+        raise ValueError("negative output size")
+    P, Q = output_hw_k(H, W, K, stride, pad)
+    b = None if bias is None else _bits(bias, (C,))
+    r = None if residual is None else _bits(residual, (N, P, Q, C))
+    y = np.empty((N, P, Q, C), dtype=np.uint16)
+    rc = lib.oracle_dwconv_ex_bf16(x.ctypes.data, w.ctypes.data,
+                                   None if b is None else b.ctypes.data,
+                                   None if r is None else r.ctypes.data, y.ctypes.data,
+                                   N, H, W, C, K, stride, pad, ACTS[activation], int(threads))
+    if rc != 0:
+        raise RuntimeError("oracle_dwconv_ex_bf16 failed")
+    return y
+
+
+def dwconv_bwd_data_bf16(dy: np.ndarray, w: np.ndarray, pad: int, stride: int = 1,
+                         H: int | None = None, W: int | None = None,
+                         threads: int = 0) -> np.ndarray:
+    """C oracle of the data gradient with bfloat16 elements (bit patterns in
+    and out): stride 1 is the flipped-tap chain of :func:`dwconv_bwd_data_f16`,
+    stride 2 the transposed stencil of :func:`dwconv_bwd_data_s2_f16` (H, W
+    required there)."""
+    lib = load()
+    dy = _bits(dy)
+    w = _bits(w)
+    N, P, Q, C = dy.shape
+    K = w.shape[0]
+    if stride == 1:
+        H, W = P - 2 * pad + K - 1, Q - 2 * pad + K - 1
+        fn = lib.oracle_dwconv_bwd_data_bf16
+    else:
+        if H is None or W is None:
+            raise ValueError("the stride-2 data gradient needs the input H and W")
+        if ((H + 2 * pad - K) // 2 + 1, (W + 2 * pad - K) // 2 + 1) != (P, Q):
+            raise ValueError("dy does not match a stride-2 forward of an H x W input")
+        fn = lib.oracle_dwconv_bwd_data_s2_bf16
+    dx = np.empty((N, H, W, C), dtype=np.uint16)
+    if fn(dy.ctypes.data, w.ctypes.data, dx.ctypes.data, N, H, W, C, K, pad, int(threads)) != 0:
+        raise RuntimeError("oracle bf16 data gradient failed")
+    return dx
 
 
 def dwconv_k_f16_numpy(x: np.ndarray, w: np.ndarray, pad: int, stride: int = 1) -> np.ndarray:

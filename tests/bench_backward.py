@@ -1,7 +1,7 @@
 """Backward of the depthwise K x K (stride 1 or 2) vs cuDNN, on one GPU.
 
     python tests/bench_backward.py [--images 64] [--K 3] [--stride 1] [--n-stage 2]
-                                   [--wgrad-n-stage S]
+                                   [--wgrad-n-stage S] [--dtype fp16|bf16]
 
 Headline shape (N x 224 x 336 x 256 fp16 input, pad K // 2; dy is
 N x P x Q x 256 with P = (224 + 2*pad - K) // stride + 1).  CUDA events, 5
@@ -49,15 +49,17 @@ def main() -> None:
     ap.add_argument("--stride", type=int, default=1, choices=[1, 2])
     ap.add_argument("--n-stage", type=int, default=2)
     ap.add_argument("--wgrad-n-stage", type=int, default=0, help="default: --n-stage")
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
     args = ap.parse_args()
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     K, S, ns = args.K, args.stride, args.n_stage
     wns = args.wgrad_n_stage or ns
     N, H, W, C, pad = args.images, 224, 336, 256, K // 2
     P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
     g = torch.Generator(device="cuda").manual_seed(0)
-    x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
-    dy = (torch.rand(N, P, Q, C, device="cuda", generator=g) * 2 - 1).half()
-    w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).half()
+    x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).to(dt)
+    dy = (torch.rand(N, P, Q, C, device="cuda", generator=g) * 2 - 1).to(dt)
+    w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).to(dt)
     xb, dyb = 2 * N * H * W * C, 2 * N * P * Q * C
     flops = 2 * N * P * Q * C * K * K
     rows = [
@@ -77,7 +79,7 @@ def main() -> None:
         us = bench_us(fn)
         out[name] = us
         nf = 2 * flops if name.startswith("cudnn") else flops
-        print(json.dumps({"variant": name, "K": K, "stride": S,
+        print(json.dumps({"variant": name, "K": K, "stride": S, "dtype": args.dtype,
                           "n_stage": wns if name == "wgrad" else ns, "images": N, "us": round(us, 1),
                           "algorithmic_GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
                           "fma_TFLOPs": round(nf / (us * 1e-6) / 1e12, 2)}), flush=True)

@@ -1,6 +1,7 @@
 """K x K taps and stride 2 (`tma_dwconv.dwconv`) vs cuDNN, on one GPU.
 
     python tests/bench_kxk.py [--images 64] [--n-stage N] [--only K,S] [--iters 20] [--no-cudnn]
+                              [--dtype fp16|bf16]
 
 Input of the headline shape (N x 224 x 336 x 256 fp16), pad K // 2, for K in
 {3, 5, 7} and stride 1 and 2.  CUDA events, 5 warm-up + 20 calls each (x is
@@ -61,15 +62,17 @@ def main() -> None:
     ap.add_argument("--no-cudnn", action="store_true")
     ap.add_argument("--only", default=None, help="one geometry, e.g. 7,1 (K,stride)")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
     args = ap.parse_args()
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     N, H, W, C = args.images, 224, 336, 256
     hbm = hbm_peak_gbps()
     g = torch.Generator(device="cuda").manual_seed(0)
-    x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
+    x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).to(dt)
     xc = x.permute(0, 3, 1, 2)  # channels-last NCHW view
     only = tuple(int(v) for v in args.only.split(",")) if args.only else None
     for K in (3, 5, 7):
-        w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).half()
+        w = ((torch.rand(K, K, C, device="cuda", generator=g) * 2 - 1) / K).to(dt)
         wc = w.permute(2, 0, 1).unsqueeze(1).contiguous(memory_format=torch.channels_last)
         for S in (1, 2):
             if only is not None and (K, S) != only:
@@ -82,7 +85,8 @@ def main() -> None:
             flops = 2 * N * P * Q * C * K * K
             t_hbm = nbytes / (hbm * 1e9) * 1e6
             t_fma = flops / (FMA_PEAK_TFLOPS * 1e12) * 1e6
-            row = {"K": K, "stride": S, "images": N, "n_stage": ns, "us": round(us, 1),
+            row = {"K": K, "stride": S, "dtype": args.dtype, "images": N, "n_stage": ns,
+                   "us": round(us, 1),
                    "GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
                    "fma_TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
                    "bound": "hbm" if t_hbm >= t_fma else "fp32_fma",

@@ -29,6 +29,20 @@ void check_common(const torch::Tensor& x, const torch::Tensor& w) {
   TORCH_CHECK(x.device() == w.device(), "x and w must be on the same device");
 }
 
+// The K x K forward and the backward take fp16 or bfloat16 (x and w alike);
+// returns true for bfloat16.
+bool check_common_16(const torch::Tensor& x, const torch::Tensor& w, const char* xname) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda(), "tensors must live on CUDA");
+  TORCH_CHECK(x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16, xname,
+              " must be fp16 or bf16");
+  TORCH_CHECK(w.scalar_type() == x.scalar_type(), "w must have ", xname, "'s dtype");
+  TORCH_CHECK(x.dim() == 4, xname, " must be 4-D NHWC");
+  TORCH_CHECK(w.dim() == 3, "w must be [R,S,C]");
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous(), xname, "/w must be contiguous");
+  TORCH_CHECK(x.device() == w.device(), xname, " and w must be on the same device");
+  return x.scalar_type() == torch::kBFloat16;
+}
+
 void check_status(int rc, const char* what) {
   if (rc == TDC_OK) return;
   if (rc == TDC_ERR_CUDA) {
@@ -178,7 +192,7 @@ torch::Tensor dwconv3x3(torch::Tensor x, torch::Tensor w, std::optional<torch::T
 torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
                        std::optional<torch::Tensor> residual, int64_t stride, int64_t pad,
                        int64_t act, int64_t n_stage) {
-  check_common(x, w);
+  const bool bf16 = check_common_16(x, w, "x");
   const int64_t K = w.size(0);
   TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7), "w must be [K,K,C] with K in {3, 5, 7}");
   TORCH_CHECK(w.size(2) == x.size(3), "channel mismatch");
@@ -196,21 +210,21 @@ torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Te
   const void* rptr = nullptr;
   if (bias.has_value()) {
     const auto& b = *bias;
-    TORCH_CHECK(b.is_cuda() && b.device() == x.device() && b.scalar_type() == torch::kHalf &&
+    TORCH_CHECK(b.is_cuda() && b.device() == x.device() && b.scalar_type() == x.scalar_type() &&
                     b.is_contiguous() && b.dim() == 1 && b.size(0) == x.size(3),
-                "bias must be a contiguous fp16 [C] tensor on x's device");
+                "bias must be a contiguous [C] tensor of x's dtype on x's device");
     bptr = b.data_ptr();
   }
   if (residual.has_value()) {
     const auto& r = *residual;
-    TORCH_CHECK(r.is_cuda() && r.device() == x.device() && r.scalar_type() == torch::kHalf &&
+    TORCH_CHECK(r.is_cuda() && r.device() == x.device() && r.scalar_type() == x.scalar_type() &&
                     r.is_contiguous() && r.sizes() == y.sizes(),
-                "residual must be a contiguous fp16 [N,P,Q,C] tensor on x's device");
+                "residual must be a contiguous [N,P,Q,C] tensor of x's dtype on x's device");
     rptr = r.data_ptr();
   }
-  check_status(tdc_dwconv_fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0),
-                              x.size(1), x.size(2), x.size(3), K, stride, pad, act, n_stage,
-                              stream_of(x)),
+  auto* fwd = bf16 ? &tdc_dwconv_fwd_bf16 : &tdc_dwconv_fwd;
+  check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
+                   x.size(2), x.size(3), K, stride, pad, act, n_stage, stream_of(x)),
                "dwconv");
   return y;
 }
@@ -265,7 +279,7 @@ torch::Tensor dwconv3x3_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t pa
 // output); input_h / input_w < 0 pick the smaller one.
 torch::Tensor dwconv_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, int64_t stride,
                               int64_t n_stage, int64_t input_h, int64_t input_w) {
-  check_common(dy, w);
+  const bool bf16 = check_common_16(dy, w, "dy");
   const int64_t K = w.size(0);
   TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7) && w.size(2) == dy.size(3),
               "w must be [K,K,C] with K in {3, 5, 7}");
@@ -274,7 +288,8 @@ torch::Tensor dwconv_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, in
   TORCH_CHECK(pad >= 0, "pad must be non-negative");
   int64_t H, W;
   if (stride == 1) {
-    TORCH_CHECK(K == 3 || pad <= K - 1, "the ", K, "x", K, " data gradient needs pad <= ", K - 1);
+    TORCH_CHECK((K == 3 && !bf16) || pad <= K - 1, "the ", K, "x", K,
+                " data gradient needs pad <= ", K - 1);
     H = dy.size(1) - 2 * pad + K - 1;
     W = dy.size(2) - 2 * pad + K - 1;
     TORCH_CHECK(input_h < 0 || input_h == H, "input_h ", input_h, " does not match dy");
@@ -294,8 +309,9 @@ torch::Tensor dwconv_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, in
   const c10::cuda::CUDAGuard guard(dy.device());
   auto dx = torch::empty({dy.size(0), H, W, dy.size(3)}, dy.options());
   if (dx.numel() == 0 || dy.numel() == 0) return dx.zero_();
-  check_status(tdc_dwconv_bwd_data(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), dy.size(0), H, W,
-                                   dy.size(3), K, stride, pad, n_stage, stream_of(dy)),
+  auto* bwd = bf16 ? &tdc_dwconv_bwd_data_bf16 : &tdc_dwconv_bwd_data;
+  check_status(bwd(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), dy.size(0), H, W, dy.size(3), K,
+                   stride, pad, n_stage, stream_of(dy)),
                "dwconv_bwd_data");
   return dx;
 }
@@ -303,8 +319,10 @@ torch::Tensor dwconv_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, in
 torch::Tensor dwconv_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t K, int64_t pad,
                                 int64_t stride, int64_t n_stage) {
   TORCH_CHECK(x.is_cuda() && dy.is_cuda() && x.device() == dy.device(), "tensors must live on CUDA");
-  TORCH_CHECK(x.scalar_type() == torch::kHalf && dy.scalar_type() == torch::kHalf,
-              "x and dy must be fp16");
+  TORCH_CHECK((x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16) &&
+                  dy.scalar_type() == x.scalar_type(),
+              "x and dy must be both fp16 or both bf16");
+  const bool bf16 = x.scalar_type() == torch::kBFloat16;
   TORCH_CHECK(x.dim() == 4 && dy.dim() == 4 && x.is_contiguous() && dy.is_contiguous(),
               "x and dy must be contiguous [N,H,W,C] / [N,P,Q,C]");
   TORCH_CHECK(K == 3 || K == 5 || K == 7, "K must be 3, 5 or 7, got ", K);
@@ -321,13 +339,14 @@ torch::Tensor dwconv_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t K, in
   auto dw = torch::zeros({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
   if (x.numel() == 0 || dy.numel() == 0) return dw;
   int64_t bytes = 0;
-  check_status(tdc_dwconv_bwd_weight_workspace(x.size(0), x.size(1), x.size(2), x.size(3), K,
-                                               stride, pad, n_stage, &bytes),
+  auto* wsq = bf16 ? &tdc_dwconv_bwd_weight_workspace_bf16 : &tdc_dwconv_bwd_weight_workspace;
+  check_status(wsq(x.size(0), x.size(1), x.size(2), x.size(3), K, stride, pad, n_stage, &bytes),
                "dwconv_bwd_weight");
   auto ws = torch::empty({(bytes + 3) / 4}, x.options().dtype(torch::kFloat32));
-  check_status(tdc_dwconv_bwd_weight(x.data_ptr(), dy.data_ptr(), dw.data_ptr<float>(), x.size(0),
-                                     x.size(1), x.size(2), x.size(3), K, stride, pad, n_stage,
-                                     ws.data_ptr(), bytes, stream_of(x)),
+  auto* bwd = bf16 ? &tdc_dwconv_bwd_weight_bf16 : &tdc_dwconv_bwd_weight;
+  check_status(bwd(x.data_ptr(), dy.data_ptr(), dw.data_ptr<float>(), x.size(0), x.size(1),
+                   x.size(2), x.size(3), K, stride, pad, n_stage, ws.data_ptr(), bytes,
+                   stream_of(x)),
                "dwconv_bwd_weight");
   return dw;
 }

@@ -48,19 +48,22 @@ struct DeviceInfo {
   int status = TDC_ERR_NO_DEVICE;
   int sms = 0;
   int ws_occupancy[3][4] = {};  // [n_stage-2][ws, probe, general, epilogue]
-  int wgrad_occupancy[3] = {};  // [n_stage-2]
+  int wgrad_occupancy[2][3] = {};  // [element type][n_stage-2]
 };
 DeviceInfo g_dev[kMaxDevices];
 
 constexpr int kMaxDynSmem = 200 * 1024;
 
+// Element type of a call: 0 = fp16 (the reference's), 1 = bfloat16.
+constexpr int kF16 = 0, kBF16 = 1;
+
 int stage_rows_for(int64_t n_stage);
 
 int wgrad_stage_rows(int64_t n_stage);
 
-template <int NS>
+template <int NS, class E>
 cudaError_t prepare_wgrad(int* occ) {
-  auto* k = &tdc::dwconv_wgrad_kernel<NS>;
+  auto* k = &tdc::dwconv_wgrad_kernel<NS, E>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   if (e != cudaSuccess) return e;
   const size_t smem = size_t(NS) * wgrad_stage_rows(NS) * (tdc::kRowBytes + tdc::kDyRowBytes) + 128;
@@ -122,9 +125,12 @@ int current_device(DeviceInfo** info, int* dev_out) {
     if (e2 == cudaSuccess) e2 = prepare_ws<2, false, tdc::kModeEpilogue>(&d.ws_occupancy[0][3]);
     if (e2 == cudaSuccess) e2 = prepare_ws<3, false, tdc::kModeEpilogue>(&d.ws_occupancy[1][3]);
     if (e2 == cudaSuccess) e2 = prepare_ws<4, false, tdc::kModeEpilogue>(&d.ws_occupancy[2][3]);
-    if (e2 == cudaSuccess) e2 = prepare_wgrad<2>(&d.wgrad_occupancy[0]);
-    if (e2 == cudaSuccess) e2 = prepare_wgrad<3>(&d.wgrad_occupancy[1]);
-    if (e2 == cudaSuccess) e2 = prepare_wgrad<4>(&d.wgrad_occupancy[2]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<2, tdc::F16>(&d.wgrad_occupancy[kF16][0]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<3, tdc::F16>(&d.wgrad_occupancy[kF16][1]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<4, tdc::F16>(&d.wgrad_occupancy[kF16][2]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<2, tdc::BF16>(&d.wgrad_occupancy[kBF16][0]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<3, tdc::BF16>(&d.wgrad_occupancy[kBF16][1]);
+    if (e2 == cudaSuccess) e2 = prepare_wgrad<4, tdc::BF16>(&d.wgrad_occupancy[kBF16][2]);
     if (e2 != cudaSuccess) {
       t_last_cuda_error = int(e2);
       d.status = TDC_ERR_CUDA;
@@ -238,7 +244,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // elements read 0.  Stores the CUresult of a failed encode for
 // tdc_last_cuda_error.
 int encode_nhwc_map(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W, int64_t C,
-                    int box_cols, int box_rows) {
+                    int box_cols, int box_rows, int dt = kF16) {
   auto fn = get_encode_fn();
   if (!fn) return TDC_ERR_TMA_ENCODE;
   const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
@@ -246,7 +252,8 @@ int encode_nhwc_map(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64
   const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(box_cols), cuuint32_t(box_rows),
                              1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(t), dims, strides,
+  CUresult r = fn(map, dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  4, const_cast<void*>(t), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) t_last_cuda_error = int(r);
@@ -261,8 +268,8 @@ int encode_x_map(CUtensorMap* map, const void* x, int64_t N, int64_t H, int64_t 
 
 // dy [N,P,Q,C] of the weight gradients: 32 columns (one strip).
 int encode_dy_map(CUtensorMap* map, const void* dy, int64_t N, int64_t P, int64_t Q, int64_t C,
-                  int stage_rows) {
-  return encode_nhwc_map(map, dy, N, P, Q, C, tdc::kStripQ, stage_rows);
+                  int stage_rows, int dt = kF16) {
+  return encode_nhwc_map(map, dy, N, P, Q, C, tdc::kStripQ, stage_rows, dt);
 }
 
 // Limits of the descriptor and of the 32-bit fields the kernel keeps.
@@ -388,36 +395,39 @@ using GeomLaunchFn = cudaError_t (*)(const CUtensorMap&, const tdc::WsParams&, i
                                      cudaStream_t);
 using GeomOccFn = cudaError_t (*)(int*, size_t);
 
-template <int NS, int MODE, int K, int S>
+template <int NS, int MODE, int K, int S, class E>
 cudaError_t geom_launch_t(const CUtensorMap& map, const tdc::WsParams& prm, int64_t grid,
                           size_t smem, cudaStream_t st) {
-  return launch_pdl(&tdc::dwconv_ws_kernel<NS, false, MODE, K, S>, grid, smem, st, map, prm);
+  return launch_pdl(&tdc::dwconv_ws_kernel<NS, false, MODE, K, S, E>, grid, smem, st, map, prm);
 }
 
-template <int NS, int MODE, int K, int S>
+template <int NS, int MODE, int K, int S, class E>
 cudaError_t geom_occ_t(int* occ, size_t smem) {
-  auto* k = &tdc::dwconv_ws_kernel<NS, false, MODE, K, S>;
+  auto* k = &tdc::dwconv_ws_kernel<NS, false, MODE, K, S, E>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
 }
 
-#define TDC_GEOM_NS(FN, MODE, K, S) {FN<2, MODE, K, S>, FN<3, MODE, K, S>, FN<4, MODE, K, S>}
-#define TDC_GEOM_MODES(FN, K, S) \
-  {TDC_GEOM_NS(FN, tdc::kModeGeneral, K, S), TDC_GEOM_NS(FN, tdc::kModeEpilogue, K, S)}
-#define TDC_GEOM_TABLE(FN)                                                     \
-  {{TDC_GEOM_MODES(FN, 3, 1), TDC_GEOM_MODES(FN, 3, 2)},                       \
-   {TDC_GEOM_MODES(FN, 5, 1), TDC_GEOM_MODES(FN, 5, 2)},                       \
-   {TDC_GEOM_MODES(FN, 7, 1), TDC_GEOM_MODES(FN, 7, 2)}}
-// [K index: 3, 5, 7][stride - 1][mode: general, epilogue][n_stage - 2]
-const GeomLaunchFn kGeomLaunch[3][2][2][3] = TDC_GEOM_TABLE(geom_launch_t);
-const GeomOccFn kGeomOcc[3][2][2][3] = TDC_GEOM_TABLE(geom_occ_t);
+#define TDC_GEOM_NS(FN, E, MODE, K, S) \
+  {FN<2, MODE, K, S, E>, FN<3, MODE, K, S, E>, FN<4, MODE, K, S, E>}
+#define TDC_GEOM_MODES(FN, E, K, S) \
+  {TDC_GEOM_NS(FN, E, tdc::kModeGeneral, K, S), TDC_GEOM_NS(FN, E, tdc::kModeEpilogue, K, S)}
+#define TDC_GEOM_TABLE(FN, E)                                                  \
+  {{TDC_GEOM_MODES(FN, E, 3, 1), TDC_GEOM_MODES(FN, E, 3, 2)},                 \
+   {TDC_GEOM_MODES(FN, E, 5, 1), TDC_GEOM_MODES(FN, E, 5, 2)},                 \
+   {TDC_GEOM_MODES(FN, E, 7, 1), TDC_GEOM_MODES(FN, E, 7, 2)}}
+// [element type][K index: 3, 5, 7][stride - 1][mode: general, epilogue][n_stage - 2]
+const GeomLaunchFn kGeomLaunch[2][3][2][2][3] = {TDC_GEOM_TABLE(geom_launch_t, tdc::F16),
+                                                 TDC_GEOM_TABLE(geom_launch_t, tdc::BF16)};
+const GeomOccFn kGeomOcc[2][3][2][2][3] = {TDC_GEOM_TABLE(geom_occ_t, tdc::F16),
+                                           TDC_GEOM_TABLE(geom_occ_t, tdc::BF16)};
 #undef TDC_GEOM_TABLE
 #undef TDC_GEOM_MODES
 #undef TDC_GEOM_NS
 
 std::mutex g_geom_mutex;
-int g_geom_occ[kMaxDevices][3][2][2][3] = {};  // 0 = not queried yet
+int g_geom_occ[kMaxDevices][2][3][2][2][3] = {};  // 0 = not queried yet
 
 int strip_in_cols(int K, int S) { return S * (tdc::kStripQ - 1) + K; }
 
@@ -454,7 +464,7 @@ WsPlan make_geom_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int S, 
 
 int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
              int64_t K, int64_t S, int64_t pad, int64_t n_stage, const Epilogue& epi,
-             void* stream) {
+             void* stream, int dt = kF16) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (S != 1 && S != 2) return TDC_ERR_STRIDE;
   if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
@@ -483,17 +493,17 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   int occ;
   {
     std::lock_guard<std::mutex> lock(g_geom_mutex);
-    occ = g_geom_occ[devi][ki][si][mi][ni];
+    occ = g_geom_occ[devi][dt][ki][si][mi][ni];
     if (occ == 0) {
-      const cudaError_t e = kGeomOcc[ki][si][mi][ni](&occ, smem);
+      const cudaError_t e = kGeomOcc[dt][ki][si][mi][ni](&occ, smem);
       if (e != cudaSuccess) return cuda_fail(e);
       occ = std::max(1, occ);
-      g_geom_occ[devi][ki][si][mi][ni] = occ;
+      g_geom_occ[devi][dt][ki][si][mi][ni] = occ;
     }
   }
   const WsPlan pl = make_geom_plan(N, P, Q, C, int(K), int(S), n_stage, dev->sms, occ);
   alignas(64) CUtensorMap map;
-  rc = encode_nhwc_map(&map, x, N, H, W, C, strip_in_cols(int(K), int(S)), stage_rows);
+  rc = encode_nhwc_map(&map, x, N, H, W, C, strip_in_cols(int(K), int(S)), stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WsParams prm{};
   prm.w = static_cast<const __half*>(w);
@@ -510,7 +520,7 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   prm.act = epi.act;
   prm.flip_taps = epi.flip_taps ? 1 : 0;
   const cudaError_t e =
-      kGeomLaunch[ki][si][mi][ni](map, prm, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
+      kGeomLaunch[dt][ki][si][mi][ni](map, prm, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
@@ -547,13 +557,13 @@ struct WgradPasses<7> {
   static constexpr int kNR[2] = {4, 3};
 };
 
-template <int NS, int K, int PASS>
+template <int NS, int K, int PASS, class E>
 cudaError_t wgrad_kxk_launch_t(const CUtensorMap& xmap, const CUtensorMap& dymap,
                                const tdc::WgradParams& g, int64_t grid, size_t smem,
                                cudaStream_t st) {
   using WP = WgradPasses<K>;
   if constexpr (PASS < WP::kCount) {
-    tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS]>
+    tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 1, E>
         <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(xmap, dymap, g);
     return cudaGetLastError();
   } else {
@@ -561,11 +571,11 @@ cudaError_t wgrad_kxk_launch_t(const CUtensorMap& xmap, const CUtensorMap& dymap
   }
 }
 
-template <int NS, int K, int PASS>
+template <int NS, int K, int PASS, class E>
 cudaError_t wgrad_kxk_occ_t(int* occ, size_t smem) {
   using WP = WgradPasses<K>;
   if constexpr (PASS < WP::kCount) {
-    auto* k = &tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS]>;
+    auto* k = &tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 1, E>;
     cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
     if (e != cudaSuccess) return e;
@@ -576,16 +586,18 @@ cudaError_t wgrad_kxk_occ_t(int* occ, size_t smem) {
   }
 }
 
-#define TDC_WGRAD_NS(FN, K, PASS) {FN<2, K, PASS>, FN<3, K, PASS>, FN<4, K, PASS>}
-#define TDC_WGRAD_TABLE(FN)                                         \
-  {{TDC_WGRAD_NS(FN, 5, 0), TDC_WGRAD_NS(FN, 5, 1)},                \
-   {TDC_WGRAD_NS(FN, 7, 0), TDC_WGRAD_NS(FN, 7, 1)}}
-// [K index: 5, 7][pass][n_stage - 2]
-const WgradLaunchFn kWgradKxkLaunch[2][2][3] = TDC_WGRAD_TABLE(wgrad_kxk_launch_t);
-const GeomOccFn kWgradKxkOcc[2][2][3] = TDC_WGRAD_TABLE(wgrad_kxk_occ_t);
+#define TDC_WGRAD_NS(FN, E, K, PASS) {FN<2, K, PASS, E>, FN<3, K, PASS, E>, FN<4, K, PASS, E>}
+#define TDC_WGRAD_TABLE(FN, E)                                      \
+  {{TDC_WGRAD_NS(FN, E, 5, 0), TDC_WGRAD_NS(FN, E, 5, 1)},          \
+   {TDC_WGRAD_NS(FN, E, 7, 0), TDC_WGRAD_NS(FN, E, 7, 1)}}
+// [element type][K index: 5, 7][pass][n_stage - 2]
+const WgradLaunchFn kWgradKxkLaunch[2][2][2][3] = {TDC_WGRAD_TABLE(wgrad_kxk_launch_t, tdc::F16),
+                                                   TDC_WGRAD_TABLE(wgrad_kxk_launch_t, tdc::BF16)};
+const GeomOccFn kWgradKxkOcc[2][2][2][3] = {TDC_WGRAD_TABLE(wgrad_kxk_occ_t, tdc::F16),
+                                            TDC_WGRAD_TABLE(wgrad_kxk_occ_t, tdc::BF16)};
 #undef TDC_WGRAD_TABLE
 #undef TDC_WGRAD_NS
-int g_wgrad_kxk_occ[kMaxDevices][2][3] = {};  // min over passes; guarded by g_geom_mutex
+int g_wgrad_kxk_occ[kMaxDevices][2][2][3] = {};  // min over passes; guarded by g_geom_mutex
 
 int wgrad_kxk_passes(int K) { return K == 5 ? WgradPasses<5>::kCount : WgradPasses<7>::kCount; }
 int wgrad_kxk_max_rows(int K) {  // the tallest pass's x window
@@ -619,7 +631,7 @@ WsPlan make_wgrad_kxk_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, in
 // Validates a K x K stride-1 weight-gradient call and plans its launch on the
 // current device (which it binds).
 int wgrad_kxk_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
-                   int64_t n_stage, WsPlan* pl, int64_t* P, int64_t* Q) {
+                   int64_t n_stage, WsPlan* pl, int64_t* P, int64_t* Q, int dt = kF16) {
   if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
   if (C % 8 != 0) return TDC_ERR_CHANNELS;
   if (pad < 0) return TDC_ERR_PAD;
@@ -641,16 +653,16 @@ int wgrad_kxk_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_
     // Every pass runs on the same grid (they share the workspace slices), so
     // the grid follows the pass with the lowest occupancy.
     std::lock_guard<std::mutex> lock(g_geom_mutex);
-    occ = g_wgrad_kxk_occ[devi][ki][ni];
+    occ = g_wgrad_kxk_occ[devi][dt][ki][ni];
     if (occ == 0) {
       occ = 1 << 20;
       for (int pass = 0; pass < 2; ++pass) {
         int o = 0;
-        const cudaError_t e = kWgradKxkOcc[ki][pass][ni](&o, smem);
+        const cudaError_t e = kWgradKxkOcc[dt][ki][pass][ni](&o, smem);
         if (e != cudaSuccess) return cuda_fail(e);
         occ = std::min(occ, std::max(1, o));
       }
-      g_wgrad_kxk_occ[devi][ki][ni] = occ;
+      g_wgrad_kxk_occ[devi][dt][ki][ni] = occ;
     }
   }
   *pl = make_wgrad_kxk_plan(N, *P, *Q, C, int(K), n_stage, dev->sms, occ);
@@ -670,33 +682,35 @@ int64_t wgrad_kxk_workspace_bytes(const WsPlan& pl, int64_t C, int64_t K) {
 using DgradS2LaunchFn = cudaError_t (*)(const CUtensorMap&, const tdc::DgradS2Params&, int64_t,
                                         size_t, cudaStream_t);
 
-template <int NS, int K, int PODD>
+template <int NS, int K, int PODD, class E>
 cudaError_t dgrad_s2_launch_t(const CUtensorMap& map, const tdc::DgradS2Params& g, int64_t grid,
                               size_t smem, cudaStream_t st) {
-  tdc::dwconv_dgrad_s2_kernel<NS, K, PODD>
+  tdc::dwconv_dgrad_s2_kernel<NS, K, PODD, E>
       <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(map, g);
   return cudaGetLastError();
 }
 
-template <int NS, int K, int PODD>
+template <int NS, int K, int PODD, class E>
 cudaError_t dgrad_s2_occ_t(int* occ, size_t smem) {
-  auto* k = &tdc::dwconv_dgrad_s2_kernel<NS, K, PODD>;
+  auto* k = &tdc::dwconv_dgrad_s2_kernel<NS, K, PODD, E>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
 }
 
-#define TDC_DGS2_NS(FN, K, PODD) {FN<2, K, PODD>, FN<3, K, PODD>, FN<4, K, PODD>}
-#define TDC_DGS2_TABLE(FN)                                          \
-  {{TDC_DGS2_NS(FN, 3, 0), TDC_DGS2_NS(FN, 3, 1)},                  \
-   {TDC_DGS2_NS(FN, 5, 0), TDC_DGS2_NS(FN, 5, 1)},                  \
-   {TDC_DGS2_NS(FN, 7, 0), TDC_DGS2_NS(FN, 7, 1)}}
-// [K index: 3, 5, 7][pad & 1][n_stage - 2]
-const DgradS2LaunchFn kDgradS2Launch[3][2][3] = TDC_DGS2_TABLE(dgrad_s2_launch_t);
-const GeomOccFn kDgradS2Occ[3][2][3] = TDC_DGS2_TABLE(dgrad_s2_occ_t);
+#define TDC_DGS2_NS(FN, E, K, PODD) {FN<2, K, PODD, E>, FN<3, K, PODD, E>, FN<4, K, PODD, E>}
+#define TDC_DGS2_TABLE(FN, E)                                       \
+  {{TDC_DGS2_NS(FN, E, 3, 0), TDC_DGS2_NS(FN, E, 3, 1)},            \
+   {TDC_DGS2_NS(FN, E, 5, 0), TDC_DGS2_NS(FN, E, 5, 1)},            \
+   {TDC_DGS2_NS(FN, E, 7, 0), TDC_DGS2_NS(FN, E, 7, 1)}}
+// [element type][K index: 3, 5, 7][pad & 1][n_stage - 2]
+const DgradS2LaunchFn kDgradS2Launch[2][3][2][3] = {TDC_DGS2_TABLE(dgrad_s2_launch_t, tdc::F16),
+                                                    TDC_DGS2_TABLE(dgrad_s2_launch_t, tdc::BF16)};
+const GeomOccFn kDgradS2Occ[2][3][2][3] = {TDC_DGS2_TABLE(dgrad_s2_occ_t, tdc::F16),
+                                           TDC_DGS2_TABLE(dgrad_s2_occ_t, tdc::BF16)};
 #undef TDC_DGS2_TABLE
 #undef TDC_DGS2_NS
-int g_dgrad_s2_occ[kMaxDevices][3][2][3] = {};  // guarded by g_geom_mutex
+int g_dgrad_s2_occ[kMaxDevices][2][3][2][3] = {};  // guarded by g_geom_mutex
 
 // dy columns of one 32-column dx strip (the TMA box width) and ring row bytes.
 constexpr int dgrad_s2_dy_cols(int K) { return tdc::kStripQ / 2 + (K - 1) / 2; }
@@ -745,7 +759,7 @@ int bwd_s2_shape(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t 
 }
 
 int dgrad_s2(const void* dy, const void* w, void* dx, int64_t N, int64_t H, int64_t W, int64_t C,
-             int64_t K, int64_t pad, int64_t n_stage, void* stream) {
+             int64_t K, int64_t pad, int64_t n_stage, void* stream, int dt = kF16) {
   int64_t P, Q;
   int rc = bwd_s2_shape(N, H, W, C, K, pad, n_stage, &P, &Q);
   if (rc != TDC_OK) return rc;
@@ -761,17 +775,17 @@ int dgrad_s2(const void* dy, const void* w, void* dx, int64_t N, int64_t H, int6
   int occ;
   {
     std::lock_guard<std::mutex> lock(g_geom_mutex);
-    occ = g_dgrad_s2_occ[devi][ki][pi][ni];
+    occ = g_dgrad_s2_occ[devi][dt][ki][pi][ni];
     if (occ == 0) {
-      const cudaError_t e = kDgradS2Occ[ki][pi][ni](&occ, smem);
+      const cudaError_t e = kDgradS2Occ[dt][ki][pi][ni](&occ, smem);
       if (e != cudaSuccess) return cuda_fail(e);
       occ = std::max(1, occ);
-      g_dgrad_s2_occ[devi][ki][pi][ni] = occ;
+      g_dgrad_s2_occ[devi][dt][ki][pi][ni] = occ;
     }
   }
   const WsPlan pl = make_dgrad_s2_plan(N, H, W, C, int(K), n_stage, dev->sms, occ);
   alignas(64) CUtensorMap map;
-  rc = encode_nhwc_map(&map, dy, N, P, Q, C, dgrad_s2_dy_cols(int(K)), pl.stage_rows);
+  rc = encode_nhwc_map(&map, dy, N, P, Q, C, dgrad_s2_dy_cols(int(K)), pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::DgradS2Params g{};
   g.w = static_cast<const __half*>(w);
@@ -783,17 +797,17 @@ int dgrad_s2(const void* dy, const void* w, void* dx, int64_t N, int64_t H, int6
   g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
   g.timeout_ns = uint64_t(g_timeout_ns.load());
   const cudaError_t e =
-      kDgradS2Launch[ki][pi][ni](map, g, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
+      kDgradS2Launch[dt][ki][pi][ni](map, g, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
-template <int NS, int K, int PASS>
+template <int NS, int K, int PASS, class E>
 cudaError_t wgrad_s2_launch_t(const CUtensorMap& xmap, const CUtensorMap& dymap,
                               const tdc::WgradParams& g, int64_t grid, size_t smem,
                               cudaStream_t st) {
   using WP = WgradPasses<K>;
   if constexpr (PASS < WP::kCount) {
-    tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 2>
+    tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 2, E>
         <<<dim3(unsigned(grid)), dim3(tdc::kWsThreads), smem, st>>>(xmap, dymap, g);
     return cudaGetLastError();
   } else {
@@ -801,11 +815,11 @@ cudaError_t wgrad_s2_launch_t(const CUtensorMap& xmap, const CUtensorMap& dymap,
   }
 }
 
-template <int NS, int K, int PASS>
+template <int NS, int K, int PASS, class E>
 cudaError_t wgrad_s2_occ_t(int* occ, size_t smem) {
   using WP = WgradPasses<K>;
   if constexpr (PASS < WP::kCount) {
-    auto* k = &tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 2>;
+    auto* k = &tdc::dwconv_wgrad_kxk_kernel<NS, K, WP::kR0[PASS], WP::kNR[PASS], 2, E>;
     cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
     if (e != cudaSuccess) return e;
@@ -816,17 +830,19 @@ cudaError_t wgrad_s2_occ_t(int* occ, size_t smem) {
   }
 }
 
-#define TDC_WGS2_NS(FN, K, PASS) {FN<2, K, PASS>, FN<3, K, PASS>, FN<4, K, PASS>}
-#define TDC_WGS2_TABLE(FN)                                          \
-  {{TDC_WGS2_NS(FN, 3, 0), TDC_WGS2_NS(FN, 3, 1)},                  \
-   {TDC_WGS2_NS(FN, 5, 0), TDC_WGS2_NS(FN, 5, 1)},                  \
-   {TDC_WGS2_NS(FN, 7, 0), TDC_WGS2_NS(FN, 7, 1)}}
-// [K index: 3, 5, 7][pass][n_stage - 2]
-const WgradLaunchFn kWgradS2Launch[3][2][3] = TDC_WGS2_TABLE(wgrad_s2_launch_t);
-const GeomOccFn kWgradS2Occ[3][2][3] = TDC_WGS2_TABLE(wgrad_s2_occ_t);
+#define TDC_WGS2_NS(FN, E, K, PASS) {FN<2, K, PASS, E>, FN<3, K, PASS, E>, FN<4, K, PASS, E>}
+#define TDC_WGS2_TABLE(FN, E)                                       \
+  {{TDC_WGS2_NS(FN, E, 3, 0), TDC_WGS2_NS(FN, E, 3, 1)},            \
+   {TDC_WGS2_NS(FN, E, 5, 0), TDC_WGS2_NS(FN, E, 5, 1)},            \
+   {TDC_WGS2_NS(FN, E, 7, 0), TDC_WGS2_NS(FN, E, 7, 1)}}
+// [element type][K index: 3, 5, 7][pass][n_stage - 2]
+const WgradLaunchFn kWgradS2Launch[2][3][2][3] = {TDC_WGS2_TABLE(wgrad_s2_launch_t, tdc::F16),
+                                                  TDC_WGS2_TABLE(wgrad_s2_launch_t, tdc::BF16)};
+const GeomOccFn kWgradS2Occ[2][3][2][3] = {TDC_WGS2_TABLE(wgrad_s2_occ_t, tdc::F16),
+                                           TDC_WGS2_TABLE(wgrad_s2_occ_t, tdc::BF16)};
 #undef TDC_WGS2_TABLE
 #undef TDC_WGS2_NS
-int g_wgrad_s2_occ[kMaxDevices][3][3] = {};  // min over passes; guarded by g_geom_mutex
+int g_wgrad_s2_occ[kMaxDevices][2][3][3] = {};  // min over passes; guarded by g_geom_mutex
 
 int wgrad_s2_passes(int K) {
   return K == 3 ? WgradPasses<3>::kCount : wgrad_kxk_passes(K);
@@ -857,7 +873,7 @@ WsPlan make_wgrad_s2_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int
 // Validates a stride-2 weight-gradient call and plans its launch on the
 // current device.
 int wgrad_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t pad,
-                  int64_t n_stage, WsPlan* pl, int64_t* P, int64_t* Q) {
+                  int64_t n_stage, WsPlan* pl, int64_t* P, int64_t* Q, int dt = kF16) {
   int rc = bwd_s2_shape(N, H, W, C, K, pad, n_stage, P, Q);
   if (rc != TDC_OK) return rc;
   if (N < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
@@ -870,16 +886,16 @@ int wgrad_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t
   int occ;
   {
     std::lock_guard<std::mutex> lock(g_geom_mutex);
-    occ = g_wgrad_s2_occ[devi][ki][ni];
+    occ = g_wgrad_s2_occ[devi][dt][ki][ni];
     if (occ == 0) {
       occ = 1 << 20;
       for (int pass = 0; pass < 2; ++pass) {
         int o = 0;
-        const cudaError_t e = kWgradS2Occ[ki][pass][ni](&o, smem);
+        const cudaError_t e = kWgradS2Occ[dt][ki][pass][ni](&o, smem);
         if (e != cudaSuccess) return cuda_fail(e);
         occ = std::min(occ, std::max(1, o));
       }
-      g_wgrad_s2_occ[devi][ki][ni] = occ;
+      g_wgrad_s2_occ[devi][dt][ki][ni] = occ;
     }
   }
   *pl = make_wgrad_s2_plan(N, *P, *Q, C, int(K), n_stage, dev->sms, occ);
@@ -888,19 +904,19 @@ int wgrad_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t
 
 int wgrad_s2(const void* x, const void* dy, float* dw, int64_t N, int64_t H, int64_t W, int64_t C,
              int64_t K, int64_t pad, int64_t n_stage, void* workspace, int64_t workspace_bytes,
-             void* stream) {
+             void* stream, int dt = kF16) {
   if (!x || !dy || !dw || !workspace) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(dy) || !aligned16(dw) || !aligned16(workspace))
     return TDC_ERR_ALIGNMENT;
   WsPlan pl;
   int64_t P, Q;
-  int rc = wgrad_s2_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  int rc = wgrad_s2_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q, dt);
   if (rc != TDC_OK) return rc;
   if (workspace_bytes < wgrad_kxk_workspace_bytes(pl, C, K)) return TDC_ERR_WORKSPACE;
   alignas(64) CUtensorMap xmap, dymap;
-  rc = encode_nhwc_map(&xmap, x, N, H, W, C, 62 + int(K), 2 * pl.stage_rows);
+  rc = encode_nhwc_map(&xmap, x, N, H, W, C, 62 + int(K), 2 * pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
-  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
   g.partial = static_cast<float*>(workspace);
@@ -912,7 +928,8 @@ int wgrad_s2(const void* x, const void* dy, float* dw, int64_t N, int64_t H, int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int ki = int(K / 2 - 1);
   for (int pass = 0; pass < wgrad_s2_passes(int(K)); ++pass) {
-    const cudaError_t e = kWgradS2Launch[ki][pass][n_stage - 2](xmap, dymap, g, pl.grid, pl.smem, st);
+    const cudaError_t e =
+        kWgradS2Launch[dt][ki][pass][n_stage - 2](xmap, dymap, g, pl.grid, pl.smem, st);
     if (e != cudaSuccess) return cuda_fail(e);
   }
   const int n = int(K * K * C);
@@ -1103,19 +1120,35 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
   return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, -1, 0, stream, epi);
 }
 
-TDC_API int tdc_dwconv_fwd(const void* x, const void* w, const void* bias, const void* residual,
-                           void* y, int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
-                           int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
-                           void* stream) {
+static int fwd_entry(int dt, const void* x, const void* w, const void* bias,
+                     const void* residual, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
+                     int64_t K, int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
+                     void* stream) {
   if (act < TDC_ACT_NONE || act > TDC_ACT_SILU) return TDC_ERR_ACT;
-  if (K == 3 && stride == 1)
+  if (dt == kF16 && K == 3 && stride == 1)
     return tdc_dwconv3x3_fwd(x, w, bias, residual, y, N, H, W, C, pad, act, n_stage, stream);
   Epilogue epi;
   epi.fused = true;
   epi.bias = bias;
   epi.residual = residual;
   epi.act = int(act);
-  return fwd_geom(x, w, y, N, H, W, C, K, stride, pad, n_stage, epi, stream);
+  return fwd_geom(x, w, y, N, H, W, C, K, stride, pad, n_stage, epi, stream, dt);
+}
+
+TDC_API int tdc_dwconv_fwd(const void* x, const void* w, const void* bias, const void* residual,
+                           void* y, int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                           int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
+                           void* stream) {
+  return fwd_entry(kF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad, act, n_stage,
+                   stream);
+}
+
+TDC_API int tdc_dwconv_fwd_bf16(const void* x, const void* w, const void* bias,
+                                const void* residual, void* y, int64_t N, int64_t H, int64_t W,
+                                int64_t C, int64_t K, int64_t stride, int64_t pad, int64_t act,
+                                int64_t n_stage, void* stream) {
+  return fwd_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad, act, n_stage,
+                   stream);
 }
 
 TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
@@ -1135,15 +1168,15 @@ TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int6
                    epi);
 }
 
-TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
-                                int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
-                                int64_t n_stage, void* stream) {
+static int bwd_data_entry(int dt, const void* dy, const void* w, void* dx, int64_t N, int64_t H,
+                          int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
+                          int64_t n_stage, void* stream) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
-  if (stride == 2) return dgrad_s2(dy, w, dx, N, H, W, C, K, pad, n_stage, stream);
-  if (K == 3) return tdc_dwconv3x3_bwd_data(dy, w, dx, N, H, W, C, pad, n_stage, stream);
+  if (stride == 2) return dgrad_s2(dy, w, dx, N, H, W, C, K, pad, n_stage, stream, dt);
+  if (K == 3 && dt == kF16) return tdc_dwconv3x3_bwd_data(dy, w, dx, N, H, W, C, pad, n_stage, stream);
   // pad' = K - 1 - pad must not be negative (pad above K - 1 leaves dx rows
-  // no output depends on; not supported for K > 3).
+  // no output depends on; supported by the fp16 3x3 path only).
   if (pad < 0 || pad > K - 1) return TDC_ERR_PAD;
   const int64_t P = H + 2 * pad - K + 1, Q = W + 2 * pad - K + 1;
   if (H < 1 || W < 1 || P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
@@ -1152,49 +1185,66 @@ TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx, int64_t
   epi.flip_taps = true;
   // dx[n,h,w,c] = sum_{r,s} dy[n, h+pad-r, w+pad-s, c] * w[r,s,c]
   //            = forward(dy, w[K-1-r][K-1-s], pad' = K - 1 - pad)
-  return fwd_geom(dy, w, dx, N, P, Q, C, K, 1, K - 1 - pad, n_stage, epi, stream);
+  return fwd_geom(dy, w, dx, N, P, Q, C, K, 1, K - 1 - pad, n_stage, epi, stream, dt);
 }
 
-TDC_API int tdc_dwconv_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
-                                            int64_t stride, int64_t pad, int64_t n_stage,
-                                            int64_t* bytes) {
+TDC_API int tdc_dwconv_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
+                                int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
+                                int64_t n_stage, void* stream) {
+  return bwd_data_entry(kF16, dy, w, dx, N, H, W, C, K, stride, pad, n_stage, stream);
+}
+
+TDC_API int tdc_dwconv_bwd_data_bf16(const void* dy, const void* w, void* dx, int64_t N,
+                                     int64_t H, int64_t W, int64_t C, int64_t K, int64_t stride,
+                                     int64_t pad, int64_t n_stage, void* stream) {
+  return bwd_data_entry(kBF16, dy, w, dx, N, H, W, C, K, stride, pad, n_stage, stream);
+}
+
+static int wgrad3x3_workspace(int dt, int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
+                              int64_t n_stage, int64_t* bytes);
+static int wgrad3x3(int dt, const void* x, const void* dy, float* dw, int64_t N, int64_t H,
+                    int64_t W, int64_t C, int64_t pad, int64_t n_stage, void* workspace,
+                    int64_t workspace_bytes, void* stream);
+
+static int bwd_weight_workspace_entry(int dt, int64_t N, int64_t H, int64_t W, int64_t C,
+                                      int64_t K, int64_t stride, int64_t pad, int64_t n_stage,
+                                      int64_t* bytes) {
   if (!bytes) return TDC_ERR_NULL_POINTER;
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
-  if (K == 3 && stride == 1)
-    return tdc_dwconv3x3_bwd_weight_workspace(N, H, W, C, pad, n_stage, bytes);
+  if (K == 3 && stride == 1) return wgrad3x3_workspace(dt, N, H, W, C, pad, n_stage, bytes);
   WsPlan pl;
   int64_t P, Q;
-  const int rc = stride == 2 ? wgrad_s2_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q)
-                             : wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  const int rc = stride == 2 ? wgrad_s2_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q, dt)
+                             : wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q, dt);
   if (rc != TDC_OK) return rc;
   *bytes = wgrad_kxk_workspace_bytes(pl, C, K);
   return TDC_OK;
 }
 
-TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int64_t N, int64_t H,
-                                  int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
-                                  int64_t n_stage, void* workspace, int64_t workspace_bytes,
-                                  void* stream) {
+static int bwd_weight_entry(int dt, const void* x, const void* dy, float* dw, int64_t N,
+                            int64_t H, int64_t W, int64_t C, int64_t K, int64_t stride,
+                            int64_t pad, int64_t n_stage, void* workspace, int64_t workspace_bytes,
+                            void* stream) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
   if (stride == 2)
-    return wgrad_s2(x, dy, dw, N, H, W, C, K, pad, n_stage, workspace, workspace_bytes, stream);
+    return wgrad_s2(x, dy, dw, N, H, W, C, K, pad, n_stage, workspace, workspace_bytes, stream,
+                    dt);
   if (K == 3)
-    return tdc_dwconv3x3_bwd_weight(x, dy, dw, N, H, W, C, pad, n_stage, workspace,
-                                    workspace_bytes, stream);
+    return wgrad3x3(dt, x, dy, dw, N, H, W, C, pad, n_stage, workspace, workspace_bytes, stream);
   if (!x || !dy || !dw || !workspace) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(dy) || !aligned16(dw) || !aligned16(workspace))
     return TDC_ERR_ALIGNMENT;
   WsPlan pl;
   int64_t P, Q;
-  int rc = wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q);
+  int rc = wgrad_kxk_plan(N, H, W, C, K, pad, n_stage, &pl, &P, &Q, dt);
   if (rc != TDC_OK) return rc;
   if (workspace_bytes < wgrad_kxk_workspace_bytes(pl, C, K)) return TDC_ERR_WORKSPACE;
   alignas(64) CUtensorMap xmap, dymap;
-  rc = encode_nhwc_map(&xmap, x, N, H, W, C, tdc::kStripQ + int(K) - 1, pl.stage_rows);
+  rc = encode_nhwc_map(&xmap, x, N, H, W, C, tdc::kStripQ + int(K) - 1, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
-  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
   g.partial = static_cast<float*>(workspace);
@@ -1205,8 +1255,8 @@ TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int6
   g.timeout_ns = uint64_t(g_timeout_ns.load());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int pass = 0; pass < wgrad_kxk_passes(int(K)); ++pass) {
-    const cudaError_t e =
-        kWgradKxkLaunch[K == 5 ? 0 : 1][pass][n_stage - 2](xmap, dymap, g, pl.grid, pl.smem, st);
+    const cudaError_t e = kWgradKxkLaunch[dt][K == 5 ? 0 : 1][pass][n_stage - 2](
+        xmap, dymap, g, pl.grid, pl.smem, st);
     if (e != cudaSuccess) return cuda_fail(e);
   }
   cudaError_t e;
@@ -1214,6 +1264,34 @@ TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int6
   e = tdc::launch_wgrad_reduce(static_cast<const float*>(workspace), dw,
                                 int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                            int64_t stride, int64_t pad, int64_t n_stage,
+                                            int64_t* bytes) {
+  return bwd_weight_workspace_entry(kF16, N, H, W, C, K, stride, pad, n_stage, bytes);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_workspace_bf16(int64_t N, int64_t H, int64_t W, int64_t C,
+                                                 int64_t K, int64_t stride, int64_t pad,
+                                                 int64_t n_stage, int64_t* bytes) {
+  return bwd_weight_workspace_entry(kBF16, N, H, W, C, K, stride, pad, n_stage, bytes);
+}
+
+TDC_API int tdc_dwconv_bwd_weight(const void* x, const void* dy, float* dw, int64_t N, int64_t H,
+                                  int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad,
+                                  int64_t n_stage, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+  return bwd_weight_entry(kF16, x, dy, dw, N, H, W, C, K, stride, pad, n_stage, workspace,
+                          workspace_bytes, stream);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_bf16(const void* x, const void* dy, float* dw, int64_t N,
+                                       int64_t H, int64_t W, int64_t C, int64_t K, int64_t stride,
+                                       int64_t pad, int64_t n_stage, void* workspace,
+                                       int64_t workspace_bytes, void* stream) {
+  return bwd_weight_entry(kBF16, x, dy, dw, N, H, W, C, K, stride, pad, n_stage, workspace,
+                          workspace_bytes, stream);
 }
 
 TDC_API int tdc_dwconv_bwd_weight_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
@@ -1271,7 +1349,7 @@ TDC_API int tdc_dwconv_bwd_s2_plan(int64_t N, int64_t H, int64_t W, int64_t C, i
 
 // Plan of the weight-gradient launch: the forward planner over dy's strips.
 int wgrad_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad, int64_t n_stage,
-               WsPlan* pl, int64_t* P, int64_t* Q) {
+               WsPlan* pl, int64_t* P, int64_t* Q, int dt = kF16) {
   if (N < 1 || H < 1 || W < 1 || C < 8) return TDC_ERR_BAD_SHAPE;
   if (C % 8 != 0) return TDC_ERR_CHANNELS;
   if (pad < 0) return TDC_ERR_PAD;
@@ -1285,7 +1363,8 @@ int wgrad_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad, int64_t 
   DeviceInfo* dev = nullptr;
   rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;
-  *pl = make_plan(N, *P, *Q, C, n_stage, dev->sms, std::max(1, dev->wgrad_occupancy[n_stage - 2]));
+  *pl = make_plan(N, *P, *Q, C, n_stage, dev->sms,
+                  std::max(1, dev->wgrad_occupancy[dt][n_stage - 2]));
   pl->stage_rows = wgrad_stage_rows(n_stage);
   pl->smem = size_t(n_stage) * pl->stage_rows * (tdc::kRowBytes + tdc::kDyRowBytes) + 128;
   return TDC_OK;
@@ -1295,33 +1374,44 @@ int64_t wgrad_workspace_bytes(const WsPlan& pl, int64_t C) {
   return pl.grid * tdc::kConsumerWarps * 9 * C * int64_t(sizeof(float));
 }
 
-TDC_API int tdc_dwconv3x3_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
-                                               int64_t pad, int64_t n_stage, int64_t* bytes) {
+static int wgrad3x3_workspace(int dt, int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
+                              int64_t n_stage, int64_t* bytes) {
   if (!bytes) return TDC_ERR_NULL_POINTER;
   WsPlan pl;
   int64_t P, Q;
-  const int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q);
+  const int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q, dt);
   if (rc != TDC_OK) return rc;
   *bytes = wgrad_workspace_bytes(pl, C);
   return TDC_OK;
 }
 
-TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, int64_t N,
-                                     int64_t H, int64_t W, int64_t C, int64_t pad,
-                                     int64_t n_stage, void* workspace, int64_t workspace_bytes,
-                                     void* stream) {
+extern "C++" template <class E>
+cudaError_t launch_wgrad3x3(int64_t n_stage, const CUtensorMap& xmap, const CUtensorMap& dymap,
+                            const tdc::WgradParams& g, const WsPlan& pl, cudaStream_t st) {
+  const dim3 grid(unsigned(pl.grid)), block(tdc::kWsThreads);
+  switch (n_stage) {
+    case 2: tdc::dwconv_wgrad_kernel<2, E><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+    case 3: tdc::dwconv_wgrad_kernel<3, E><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+    default: tdc::dwconv_wgrad_kernel<4, E><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
+  }
+  return cudaGetLastError();
+}
+
+static int wgrad3x3(int dt, const void* x, const void* dy, float* dw, int64_t N, int64_t H,
+                    int64_t W, int64_t C, int64_t pad, int64_t n_stage, void* workspace,
+                    int64_t workspace_bytes, void* stream) {
   if (!x || !dy || !dw || !workspace) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(dy) || !aligned16(dw) || !aligned16(workspace))
     return TDC_ERR_ALIGNMENT;
   WsPlan pl;
   int64_t P, Q;
-  int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q);
+  int rc = wgrad_plan(N, H, W, C, pad, n_stage, &pl, &P, &Q, dt);
   if (rc != TDC_OK) return rc;
   if (workspace_bytes < wgrad_workspace_bytes(pl, C)) return TDC_ERR_WORKSPACE;
   alignas(64) CUtensorMap xmap, dymap;
-  rc = encode_x_map(&xmap, x, N, H, W, C, pl.stage_rows);
+  rc = encode_nhwc_map(&xmap, x, N, H, W, C, tdc::kInCols, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
-  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
+  rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
   g.partial = static_cast<float*>(workspace);
@@ -1331,18 +1421,25 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, i
   g.full_units = pl.full_units; g.tail_strips = pl.tail_strips;
   g.timeout_ns = uint64_t(g_timeout_ns.load());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 grid(unsigned(pl.grid)), block(tdc::kWsThreads);
-  switch (n_stage) {
-    case 2: tdc::dwconv_wgrad_kernel<2><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
-    case 3: tdc::dwconv_wgrad_kernel<3><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
-    default: tdc::dwconv_wgrad_kernel<4><<<grid, block, pl.smem, st>>>(xmap, dymap, g); break;
-  }
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = dt == kBF16 ? launch_wgrad3x3<tdc::BF16>(n_stage, xmap, dymap, g, pl, st)
+                              : launch_wgrad3x3<tdc::F16>(n_stage, xmap, dymap, g, pl, st);
   if (e != cudaSuccess) return cuda_fail(e);
   const int n = int(9 * C);
   e = tdc::launch_wgrad_reduce(static_cast<const float*>(workspace), dw,
                                 int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+TDC_API int tdc_dwconv3x3_bwd_weight_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
+                                               int64_t pad, int64_t n_stage, int64_t* bytes) {
+  return wgrad3x3_workspace(kF16, N, H, W, C, pad, n_stage, bytes);
+}
+
+TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, int64_t N,
+                                     int64_t H, int64_t W, int64_t C, int64_t pad,
+                                     int64_t n_stage, void* workspace, int64_t workspace_bytes,
+                                     void* stream) {
+  return wgrad3x3(kF16, x, dy, dw, N, H, W, C, pad, n_stage, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

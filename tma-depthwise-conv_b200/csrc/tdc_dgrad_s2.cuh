@@ -112,7 +112,7 @@ __host__ __device__ __forceinline__ DgradS2Seg dgrad_s2_segment(int h0, int rows
 // PODD = pad & 1: the parity of v + pad for the warp's first column, which
 // fixes at compile time which taps (and which dy column of the lane's
 // registers) each of the 8 columns uses.
-template <int NS, int K, int PODD>
+template <int NS, int K, int PODD, class E = F16>
 __global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
     dwconv_dgrad_s2_kernel(const __grid_constant__ CUtensorMap dymap,
                            const __grid_constant__ DgradS2Params g) {
@@ -266,9 +266,9 @@ __global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
                 if (((m + PODD + s) & 1) != 0) continue;  // v + pad - s must be even
                 // dy column of (m, s) relative to the warp's first one
                 const int j = (m + PODD - s) / 2 - PODD + G::kHalf;
-                fma2_f16f32(dr[j], wt[(K - 1 - 2 * u) * K + s], ae[i].v[2 * m], ae[i].v[2 * m + 1]);
+                fma2<E>(dr[j], wt[(K - 1 - 2 * u) * K + s], ae[i].v[2 * m], ae[i].v[2 * m + 1]);
                 if (u >= 1)
-                  fma2_f16f32(dr[j], wt[(K - 2 * u) * K + s], ao[i].v[2 * m], ao[i].v[2 * m + 1]);
+                  fma2<E>(dr[j], wt[(K - 2 * u) * K + s], ao[i].v[2 * m], ao[i].v[2 * m + 1]);
               }
             }
           }
@@ -284,13 +284,13 @@ __global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
 #pragma unroll
               for (int m = 0; m < kColsPerWarp; ++m)
                 *reinterpret_cast<uint32_t*>(dst + m * dx_col_stride) =
-                    pack_half2_rn(a.v[2 * m], a.v[2 * m + 1]);
+                    pack2_rn<E>(a.v[2 * m], a.v[2 * m + 1]);
             } else {
 #pragma unroll
               for (int m = 0; m < kColsPerWarp; ++m)
                 if (m < n_valid)
                   *reinterpret_cast<uint32_t*>(dst + m * dx_col_stride) =
-                      pack_half2_rn(a.v[2 * m], a.v[2 * m + 1]);
+                      pack2_rn<E>(a.v[2 * m], a.v[2 * m + 1]);
             }
           }
         }

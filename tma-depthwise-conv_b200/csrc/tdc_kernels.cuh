@@ -269,7 +269,7 @@ static_assert(direct_window(7, 1) == Geom<7, 1>::kWindow && direct_window(7, 2) 
 // inputs are consumed left to right, so every output sees its taps in (r, s)
 // lexicographic order.  The FMAs take the fp16 operands directly
 // (fma.rn.f32.f16), issuing on both FMA pipes with no conversion instruction.
-template <int K, int S, int U>
+template <int K, int S, int U, class E>
 __device__ __forceinline__ void feed_row(const uint32_t (&xr)[Geom<K, S>::kWarpIn],
                                          const uint32_t (&wt)[K * K],
                                          RowAcc (&acc)[Geom<K, S>::kNacc]) {
@@ -290,7 +290,7 @@ __device__ __forceinline__ void feed_row(const uint32_t (&xr)[Geom<K, S>::kWarpI
           a.v[2 * m] = 0.f;
           a.v[2 * m + 1] = 0.f;
         }
-        fma2_f16f32(xr[j], wt[r * K + s], a.v[2 * m], a.v[2 * m + 1]);
+        fma2<E>(xr[j], wt[r * K + s], a.v[2 * m], a.v[2 * m + 1]);
       }
     }
   }
@@ -310,11 +310,13 @@ __host__ __device__ constexpr int ws_min_blocks() {
 // zero-fills the missing channels; their lanes neither read taps nor store)
 // and can flip the taps (the data gradient); kModeEpilogue adds the fused
 // epilogue.  kModeWs is the ws call of the reference surface (3x3, stride 1).
-template <int NS, bool PROBE, int MODE = kModeWs, int K = 3, int S = 1>
+// E (F16 / BF16) is the element type; the ws surface is fp16 only.
+template <int NS, bool PROBE, int MODE = kModeWs, int K = 3, int S = 1, class E = F16>
 __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
     dwconv_ws_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
   using G = Geom<K, S>;
   static_assert(MODE != kModeWs || (K == 3 && S == 1), "the ws surface is 3x3, stride 1");
+  static_assert(MODE != kModeWs || std::is_same_v<E, F16>, "the ws surface is fp16");
   __shared__ __align__(8) uint64_t full_bar[NS];
   __shared__ __align__(8) uint64_t empty_bar[NS];
   __shared__ volatile int abort_flag;
@@ -437,9 +439,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
     float bias0 = 0.f, bias1 = 0.f;
     if constexpr (MODE == kModeEpilogue) {
       if (p.bias != nullptr && chan_ok) {
-        const __half2 bh = *reinterpret_cast<const __half2*>(p.bias + c0 + 2 * lane);
-        bias0 = __low2float(bh);
-        bias1 = __high2float(bh);
+        unpack2<E>(*reinterpret_cast<const uint32_t*>(p.bias + c0 + 2 * lane), bias0, bias1);
       }
     }
     __half* yrow = p.y + ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
@@ -490,9 +490,10 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
         if (p.residual != nullptr) {
 #pragma unroll
           for (int m = 0; m < kColsPerWarp; ++m) {
-            const __half2 rh = *reinterpret_cast<const __half2*>(&res[m]);
-            t[2 * m] += __low2float(rh);
-            t[2 * m + 1] += __high2float(rh);
+            float r0, r1;
+            unpack2<E>(res[m], r0, r1);
+            t[2 * m] += r0;
+            t[2 * m + 1] += r1;
           }
         }
       } else {
@@ -504,7 +505,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
       for (int m = 0; m < kColsPerWarp; ++m)
         if (m < n_valid)
           *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
-              pack_half2_rn(fin.v[2 * m], fin.v[2 * m + 1]);
+              pack2_rn<E>(fin.v[2 * m], fin.v[2 * m + 1]);
     };
 
     if constexpr (G::kDirect) {
@@ -570,7 +571,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
 #pragma unroll
                 for (int m = 0; m < kColsPerWarp; ++m) {
                   if (r == 0 && s2 == 0) { a[t].v[2 * m] = 0.f; a[t].v[2 * m + 1] = 0.f; }
-                  fma2_f16f32(xr[S * m + s2], wt[r * K + s2], a[t].v[2 * m], a[t].v[2 * m + 1]);
+                  fma2<E>(xr[S * m + s2], wt[r * K + s2], a[t].v[2 * m], a[t].v[2 * m + 1]);
                 }
             }
           }
@@ -642,7 +643,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
           if constexpr (kCompletes) {
             if (i >= K - 1) load_res((i - (K - 1)) / S, res);
           }
-          feed_row<K, S, U>(xr, wt, acc);
+          feed_row<K, S, U, E>(xr, wt, acc);
           if constexpr (kCompletes) {
             if (i >= K - 1) {
               constexpr int kFin = pmod((U - (K - 1) - pmod(U - (K - 1), S)) / S, G::kNacc);

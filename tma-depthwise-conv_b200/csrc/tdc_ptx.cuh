@@ -6,6 +6,7 @@
 #include <cuda.h>        // CUtensorMap (type only; no driver symbols are linked)
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 namespace tdc {
 
@@ -126,6 +127,60 @@ __device__ __forceinline__ void fma2_f16f32(uint32_t x2, uint32_t w2, float& acc
 __device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---- element types ------------------------------------------------------------
+// Activations and filters are 16-bit: fp16 (F16, the reference's type) or
+// bfloat16 (BF16).  The kernels move them as raw 16-bit pairs (one uint32 =
+// two channels) and only these helpers interpret them.  Products of two
+// elements are exact in fp32 for both types, so fma(x, w, acc) equals
+// acc + x*w with one rounding, as the CPU's fmaf.
+struct F16 {};
+struct BF16 {};
+
+// acc{0,1} += x.{lo,hi} * w.{lo,hi}: fma.rn.f32.f16 / fma.rn.f32.bf16.
+template <class E>
+__device__ __forceinline__ void fma2(uint32_t x2, uint32_t w2, float& acc0, float& acc1);
+template <>
+__device__ __forceinline__ void fma2<F16>(uint32_t x2, uint32_t w2, float& acc0, float& acc1) {
+  fma2_f16f32(x2, w2, acc0, acc1);
+}
+template <>
+__device__ __forceinline__ void fma2<BF16>(uint32_t x2, uint32_t w2, float& acc0, float& acc1) {
+  asm("{\n"
+      " .reg .b16 xl, xh, wl, wh;\n"
+      " mov.b32 {xl, xh}, %2;\n"
+      " mov.b32 {wl, wh}, %3;\n"
+      " fma.rn.f32.bf16 %0, xl, wl, %0;\n"
+      " fma.rn.f32.bf16 %1, xh, wh, %1;\n"
+      "}\n"
+      : "+f"(acc0), "+f"(acc1)
+      : "r"(x2), "r"(w2));
+}
+
+// Two fp32 values rounded to nearest-even and packed (lo in the low half).
+template <class E>
+__device__ __forceinline__ uint32_t pack2_rn(float lo, float hi) {
+  if constexpr (std::is_same_v<E, BF16>) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+  } else {
+    return pack_half2_rn(lo, hi);
+  }
+}
+
+// A packed pair of elements as two fp32 values (exact).
+template <class E>
+__device__ __forceinline__ void unpack2(uint32_t v, float& lo, float& hi) {
+  if constexpr (std::is_same_v<E, BF16>) {
+    lo = __uint_as_float(v << 16);
+    hi = __uint_as_float(v & 0xffff0000u);
+  } else {
+    const __half2 h = *reinterpret_cast<const __half2*>(&v);
+    lo = __low2float(h);
+    hi = __high2float(h);
+  }
 }
 
 }  // namespace tdc

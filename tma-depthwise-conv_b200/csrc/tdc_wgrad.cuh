@@ -44,7 +44,7 @@ __device__ __forceinline__ WsParams wgrad_as_ws(const WgradParams& g) {
   return p;
 }
 
-template <int NS>
+template <int NS, class E = F16>
 __global__ void __launch_bounds__(kWsThreads, 1) dwconv_wgrad_kernel(
     const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
     const __grid_constant__ WgradParams g) {
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) dwconv_wgrad_kernel(
           for (int m = 0; m < kColsPerWarp; ++m)
 #pragma unroll
             for (int s = 0; s < 3; ++s)
-              fma2_f16f32(xr[m + s], dyw[r][m], acc[2 * (r * 3 + s)], acc[2 * (r * 3 + s) + 1]);
+              fma2<E>(xr[m + s], dyw[r][m], acc[2 * (r * 3 + s)], acc[2 * (r * 3 + s) + 1]);
         }
       }
       if (++lr == g.stage_rows || i == rows_in - 1) {
@@ -263,7 +263,7 @@ struct WgradGeom {
   static constexpr int kXWarp = S * (kColsPerWarp - 1) + K;   // x columns one warp reads
 };
 
-template <int NS, int K, int R0, int NR, int S = 1>
+template <int NS, int K, int R0, int NR, int S = 1, class E = F16>
 __global__ void __launch_bounds__(kWsThreads, 3)
     dwconv_wgrad_kxk_kernel(const __grid_constant__ CUtensorMap xmap,
                             const __grid_constant__ CUtensorMap dymap,
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kWsThreads, 3)
             for (int s2 = 0; s2 < K; ++s2)
 #pragma unroll
               for (int m = 0; m < kColsPerWarp; ++m)
-                fma2_f16f32(xr[S * m + s2], dyr[t][m], acc[2 * (r * K + s2)],
+                fma2<E>(xr[S * m + s2], dyr[t][m], acc[2 * (r * K + s2)],
                             acc[2 * (r * K + s2) + 1]);
           }
         }

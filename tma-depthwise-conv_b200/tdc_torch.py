@@ -175,11 +175,15 @@ def _backward_k(ctx, dy):
     k, s = ctx.geometry
     x, w = ctx.saved_tensors
     dx = dw = db = None
+    # 3x3 stride 1 in fp16 has its own ops (any pad); everything else, bf16
+    # included, goes through the K x K ops.
+    own_3x3 = (k, s) == (3, 1) and x.dtype == torch.float16
+    dy = dy.to(x.dtype)
     if ctx.needs_input_grad[0]:
-        dx = (dwconv3x3_bwd_data_op(dy, w, ctx.pad) if (k, s) == (3, 1)
+        dx = (dwconv3x3_bwd_data_op(dy, w, ctx.pad) if own_3x3
               else dwconv_bwd_data_op(dy, w, ctx.pad, s, x.shape[1], x.shape[2]))
     if ctx.needs_input_grad[1]:
-        dw = (dwconv3x3_bwd_weight_op(x, dy, ctx.pad) if (k, s) == (3, 1)
+        dw = (dwconv3x3_bwd_weight_op(x, dy, ctx.pad) if own_3x3
               else dwconv_bwd_weight_op(x, dy, k, ctx.pad, s)).to(w.dtype)
     if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
         db = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(ctx.bias_dtype)
@@ -201,11 +205,13 @@ def dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, bias: Optional[torch.Tenso
 
 class DepthwiseConv2d(nn.Module):
     """``nn.Conv2d(C, C, K, stride, padding, groups=C, bias=bias)`` for fp16
-    channels-last NCHW inputs (NHWC memory), on the sm_100a kernels, K in
-    {3, 5, 7}, stride 1 or 2 (forward and backward).
+    or bf16 channels-last NCHW inputs (NHWC memory), on the sm_100a kernels,
+    K in {3, 5, 7}, stride 1 or 2 (forward and backward).  bf16 inputs run in
+    bf16 (3x3 stride 1 with padding up to 2); anything else is converted to
+    fp16.
 
     Parameters keep ``nn.Conv2d``'s layout (weight [C, 1, K, K], bias [C]), so
-    state dicts load unchanged.  Inputs that are not fp16 CUDA tensors in
+    state dicts load unchanged.  Inputs that are not fp16 or bf16 CUDA tensors in
     channels-last layout are converted (one copy).
     """
 
@@ -241,10 +247,11 @@ class DepthwiseConv2d(nn.Module):
         return m
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        x = x.to(torch.float16).contiguous(memory_format=torch.channels_last)
+        dt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float16
+        x = x.to(dt).contiguous(memory_format=torch.channels_last)
         x_nhwc = x.permute(0, 2, 3, 1)                                  # contiguous view, no copy
-        w_rsc = self.weight.to(torch.float16)[:, 0].permute(1, 2, 0)   # [K,K,C]
-        b = None if self.bias is None else self.bias.to(torch.float16)
+        w_rsc = self.weight.to(dt)[:, 0].permute(1, 2, 0)              # [K,K,C]
+        b = None if self.bias is None else self.bias.to(dt)
         y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
         return y.permute(0, 3, 1, 2)                                    # NCHW view, channels-last memory
 

@@ -54,12 +54,16 @@ def ref_dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, pad: int) -> torch.Ten
 
 # ------------------------------ validation ---------------------------------
 
-def _check(x: torch.Tensor, w: torch.Tensor, pad: int) -> None:
-    # Same checks and messages as the reference (tma_dwconv.py:39-53).
+def _check(x: torch.Tensor, w: torch.Tensor, pad: int, bf16_ok: bool = False) -> None:
+    # Same checks and messages as the reference (tma_dwconv.py:39-53); the
+    # K x K forward (``dwconv``) also takes bfloat16.
     if not (x.is_cuda and w.is_cuda):
         raise ValueError("x and w must be CUDA tensors")
-    if x.dtype != torch.float16 or w.dtype != torch.float16:
-        raise ValueError("x and w must be fp16")
+    if bf16_ok and x.dtype == torch.bfloat16:
+        if w.dtype != torch.bfloat16:
+            raise ValueError("x and w must have the same dtype")
+    elif x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise ValueError("x and w must be fp16" + (" or both bf16" if bf16_ok else ""))
     if x.dim() != 4:
         raise ValueError(f"x must be [N,H,W,C], got shape {tuple(x.shape)}")
     if w.dim() != 3:
@@ -211,19 +215,20 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int
            activation: str = "none", n_stage: int | None = None) -> torch.Tensor:
     """K x K depthwise forward, K in {3, 5, 7}, stride 1 or 2 (beyond the reference surface).
 
-    ``y[n,p,q,c] = round_fp16(epilogue(sum_{r,s} x[n, stride*p+r-pad, stride*q+s-pad, c] * w[r,s,c]))``,
-    fp32 sums in (r, s) order from zero, zero outside the image.  The
-    epilogue is ``dwconv3x3``'s.  ``pad`` defaults to K // 2, ``n_stage`` to
-    ``DWCONV_STAGES[(K, stride)]``.  3x3 stride 1 is ``dwconv3x3``.
+    ``y[n,p,q,c] = round(epilogue(sum_{r,s} x[n, stride*p+r-pad, stride*q+s-pad, c] * w[r,s,c]))``,
+    fp32 sums in (r, s) order from zero, zero outside the image, one
+    rounding to x's dtype (fp16 or bfloat16).  The epilogue is
+    ``dwconv3x3``'s.  ``pad`` defaults to K // 2, ``n_stage`` to
+    ``DWCONV_STAGES[(K, stride)]``.  For fp16, 3x3 stride 1 is ``dwconv3x3``.
 
     Args:
-        x: [N, H, W, C] fp16 CUDA, contiguous, C % 8 == 0.   w: [K, K, C] fp16.
-        bias: [C] fp16 or None.   residual: [N, P, Q, C] fp16 or None, with
+        x: [N, H, W, C] fp16 or bf16 CUDA, contiguous, C % 8 == 0.   w: [K, K, C], x's dtype.
+        bias: [C] or None.   residual: [N, P, Q, C] or None (x's dtype), with
         P = (H + 2*pad - K) // stride + 1 and Q likewise.
     """
     if w.dim() == 3 and pad is None:
         pad = int(w.shape[0]) // 2
-    _check(x, w, pad)
+    _check(x, w, pad, bf16_ok=True)
     K = int(w.shape[0])
     if K not in (3, 5, 7) or w.shape[1] != K:
         raise ValueError(f"w must be [K,K,C] with K in {{3, 5, 7}}, got shape {tuple(w.shape)}")
