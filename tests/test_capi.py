@@ -492,3 +492,34 @@ def test_host_pipeline_argument_errors(lib):
     assert hp(N=0, xh=0, wh=0, yh=0, xd=0, wd=0, yd=0) == 0  # empty: no-op
     if not torch.cuda.is_available():
         assert hp() == CODES["TDC_ERR_NO_DEVICE"]
+
+
+def test_bf16_entry_points_validate_like_fp16(lib):
+    p = C.c_void_p
+    def fw(fn, K=3, S=1, C_=64, pad=1, act=0, ns=2, x=16):
+        return fn(p(x) if x else None, p(16), None, None, p(16), i64(2), i64(16), i64(16), i64(C_),
+                  i64(K), i64(S), i64(pad), i64(act), i64(ns), None)
+    def bd(fn, K=3, S=1, C_=64, pad=1, ns=2):
+        return fn(p(16), p(16), p(16), i64(2), i64(16), i64(16), i64(C_), i64(K), i64(S), i64(pad),
+                  i64(ns), None)
+    def bw(fn, K=3, S=1, C_=64, pad=1, ns=2):
+        return fn(p(16), p(16), p(16), i64(2), i64(16), i64(16), i64(C_), i64(K), i64(S), i64(pad),
+                  i64(ns), p(16), i64(1 << 30), None)
+    for f16, b16 in ((lib.tdc_dwconv_fwd, lib.tdc_dwconv_fwd_bf16),):
+        for kw in ({"K": 4}, {"S": 3}, {"C_": 12}, {"pad": -1}, {"act": 9}, {"ns": 5}, {"x": 0}):
+            assert fw(b16, **kw) == fw(f16, **kw) != 0, kw
+    for f16, b16 in ((lib.tdc_dwconv_bwd_data, lib.tdc_dwconv_bwd_data_bf16),
+                     (lib.tdc_dwconv_bwd_weight, lib.tdc_dwconv_bwd_weight_bf16)):
+        for kw in ({"K": 4}, {"S": 3}, {"C_": 12}, {"pad": -1}, {"ns": 5}):
+            fn = bd if f16 is lib.tdc_dwconv_bwd_data else bw
+            assert fn(b16, **kw) == fn(f16, **kw) != 0, kw
+    # the 3x3 stride-1 bf16 data gradient takes the K x K path: pad <= 2
+    assert bd(lib.tdc_dwconv_bwd_data_bf16, pad=3) == CODES["TDC_ERR_PAD"]
+    b = i64()
+    assert lib.tdc_dwconv_bwd_weight_workspace_bf16(i64(2), i64(16), i64(16), i64(64), i64(3), i64(1),
+                                                    i64(1), i64(2), None) == CODES["TDC_ERR_NULL_POINTER"]
+    if not torch.cuda.is_available():
+        assert fw(lib.tdc_dwconv_fwd_bf16) == CODES["TDC_ERR_NO_DEVICE"]
+        assert bd(lib.tdc_dwconv_bwd_data_bf16) == CODES["TDC_ERR_NO_DEVICE"]
+        assert lib.tdc_dwconv_bwd_weight_workspace_bf16(i64(2), i64(16), i64(16), i64(64), i64(3), i64(1),
+                                                        i64(1), i64(2), C.byref(b)) == CODES["TDC_ERR_NO_DEVICE"]
