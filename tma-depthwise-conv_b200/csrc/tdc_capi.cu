@@ -1028,9 +1028,16 @@ TDC_API int tdc_dwconv_v0(const void* x, const void* w, void* y, int64_t N, int6
   DeviceInfo* dev = nullptr;
   rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;
-  tdc::V0Params prm{N, H, W, C, P, Q, pad, N * P * Q * (C / 8)};
+  // Bands of up to 16 output rows (the 2 halo rows re-read per band mostly
+  // hit L2), fewer when that leaves too few threads to fill the GPU.
+  int64_t band_rows = std::min<int64_t>(16, P);
+  const int64_t per_band = N * Q * (C / 8);
+  while (band_rows > 1 && per_band * ((P + band_rows - 1) / band_rows) < int64_t(dev->sms) * 1024)
+    band_rows = (band_rows + 1) / 2;
+  const int64_t bands = (P + band_rows - 1) / band_rows;
+  tdc::V0Params prm{N, H, W, C, P, Q, pad, C / 8, bands, band_rows, per_band * bands};
   const int threads = 256;
-  const int64_t want = (prm.total_vecs + threads - 1) / threads;
+  const int64_t want = (prm.total + threads - 1) / threads;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(want, int64_t(dev->sms) * 32));
   tdc::dwconv_v0_kernel<<<dim3(unsigned(blocks)), dim3(threads), 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(x), static_cast<const uint4*>(w), static_cast<uint4*>(y), prm);
