@@ -122,7 +122,8 @@ TDC_API int tdc_dwconv_ws_host(const void* x_host, const void* w_host, void* y_h
  *   t = sum_{r,s} x*w  (as above);  t += bias[c];  t = act(t);  t += residual[n,p,q,c]
  *   y = fp16_rne(t)
  * act: TDC_ACT_NONE, TDC_ACT_RELU (t < 0 ? +0 : t), TDC_ACT_RELU6
- * (min(relu(t), 6)), TDC_ACT_SILU (t / (1 + expf(-t))).
+ * (min(relu(t), 6)), TDC_ACT_SILU (t / (1 + expf(-t))), TDC_ACT_HARDSWISH
+ * (t * min(max(t + 3, 0), 6) / 6, rounded in that order).
  * bias: fp16 [C] or NULL; residual: fp16 [N,P,Q,C] or NULL (may be y itself).
  * No counterpart in the reference; the epilogue is what a depthwise block
  * applies next (bias, activation, skip connection), saving a full pass over y. */
@@ -130,6 +131,7 @@ TDC_API int tdc_dwconv_ws_host(const void* x_host, const void* w_host, void* y_h
 #define TDC_ACT_RELU  1
 #define TDC_ACT_RELU6 2
 #define TDC_ACT_SILU  3
+#define TDC_ACT_HARDSWISH 4
 
 TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
                               const void* residual, void* y,

@@ -110,12 +110,19 @@ void oracle_output_hw(int64_t H, int64_t W, int64_t pad, int64_t* P, int64_t* Q)
 }
 
 /* Activation codes of the general forward's fused epilogue. */
-enum { ORACLE_ACT_NONE = 0, ORACLE_ACT_RELU = 1, ORACLE_ACT_RELU6 = 2, ORACLE_ACT_SILU = 3 };
+enum { ORACLE_ACT_NONE = 0, ORACLE_ACT_RELU = 1, ORACLE_ACT_RELU6 = 2, ORACLE_ACT_SILU = 3,
+       ORACLE_ACT_HARDSWISH = 4 };
 
 static float oracle_act(float t, int act) {
   if (act == ORACLE_ACT_RELU) return t < 0.0f ? 0.0f : t;
   if (act == ORACLE_ACT_RELU6) return t < 0.0f ? 0.0f : (t > 6.0f ? 6.0f : t);
   if (act == ORACLE_ACT_SILU) return t / (1.0f + expf(-t));
+  if (act == ORACLE_ACT_HARDSWISH) {
+    /* t * clamp(t + 3, 0, 6) / 6: one rounded multiply, one division */
+    float h = t + 3.0f;
+    h = h < 0.0f ? 0.0f : (h > 6.0f ? 6.0f : h);
+    return (t * h) / 6.0f;
+  }
   return t;
 }
 

@@ -99,7 +99,7 @@ def dwconv_f16(x: np.ndarray, w: np.ndarray, pad: int, threads: int = 0) -> np.n
     return y
 
 
-ACTS = {"none": 0, "relu": 1, "relu6": 2, "silu": 3}
+ACTS = {"none": 0, "relu": 1, "relu6": 2, "silu": 3, "hardswish": 4}
 
 
 def dwconv_ex_f16(x: np.ndarray, w: np.ndarray, pad: int, bias: np.ndarray | None = None,
@@ -274,6 +274,9 @@ def dwconv_ex_f16_numpy(x, w, pad, bias=None, residual=None, activation="none"):
     elif activation == "silu":
         with np.errstate(over="ignore"):
             t = (t / (np.float32(1) + np.exp(-t))).astype(np.float32)
+    elif activation == "hardswish":
+        h = np.clip(t + np.float32(3), np.float32(0), np.float32(6)).astype(np.float32)
+        t = ((t * h).astype(np.float32) / np.float32(6)).astype(np.float32)
     if residual is not None:
         t = t + np.asarray(residual, np.float16).astype(np.float32)
     return t.astype(np.float16)

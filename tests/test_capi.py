@@ -110,7 +110,7 @@ def test_general_forward_argument_errors(lib):
     def fwd(C_=72, act=0, bias=None, res=None, x=16, ns=2):
         return lib.tdc_dwconv3x3_fwd(p(x), p(16), bias, res, p(16), i64(2), i64(16), i64(16),
                                      i64(C_), i64(1), i64(act), i64(ns), None)
-    assert fwd(act=4) == CODES["TDC_ERR_ACT"]
+    assert fwd(act=5) == CODES["TDC_ERR_ACT"]
     assert fwd(act=-1) == CODES["TDC_ERR_ACT"]
     assert fwd(C_=12) == CODES["TDC_ERR_CHANNELS"]
     assert fwd(ns=5) == CODES["TDC_ERR_N_STAGE"]

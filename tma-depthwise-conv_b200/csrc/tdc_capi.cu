@@ -1118,7 +1118,7 @@ TDC_API int tdc_dwconv_ws_host(const void* x_host, const void* w_host, void* y_h
 TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
                               const void* residual, void* y, int64_t N, int64_t H, int64_t W,
                               int64_t C, int64_t pad, int64_t act, int64_t n_stage, void* stream) {
-  if (act < TDC_ACT_NONE || act > TDC_ACT_SILU) return TDC_ERR_ACT;
+  if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
   Epilogue epi;
   epi.fused = true;
   epi.bias = bias;
@@ -1131,7 +1131,7 @@ static int fwd_entry(int dt, const void* x, const void* w, const void* bias,
                      const void* residual, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
                      int64_t K, int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
                      void* stream) {
-  if (act < TDC_ACT_NONE || act > TDC_ACT_SILU) return TDC_ERR_ACT;
+  if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
   if (dt == kF16 && K == 3 && stride == 1)
     return tdc_dwconv3x3_fwd(x, w, bias, residual, y, N, H, W, C, pad, act, n_stage, stream);
   Epilogue epi;

@@ -248,11 +248,18 @@ struct RowAcc {
 //   t = acc; t += bias[c]; t = act(t); t += residual[n,p,q,c]
 // relu: t < 0 ? +0 : t;  relu6: min(relu(t), 6) (both exact);
 // silu: t / (1 + exp(-t)) with the fast exp and divide intrinsics (a few fp32
-// ulp, far below the fp16 rounding of the result).
+// ulp, far below the fp16 rounding of the result); hardswish:
+// t * clamp(t + 3, 0, 6) / 6 with a rounded multiply and an IEEE division
+// (exact restatement in the oracle).
 __device__ __forceinline__ float apply_act(float t, int act) {
   if (act == TDC_ACT_RELU) return t < 0.f ? 0.f : t;
   if (act == TDC_ACT_RELU6) return t < 0.f ? 0.f : (t > 6.f ? 6.f : t);
   if (act == TDC_ACT_SILU) return __fdividef(t, 1.f + __expf(-t));
+  if (act == TDC_ACT_HARDSWISH) {
+    float h = t + 3.f;
+    h = h < 0.f ? 0.f : (h > 6.f ? 6.f : h);
+    return (t * h) / 6.f;  // IEEE division: the oracle's arithmetic, bit for bit
+  }
   return t;
 }
 
@@ -535,6 +542,10 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
           case TDC_ACT_SILU:
 #pragma unroll
             for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_SILU);
+            break;
+          case TDC_ACT_HARDSWISH:
+#pragma unroll
+            for (int k = 0; k < 2 * kColsPerWarp; ++k) t[k] = apply_act(t[k], TDC_ACT_HARDSWISH);
             break;
           default:
             break;

@@ -21,6 +21,12 @@ an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
   (depthwise, dilation 1, symmetric integer padding, zeros padding mode,
   C % 8 == 0; 3x3 / 5x5 / 7x7 at stride 1 or 2) for a ``DepthwiseConv2d``
   sharing its parameters.
+* ``fuse_depthwise_bn_act(model)`` — for inference: a depthwise convolution
+  followed by ``BatchNorm2d`` (and ReLU / ReLU6 / SiLU / Hardswish) in an
+  ``nn.Sequential`` (torchvision's ``Conv2dNormActivation``) becomes one
+  ``DepthwiseConv2d`` with the normalisation folded into its weight and bias
+  and the activation in the kernel's fused epilogue: one pass over the
+  activations instead of three.
 
 The reference (haowen-han/tma-depthwise-conv) has a forward-only Python API
 (``tma_dwconv.py``); everything here is beyond that surface and is built on
@@ -34,6 +40,7 @@ import torch
 from torch import nn
 
 import _tma_dwconv_C as _C  # type: ignore
+import tma_dwconv as _T
 from tma_dwconv import DWCONV_STAGES
 
 #: (K, stride) pairs the kernels implement, forward and backward.
@@ -203,6 +210,12 @@ def dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, bias: Optional[torch.Tenso
 
 # ------------------------------ nn.Conv2d stand-in ---------------------------
 
+#: Activations the fused epilogue implements, with their PyTorch equivalents
+#: (used when a gradient is needed: the custom op's autograd covers conv + bias).
+_TORCH_ACTS = {"none": None, "relu": torch.nn.functional.relu, "relu6": torch.nn.functional.relu6,
+               "silu": torch.nn.functional.silu, "hardswish": torch.nn.functional.hardswish}
+
+
 class DepthwiseConv2d(nn.Module):
     """``nn.Conv2d(C, C, K, stride, padding, groups=C, bias=bias)`` for fp16
     or bf16 channels-last NCHW inputs (NHWC memory), on the sm_100a kernels,
@@ -217,11 +230,14 @@ class DepthwiseConv2d(nn.Module):
 
     def __init__(self, channels: int, kernel_size: int = 3, stride: int = 1,
                  padding: Optional[int] = None, bias: bool = True, device=None,
-                 dtype=torch.float16):
+                 dtype=torch.float16, activation: str = "none"):
         super().__init__()
         if (kernel_size, stride) not in GEOMETRIES:
             raise ValueError(f"kernel_size must be 3, 5 or 7 and stride 1 or 2, got "
                              f"{kernel_size}, {stride}")
+        if activation not in _TORCH_ACTS:
+            raise ValueError(f"activation must be one of {sorted(_TORCH_ACTS)}, got {activation!r}")
+        self.activation = activation
         self.channels = channels
         self.kernel_size = int(kernel_size)
         self.stride = int(stride)
@@ -244,6 +260,7 @@ class DepthwiseConv2d(nn.Module):
         m.padding = int(conv.padding[0])
         m.weight = conv.weight
         m.bias = conv.bias
+        m.activation = "none"
         return m
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -252,12 +269,23 @@ class DepthwiseConv2d(nn.Module):
         x_nhwc = x.permute(0, 2, 3, 1)                                  # contiguous view, no copy
         w_rsc = self.weight.to(dt)[:, 0].permute(1, 2, 0)              # [K,K,C]
         b = None if self.bias is None else self.bias.to(dt)
-        y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
+        act = self.activation
+        needs_grad = torch.is_grad_enabled() and (
+            x.requires_grad or self.weight.requires_grad or (b is not None and b.requires_grad))
+        if act != "none" and not needs_grad:
+            # inference: the activation runs in the kernel's fused epilogue
+            y = _T.dwconv(x_nhwc, w_rsc.contiguous(), self.padding, stride=self.stride, bias=b,
+                          activation=act)
+        else:
+            y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
+            if act != "none":  # the custom op's autograd covers conv + bias
+                y = _TORCH_ACTS[act](y)
         return y.permute(0, 3, 1, 2)                                    # NCHW view, channels-last memory
 
     def extra_repr(self) -> str:
+        act = "" if self.activation == "none" else f", activation={self.activation}"
         return (f"{self.channels}, kernel_size={self.kernel_size}, stride={self.stride}, "
-                f"padding={self.padding}, bias={self.bias is not None}")
+                f"padding={self.padding}, bias={self.bias is not None}{act}")
 
 
 class DepthwiseConv3x3(DepthwiseConv2d):
@@ -296,3 +324,71 @@ def convert_depthwise_convs(model: nn.Module, forward_only: bool = False) -> int
         else:
             count += convert_depthwise_convs(child, forward_only)
     return count
+
+
+_FUSABLE_ACTS = {nn.ReLU: "relu", nn.ReLU6: "relu6", nn.SiLU: "silu", nn.Hardswish: "hardswish"}
+
+
+def _fold_bn(conv: nn.Module, bn: nn.BatchNorm2d, activation: str) -> DepthwiseConv2d:
+    """conv (a depthwise nn.Conv2d or a DepthwiseConv2d) followed by bn in
+    inference: w' = w * g, b' = (b - mean) * g + beta, g = gamma / sqrt(var + eps),
+    computed in float32 and stored in the convolution's dtype."""
+    w = conv.weight.detach().float()
+    c = w.shape[0]
+    b = conv.bias.detach().float() if conv.bias is not None else torch.zeros(c, device=w.device)
+    gamma = bn.weight.detach().float() if bn.weight is not None else torch.ones(c, device=w.device)
+    beta = bn.bias.detach().float() if bn.bias is not None else torch.zeros(c, device=w.device)
+    g = gamma / torch.sqrt(bn.running_var.detach().float() + bn.eps)
+    k = conv.kernel_size[0] if isinstance(conv.kernel_size, tuple) else conv.kernel_size
+    stride = conv.stride[0] if isinstance(conv.stride, tuple) else conv.stride
+    pad = conv.padding[0] if isinstance(conv.padding, tuple) else conv.padding
+    m = DepthwiseConv2d(c, int(k), int(stride), int(pad), bias=True, device=w.device,
+                        dtype=conv.weight.dtype, activation=activation)
+    with torch.no_grad():
+        m.weight.copy_(w * g[:, None, None, None])
+        m.bias.copy_((b - bn.running_mean.detach().float()) * g + beta)
+    return m
+
+
+def _fuse_in_sequential(seq: nn.Sequential) -> int:
+    items = list(seq._modules.items())
+    count, i = 0, 0
+    while i + 1 < len(items):
+        (k0, m0), (k1, m1) = items[i], items[i + 1]
+        conv_ok = _eligible(m0, True) or (type(m0) in (DepthwiseConv2d, DepthwiseConv3x3)
+                                          and m0.activation == "none")
+        if (conv_ok and isinstance(m1, nn.BatchNorm2d) and m1.running_mean is not None
+                and m1.num_features == m0.weight.shape[0]):
+            if m1.training:
+                raise ValueError("fuse_depthwise_bn_act folds running statistics: call model.eval() first")
+            act, k2 = "none", None
+            if i + 2 < len(items) and type(items[i + 2][1]) in _FUSABLE_ACTS:
+                k2 = items[i + 2][0]
+                act = _FUSABLE_ACTS[type(items[i + 2][1])]
+            seq._modules[k0] = _fold_bn(m0, m1, act)
+            seq._modules[k1] = nn.Identity()
+            if k2 is not None:
+                seq._modules[k2] = nn.Identity()
+            count += 1
+            i += 3 if k2 is not None else 2
+        else:
+            i += 1
+    return count
+
+
+def fuse_depthwise_bn_act(model: nn.Module) -> int:
+    """Fuse, for inference, every depthwise convolution that an ``nn.Sequential``
+    follows with ``BatchNorm2d`` (and optionally ReLU / ReLU6 / SiLU /
+    Hardswish), e.g. torchvision's ``Conv2dNormActivation`` blocks of
+    MobileNet / EfficientNet.  The convolution (an eligible ``nn.Conv2d`` or a
+    ``DepthwiseConv2d``) becomes a ``DepthwiseConv2d`` holding the folded
+    weight and bias (new tensors, the convolution's dtype) with the activation
+    in the kernel's epilogue; the normalisation and activation modules become
+    ``nn.Identity``.  The model must be in eval mode (running statistics are
+    folded).  Returns the number of fused blocks.
+    """
+    count = _fuse_in_sequential(model) if isinstance(model, nn.Sequential) else 0
+    for child in model.children():
+        count += fuse_depthwise_bn_act(child)
+    return count
+

@@ -25,7 +25,7 @@ __all__ = ["dwconv_v0", "dwconv_ws", "dwconv_ws_probe", "ref_dwconv",
            "CONSUMER_WARPS", "ACTIVATIONS"]
 
 #: Activations the general forward fuses into its epilogue.
-ACTIVATIONS = {"none": 0, "relu": 1, "relu6": 2, "silu": 3}
+ACTIVATIONS = {"none": 0, "relu": 1, "relu6": 2, "silu": 3, "hardswish": 4}
 
 #: Consumer warps per CTA of the ws kernel (divide stall columns 1 and 3 by it
 #: for per-warp figures, as the reference's probe report does).
@@ -191,7 +191,8 @@ def dwconv3x3(x: torch.Tensor, w: torch.Tensor, pad: int = 1,
     Args:
         x: [N, H, W, C] fp16 CUDA, contiguous.   w: [3, 3, C] fp16.
         bias: [C] fp16 or None.   residual: [N, P, Q, C] fp16 or None.
-        activation: "none", "relu" (t < 0 ? 0 : t), "relu6", "silu" (t / (1 + exp(-t))).
+        activation: "none", "relu" (t < 0 ? 0 : t), "relu6", "silu" (t / (1 + exp(-t))),
+            "hardswish" (t * clamp(t + 3, 0, 6) / 6).
     """
     _check(x, w, pad)
     if w.shape[0] != 3 or w.shape[1] != 3:
