@@ -143,7 +143,11 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
  *   y[n,p,q,c] = fp16_rne(epilogue( chain_{r<K, s<K} x[n, S*p+r-pad, S*q+s-pad, c] * w[r,s,c] ))
  * fp32 chain from +0 in (r, s) lexicographic order.  w: [K, K, C] fp16;
  * P = (H + 2*pad - K) / S + 1, Q likewise; C % 8 == 0.  (K, stride) = (3, 1)
- * is tdc_dwconv3x3_fwd.  No counterpart in the reference (3x3, stride 1 only). */
+ * is tdc_dwconv3x3_fwd.  n_stage 2, 3 or 4 runs the ws kernel with that ring
+ * depth; n_stage 0 leaves the choice to the library: the plain kernel
+ * (tdc_dwconv_fwd_plain) where tdc_dwconv_fwd_uses_plain says so, else the
+ * ws kernel at the geometry's default depth.  The result is the same bit
+ * for bit either way.  No counterpart in the reference (3x3, stride 1 only). */
 TDC_API int tdc_dwconv_fwd(const void* x, const void* w, const void* bias,
                            const void* residual, void* y,
                            int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
@@ -160,6 +164,31 @@ TDC_API int tdc_dwconv_fwd_bf16(const void* x, const void* w, const void* bias,
                                 int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
                                 int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
                                 void* stream);
+
+/* Plain K x K forward: global loads through L1, no TMA, no shared memory, no
+ * pipeline.  A thread owns one channel pair of one output column over a band
+ * of band_rows output rows (0 = chosen from the shape: the full height unless
+ * that leaves fewer than two waves of threads).  For shapes the ws kernel's
+ * 32-column x 64-channel strips fit badly (few channels, narrow images).
+ * Same arguments (band_rows in place of n_stage), arithmetic and result, bit
+ * for bit, as tdc_dwconv_fwd.  No counterpart in the reference. */
+TDC_API int tdc_dwconv_fwd_plain(const void* x, const void* w, const void* bias,
+                                 const void* residual, void* y,
+                                 int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                 int64_t stride, int64_t pad, int64_t act, int64_t band_rows,
+                                 void* stream);
+
+/* tdc_dwconv_fwd_plain for bfloat16 tensors (as tdc_dwconv_fwd_bf16). */
+TDC_API int tdc_dwconv_fwd_plain_bf16(const void* x, const void* w, const void* bias,
+                                      const void* residual, void* y,
+                                      int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                      int64_t stride, int64_t pad, int64_t act,
+                                      int64_t band_rows, void* stream);
+
+/* 1 if tdc_dwconv_fwd with n_stage 0 runs the plain kernel on this shape,
+ * else 0 (pure host arithmetic). */
+TDC_API int tdc_dwconv_fwd_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                      int64_t stride, int64_t pad);
 
 /* Launch plan tdc_dwconv_fwd would use (same layout as tdc_ws_plan's
  * plan[0..7]; pure host arithmetic).  For K >= 5 at stride 1 and 7x7 at

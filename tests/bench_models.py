@@ -1,0 +1,188 @@
+"""Whole-model inference with the depthwise layers on these kernels, on one GPU.
+
+    python tests/bench_models.py [--batch 64] [--size 224] [--iters 20] [--graphs]
+    python tests/bench_models.py --layers [--batch 64]
+
+torchvision MobileNetV2, MobileNetV3-Large and EfficientNet-B0 (random
+weights, random BatchNorm statistics), fp16, channels-last, eval mode.  Per
+model, ms per forward (CUDA events, 5 warm-up + `iters` calls) for:
+  cudnn        the unmodified model (cuDNN depthwise + BatchNorm + activation)
+  converted    tdc_torch.convert_depthwise_convs: depthwise convs on these kernels
+  fused        tdc_torch.fuse_depthwise_bn_act: BatchNorm folded, activation in
+               the depthwise kernel's epilogue
+and the largest logit difference of each variant against the unmodified
+model.  Eager calls include the host's per-layer launch cost; ``--graphs``
+captures each variant's forward once in a CUDA graph and times replays (GPU
+time only).  Prints one JSON line per model.
+
+``--layers`` instead times every distinct depthwise layer of the three models
+alone (input shape recorded by forward hooks): cuDNN's channels-last conv2d,
+the ws kernel (``_C.dwconv_k`` at the default ring depth) and the plain kernel
+(``_C.dwconv_plain``), each as 20 back-to-back calls replayed from a CUDA
+graph, the kernel the automatic choice takes, and the algorithmic bytes (x
+read + y written) per call.  A script,
+not a test.
+"""
+from __future__ import annotations
+
+import argparse
+import copy
+import json
+import os
+import sys
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path[:0] = [os.path.join(REPO, "tma-depthwise-conv_b200")]
+
+import torch  # noqa: E402
+import torchvision  # noqa: E402
+
+import tdc_torch  # noqa: E402
+
+
+def bench_ms(fn, warmup=5, iters=20) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def graphed(m, x):
+    """Capture ``m(x)`` in a CUDA graph; returns the replay callable."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            m(x)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        m(x)
+    return g.replay
+
+
+def randomize_bn(model: torch.nn.Module, seed: int) -> None:
+    g = torch.Generator().manual_seed(seed)
+    for m in model.modules():
+        if isinstance(m, torch.nn.BatchNorm2d):
+            c = m.num_features
+            m.running_mean.copy_(torch.randn(c, generator=g) * 0.2)
+            m.running_var.copy_(torch.rand(c, generator=g) + 0.5)
+            m.weight.data.copy_(torch.rand(c, generator=g) + 0.5)
+            m.bias.data.copy_(torch.randn(c, generator=g) * 0.2)
+
+
+def depthwise_layers(batch: int, size: int):
+    """Distinct (N, H, W, C, K, stride, pad) of the models' depthwise convs."""
+    seen = []
+    for arch in ("mobilenet_v2", "mobilenet_v3_large", "efficientnet_b0"):
+        model = getattr(torchvision.models, arch)().eval()
+        hooks = []
+        for m in model.modules():
+            if (isinstance(m, torch.nn.Conv2d) and m.groups == m.in_channels == m.out_channels
+                    and m.in_channels > 1):
+                def hook(mod, inp, _out, arch=arch):
+                    n, c, h, w = inp[0].shape
+                    key = (n, h, w, c, mod.kernel_size[0], mod.stride[0], mod.padding[0])
+                    if key not in [k for k, _ in seen]:
+                        seen.append((key, arch))
+                hooks.append(m.register_forward_hook(hook))
+        with torch.no_grad():
+            model(torch.zeros(1, 3, size, size))
+        for h in hooks:
+            h.remove()
+    return [((batch,) + key[1:], arch) for key, arch in seen]
+
+
+def graph_of(fn, reps=20):
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    return g.replay
+
+
+def bench_layers(batch: int, size: int, iters: int) -> None:
+    import tma_dwconv as T
+    reps = 20
+    tot_c = tot_t = 0.0
+    for (n, h, w, c, k, s, pad), arch in depthwise_layers(batch, size):
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(n, h, w, c, device="cuda", generator=g).half()
+        wt = (torch.randn(k, k, c, device="cuda", generator=g) / k).half()
+        x_nchw = x.permute(0, 3, 1, 2)                        # channels-last view
+        w_conv = wt.permute(2, 0, 1).unsqueeze(1).contiguous()
+        cudnn = graph_of(lambda: torch.nn.functional.conv2d(x_nchw, w_conv, None, s, pad,
+                                                            groups=c), reps)
+        ws = graph_of(lambda: T._C.dwconv_k(x, wt, None, None, s, pad, 0,
+                                            T.DWCONV_STAGES[(k, s)]), reps)
+        plain = graph_of(lambda: T._C.dwconv_plain(x, wt, None, None, s, pad, 0, 0), reps)
+        p, q = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+        nbytes = 2 * n * c * (h * w + p * q)
+        t_c = bench_ms(cudnn, iters=iters) / reps * 1e3
+        t_w = bench_ms(ws, iters=iters) / reps * 1e3
+        t_p = bench_ms(plain, iters=iters) / reps * 1e3
+        use_plain = T.uses_plain(n, h, w, c, k, s, pad)
+        t_t = t_p if use_plain else t_w
+        tot_c, tot_t = tot_c + t_c, tot_t + t_t
+        print(json.dumps({"model": arch, "N": n, "H": h, "W": w, "C": c, "K": k, "stride": s,
+                          "MB": round(nbytes / 1e6, 2), "cudnn_us": round(t_c, 2),
+                          "ws_us": round(t_w, 2), "plain_us": round(t_p, 2),
+                          "auto": "plain" if use_plain else "ws",
+                          "auto_GBps": round(nbytes / t_t / 1e3, 1),
+                          "speedup_auto": round(t_c / t_t, 3)}), flush=True)
+    print(json.dumps({"layers_total_cudnn_us": round(tot_c, 1),
+                      "layers_total_auto_us": round(tot_t, 1)}), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--size", type=int, default=224)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--graphs", action="store_true", help="time CUDA-graph replays")
+    ap.add_argument("--layers", action="store_true", help="time each depthwise layer alone")
+    args = ap.parse_args()
+    if args.layers:
+        bench_layers(args.batch, args.size, args.iters)
+        return
+    x = torch.randn(args.batch, 3, args.size, args.size, device="cuda").half()
+    x = x.to(memory_format=torch.channels_last)
+    for arch in ("mobilenet_v2", "mobilenet_v3_large", "efficientnet_b0"):
+        torch.manual_seed(0)
+        base = getattr(torchvision.models, arch)()
+        randomize_bn(base, 1)
+        base = base.eval().cuda().half().to(memory_format=torch.channels_last)
+        converted = copy.deepcopy(base)
+        n_conv = tdc_torch.convert_depthwise_convs(converted)
+        fused = copy.deepcopy(base)
+        n_fused = tdc_torch.fuse_depthwise_bn_act(fused)
+        row = {"model": arch, "batch": args.batch, "size": args.size,
+               "depthwise_converted": n_conv, "blocks_fused": n_fused,
+               "mode": "cuda_graph" if args.graphs else "eager"}
+        with torch.no_grad():
+            ref = base(x).float()
+            for name, m in (("cudnn", base), ("converted", converted), ("fused", fused)):
+                fn = graphed(m, x) if args.graphs else (lambda: m(x))
+                row[f"{name}_ms"] = round(bench_ms(fn, iters=args.iters), 3)
+                if name != "cudnn":
+                    row[f"{name}_max_logit_diff"] = round((m(x).float() - ref).abs().max().item(), 4)
+            row["logit_scale"] = round(ref.abs().max().item(), 3)
+        row["speedup_fused_vs_cudnn"] = round(row["cudnn_ms"] / row["fused_ms"], 3)
+        print(json.dumps(row), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -557,3 +557,140 @@ def test_v0_bands_store_every_output_row_once(N, H, W, Cc, pad):
                 if 0 <= o < rows:
                     assert ((i % 3) - r) % 3 == o % 3
     assert sorted(stored) == list(range(P))
+
+
+def test_plain_forward_argument_errors(lib):
+    p = C.c_void_p
+    def fwd(K=5, stride=2, C_=72, pad=2, H=16, act=0, band=0, N=2, x=16, f=None):
+        f = f or lib.tdc_dwconv_fwd_plain
+        return f(p(x), p(16), None, None, p(16), i64(N), i64(H), i64(16), i64(C_), i64(K),
+                 i64(stride), i64(pad), i64(act), i64(band), None)
+    for f in (lib.tdc_dwconv_fwd_plain, lib.tdc_dwconv_fwd_plain_bf16):
+        assert fwd(K=4, f=f) == CODES["TDC_ERR_FILTER_SHAPE"]
+        assert fwd(stride=3, f=f) == CODES["TDC_ERR_STRIDE"]
+        assert fwd(C_=12, f=f) == CODES["TDC_ERR_CHANNELS"]
+        assert fwd(pad=-1, f=f) == CODES["TDC_ERR_PAD"]
+        assert fwd(act=5, f=f) == CODES["TDC_ERR_ACT"]
+        assert fwd(band=-1, f=f) == CODES["TDC_ERR_BAD_SHAPE"]
+        assert fwd(K=7, H=2, pad=2, f=f) == CODES["TDC_ERR_BAD_SHAPE"]
+        assert fwd(x=24, f=f) == CODES["TDC_ERR_ALIGNMENT"]
+        assert fwd(x=0, f=f) == CODES["TDC_ERR_NULL_POINTER"]
+        assert fwd(N=0, f=f) == CODES["TDC_OK"]
+        if not torch.cuda.is_available():
+            assert fwd(f=f) == CODES["TDC_ERR_NO_DEVICE"]
+    # n_stage 0 = automatic: argument checks as before, no device here
+    r = lib.tdc_dwconv_fwd(p(16), p(16), None, None, p(16), i64(2), i64(16), i64(16), i64(72),
+                           i64(5), i64(2), i64(2), i64(0), i64(0), None)
+    if not torch.cuda.is_available():
+        assert r == CODES["TDC_ERR_NO_DEVICE"]
+
+
+def uses_plain(N, H, W, Cc, K, S, pad):
+    """Restates tdc_dwconv_fwd_uses_plain: the plain kernel when less than
+    half of the ws strips' lanes x columns hold outputs, at stride 2 only
+    for 7-column-like outputs (fill_q <= 1/4) or layers under 64 MB."""
+    P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
+    fill_c = Cc / (64 * -(-Cc // 64))
+    fill_q = Q / (32 * -(-Q // 32))
+    if fill_c * fill_q >= 0.5:
+        return False
+    nbytes = 2 * N * Cc * (H * W + P * Q)
+    return S == 1 or fill_q <= 0.25 or nbytes < 64e6
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+def test_automatic_kernel_choice(lib, K, S):
+    for (N, H, W, Cc) in [(64, 224, 336, 256), (64, 112, 112, 16), (64, 56, 56, 72),
+                          (64, 14, 14, 576), (64, 7, 7, 960), (8, 56, 56, 256),
+                          (64, 28, 28, 240), (256, 28, 28, 240), (2, 20, 40, 64),
+                          (1, 9, 100, 256), (256, 56, 56, 72), (256, 112, 112, 96)]:
+        pad = K // 2
+        got = lib.tdc_dwconv_fwd_uses_plain(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(S),
+                                            i64(pad))
+        assert got == int(uses_plain(N, H, W, Cc, K, S, pad)), (N, H, W, Cc)
+    # the headline shape stays on the ws kernel; a 16-channel layer does not;
+    # a large stride-2 layer with 14-column outputs stays, its batch-64 form not
+    assert lib.tdc_dwconv_fwd_uses_plain(i64(64), i64(224), i64(336), i64(256), i64(3), i64(1), i64(1)) == 0
+    assert lib.tdc_dwconv_fwd_uses_plain(i64(64), i64(112), i64(112), i64(16), i64(3), i64(1), i64(1)) == 1
+    assert lib.tdc_dwconv_fwd_uses_plain(i64(256), i64(28), i64(28), i64(192), i64(3), i64(2), i64(1)) == 0
+    assert lib.tdc_dwconv_fwd_uses_plain(i64(64), i64(28), i64(28), i64(192), i64(3), i64(2), i64(1)) == 1
+    assert lib.tdc_dwconv_fwd_uses_plain(i64(1), i64(16), i64(16), i64(12), i64(3), i64(1), i64(1)) == 0
+
+
+def plain_cols(K):
+    return {3: 8, 5: 4, 7: 2}[K]
+
+
+def plain_threads(N, P, Q, Cc, K, band_rows):
+    """Restates dwconv_plain_kernel's thread -> (n, band, chunk, column
+    group, pair) decomposition; yields (n, p0, rows, q0, n_valid, cp)."""
+    cpairs = Cc // 2
+    clog = 3 if cpairs % 8 == 0 else 2
+    chunks = cpairs >> clog
+    QT = plain_cols(K)
+    qgroups = -(-Q // QT)
+    bands = -(-P // band_rows)
+    total = N * bands * chunks * qgroups * (1 << clog)
+    for t in range(total):
+        r = t >> clog
+        qg = r % qgroups; r //= qgroups
+        chunk = r % chunks; r //= chunks
+        band = r % bands
+        n = r // bands
+        cp = (chunk << clog) + (t & ((1 << clog) - 1))
+        p0 = band * band_rows
+        yield n, p0, min(band_rows, P - p0), qg * QT, min(QT, Q - qg * QT), cp
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("N,P,Q,Cc,band_rows", [(2, 7, 7, 72, 3), (1, 5, 9, 16, 5),
+                                                (3, 4, 3, 40, 1), (1, 10, 2, 8, 4),
+                                                (1, 3, 17, 24, 2)])
+def test_plain_threads_cover_every_output_once(K, N, P, Q, Cc, band_rows):
+    seen = {}
+    for n, p0, rows, q0, n_valid, cp in plain_threads(N, P, Q, Cc, K, band_rows):
+        assert 0 <= cp < Cc // 2 and rows >= 1 and 1 <= n_valid <= plain_cols(K)
+        for o in range(rows):
+            for m in range(n_valid):
+                key = (n, p0 + o, q0 + m, cp)
+                assert key not in seen
+                seen[key] = 1
+    assert len(seen) == N * P * Q * (Cc // 2)
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+def test_plain_row_loop_feeds_each_output_its_taps_in_order(K, S):
+    """Replays the kernel's row loop (unrolled by L = S * ceil(K/S) rows) for
+    band heights 1..12: every output row gets tap rows r = 0..K-1 in order,
+    starts its accumulator set at r = 0, is stored at r = K-1, and no two
+    outputs in flight share an accumulator set."""
+    A = -(-K // S)
+    L = S * A
+    for rows in range(1, 13):
+        n_in = S * (rows - 1) + K
+        taps = {o: [] for o in range(rows)}
+        owner = {}  # accumulator set -> output using it
+        stored = []
+        for i0 in range(0, n_in, L):
+            for U in range(L):
+                i = i0 + U
+                if i >= n_in:
+                    continue
+                for r in range(K):
+                    if (U - r) % S != 0:
+                        continue
+                    o = i0 // S + (U - r) // S
+                    assert o == (i - r) // S and (i - r) % S == 0
+                    if o < 0 or o >= rows:
+                        continue
+                    a = ((U - r) // S) % A
+                    if r == 0:
+                        assert a not in owner
+                        owner[a] = o
+                    assert owner.get(a) == o
+                    taps[o].append(r)
+                    if r == K - 1:
+                        stored.append(o)
+                        del owner[a]
+        assert all(taps[o] == list(range(K)) for o in range(rows)), rows
+        assert sorted(stored) == list(range(rows))

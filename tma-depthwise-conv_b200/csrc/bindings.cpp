@@ -199,7 +199,8 @@ torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Te
   TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
   TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
   TORCH_CHECK(pad >= 0, "pad must be non-negative");
-  TORCH_CHECK(n_stage >= 2 && n_stage <= 4, "n_stage must be one of {2, 3, 4}, got ", n_stage);
+  TORCH_CHECK(n_stage == 0 || (n_stage >= 2 && n_stage <= 4),
+              "n_stage must be one of {2, 3, 4} (or 0: chosen from the shape), got ", n_stage);
   TORCH_CHECK(x.size(1) + 2 * pad >= K && x.size(2) + 2 * pad >= K, "input too small for a ", K,
               "x", K, " kernel with pad ", pad);
   const c10::cuda::CUDAGuard guard(x.device());
@@ -226,6 +227,48 @@ torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Te
   check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
                    x.size(2), x.size(3), K, stride, pad, act, n_stage, stream_of(x)),
                "dwconv");
+  return y;
+}
+
+// The plain K x K forward (no TMA): same checks and epilogue as dwconv_k,
+// band_rows (0 = from the shape) in place of n_stage.
+torch::Tensor dwconv_plain(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
+                           std::optional<torch::Tensor> residual, int64_t stride, int64_t pad,
+                           int64_t act, int64_t band_rows) {
+  const bool bf16 = check_common_16(x, w, "x");
+  const int64_t K = w.size(0);
+  TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7), "w must be [K,K,C] with K in {3, 5, 7}");
+  TORCH_CHECK(w.size(2) == x.size(3), "channel mismatch");
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(band_rows >= 0, "band_rows must be non-negative (0: chosen from the shape)");
+  TORCH_CHECK(x.size(1) + 2 * pad >= K && x.size(2) + 2 * pad >= K, "input too small for a ", K,
+              "x", K, " kernel with pad ", pad);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t P = (x.size(1) + 2 * pad - K) / stride + 1;
+  const int64_t Q = (x.size(2) + 2 * pad - K) / stride + 1;
+  auto y = torch::empty({x.size(0), P, Q, x.size(3)}, x.options());
+  const void* bptr = nullptr;
+  const void* rptr = nullptr;
+  if (bias.has_value()) {
+    const auto& b = *bias;
+    TORCH_CHECK(b.is_cuda() && b.device() == x.device() && b.scalar_type() == x.scalar_type() &&
+                    b.is_contiguous() && b.dim() == 1 && b.size(0) == x.size(3),
+                "bias must be a contiguous [C] tensor of x's dtype on x's device");
+    bptr = b.data_ptr();
+  }
+  if (residual.has_value()) {
+    const auto& r = *residual;
+    TORCH_CHECK(r.is_cuda() && r.device() == x.device() && r.scalar_type() == x.scalar_type() &&
+                    r.is_contiguous() && r.sizes() == y.sizes(),
+                "residual must be a contiguous [N,P,Q,C] tensor of x's dtype on x's device");
+    rptr = r.data_ptr();
+  }
+  auto* fwd = bf16 ? &tdc_dwconv_fwd_plain_bf16 : &tdc_dwconv_fwd_plain;
+  check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
+                   x.size(2), x.size(3), K, stride, pad, act, band_rows, stream_of(x)),
+               "dwconv_plain");
   return y;
 }
 
@@ -430,6 +473,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "K x K (3, 5, 7) depthwise forward, stride 1 or 2, optional fused epilogue",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
         py::arg("pad"), py::arg("act"), py::arg("n_stage"));
+  m.def("dwconv_plain", &tma_dwconv::dwconv_plain,
+        "plain (no TMA) K x K depthwise forward, the same result as dwconv_k",
+        py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
+        py::arg("pad"), py::arg("act"), py::arg("band_rows"));
+  m.def("dwconv_uses_plain",
+        [](int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad) {
+          return tdc_dwconv_fwd_uses_plain(N, H, W, C, K, stride, pad) != 0;
+        },
+        "whether dwconv_k with n_stage 0 runs the plain kernel on this shape");
   m.def("dwconv3x3", &tma_dwconv::dwconv3x3,
         "General forward: C % 8, fused bias / activation / residual epilogue.",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("bias"), pybind11::arg("residual"),

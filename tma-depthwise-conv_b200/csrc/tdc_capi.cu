@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -30,6 +31,7 @@
 #include "tdc_kernels.cuh"
 #include "tdc_wgrad.cuh"
 #include "tdc_dgrad_s2.cuh"
+#include "tdc_plain.cuh"
 
 namespace {
 
@@ -287,11 +289,11 @@ int check_ws_limits(int64_t N, int64_t H, int64_t W, int64_t C, int64_t P, int64
 // of back-to-back calls on small problems (8 x 56 x 56 x 256: 10.25 -> 8.3-8.5
 // us per call; 64 x 224 x 336 x 256 unchanged within noise).
 template <class... Args>
-cudaError_t launch_pdl(void (*kernel)(Args...), int64_t grid, size_t smem, cudaStream_t st,
-                       Args... args) {
+cudaError_t launch_pdl_block(void (*kernel)(Args...), int64_t grid, unsigned block, size_t smem,
+                             cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(tdc::kWsThreads);
+  cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -300,6 +302,12 @@ cudaError_t launch_pdl(void (*kernel)(Args...), int64_t grid, size_t smem, cudaS
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <class... Args>
+cudaError_t launch_pdl(void (*kernel)(Args...), int64_t grid, size_t smem, cudaStream_t st,
+                       Args... args) {
+  return launch_pdl_block(kernel, grid, unsigned(tdc::kWsThreads), smem, st, args...);
 }
 
 template <int NS, bool PROBE, int MODE = tdc::kModeWs>
@@ -521,6 +529,102 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   prm.flip_taps = epi.flip_taps ? 1 : 0;
   const cudaError_t e =
       kGeomLaunch[dt][ki][si][mi][ni](map, prm, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+// ---------------------------------------------------------------------------
+// Plain forward (tdc_plain.cuh) for the shapes the ws strips fit badly, and
+// the choice between it and the ws kernel.
+// ---------------------------------------------------------------------------
+using PlainLaunchFn = cudaError_t (*)(const tdc::PlainParams&, int64_t, cudaStream_t);
+
+template <int K, int S, class E, bool EPI>
+cudaError_t plain_launch_t(const tdc::PlainParams& prm, int64_t grid, cudaStream_t st) {
+  return launch_pdl_block(&tdc::dwconv_plain_kernel<K, S, E, EPI>, grid,
+                          unsigned(tdc::kPlainThreads), 0, st, prm);
+}
+
+#define TDC_PLAIN_EPI(E, K, S) {plain_launch_t<K, S, E, false>, plain_launch_t<K, S, E, true>}
+#define TDC_PLAIN_TABLE(E)                                                  \
+  {{TDC_PLAIN_EPI(E, 3, 1), TDC_PLAIN_EPI(E, 3, 2)},                        \
+   {TDC_PLAIN_EPI(E, 5, 1), TDC_PLAIN_EPI(E, 5, 2)},                        \
+   {TDC_PLAIN_EPI(E, 7, 1), TDC_PLAIN_EPI(E, 7, 2)}}
+// [element type][K index: 3, 5, 7][stride - 1][epilogue]
+const PlainLaunchFn kPlainLaunch[2][3][2][2] = {TDC_PLAIN_TABLE(tdc::F16),
+                                                TDC_PLAIN_TABLE(tdc::BF16)};
+#undef TDC_PLAIN_TABLE
+#undef TDC_PLAIN_EPI
+
+// Output rows per thread of the plain kernel: the whole height unless that
+// leaves fewer than 384 threads per SM (about one wave at the kernels' 120-160
+// registers), in which case the height is cut into bands, each re-reading its
+// K - S halo rows.  Measured on MobileNet / EfficientNet layers at batch 64
+// (us, band rows 1 / 2 / 4 / 7 / 14): 112 x 112 x 16: 39 / 29 / 24 / 24 / 26;
+// 14 x 14 x 576: 26 / 20 / 17 / 15 / 17; 7 x 7 x 960 5x5: 32 / 25 / 17 / 15.
+int64_t plain_band_rows(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t K, int64_t sms) {
+  const int64_t qgroups = (Q + tdc::plain_cols(int(K)) - 1) / tdc::plain_cols(int(K));
+  const int64_t per_band = std::max<int64_t>(1, N * qgroups * (C / 2));
+  const int64_t want = 384 * std::max<int64_t>(1, sms);
+  const int64_t bands = std::min<int64_t>(P, std::max<int64_t>(1, (want + per_band - 1) / per_band));
+  return (P + bands - 1) / bands;
+}
+
+int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
+              int64_t K, int64_t S, int64_t pad, int64_t band_rows, const Epilogue& epi,
+              void* stream, int dt) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (S != 1 && S != 2) return TDC_ERR_STRIDE;
+  if (N < 0 || H < 1 || W < 1 || C < 0 || band_rows < 0) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0 && !epi.flip_taps) return TDC_ERR_PAD;
+  if (pad > (1 << 28) || pad < -(1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  if (N == 0 || C == 0) return TDC_OK;
+  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
+      (epi.residual && !aligned16(epi.residual)))
+    return TDC_ERR_ALIGNMENT;
+  // 32-bit row / column arithmetic in the kernel (S * p0 - pad, S * q - pad + s)
+  // and a 32-bit thread index.
+  const int64_t i32 = 0x7fffffffll;
+  if (N > i32 || C > i32 || H + 2 * std::abs(pad) > i32 || W + 2 * std::abs(pad) > i32)
+    return TDC_ERR_TOO_LARGE;
+  if (N * Q > i32 || N * Q * (C / 2) > i32) return TDC_ERR_TOO_LARGE;
+  if (H * W > i32 || H * W * (C / 2) > i32) return TDC_ERR_TOO_LARGE;  // 32-bit image offsets
+  DeviceInfo* dev = nullptr;
+  int rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  const int64_t cpairs = C / 2;
+  const int chunk_log2 = cpairs % 8 == 0 ? 3 : 2;  // 32- or 16-byte chunks (C % 8 == 0)
+  const int64_t qgroups = (Q + tdc::plain_cols(int(K)) - 1) / tdc::plain_cols(int(K));
+  const int64_t rows =
+      band_rows > 0 ? std::min(band_rows, P) : plain_band_rows(N, P, Q, C, K, dev->sms);
+  const int64_t bands = (P + rows - 1) / rows;
+  const int64_t total = N * qgroups * cpairs * bands;  // < 2^62: both factors < 2^31
+  if (total > 0xffffffffll - tdc::kPlainThreads) return TDC_ERR_TOO_LARGE;
+  tdc::PlainParams prm{};
+  prm.x = static_cast<const uint32_t*>(x);
+  prm.w = static_cast<const uint32_t*>(w);
+  prm.bias = static_cast<const uint32_t*>(epi.bias);
+  prm.residual = static_cast<const uint32_t*>(epi.residual);
+  prm.y = static_cast<uint32_t*>(y);
+  prm.total = uint32_t(total);
+  prm.H = int32_t(H); prm.W = int32_t(W); prm.P = int32_t(P); prm.Q = int32_t(Q);
+  prm.qgroups = int32_t(qgroups);
+  prm.cpairs = int32_t(cpairs);
+  prm.chunk_log2 = chunk_log2;
+  prm.chunks = int32_t(cpairs >> chunk_log2);
+  prm.bands = int32_t(bands);
+  prm.band_rows = int32_t(rows);
+  prm.pad = int32_t(pad);
+  prm.act = epi.act;
+  prm.flip_taps = epi.flip_taps ? 1 : 0;
+  const bool with_epilogue =
+      epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
+  const int64_t grid = (total + tdc::kPlainThreads - 1) / tdc::kPlainThreads;
+  const cudaError_t e = kPlainLaunch[dt][K / 2 - 1][S - 1][with_epilogue ? 1 : 0](
+      prm, grid, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
@@ -1127,11 +1231,52 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
   return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, -1, 0, stream, epi);
 }
 
+// Ring depth of the ws forward per geometry when the caller leaves it to the
+// library (n_stage = 0), measured at 64 x 224 x 336 x 256.
+int default_fwd_stages(int64_t K, int64_t S) {
+  static const int kStages[3][2] = {{2, 4}, {4, 2}, {3, 4}};  // [K: 3, 5, 7][stride - 1]
+  return (K == 3 || K == 5 || K == 7) && (S == 1 || S == 2) ? kStages[K / 2 - 1][S - 1] : 2;
+}
+
+// Whether the plain kernel beats the ws kernel on this shape.  The ws kernel
+// works in strips of 32 output columns x 64 channels; fill_c and fill_q are
+// the fractions of a strip's lanes and columns that hold real outputs.  From
+// both kernels timed on the 28 depthwise layers of MobileNetV2 / V3-Large /
+// EfficientNet-B0 at batch 64 and 256: with fill_c * fill_q >= 0.5 the ws
+// kernel wins or ties everywhere; below it the plain kernel wins at stride 1
+// (e.g. 14 x 14 x 576: 10.3 vs 12.8 us, 112 x 112 x 16: 18.2 vs 44.4 us) and
+// at stride 2 on 7-column outputs or layers under 64 MB, while larger
+// stride-2 layers with wider outputs stay on the ws kernel (28 x 28 x 192 at
+// batch 256: 20.2 vs 26.1 us).
+bool prefer_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                  int64_t pad) {
+  if (K != 3 && K != 5 && K != 7) return false;
+  if ((S != 1 && S != 2) || C <= 0 || C % 8 != 0 || N <= 0) return false;
+  if (H + 2 * pad < K || W + 2 * pad < K) return false;
+  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  const double fill_c = double(C) / double(64 * ((C + 63) / 64));
+  const double fill_q = double(Q) / double(32 * ((Q + 31) / 32));
+  if (fill_c * fill_q >= 0.5) return false;
+  const double bytes = 2.0 * double(N) * double(C) * (double(H) * double(W) + double(P) * double(Q));
+  return S == 1 || fill_q <= 0.25 || bytes < 64e6;
+}
+
 static int fwd_entry(int dt, const void* x, const void* w, const void* bias,
                      const void* residual, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
                      int64_t K, int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
                      void* stream) {
   if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
+  if (n_stage == 0) {  // automatic: the kernel and ring depth follow the shape
+    if (prefer_plain(N, H, W, C, K, stride, pad)) {
+      Epilogue epi;
+      epi.fused = true;
+      epi.bias = bias;
+      epi.residual = residual;
+      epi.act = int(act);
+      return fwd_plain(x, w, y, N, H, W, C, K, stride, pad, 0, epi, stream, dt);
+    }
+    n_stage = default_fwd_stages(K, stride);
+  }
   if (dt == kF16 && K == 3 && stride == 1)
     return tdc_dwconv3x3_fwd(x, w, bias, residual, y, N, H, W, C, pad, act, n_stage, stream);
   Epilogue epi;
@@ -1156,6 +1301,40 @@ TDC_API int tdc_dwconv_fwd_bf16(const void* x, const void* w, const void* bias,
                                 int64_t n_stage, void* stream) {
   return fwd_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad, act, n_stage,
                    stream);
+}
+
+static int plain_entry(int dt, const void* x, const void* w, const void* bias,
+                       const void* residual, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
+                       int64_t K, int64_t stride, int64_t pad, int64_t act, int64_t band_rows,
+                       void* stream) {
+  if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
+  Epilogue epi;
+  epi.fused = true;
+  epi.bias = bias;
+  epi.residual = residual;
+  epi.act = int(act);
+  return fwd_plain(x, w, y, N, H, W, C, K, stride, pad, band_rows, epi, stream, dt);
+}
+
+TDC_API int tdc_dwconv_fwd_plain(const void* x, const void* w, const void* bias,
+                                 const void* residual, void* y, int64_t N, int64_t H, int64_t W,
+                                 int64_t C, int64_t K, int64_t stride, int64_t pad, int64_t act,
+                                 int64_t band_rows, void* stream) {
+  return plain_entry(kF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad, act, band_rows,
+                     stream);
+}
+
+TDC_API int tdc_dwconv_fwd_plain_bf16(const void* x, const void* w, const void* bias,
+                                      const void* residual, void* y, int64_t N, int64_t H,
+                                      int64_t W, int64_t C, int64_t K, int64_t stride,
+                                      int64_t pad, int64_t act, int64_t band_rows, void* stream) {
+  return plain_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad, act, band_rows,
+                     stream);
+}
+
+TDC_API int tdc_dwconv_fwd_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                      int64_t stride, int64_t pad) {
+  return prefer_plain(N, H, W, C, K, stride, pad) ? 1 : 0;
 }
 
 TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,

@@ -158,10 +158,8 @@ def dwconv_op(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], st
               pad: int) -> torch.Tensor:
     """Depthwise K x K forward with an optional fused bias: x [N,H,W,C] fp16,
     w [K,K,C] fp16, bias [C] fp16 or None -> [N,P,Q,C]."""
-    k = int(w.shape[0])
     b = None if bias is None else bias.contiguous()
-    return _C.dwconv_k(x.contiguous(), w.contiguous(), b, None, stride, pad, 0,
-                       DWCONV_STAGES[(k, stride)])
+    return _C.dwconv_k(x.contiguous(), w.contiguous(), b, None, stride, pad, 0, 0)
 
 
 @dwconv_op.register_fake
@@ -272,10 +270,12 @@ class DepthwiseConv2d(nn.Module):
         act = self.activation
         needs_grad = torch.is_grad_enabled() and (
             x.requires_grad or self.weight.requires_grad or (b is not None and b.requires_grad))
-        if act != "none" and not needs_grad:
-            # inference: the activation runs in the kernel's fused epilogue
-            y = _T.dwconv(x_nhwc, w_rsc.contiguous(), self.padding, stride=self.stride, bias=b,
-                          activation=act)
+        if not needs_grad:
+            # inference: straight to the extension (which checks its arguments),
+            # without the custom op's dispatch; the activation runs in the
+            # kernel's fused epilogue
+            y = _C.dwconv_k(x_nhwc, w_rsc.contiguous(), None if b is None else b.contiguous(),
+                            None, self.stride, self.padding, _T.ACTIVATIONS[act], 0)
         else:
             y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
             if act != "none":  # the custom op's autograd covers conv + bias

@@ -219,8 +219,12 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int
     ``y[n,p,q,c] = round(epilogue(sum_{r,s} x[n, stride*p+r-pad, stride*q+s-pad, c] * w[r,s,c]))``,
     fp32 sums in (r, s) order from zero, zero outside the image, one
     rounding to x's dtype (fp16 or bfloat16).  The epilogue is
-    ``dwconv3x3``'s.  ``pad`` defaults to K // 2, ``n_stage`` to
-    ``DWCONV_STAGES[(K, stride)]``.  For fp16, 3x3 stride 1 is ``dwconv3x3``.
+    ``dwconv3x3``'s.  ``pad`` defaults to K // 2.  ``n_stage`` 2, 3 or 4 runs
+    the TMA ring kernel with that depth (for fp16, 3x3 stride 1 is
+    ``dwconv3x3``); None leaves the kernel to the library: ``dwconv_plain``
+    where ``uses_plain`` says so (few channels, narrow images), else the ring
+    kernel at ``DWCONV_STAGES[(K, stride)]``.  The result is the same bit for
+    bit either way.
 
     Args:
         x: [N, H, W, C] fp16 or bf16 CUDA, contiguous, C % 8 == 0.   w: [K, K, C], x's dtype.
@@ -237,14 +241,44 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int
         raise ValueError(f"stride must be 1 or 2, got {stride}")
     if x.shape[3] % 8 != 0:
         raise ValueError("dwconv requires C % 8 == 0")
-    if n_stage is None:
-        n_stage = DWCONV_STAGES[(K, stride)]
-    if n_stage not in (2, 3, 4):
+    if n_stage is not None and n_stage not in (2, 3, 4):
         raise ValueError(f"n_stage must be one of {{2, 3, 4}}, got {n_stage}")
     if activation not in ACTIVATIONS:
         raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
     return _C.dwconv_k(x, w, bias, residual, int(stride), int(pad), ACTIVATIONS[activation],
-                       int(n_stage))
+                       0 if n_stage is None else int(n_stage))
+
+
+def dwconv_plain(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int = 1,
+                 bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                 activation: str = "none", band_rows: int = 0) -> torch.Tensor:
+    """``dwconv`` on the plain kernel: global loads through L1, no TMA, no
+    shared memory.  A thread owns one channel pair of one output column over
+    ``band_rows`` output rows (0: chosen from the shape).  Same arguments
+    (``band_rows`` for ``n_stage``) and the same result, bit for bit."""
+    if w.dim() == 3 and pad is None:
+        pad = int(w.shape[0]) // 2
+    _check(x, w, pad, bf16_ok=True)
+    K = int(w.shape[0])
+    if K not in (3, 5, 7) or w.shape[1] != K:
+        raise ValueError(f"w must be [K,K,C] with K in {{3, 5, 7}}, got shape {tuple(w.shape)}")
+    if stride not in (1, 2):
+        raise ValueError(f"stride must be 1 or 2, got {stride}")
+    if x.shape[3] % 8 != 0:
+        raise ValueError("dwconv_plain requires C % 8 == 0")
+    if band_rows < 0:
+        raise ValueError(f"band_rows must be non-negative, got {band_rows}")
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
+    return _C.dwconv_plain(x, w, bias, residual, int(stride), int(pad), ACTIVATIONS[activation],
+                           int(band_rows))
+
+
+def uses_plain(N: int, H: int, W: int, C: int, K: int = 3, stride: int = 1,
+               pad: int | None = None) -> bool:
+    """Whether ``dwconv`` with ``n_stage=None`` runs the plain kernel on this shape."""
+    return bool(_C.dwconv_uses_plain(int(N), int(H), int(W), int(C), int(K), int(stride),
+                                     int(K // 2 if pad is None else pad)))
 
 
 def device_status(device: int | None = None, clear: bool = True):
