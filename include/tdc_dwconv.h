@@ -190,6 +190,34 @@ TDC_API int tdc_dwconv_fwd_plain_bf16(const void* x, const void* w, const void* 
 TDC_API int tdc_dwconv_fwd_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
                                       int64_t stride, int64_t pad);
 
+/* Plain weight gradient of the K x K forward (K = 3, 5, 7, stride 1 or 2):
+ * dw [K,K,C] fp32 as tdc_dwconv_bwd_weight, for the same small shapes as
+ * tdc_dwconv_fwd_plain.  A thread keeps one channel pair's K*K sums of one
+ * (image, band of dy rows); a CTA adds its units up in a fixed order and
+ * writes one slice of its channels, so the workspace
+ * (tdc_dwconv_bwd_weight_plain_workspace) is about units / 16 x K*K x C
+ * floats rather than the ws kernels' grid x 4 x K*K x C; a fixed-order
+ * reduction sums the slices (deterministic).  N = 0 writes zeros.  No
+ * counterpart in the reference. */
+TDC_API int tdc_dwconv_bwd_weight_plain_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
+                                                  int64_t K, int64_t stride, int64_t pad,
+                                                  int64_t* bytes);
+TDC_API int tdc_dwconv_bwd_weight_plain(const void* x, const void* dy, float* dw,
+                                        int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                        int64_t stride, int64_t pad, void* workspace,
+                                        int64_t workspace_bytes, void* stream);
+TDC_API int tdc_dwconv_bwd_weight_plain_bf16(const void* x, const void* dy, float* dw,
+                                             int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                             int64_t stride, int64_t pad, void* workspace,
+                                             int64_t workspace_bytes, void* stream);
+
+/* 1 if tdc_dwconv_bwd_weight(_workspace) with n_stage 0 run the plain kernel
+ * on this shape, else 0 (pure host arithmetic): output width Q <= 16 or
+ * C <= 16 (a plain thread walks the whole width, so wide images with more
+ * channels stay on the ws kernels). */
+TDC_API int tdc_dwconv_bwd_weight_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C,
+                                             int64_t K, int64_t stride, int64_t pad);
+
 /* Launch plan tdc_dwconv_fwd would use (same layout as tdc_ws_plan's
  * plan[0..7]; pure host arithmetic).  For K >= 5 at stride 1 and 7x7 at
  * stride 2 the kernel holds the K input rows of one output row at once, and
@@ -262,9 +290,15 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
  *                     s = K-1 .. 0 with v + pad - s even, of
  *                     fma(dy[n, (h+pad-r)/2, (v+pad-s)/2, c], w[r,s,c], acc)
  *     from +0 (dy = 0 outside [0,P) x [0,Q)), one fp16 rounding.
+ *     n_stage 0 leaves the kernel to the library: at stride 1 the plain
+ *     kernel (tdc_dwconv_fwd_plain with flipped taps) where
+ *     tdc_dwconv_fwd_uses_plain(N, P, Q, C, K, 1, K - 1 - pad) says so, else
+ *     the default ring depth; the result is the same bit for bit.
  *   tdc_dwconv_bwd_weight: dw [K,K,C] fp32 (written), deterministic like
  *     tdc_dwconv3x3_bwd_weight, with a caller workspace of at least the size
- *     tdc_dwconv_bwd_weight_workspace reports (same stride argument).  At
+ *     tdc_dwconv_bwd_weight_workspace reports (same stride and n_stage
+ *     arguments; n_stage 0 picks tdc_dwconv_bwd_weight_plain where
+ *     tdc_dwconv_bwd_weight_uses_plain says so, else the default depth).  At
  *     stride 1, K = 3 is tdc_dwconv3x3_bwd_weight.  At stride 2,
  *       dw[r,s,c] = sum_{n,p,q} x[n, 2p+r-pad, 2q+s-pad, c] * dy[n,p,q,c]
  *     with P = (H + 2*pad - K)/2 + 1 (x rows and columns that no output

@@ -2,6 +2,8 @@
 
     python tests/bench_models.py [--batch 64] [--size 224] [--iters 20] [--graphs]
     python tests/bench_models.py --layers [--batch 64]
+    python tests/bench_models.py --layers-bwd [--batch 64]
+    python tests/bench_models.py --train [--batch 64]
 
 torchvision MobileNetV2, MobileNetV3-Large and EfficientNet-B0 (random
 weights, random BatchNorm statistics), fp16, channels-last, eval mode.  Per
@@ -20,8 +22,17 @@ alone (input shape recorded by forward hooks): cuDNN's channels-last conv2d,
 the ws kernel (``_C.dwconv_k`` at the default ring depth) and the plain kernel
 (``_C.dwconv_plain``), each as 20 back-to-back calls replayed from a CUDA
 graph, the kernel the automatic choice takes, and the algorithmic bytes (x
-read + y written) per call.  A script,
-not a test.
+read + y written) per call.  ``--layers-bwd`` does the same for the
+gradients: cuDNN's data and weight gradients (``aten.convolution_backward``)
+against ``_C.dwconv_bwd_data`` and ``_C.dwconv_bwd_weight`` with the
+automatic kernel choice (n_stage 0) and with the ws kernels at their default
+depths, and the plain weight gradient.  ``--train`` times a training step
+(forward, loss, backward; BatchNorm in training mode) of each model, stock
+against ``convert_depthwise_convs``, eager (use a batch of 128 or more so the
+GPU, not the host's launches, sets the time).  Both fp16 models' losses
+and depthwise weight gradients are compared with an fp32 copy of the model
+(relative L2 distance per layer: largest and median).
+A script, not a test.
 """
 from __future__ import annotations
 
@@ -147,6 +158,90 @@ def bench_layers(batch: int, size: int, iters: int) -> None:
                       "layers_total_auto_us": round(tot_t, 1)}), flush=True)
 
 
+def bench_layers_bwd(batch: int, size: int, iters: int) -> None:
+    import tma_dwconv as T
+    reps = 10
+    names = ("cudnn_dx", "cudnn_dw", "dx_auto", "dx_ws", "dw_auto", "dw_ws", "dw_plain")
+    tot = dict.fromkeys(names, 0.0)
+    conv_bwd = torch.ops.aten.convolution_backward
+    for (n, h, w, c, k, s, pad), arch in depthwise_layers(batch, size):
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(n, h, w, c, device="cuda", generator=g).half()
+        wt = (torch.randn(k, k, c, device="cuda", generator=g) / k).half()
+        p, q = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+        dy = torch.randn(n, p, q, c, device="cuda", generator=g).half()
+        x_nchw, dy_nchw = x.permute(0, 3, 1, 2), dy.permute(0, 3, 1, 2)
+        w_conv = wt.permute(2, 0, 1).unsqueeze(1).contiguous()
+
+        def cudnn(mask):
+            return lambda: conv_bwd(dy_nchw, x_nchw, w_conv, None, [s, s], [pad, pad], [1, 1],
+                                    False, [0, 0], c, mask)
+        dx_stage, dw_stage = tdc_torch.BWD_STAGES[(k, s)]
+        fns = {
+            "cudnn_dx": cudnn([True, False, False]),
+            "cudnn_dw": cudnn([False, True, False]),
+            "dx_auto": lambda: T._C.dwconv_bwd_data(dy, wt, pad, s, 0, h, w),
+            "dx_ws": lambda: T._C.dwconv_bwd_data(dy, wt, pad, s, dx_stage, h, w),
+            "dw_auto": lambda: T._C.dwconv_bwd_weight(x, dy, k, pad, s, 0),
+            "dw_ws": lambda: T._C.dwconv_bwd_weight(x, dy, k, pad, s, dw_stage),
+            "dw_plain": lambda: T._C.dwconv_bwd_weight_plain(x, dy, k, pad, s),
+        }
+        row = {"model": arch, "N": n, "H": h, "W": w, "C": c, "K": k, "stride": s,
+               "dw_uses_plain": bool(T._C.dwconv_bwd_weight_uses_plain(n, h, w, c, k, s, pad))}
+        for name, fn in fns.items():
+            t = bench_ms(graph_of(fn, reps), iters=iters) / reps * 1e3
+            row[name + "_us"] = round(t, 2)
+            tot[name] += t
+        print(json.dumps(row), flush=True)
+    print(json.dumps({"totals_us": {k_: round(v, 1) for k_, v in tot.items()}}), flush=True)
+
+
+def bench_train(batch: int, size: int, iters: int) -> None:
+    x = torch.randn(batch, 3, size, size, device="cuda").half()
+    x = x.to(memory_format=torch.channels_last)
+    for arch in ("mobilenet_v2", "mobilenet_v3_large", "efficientnet_b0"):
+        torch.manual_seed(0)
+        base = getattr(torchvision.models, arch)().train().cuda().half()
+        base = base.to(memory_format=torch.channels_last)
+        converted = copy.deepcopy(base)
+        n_conv = tdc_torch.convert_depthwise_convs(converted)
+        ref32 = copy.deepcopy(base).float()
+        row = {"model": arch, "batch": batch, "size": size, "depthwise_converted": n_conv}
+        grads = {}
+        for name, m in (("fp32", ref32), ("cudnn", base), ("converted", converted)):
+            xin = x.float() if name == "fp32" else x
+
+            def step(m=m, xin=xin):
+                # a sum, not a mean: keeps the fp16 gradients of the first
+                # layers above fp16's underflow (no loss scaling here)
+                loss = m(xin).float().square().sum()
+                loss.backward()
+                return loss
+            for p_ in m.parameters():
+                p_.grad = None
+            first = step()
+            dws = [mod.weight.grad.float().clone() for mod in m.modules()
+                   if isinstance(mod, tdc_torch.DepthwiseConv2d)
+                   or (isinstance(mod, torch.nn.Conv2d) and mod.groups == mod.in_channels > 1)]
+            grads[name] = (first.item(), dws)
+            for p_ in m.parameters():
+                p_.grad = None
+            if name != "fp32":
+                row[f"{name}_ms"] = round(bench_ms(step, iters=iters), 3)
+        (lr, gr), (l0, g0), (l1, g1) = grads["fp32"], grads["cudnn"], grads["converted"]
+
+        def rel(ga, gb):  # per depthwise layer, relative L2 distance of gb from ga
+            return [((b - a).norm() / a.norm()).item() for a, b in zip(ga, gb)]
+        for tag, (l_, g_) in (("cudnn", (l0, g0)), ("converted", (l1, g1))):
+            d = rel(gr, g_)
+            row[f"{tag}_vs_fp32"] = {"loss": abs(l_ - lr) / abs(lr),
+                                     "dw_max": round(max(d), 4),
+                                     "dw_median": round(sorted(d)[len(d) // 2], 4),
+                                     "finite": all(bool(t.isfinite().all()) for t in g_)}
+        row["speedup"] = round(row["cudnn_ms"] / row["converted_ms"], 3)
+        print(json.dumps(row), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=64)
@@ -154,7 +249,15 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--graphs", action="store_true", help="time CUDA-graph replays")
     ap.add_argument("--layers", action="store_true", help="time each depthwise layer alone")
+    ap.add_argument("--layers-bwd", action="store_true", help="time each layer's gradients")
+    ap.add_argument("--train", action="store_true", help="time a training step per model")
     args = ap.parse_args()
+    if args.train:
+        bench_train(args.batch, args.size, args.iters)
+        return
+    if args.layers_bwd:
+        bench_layers_bwd(args.batch, args.size, args.iters)
+        return
     if args.layers:
         bench_layers(args.batch, args.size, args.iters)
         return

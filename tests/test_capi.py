@@ -694,3 +694,84 @@ def test_plain_row_loop_feeds_each_output_its_taps_in_order(K, S):
                         del owner[a]
         assert all(taps[o] == list(range(K)) for o in range(rows)), rows
         assert sorted(stored) == list(range(rows))
+
+
+def test_plain_weight_gradient_argument_errors(lib):
+    p = C.c_void_p
+    b = i64()
+    def ws(K=5, stride=1, C_=72, pad=2, H=16, N=2):
+        return lib.tdc_dwconv_bwd_weight_plain_workspace(i64(N), i64(H), i64(16), i64(C_), i64(K),
+                                                         i64(stride), i64(pad), C.byref(b))
+    def wg(K=5, stride=1, C_=72, pad=2, H=16, N=2, x=16, dw=16, f=None):
+        f = f or lib.tdc_dwconv_bwd_weight_plain
+        return f(p(x), p(16), p(dw), i64(N), i64(H), i64(16), i64(C_), i64(K), i64(stride),
+                 i64(pad), p(16), i64(1 << 20), None)
+    assert ws(K=4) == CODES["TDC_ERR_FILTER_SHAPE"]
+    assert ws(stride=3) == CODES["TDC_ERR_STRIDE"]
+    assert ws(C_=12) == CODES["TDC_ERR_CHANNELS"]
+    assert ws(pad=-1) == CODES["TDC_ERR_PAD"]
+    assert ws(K=7, H=2, pad=2) == CODES["TDC_ERR_BAD_SHAPE"]
+    assert lib.tdc_dwconv_bwd_weight_plain_workspace(i64(2), i64(16), i64(16), i64(64), i64(3),
+                                                     i64(1), i64(1), None) == CODES["TDC_ERR_NULL_POINTER"]
+    for f in (lib.tdc_dwconv_bwd_weight_plain, lib.tdc_dwconv_bwd_weight_plain_bf16):
+        assert wg(K=4, f=f) == CODES["TDC_ERR_FILTER_SHAPE"]
+        assert wg(stride=0, f=f) == CODES["TDC_ERR_STRIDE"]
+        assert wg(C_=12, f=f) == CODES["TDC_ERR_CHANNELS"]
+        assert wg(x=0, f=f) == CODES["TDC_ERR_NULL_POINTER"]
+        assert wg(dw=0, f=f) == CODES["TDC_ERR_NULL_POINTER"]
+        assert wg(x=24, f=f) == CODES["TDC_ERR_ALIGNMENT"]
+        if not torch.cuda.is_available():
+            assert wg(f=f) == CODES["TDC_ERR_NO_DEVICE"]
+            assert ws() == CODES["TDC_ERR_NO_DEVICE"]
+
+
+def wgrad_uses_plain(N, H, W, Cc, K, S, pad):
+    """Restates tdc_dwconv_bwd_weight_uses_plain: output width <= 16 or at
+    most 16 channels."""
+    Q = (W + 2 * pad - K) // S + 1
+    return Q <= 16 or Cc <= 16
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+def test_weight_gradient_choice(lib, K, S):
+    for (N, H, W, Cc) in [(64, 224, 336, 256), (64, 112, 112, 16), (64, 14, 14, 576),
+                          (64, 7, 7, 960), (256, 28, 28, 192), (2, 20, 40, 64),
+                          (64, 112, 112, 32), (64, 56, 56, 72), (64, 33, 33, 64)]:
+        args = [i64(v) for v in (N, H, W, Cc, K, S, K // 2)]
+        assert lib.tdc_dwconv_bwd_weight_uses_plain(*args) == int(
+            wgrad_uses_plain(N, H, W, Cc, K, S, K // 2)), (N, H, W, Cc)
+    assert lib.tdc_dwconv_bwd_weight_uses_plain(i64(64), i64(7), i64(7), i64(960), i64(5), i64(1), i64(2)) == 1
+    assert lib.tdc_dwconv_bwd_weight_uses_plain(i64(64), i64(56), i64(56), i64(72), i64(3), i64(1), i64(1)) == 0
+
+
+def wgrad_plain_plan(N, P, Cc, K, sms=148):
+    """Restates wgrad_plain_plan: bands of dy rows for about 1024 threads per
+    SM counting the K tap rows; units (image, band) dealt 16 or 32 to a CTA."""
+    cpairs = Cc // 2
+    clog = 3 if cpairs % 8 == 0 else 2
+    per_band = max(1, N * cpairs * K)
+    bands = min(P, max(1, -(-1024 * sms // per_band)))
+    band_rows = -(-P // bands)
+    bands = -(-P // band_rows)
+    units = N * bands
+    upc = 128 >> clog
+    return dict(band_rows=band_rows, bands=bands, units=units, upc=upc,
+                ugroups=-(-units // upc), chunks=cpairs >> clog, cpc=1 << clog)
+
+
+@pytest.mark.parametrize("N,P,Cc,K", [(64, 7, 960, 5), (64, 112, 16, 3), (3, 5, 72, 7),
+                                      (1, 1, 8, 3), (256, 14, 184, 3)])
+def test_plain_weight_gradient_units_cover_every_dy_row_once(N, P, Cc, K):
+    pl = wgrad_plain_plan(N, P, Cc, K)
+    seen = set()
+    for ugroup in range(pl["ugroups"]):          # blockIdx.x / chunks
+        for ul in range(pl["upc"]):              # threadIdx.x >> chunk_log2
+            u = ugroup * pl["upc"] + ul
+            if u >= pl["units"]:
+                continue
+            n, band = divmod(u, pl["bands"])
+            for pr in range(band * pl["band_rows"], min(P, (band + 1) * pl["band_rows"])):
+                assert (n, pr) not in seen
+                seen.add((n, pr))
+    assert len(seen) == N * P
+    assert pl["chunks"] * pl["cpc"] == Cc // 2

@@ -146,3 +146,82 @@ def test_graph_capture_and_streams():
     g.replay()
     torch.cuda.synchronize()
     assert np.array_equal(_bits(y), want)
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("N,H,W,C", [(4, 14, 14, 200), (2, 7, 7, 96), (3, 23, 30, 16),
+                                     (2, 19, 40, 64)])
+def test_automatic_data_gradient_matches_oracle(K, N, H, W, C):
+    """Stride-1 data gradient with n_stage 0: the plain kernel with flipped
+    taps where the shape calls for it, bit for bit with the oracle and with
+    the ring kernel."""
+    for pad in sorted({0, K // 2, K - 1}):
+        P, Q = H + 2 * pad - K + 1, W + 2 * pad - K + 1
+        if P < 1 or Q < 1:
+            continue
+        g = torch.Generator().manual_seed(K * 7 + pad)
+        dy = torch.randn(N, P, Q, C, generator=g).half()
+        w = (torch.randn(K, K, C, generator=g) / K).half()
+        want = oracle.dwconv_bwd_data_f16(dy.numpy(), w.numpy(), pad).view(np.uint16)
+        auto = T._C.dwconv_bwd_data(dy.cuda(), w.cuda(), pad, 1, 0, H, W)
+        ring = T._C.dwconv_bwd_data(dy.cuda(), w.cuda(), pad, 1, T.DWCONV_STAGES[(K, 1)], H, W)
+        assert np.array_equal(_bits(auto), want), pad
+        assert np.array_equal(_bits(ring), want), pad
+
+
+def _wgrad_ref(x, dy, pad, K, S):
+    xf = x.float().numpy().astype(np.float64)
+    dyf = dy.float().numpy().astype(np.float64)
+    ref = oracle.dwconv_bwd_weight_f64(xf, dyf, pad, K, stride=S)
+    scale = oracle.dwconv_bwd_weight_f64(np.abs(xf), np.abs(dyf), pad, K, stride=S)
+    return ref, scale
+
+
+@pytest.mark.parametrize("K,S", GEOMS)
+@pytest.mark.parametrize("N,H,W,C,pad", [
+    (4, 14, 14, 200, None), (3, 7, 7, 96, None), (2, 23, 30, 16, 0), (2, 19, 40, 72, "big"),
+    (1, 1, 20, 8, None), (5, 9, 3, 24, None),
+])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_plain_weight_gradient_close_to_float64(K, S, N, H, W, C, pad, dtype):
+    """The plain weight gradient: within 5e-4 of sum |x * dy| of the float64
+    oracle (the bar of the ring kernels' weight gradients), bit-reproducible."""
+    pad = K - 1 if pad == "big" else (K // 2 if pad is None else pad)
+    if H + 2 * pad < K or W + 2 * pad < K:
+        pytest.skip("no output")
+    P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
+    g = torch.Generator().manual_seed(K * 10 + S + C)
+    x = torch.randn(N, H, W, C, generator=g).to(dtype)
+    dy = torch.randn(N, P, Q, C, generator=g).to(dtype)
+    ref, scale = _wgrad_ref(x, dy, pad, K, S)
+    a = T._C.dwconv_bwd_weight_plain(x.cuda(), dy.cuda(), K, pad, S)
+    b = T._C.dwconv_bwd_weight_plain(x.cuda(), dy.cuda(), K, pad, S)
+    dw = a.cpu().numpy()
+    assert dw.dtype == np.float32 and dw.shape == (K, K, C)
+    assert (np.abs(dw - ref) <= 5e-4 * scale + 1e-6).all(), np.abs(dw - ref).max()
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+@pytest.mark.parametrize("K,S", GEOMS)
+def test_automatic_weight_gradient(K, S):
+    """n_stage 0: the plain kernel where the shape calls for it (the same bits
+    as calling it directly), the ring kernel elsewhere; both within the bar."""
+    for (N, H, W, C) in [(8, 14, 14, 480), (4, 40, 72, 64)]:
+        pad = K // 2
+        P, Q = (H + 2 * pad - K) // S + 1, (W + 2 * pad - K) // S + 1
+        g = torch.Generator().manual_seed(K + S + C)
+        x = torch.randn(N, H, W, C, generator=g).half()
+        dy = torch.randn(N, P, Q, C, generator=g).half()
+        ref, scale = _wgrad_ref(x, dy, pad, K, S)
+        auto = T._C.dwconv_bwd_weight(x.cuda(), dy.cuda(), K, pad, S, 0)
+        assert (np.abs(auto.cpu().numpy() - ref) <= 5e-4 * scale + 1e-6).all()
+        if T._C.dwconv_bwd_weight_uses_plain(N, H, W, C, K, S, pad):
+            plain = T._C.dwconv_bwd_weight_plain(x.cuda(), dy.cuda(), K, pad, S)
+            assert torch.equal(auto.view(torch.int32), plain.view(torch.int32))
+
+
+def test_plain_weight_gradient_empty_batch_is_zero():
+    x = torch.empty(0, 9, 9, 64, device="cuda", dtype=torch.float16)
+    dy = torch.empty(0, 9, 9, 64, device="cuda", dtype=torch.float16)
+    dw = T._C.dwconv_bwd_weight_plain(x, dy, 3, 1, 1)
+    assert dw.shape == (3, 3, 64) and not dw.any()

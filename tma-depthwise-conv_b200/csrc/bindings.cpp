@@ -272,6 +272,41 @@ torch::Tensor dwconv_plain(torch::Tensor x, torch::Tensor w, std::optional<torch
   return y;
 }
 
+// The plain weight gradient (no TMA; workspace per channel chunk).
+torch::Tensor dwconv_bwd_weight_plain(torch::Tensor x, torch::Tensor dy, int64_t K, int64_t pad,
+                                      int64_t stride) {
+  TORCH_CHECK(x.is_cuda() && dy.is_cuda() && x.device() == dy.device(), "tensors must live on CUDA");
+  TORCH_CHECK((x.scalar_type() == torch::kHalf || x.scalar_type() == torch::kBFloat16) &&
+                  dy.scalar_type() == x.scalar_type(),
+              "x and dy must be both fp16 or both bf16");
+  const bool bf16 = x.scalar_type() == torch::kBFloat16;
+  TORCH_CHECK(x.dim() == 4 && dy.dim() == 4 && x.is_contiguous() && dy.is_contiguous(),
+              "x and dy must be contiguous [N,H,W,C] / [N,P,Q,C]");
+  TORCH_CHECK(K == 3 || K == 5 || K == 7, "K must be 3, 5 or 7, got ", K);
+  TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(pad >= 0, "pad must be non-negative");
+  TORCH_CHECK(x.size(1) + 2 * pad >= K && x.size(2) + 2 * pad >= K,
+              "x is smaller than a ", K, "x", K, " kernel with pad ", pad, " needs");
+  TORCH_CHECK(dy.size(0) == x.size(0) && dy.size(3) == x.size(3) &&
+                  dy.size(1) == (x.size(1) + 2 * pad - K) / stride + 1 &&
+                  dy.size(2) == (x.size(2) + 2 * pad - K) / stride + 1,
+              "dy must be [N, (H+2*pad-K)/stride+1, (W+2*pad-K)/stride+1, C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dw = torch::empty({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
+  if (x.size(3) == 0) return dw;
+  int64_t bytes = 0;
+  check_status(tdc_dwconv_bwd_weight_plain_workspace(x.size(0), x.size(1), x.size(2), x.size(3),
+                                                     K, stride, pad, &bytes),
+               "dwconv_bwd_weight_plain");
+  auto ws = torch::empty({std::max<int64_t>(4, (bytes + 3) / 4)}, x.options().dtype(torch::kFloat32));
+  auto* bwd = bf16 ? &tdc_dwconv_bwd_weight_plain_bf16 : &tdc_dwconv_bwd_weight_plain;
+  check_status(bwd(x.data_ptr(), dy.data_ptr(), dw.data_ptr<float>(), x.size(0), x.size(1),
+                   x.size(2), x.size(3), K, stride, pad, ws.data_ptr(), bytes, stream_of(x)),
+               "dwconv_bwd_weight_plain");
+  return dw;
+}
+
 // Data gradient: dy [N,P,Q,C] -> dx [N,H,W,C] with H = P - 2*pad + 2.
 torch::Tensor dwconv3x3_bwd_data(torch::Tensor dy, torch::Tensor w, int64_t pad, int64_t n_stage) {
   check_common(dy, w);
@@ -379,8 +414,10 @@ torch::Tensor dwconv_bwd_weight(torch::Tensor x, torch::Tensor dy, int64_t K, in
                   dy.size(2) == (x.size(2) + 2 * pad - K) / stride + 1,
               "dy must be [N, (H+2*pad-K)/stride+1, (W+2*pad-K)/stride+1, C]");
   const c10::cuda::CUDAGuard guard(x.device());
-  auto dw = torch::zeros({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
-  if (x.numel() == 0 || dy.numel() == 0) return dw;
+  // Every kernel path writes all of dw; only an empty problem needs zeros.
+  if (x.numel() == 0 || dy.numel() == 0)
+    return torch::zeros({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
+  auto dw = torch::empty({K, K, x.size(3)}, x.options().dtype(torch::kFloat32));
   int64_t bytes = 0;
   auto* wsq = bf16 ? &tdc_dwconv_bwd_weight_workspace_bf16 : &tdc_dwconv_bwd_weight_workspace;
   check_status(wsq(x.size(0), x.size(1), x.size(2), x.size(3), K, stride, pad, n_stage, &bytes),
@@ -477,6 +514,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "plain (no TMA) K x K depthwise forward, the same result as dwconv_k",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
         py::arg("pad"), py::arg("act"), py::arg("band_rows"));
+  m.def("dwconv_bwd_weight_plain", &tma_dwconv::dwconv_bwd_weight_plain,
+        "plain (no TMA) weight gradient dw [K,K,C] fp32, deterministic",
+        py::arg("x"), py::arg("dy"), py::arg("K"), py::arg("pad"), py::arg("stride"));
+  m.def("dwconv_bwd_weight_uses_plain",
+        [](int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad) {
+          return tdc_dwconv_bwd_weight_uses_plain(N, H, W, C, K, stride, pad) != 0;
+        },
+        "whether dwconv_bwd_weight with n_stage 0 runs the plain kernel on this shape");
   m.def("dwconv_uses_plain",
         [](int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t stride, int64_t pad) {
           return tdc_dwconv_fwd_uses_plain(N, H, W, C, K, stride, pad) != 0;

@@ -628,6 +628,128 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
+// Plain weight gradient (tdc_plain.cuh): bands of dy rows chosen for about
+// 1024 threads per SM counting the K tap rows, the units of one channel
+// chunk summed per CTA, one workspace slice per unit group.
+struct WgradPlainPlan {
+  int64_t band_rows = 1, bands = 1, units = 0, ugroups = 0, chunks = 0;
+  int chunk_log2 = 3;
+};
+
+int wgrad_plain_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                     int64_t pad, int64_t sms, WgradPlainPlan* pl, int64_t* P, int64_t* Q) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (S != 1 && S != 2) return TDC_ERR_STRIDE;
+  if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pad < 0) return TDC_ERR_PAD;
+  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
+  *P = (H + 2 * pad - K) / S + 1;
+  *Q = (W + 2 * pad - K) / S + 1;
+  const int64_t i32 = 0x7fffffffll;
+  const int64_t cpairs = C / 2;
+  if (N > i32 || C > i32 || H + 2 * pad > i32 || W + 2 * pad > i32) return TDC_ERR_TOO_LARGE;
+  if (H * W > i32 || H * W * cpairs > i32 || *P * *Q > i32 || *P * *Q * cpairs > i32)
+    return TDC_ERR_TOO_LARGE;  // 32-bit offsets within an image
+  pl->chunk_log2 = cpairs % 8 == 0 ? 3 : 2;
+  pl->chunks = cpairs >> pl->chunk_log2;
+  const int64_t per_band = std::max<int64_t>(1, N * cpairs * K);
+  const int64_t want = 1024 * std::max<int64_t>(1, sms);
+  const int64_t bands = std::min<int64_t>(*P, std::max<int64_t>(1, (want + per_band - 1) / per_band));
+  pl->band_rows = (*P + bands - 1) / bands;
+  pl->bands = (*P + pl->band_rows - 1) / pl->band_rows;
+  pl->units = N * pl->bands;
+  const int64_t upc = tdc::kPlainThreads >> pl->chunk_log2;
+  pl->ugroups = (pl->units + upc - 1) / upc;
+  if (pl->units > i32 || pl->ugroups * std::max<int64_t>(1, pl->chunks) > i32)
+    return TDC_ERR_TOO_LARGE;
+  return TDC_OK;
+}
+
+using WgradPlainLaunchFn = cudaError_t (*)(const tdc::WgradPlainParams&, int64_t, cudaStream_t);
+
+// One CTA row per tap row (grid.y = K).
+template <int K, int S, class E>
+cudaError_t wgrad_plain_launch_t(const tdc::WgradPlainParams& prm, int64_t grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid), unsigned(K));
+  cfg.blockDim = dim3(unsigned(tdc::kPlainThreads));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, &tdc::dwconv_wgrad_plain_kernel<K, S, E>, prm);
+}
+
+#define TDC_WGP_S(E, K) {wgrad_plain_launch_t<K, 1, E>, wgrad_plain_launch_t<K, 2, E>}
+#define TDC_WGP_TABLE(E) {TDC_WGP_S(E, 3), TDC_WGP_S(E, 5), TDC_WGP_S(E, 7)}
+// [element type][K index: 3, 5, 7][stride - 1]
+const WgradPlainLaunchFn kWgradPlainLaunch[2][3][2] = {TDC_WGP_TABLE(tdc::F16),
+                                                       TDC_WGP_TABLE(tdc::BF16)};
+#undef TDC_WGP_TABLE
+#undef TDC_WGP_S
+
+int wgrad_plain_workspace(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                          int64_t pad, int64_t* bytes) {
+  if (!bytes) return TDC_ERR_NULL_POINTER;
+  int64_t P, Q;
+  WgradPlainPlan pl;
+  int rc = wgrad_plain_plan(N, H, W, C, K, S, pad, 1, &pl, &P, &Q);  // shape checks first
+  if (rc != TDC_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  rc = wgrad_plain_plan(N, H, W, C, K, S, pad, dev->sms, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  *bytes = pl.ugroups * K * K * C * int64_t(sizeof(float));
+  return TDC_OK;
+}
+
+int wgrad_plain(int dt, const void* x, const void* dy, float* dw, int64_t N, int64_t H, int64_t W,
+                int64_t C, int64_t K, int64_t S, int64_t pad, void* workspace,
+                int64_t workspace_bytes, void* stream) {
+  int64_t P, Q;
+  WgradPlainPlan pl;
+  int rc = wgrad_plain_plan(N, H, W, C, K, S, pad, 1, &pl, &P, &Q);  // shape checks first
+  if (rc != TDC_OK) return rc;
+  if (C == 0) return TDC_OK;
+  if (!dw) return TDC_ERR_NULL_POINTER;
+  if (N > 0 && (!x || !dy || !workspace)) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(dw) || (N > 0 && (!aligned16(x) || !aligned16(dy) || !aligned16(workspace))))
+    return TDC_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0) {  // no products: the gradient is zero
+    const cudaError_t e = cudaMemsetAsync(dw, 0, size_t(K * K * C) * sizeof(float), st);
+    return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+  }
+  rc = wgrad_plain_plan(N, H, W, C, K, S, pad, dev->sms, &pl, &P, &Q);
+  if (rc != TDC_OK) return rc;
+  if (workspace_bytes < pl.ugroups * K * K * C * int64_t(sizeof(float))) return TDC_ERR_WORKSPACE;
+  tdc::WgradPlainParams prm{};
+  prm.x = static_cast<const uint32_t*>(x);
+  prm.dy = static_cast<const uint32_t*>(dy);
+  prm.partial = static_cast<float*>(workspace);
+  prm.H = int32_t(H); prm.W = int32_t(W); prm.P = int32_t(P); prm.Q = int32_t(Q);
+  prm.cpairs = int32_t(C / 2);
+  prm.chunk_log2 = pl.chunk_log2;
+  prm.chunks = int32_t(pl.chunks);
+  prm.bands = int32_t(pl.bands);
+  prm.band_rows = int32_t(pl.band_rows);
+  prm.units = int32_t(pl.units);
+  prm.pad = int32_t(pad);
+  cudaError_t e = kWgradPlainLaunch[dt][K / 2 - 1][S - 1](prm, pl.chunks * pl.ugroups, st);
+  if (e == cudaSuccess)
+    e = tdc::launch_wgrad_reduce(static_cast<const float*>(workspace), dw, int32_t(pl.ugroups),
+                                 int32_t(K * K * C), st);
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
 // ---------------------------------------------------------------------------
 // Weight gradient of the K x K (K = 5, 7) stride-1 forward.
 // ---------------------------------------------------------------------------
@@ -1261,6 +1383,29 @@ bool prefer_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t
   return S == 1 || fill_q <= 0.25 || bytes < 64e6;
 }
 
+// Whether the weight gradient with n_stage = 0 runs the plain kernel: narrow
+// outputs (Q <= 16, half a ws strip or less) or at most 16 channels.  A plain
+// thread walks the whole output width, so wide images with more channels stay
+// on the ws kernels.  Measured on the 28 depthwise layers of MobileNetV2 /
+// V3-Large / EfficientNet-B0 at batch 64 (us, plain vs ws): 7 x 7 x 960 5x5
+// 19.5 vs 159, 14 x 14 x 576 21.9 vs 27.5, 112 x 112 x 16 30.6 vs 48.3;
+// 112 x 112 x 32 66.7 vs 49.0, 56 x 56 x 72 47.3 vs 34.5.
+bool prefer_plain_wgrad(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                        int64_t pad) {
+  if (K != 3 && K != 5 && K != 7) return false;
+  if ((S != 1 && S != 2) || C <= 0 || C % 8 != 0 || N <= 0 || pad < 0) return false;
+  if (H + 2 * pad < K || W + 2 * pad < K) return false;
+  const int64_t Q = (W + 2 * pad - K) / S + 1;
+  return Q <= 16 || C <= 16;
+}
+
+// Ring depth of the ws weight gradients when the caller leaves it to the
+// library (n_stage = 0), measured at 64 x 224 x 336 x 256.
+int default_wgrad_stages(int64_t K, int64_t S) {
+  static const int kStages[3][2] = {{2, 4}, {4, 4}, {3, 3}};  // [K: 3, 5, 7][stride - 1]
+  return (K == 3 || K == 5 || K == 7) && (S == 1 || S == 2) ? kStages[K / 2 - 1][S - 1] : 2;
+}
+
 static int fwd_entry(int dt, const void* x, const void* w, const void* bias,
                      const void* residual, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
                      int64_t K, int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
@@ -1337,6 +1482,33 @@ TDC_API int tdc_dwconv_fwd_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C
   return prefer_plain(N, H, W, C, K, stride, pad) ? 1 : 0;
 }
 
+TDC_API int tdc_dwconv_bwd_weight_plain_workspace(int64_t N, int64_t H, int64_t W, int64_t C,
+                                                  int64_t K, int64_t stride, int64_t pad,
+                                                  int64_t* bytes) {
+  return wgrad_plain_workspace(N, H, W, C, K, stride, pad, bytes);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_plain(const void* x, const void* dy, float* dw, int64_t N,
+                                        int64_t H, int64_t W, int64_t C, int64_t K,
+                                        int64_t stride, int64_t pad, void* workspace,
+                                        int64_t workspace_bytes, void* stream) {
+  return wgrad_plain(kF16, x, dy, dw, N, H, W, C, K, stride, pad, workspace, workspace_bytes,
+                     stream);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_plain_bf16(const void* x, const void* dy, float* dw, int64_t N,
+                                             int64_t H, int64_t W, int64_t C, int64_t K,
+                                             int64_t stride, int64_t pad, void* workspace,
+                                             int64_t workspace_bytes, void* stream) {
+  return wgrad_plain(kBF16, x, dy, dw, N, H, W, C, K, stride, pad, workspace, workspace_bytes,
+                     stream);
+}
+
+TDC_API int tdc_dwconv_bwd_weight_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C,
+                                             int64_t K, int64_t stride, int64_t pad) {
+  return prefer_plain_wgrad(N, H, W, C, K, stride, pad) ? 1 : 0;
+}
+
 TDC_API int tdc_dwconv3x3_bwd_data(const void* dy, const void* w, void* dx, int64_t N, int64_t H,
                                    int64_t W, int64_t C, int64_t pad, int64_t n_stage,
                                    void* stream) {
@@ -1359,6 +1531,18 @@ static int bwd_data_entry(int dt, const void* dy, const void* w, void* dx, int64
                           int64_t n_stage, void* stream) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (n_stage == 0) {  // automatic: the kernel and ring depth follow the shape
+    if (stride == 1 && pad >= 0 && pad <= K - 1 && H >= 1 && W >= 1) {
+      const int64_t P = H + 2 * pad - K + 1, Q = W + 2 * pad - K + 1;
+      if (P >= 1 && Q >= 1 && prefer_plain(N, P, Q, C, K, 1, K - 1 - pad)) {
+        Epilogue epi;
+        epi.fused = true;
+        epi.flip_taps = true;
+        return fwd_plain(dy, w, dx, N, P, Q, C, K, 1, K - 1 - pad, 0, epi, stream, dt);
+      }
+    }
+    n_stage = stride == 2 ? 2 : default_fwd_stages(K, 1);
+  }
   if (stride == 2) return dgrad_s2(dy, w, dx, N, H, W, C, K, pad, n_stage, stream, dt);
   if (K == 3 && dt == kF16) return tdc_dwconv3x3_bwd_data(dy, w, dx, N, H, W, C, pad, n_stage, stream);
   // pad' = K - 1 - pad must not be negative (pad above K - 1 leaves dx rows
@@ -1398,6 +1582,11 @@ static int bwd_weight_workspace_entry(int dt, int64_t N, int64_t H, int64_t W, i
   if (!bytes) return TDC_ERR_NULL_POINTER;
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (n_stage == 0) {  // automatic: must agree with bwd_weight_entry
+    if (prefer_plain_wgrad(N, H, W, C, K, stride, pad))
+      return wgrad_plain_workspace(N, H, W, C, K, stride, pad, bytes);
+    n_stage = default_wgrad_stages(K, stride);
+  }
   if (K == 3 && stride == 1) return wgrad3x3_workspace(dt, N, H, W, C, pad, n_stage, bytes);
   WsPlan pl;
   int64_t P, Q;
@@ -1414,6 +1603,12 @@ static int bwd_weight_entry(int dt, const void* x, const void* dy, float* dw, in
                             void* stream) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (stride != 1 && stride != 2) return TDC_ERR_STRIDE;
+  if (n_stage == 0) {  // automatic: the kernel follows the shape
+    if (prefer_plain_wgrad(N, H, W, C, K, stride, pad))
+      return wgrad_plain(dt, x, dy, dw, N, H, W, C, K, stride, pad, workspace, workspace_bytes,
+                         stream);
+    n_stage = default_wgrad_stages(K, stride);
+  }
   if (stride == 2)
     return wgrad_s2(x, dy, dw, N, H, W, C, K, pad, n_stage, workspace, workspace_bytes, stream,
                     dt);

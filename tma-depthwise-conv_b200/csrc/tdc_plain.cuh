@@ -169,4 +169,118 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
   }
 }
 
+// ============================================================================
+// Plain weight gradient (K = 3, 5, 7, stride 1 or 2) for the same small
+// shapes:  dw[r,s,c] = sum_{n,p,q} x[n, S*p+r-pad, S*q+s-pad, c] * dy[n,p,q,c].
+//
+// The ws-family weight gradients give every CTA a workspace slice of all C
+// channels per consumer warp, which is cheap against a 5 GB input but not
+// against a 12 MB one (7 x 7 x 960 at batch 64, 5x5: ~170 MB of partial sums
+// for 12 MB of x and dy).  Here a CTA owns one tap row r (blockIdx.y), one
+// channel chunk and kPlainThreads / chunk_pairs units (image, band of dy
+// rows); a thread keeps the K sums of row r for one channel pair of one unit.
+// The CTA adds its units up in a fixed order (a butterfly over the units of a
+// warp, then the warps in order) and writes row r's taps of one slice of its
+// chunk's channels.  The workspace is ugroups x K*K x C floats (ugroups =
+// CTAs per chunk and row), and dwconv_wgrad_reduce_kernel sums the slices in
+// a fixed order: deterministic, like the ws kernels.  Per dy row and 8-column
+// chunk a thread loads the chunk's dy pairs and the S*7 + K x pairs of input
+// row S*p + r - pad under them; each tap's sum takes the chunk's 8 products
+// in column order.
+// ============================================================================
+constexpr int kWgradPlainCols = 8;  // dy columns per chunk
+
+struct WgradPlainParams {
+  const uint32_t* x;   // [N, H, W, C] as channel pairs
+  const uint32_t* dy;  // [N, P, Q, C] as channel pairs
+  float* partial;      // [ugroups][K*K][C]
+  int32_t H, W, P, Q;
+  int32_t cpairs, chunk_log2, chunks;
+  int32_t bands, band_rows;
+  int32_t units;       // N * bands
+  int32_t pad;
+};
+
+template <int K, int S, class E>
+__global__ void __launch_bounds__(kPlainThreads) dwconv_wgrad_plain_kernel(WgradPlainParams p) {
+  constexpr int QC = kWgradPlainCols;
+  constexpr int NI = S * (QC - 1) + K;  // x columns under one dy chunk
+  constexpr int kWarps = kPlainThreads / 32;
+  static_assert(NI <= 32, "column mask");
+  __shared__ float red[kWarps][K * 2][8];
+  griddep_wait();
+  const int r = int(blockIdx.y);                  // tap row of this CTA
+  const int cpc = 1 << p.chunk_log2;              // channel pairs per chunk
+  const int upc = kPlainThreads >> p.chunk_log2;  // units per CTA
+  const int chunk = int(blockIdx.x % uint32_t(p.chunks));
+  const int ugroup = int(blockIdx.x / uint32_t(p.chunks));
+  const int cp_in = int(threadIdx.x) & (cpc - 1);
+  const int cp = chunk * cpc + cp_in;
+  const int u = ugroup * upc + (int(threadIdx.x) >> p.chunk_log2);
+
+  float acc[K][2];
+#pragma unroll
+  for (int s = 0; s < K; ++s) { acc[s][0] = 0.f; acc[s][1] = 0.f; }
+  if (u < p.units) {
+    const int n = u / p.bands;
+    const int band = u - n * p.bands;
+    const int p0 = band * p.band_rows;
+    const int p1 = min(p.P, p0 + p.band_rows);
+    const uint32_t* xn = p.x + int64_t(n) * p.H * p.W * p.cpairs + cp;
+    const uint32_t* dyn = p.dy + int64_t(n) * p.P * p.Q * p.cpairs + cp;
+    for (int pr = p0; pr < p1; ++pr) {
+      const int h = S * pr + r - p.pad;
+      if (unsigned(h) >= unsigned(p.H)) continue;  // the whole row is padding
+      for (int q0 = 0; q0 < p.Q; q0 += QC) {
+        uint32_t d[QC];
+        uint32_t off = uint32_t((pr * p.Q + q0) * p.cpairs);
+#pragma unroll
+        for (int m = 0; m < QC; ++m) {
+          d[m] = q0 + m < p.Q ? __ldg(dyn + off) : 0u;
+          off += uint32_t(p.cpairs);
+        }
+        const int w0 = S * q0 - p.pad;
+        uint32_t xv[NI];
+        off = uint32_t((h * p.W + w0) * p.cpairs);  // wraps below 0; used only inside
+#pragma unroll
+        for (int j = 0; j < NI; ++j) {
+          xv[j] = unsigned(w0 + j) < unsigned(p.W) ? __ldg(xn + off) : 0u;
+          off += uint32_t(p.cpairs);
+        }
+#pragma unroll
+        for (int s = 0; s < K; ++s) {
+#pragma unroll
+          for (int m = 0; m < QC; ++m) fma2<E>(xv[S * m + s], d[m], acc[s][0], acc[s][1]);
+        }
+      }
+    }
+  }
+  // Fixed-order sum over the CTA's units: a butterfly over the units of a
+  // warp (lanes cp_in + i * cpc), then warps 0 .. kWarps-1 in order.
+  const int lane = int(threadIdx.x) & 31, warp = int(threadIdx.x) >> 5;
+#pragma unroll
+  for (int s = 0; s < K; ++s) {
+#pragma unroll
+    for (int c2 = 0; c2 < 2; ++c2) {
+      float v = acc[s][c2];
+      for (int off = 16; off >= cpc; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane < cpc) red[warp][2 * s + c2][lane] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < unsigned(cpc)) {
+    float* slice = p.partial + (int64_t(ugroup) * K * K + r * K) * (2 * p.cpairs) + 2 * cp;
+#pragma unroll
+    for (int s = 0; s < K; ++s) {
+      float s0 = red[0][2 * s][cp_in], s1 = red[0][2 * s + 1][cp_in];
+#pragma unroll
+      for (int wi = 1; wi < kWarps; ++wi) {
+        s0 += red[wi][2 * s][cp_in];
+        s1 += red[wi][2 * s + 1][cp_in];
+      }
+      *reinterpret_cast<float2*>(slice + int64_t(s) * (2 * p.cpairs)) = make_float2(s0, s1);
+    }
+  }
+}
+
 }  // namespace tdc

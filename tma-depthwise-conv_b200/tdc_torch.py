@@ -47,7 +47,8 @@ from tma_dwconv import DWCONV_STAGES
 GEOMETRIES = tuple(DWCONV_STAGES)
 TRAINABLE = GEOMETRIES
 
-#: n_stage of the data / weight gradient per (K, stride), measured at
+#: n_stage of the ring kernels' data / weight gradients per (K, stride) (the
+#: custom ops pass 0 and let the library pick the kernel by shape), measured at
 #: 64 x 224 x 336 x 256 (stride 1 data gradient: the forward's table; weight
 #: gradient, 2 / 3 / 4 stages, us: 5x5 1618 / 1540 / 1479, 7x7 3218 / 2840 /
 #: 2890; stride 2: 3x3 526 / 467 / 458, 5x5 792 / 806 / 633, 7x7 1184 / 1101 /
@@ -130,9 +131,7 @@ def dwconv_bwd_data_op(dy: torch.Tensor, w: torch.Tensor, pad: int, stride: int,
                        input_w: int) -> torch.Tensor:
     """dx [N,H,W,C] of the K x K forward, from dy [N,P,Q,C] and w [K,K,C]
     (H = input_h, W = input_w: at stride 2, dy does not determine them)."""
-    k = int(w.shape[0])
-    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, stride,
-                              BWD_STAGES[(k, stride)][0], input_h, input_w)
+    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, stride, 0, input_h, input_w)
 
 
 @dwconv_bwd_data_op.register_fake
@@ -144,8 +143,7 @@ def _(dy, w, pad, stride, input_h, input_w):
 def dwconv_bwd_weight_op(x: torch.Tensor, dy: torch.Tensor, k: int, pad: int,
                          stride: int) -> torch.Tensor:
     """dw [K,K,C] (fp32) of the K x K forward, from x and dy."""
-    return _C.dwconv_bwd_weight(x.contiguous(), dy.contiguous(), k, pad, stride,
-                                BWD_STAGES[(k, stride)][1])
+    return _C.dwconv_bwd_weight(x.contiguous(), dy.contiguous(), k, pad, stride, 0)
 
 
 @dwconv_bwd_weight_op.register_fake
@@ -180,16 +178,14 @@ def _backward_k(ctx, dy):
     k, s = ctx.geometry
     x, w = ctx.saved_tensors
     dx = dw = db = None
-    # 3x3 stride 1 in fp16 has its own ops (any pad); everything else, bf16
-    # included, goes through the K x K ops.
-    own_3x3 = (k, s) == (3, 1) and x.dtype == torch.float16
+    # Both gradients of every geometry go through the K x K ops, whose
+    # kernels follow the shape (plain kernels for narrow layers, the ring
+    # kernels otherwise; the 3x3 fp16 paths take any pad).
     dy = dy.to(x.dtype)
     if ctx.needs_input_grad[0]:
-        dx = (dwconv3x3_bwd_data_op(dy, w, ctx.pad) if own_3x3
-              else dwconv_bwd_data_op(dy, w, ctx.pad, s, x.shape[1], x.shape[2]))
+        dx = dwconv_bwd_data_op(dy, w, ctx.pad, s, x.shape[1], x.shape[2])
     if ctx.needs_input_grad[1]:
-        dw = (dwconv3x3_bwd_weight_op(x, dy, ctx.pad) if own_3x3
-              else dwconv_bwd_weight_op(x, dy, k, ctx.pad, s)).to(w.dtype)
+        dw = dwconv_bwd_weight_op(x, dy, k, ctx.pad, s).to(w.dtype)
     if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
         db = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(ctx.bias_dtype)
     return dx, dw, db, None, None
