@@ -162,3 +162,54 @@ def test_module_trains_7x7():
     got.float().sum().backward()
     assert conv.weight.grad is not None and conv.weight.grad.shape == (64, 1, 7, 7)
     assert conv.bias.grad is not None and torch.isfinite(conv.weight.grad).all()
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_eager_function_matches_custom_op(K, S, dtype):
+    """tdc_torch.dwconv in eager mode (an autograd Function calling the
+    extension directly) and torch.ops.tdc.dwconv (the custom op, used under
+    torch.compile): the same y, dx, dw and db, bit for bit."""
+    import tdc_torch
+    g = torch.Generator().manual_seed(K * 3 + S)
+    x0 = torch.randn(3, 14, 14, 72, generator=g).to(dtype).cuda()
+    w0 = (torch.randn(K, K, 72, generator=g) / K).to(dtype).cuda()
+    b0 = torch.randn(72, generator=g).to(dtype).cuda()
+    outs = []
+    for fn in (lambda x, w, b: tdc_torch.dwconv(x, w, b, S, K // 2),
+               lambda x, w, b: torch.ops.tdc.dwconv(x, w, b, S, K // 2)):
+        x, w, b = (t.clone().requires_grad_() for t in (x0, w0, b0))
+        y = fn(x, w, b)
+        dy = torch.randn(y.shape, generator=torch.Generator().manual_seed(9)).to(dtype).cuda()
+        y.backward(dy)
+        outs.append([t.detach().view(torch.int16) for t in (y, x.grad, w.grad, b.grad)])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_module_training_path_matches_custom_op(K, S, dtype):
+    """DepthwiseConv2d in eager training (one autograd Function over the
+    module's own weight layout) against torch.ops.tdc.dwconv on the re-laid-out
+    weight: the same y, x.grad, weight.grad (cast to the parameter dtype) and
+    bias.grad, bit for bit."""
+    import tdc_torch
+    torch.manual_seed(K + S)
+    conv = torch.nn.Conv2d(72, 72, K, stride=S, padding=K // 2, groups=72).cuda().to(dtype)
+    mod = tdc_torch.DepthwiseConv2d.from_conv2d(conv)
+    x0 = torch.randn(3, 72, 14, 15, device="cuda").to(dtype).to(memory_format=torch.channels_last)
+    x = x0.clone().requires_grad_()
+    y = mod(x)
+    gy = torch.randn(y.shape, device="cuda").to(dtype).to(memory_format=torch.channels_last)
+    y.backward(gy)
+    xr = x0.permute(0, 2, 3, 1).contiguous().requires_grad_()
+    wr = conv.weight.detach()[:, 0].permute(1, 2, 0).contiguous().requires_grad_()
+    br = conv.bias.detach().clone().requires_grad_()
+    yr = torch.ops.tdc.dwconv(xr, wr, br, S, K // 2)
+    yr.backward(gy.permute(0, 2, 3, 1).contiguous())
+    bits = lambda t: t.detach().contiguous().view(torch.int16)
+    assert torch.equal(bits(y.permute(0, 2, 3, 1)), bits(yr))
+    assert torch.equal(bits(x.grad.permute(0, 2, 3, 1)), bits(xr.grad))
+    assert torch.equal(bits(mod.weight.grad[:, 0].permute(1, 2, 0)), bits(wr.grad))
+    assert torch.equal(bits(mod.bias.grad), bits(br.grad))

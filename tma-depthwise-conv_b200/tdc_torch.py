@@ -174,38 +174,121 @@ def _setup_context_k(ctx, inputs, output):
     ctx.bias_dtype = None if bias is None else bias.dtype
 
 
-def _backward_k(ctx, dy):
-    k, s = ctx.geometry
-    x, w = ctx.saved_tensors
+def _grads_k(needs, x, w, dy, k, s, pad, bias_dtype, bwd_data, bwd_weight):
+    """dx, dw, db of the K x K forward.  Both gradients of every geometry go
+    through the K x K entry points, whose kernels follow the shape (plain
+    kernels for narrow layers, the ring kernels otherwise; the 3x3 fp16 paths
+    take any pad)."""
     dx = dw = db = None
-    # Both gradients of every geometry go through the K x K ops, whose
-    # kernels follow the shape (plain kernels for narrow layers, the ring
-    # kernels otherwise; the 3x3 fp16 paths take any pad).
     dy = dy.to(x.dtype)
-    if ctx.needs_input_grad[0]:
-        dx = dwconv_bwd_data_op(dy, w, ctx.pad, s, x.shape[1], x.shape[2])
-    if ctx.needs_input_grad[1]:
-        dw = dwconv_bwd_weight_op(x, dy, k, ctx.pad, s).to(w.dtype)
-    if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
-        db = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(ctx.bias_dtype)
+    if needs[0]:
+        dx = bwd_data(dy, w, pad, s, x.shape[1], x.shape[2])
+    if needs[1]:
+        dw = bwd_weight(x, dy, k, pad, s).to(w.dtype)
+    if bias_dtype is not None and needs[2]:
+        db = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(bias_dtype)
     return dx, dw, db, None, None
+
+
+def _backward_k(ctx, dy):
+    x, w = ctx.saved_tensors
+    return _grads_k(ctx.needs_input_grad, x, w, dy, *ctx.geometry, ctx.pad, ctx.bias_dtype,
+                    dwconv_bwd_data_op, dwconv_bwd_weight_op)
 
 
 dwconv_op.register_autograd(_backward_k, setup_context=_setup_context_k)
 
 
+def _bwd_data_eager(dy, w, pad, stride, input_h, input_w):
+    return _C.dwconv_bwd_data(dy.contiguous(), w.contiguous(), pad, stride, 0, input_h, input_w)
+
+
+def _bwd_weight_eager(x, dy, k, pad, stride):
+    return _C.dwconv_bwd_weight(x.contiguous(), dy.contiguous(), k, pad, stride, 0)
+
+
+class _DwconvFunction(torch.autograd.Function):
+    """``torch.ops.tdc.dwconv`` and its autograd formula for eager mode, calling
+    the extension directly: a custom op's dispatch costs ~46 us of host time
+    per forward with autograd and ~17 us per backward op (measured), against
+    ~10 us for this Function, which matters for small layers in training.
+    Under ``torch.compile`` the custom op is used (it has fake kernels)."""
+
+    @staticmethod
+    def forward(ctx, x, w, bias, stride, pad):
+        b = None if bias is None else bias.contiguous()
+        y = _C.dwconv_k(x.contiguous(), w.contiguous(), b, None, stride, pad, 0, 0)
+        ctx.save_for_backward(x, w)
+        ctx.geometry = (int(w.shape[0]), int(stride))
+        ctx.pad = pad
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        return _grads_k(ctx.needs_input_grad, x, w, dy, *ctx.geometry, ctx.pad, ctx.bias_dtype,
+                        _bwd_data_eager, _bwd_weight_eager)
+
+
+class _DepthwiseConvFunction(torch.autograd.Function):
+    """The autograd path of ``DepthwiseConv2d`` in eager mode: one node from
+    the module's own tensors (x [N,C,H,W] channels-last in the compute dtype,
+    weight [C,1,K,K] and bias [C] in any float dtype) to y [N,C,P,Q]
+    channels-last.  The [K,K,C] re-layout of the weight and the dtype casts
+    happen inside, and the weight gradient comes back in the parameter's
+    layout and dtype in one copy, so a training step adds no autograd nodes
+    (and their backward copies) for them."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, stride, pad, dt):
+        x_nhwc = x.permute(0, 2, 3, 1)                   # contiguous view, no copy
+        w_rsc = weight.to(dt)[:, 0].permute(1, 2, 0).contiguous()
+        b = None if bias is None else bias.to(dt).contiguous()
+        y = _C.dwconv_k(x_nhwc, w_rsc, b, None, stride, pad, 0, 0)
+        ctx.save_for_backward(x_nhwc, w_rsc)
+        ctx.conf = (int(weight.shape[-1]), stride, pad, weight.dtype,
+                    None if bias is None else bias.dtype)
+        return y.permute(0, 3, 1, 2)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x_nhwc, w_rsc = ctx.saved_tensors
+        k, stride, pad, w_dtype, b_dtype = ctx.conf
+        dy = gy.permute(0, 2, 3, 1).to(x_nhwc.dtype).contiguous()
+        gx = gw = gb = None
+        if ctx.needs_input_grad[0]:
+            gx = _C.dwconv_bwd_data(dy, w_rsc, pad, stride, 0, x_nhwc.shape[1],
+                                    x_nhwc.shape[2]).permute(0, 3, 1, 2)
+        if ctx.needs_input_grad[1]:
+            dw = _C.dwconv_bwd_weight(x_nhwc, dy, k, pad, stride, 0)  # [K,K,C] fp32
+            gw = torch.empty((dw.shape[2], 1, k, k), dtype=w_dtype, device=dw.device)
+            gw[:, 0].copy_(dw.permute(2, 0, 1))                        # transpose + cast
+        if b_dtype is not None and ctx.needs_input_grad[2]:
+            gb = dy.sum(dim=(0, 1, 2), dtype=torch.float32).to(b_dtype)
+        return gx, gw, gb, None, None, None
+
+
+def _dwconv_autograd(x, w, bias, stride: int, pad: int) -> torch.Tensor:
+    if torch.compiler.is_compiling():
+        return dwconv_op(x, w, bias, stride, pad)
+    return _DwconvFunction.apply(x, w, bias, stride, pad)
+
+
 def dwconv(x_nhwc: torch.Tensor, w_rsc: torch.Tensor, bias: Optional[torch.Tensor] = None,
            stride: int = 1, pad: Optional[int] = None) -> torch.Tensor:
-    """Depthwise K x K on NHWC fp16 tensors (differentiable at stride 1 and 2)."""
+    """Depthwise K x K on NHWC fp16 / bf16 tensors (differentiable at stride 1
+    and 2); the custom op under ``torch.compile``, a lighter autograd
+    Function in eager mode (same kernels, same results)."""
     if pad is None:
         pad = int(w_rsc.shape[0]) // 2
-    return dwconv_op(x_nhwc, w_rsc, bias, int(stride), int(pad))
+    return _dwconv_autograd(x_nhwc, w_rsc, bias, int(stride), int(pad))
 
 
 # ------------------------------ nn.Conv2d stand-in ---------------------------
 
 #: Activations the fused epilogue implements, with their PyTorch equivalents
-#: (used when a gradient is needed: the custom op's autograd covers conv + bias).
+#: (used when a gradient is needed: the op's autograd formula covers conv + bias).
 _TORCH_ACTS = {"none": None, "relu": torch.nn.functional.relu, "relu6": torch.nn.functional.relu6,
                "silu": torch.nn.functional.silu, "hardswish": torch.nn.functional.hardswish}
 
@@ -260,21 +343,28 @@ class DepthwiseConv2d(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float16
         x = x.to(dt).contiguous(memory_format=torch.channels_last)
+        act = self.activation
+        needs_grad = torch.is_grad_enabled() and (
+            x.requires_grad or self.weight.requires_grad
+            or (self.bias is not None and self.bias.requires_grad))
+        if needs_grad and not torch.compiler.is_compiling():
+            # training, eager: one autograd node for conv + bias (the
+            # activation, if any, runs outside the kernel)
+            y = _DepthwiseConvFunction.apply(x, self.weight, self.bias, self.stride,
+                                             self.padding, dt)
+            return y if act == "none" else _TORCH_ACTS[act](y)
         x_nhwc = x.permute(0, 2, 3, 1)                                  # contiguous view, no copy
         w_rsc = self.weight.to(dt)[:, 0].permute(1, 2, 0)              # [K,K,C]
         b = None if self.bias is None else self.bias.to(dt)
-        act = self.activation
-        needs_grad = torch.is_grad_enabled() and (
-            x.requires_grad or self.weight.requires_grad or (b is not None and b.requires_grad))
         if not needs_grad:
             # inference: straight to the extension (which checks its arguments),
             # without the custom op's dispatch; the activation runs in the
             # kernel's fused epilogue
             y = _C.dwconv_k(x_nhwc, w_rsc.contiguous(), None if b is None else b.contiguous(),
                             None, self.stride, self.padding, _T.ACTIVATIONS[act], 0)
-        else:
+        else:  # under torch.compile: the custom op, which has fake kernels
             y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
-            if act != "none":  # the custom op's autograd covers conv + bias
+            if act != "none":  # the autograd formula covers conv + bias
                 y = _TORCH_ACTS[act](y)
         return y.permute(0, 3, 1, 2)                                    # NCHW view, channels-last memory
 
