@@ -121,3 +121,31 @@ def test_convert_depthwise_convs_eligibility():
     assert all(isinstance(m, nn.Conv2d) for m in list(model)[4:])
     with pytest.raises(ValueError, match="kernel_size must be 3, 5 or 7"):
         tdc_torch.DepthwiseConv2d(64, 9)
+
+
+def test_convs_that_add_to_conv2d_are_not_converted():
+    """A depthwise conv whose module does more than nn.Conv2d's computation
+    keeps it: a subclass that pads in forward (like timm's Conv2dSame), a
+    parametrized weight (weight norm) and a conv with a forward hook.  A
+    subclass that only adds attributes is still converted."""
+    import tdc_torch
+    nn = torch.nn
+
+    class PadInForward(nn.Conv2d):  # "same" padding done by hand, as in TF ports
+        def forward(self, x):
+            return super().forward(nn.functional.pad(x, (0, 1, 0, 1)))
+
+    class Tagged(nn.Conv2d):  # computation unchanged
+        tag = "dw"
+
+    hooked = nn.Conv2d(64, 64, 3, padding=1, groups=64)
+    hooked.register_forward_hook(lambda *a: None)
+    normed = nn.utils.parametrizations.weight_norm(nn.Conv2d(64, 64, 3, padding=1, groups=64))
+    model = nn.Sequential(PadInForward(64, 64, 3, stride=2, groups=64), normed, hooked,
+                          Tagged(64, 64, 3, padding=1, groups=64))
+    assert tdc_torch.convert_depthwise_convs(model) == 1
+    assert type(model[0]) is PadInForward and type(model[2]) is nn.Conv2d
+    assert isinstance(model[3], tdc_torch.DepthwiseConv2d)
+    assert nn.utils.parametrize.is_parametrized(model[1])
+    fuse = nn.Sequential(PadInForward(64, 64, 3, stride=2, groups=64), nn.BatchNorm2d(64)).eval()
+    assert tdc_torch.fuse_depthwise_bn_act(fuse) == 0

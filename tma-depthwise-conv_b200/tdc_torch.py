@@ -38,6 +38,7 @@ from typing import Optional
 
 import torch
 from torch import nn
+from torch.nn.utils import parametrize as _parametrize
 
 import _tma_dwconv_C as _C  # type: ignore
 import tma_dwconv as _T
@@ -382,8 +383,25 @@ class DepthwiseConv3x3(DepthwiseConv2d):
         super().__init__(channels, 3, 1, padding, bias, device, dtype)
 
 
+def _plain_conv2d(m: nn.Module) -> bool:
+    """An ``nn.Conv2d`` whose computation is ``nn.Conv2d``'s own.  Subclasses
+    that override ``forward`` or ``_conv_forward`` (timm's ``Conv2dSame``
+    pads in ``forward``; QAT convolutions fake-quantise the weight), convs
+    with a parametrized weight (weight norm, spectral norm) and convs with
+    forward hooks are left alone: swapping them would silently drop what
+    they add."""
+    if not isinstance(m, nn.Conv2d):
+        return False
+    cls = type(m)
+    if cls.forward is not nn.Conv2d.forward or cls._conv_forward is not nn.Conv2d._conv_forward:
+        return False
+    if _parametrize.is_parametrized(m):
+        return False
+    return not (m._forward_hooks or m._forward_pre_hooks)
+
+
 def _eligible(m: nn.Module, forward_only: bool) -> bool:
-    if not (isinstance(m, nn.Conv2d) and m.dilation == (1, 1)
+    if not (_plain_conv2d(m) and m.dilation == (1, 1)
             and m.groups == m.in_channels == m.out_channels and m.in_channels % 8 == 0
             and m.padding_mode == "zeros" and isinstance(m.padding, tuple)
             and m.padding[0] == m.padding[1]
