@@ -165,6 +165,27 @@ TDC_API int tdc_dwconv_fwd_bf16(const void* x, const void* w, const void* bias,
                                 int64_t stride, int64_t pad, int64_t act, int64_t n_stage,
                                 void* stream);
 
+/* tdc_dwconv_fwd (and _bf16) with each side's zero padding given separately:
+ *   y[n,p,q,c] = epilogue(chain_{r,s} x[n, S*p+r-pad_top, S*q+s-pad_left, c] * w[r,s,c])
+ * with P = (H + pad_top + pad_bottom - K)/S + 1 and Q likewise, e.g.
+ * TensorFlow's "SAME" padding at stride 2, which puts the odd row and column
+ * at the bottom / right (3x3 on 112 x 112: top 0, bottom 1).  Same kernels,
+ * arithmetic and n_stage meaning (0 = chosen from the shape) as
+ * tdc_dwconv_fwd; every pad >= 0.  No counterpart in the reference
+ * (symmetric padding only). */
+TDC_API int tdc_dwconv_fwd_asym(const void* x, const void* w, const void* bias,
+                                const void* residual, void* y,
+                                int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                int64_t stride, int64_t pad_top, int64_t pad_bottom,
+                                int64_t pad_left, int64_t pad_right, int64_t act,
+                                int64_t n_stage, void* stream);
+TDC_API int tdc_dwconv_fwd_asym_bf16(const void* x, const void* w, const void* bias,
+                                     const void* residual, void* y,
+                                     int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                     int64_t stride, int64_t pad_top, int64_t pad_bottom,
+                                     int64_t pad_left, int64_t pad_right, int64_t act,
+                                     int64_t n_stage, void* stream);
+
 /* Plain K x K forward: global loads through L1, no TMA, no shared memory, no
  * pipeline.  A thread owns one channel pair of one output column over a band
  * of band_rows output rows (0 = chosen from the shape: the full height unless

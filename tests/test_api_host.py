@@ -149,3 +149,31 @@ def test_convs_that_add_to_conv2d_are_not_converted():
     assert nn.utils.parametrize.is_parametrized(model[1])
     fuse = nn.Sequential(PadInForward(64, 64, 3, stride=2, groups=64), nn.BatchNorm2d(64)).eval()
     assert tdc_torch.fuse_depthwise_bn_act(fuse) == 0
+
+
+def test_same_padding_rule():
+    """TensorFlow's "same": ceil(n / stride) outputs, total padding
+    max((out - 1) * stride + K - n, 0), the odd one at the bottom / right."""
+    for n in range(1, 40):
+        for K in (3, 5, 7):
+            for S in (1, 2):
+                t, b, l, r = T.same_padding(n, n + 1, K, S)
+                assert (n + t + b - K) // S + 1 == -(-n // S)
+                assert (n + 1 + l + r - K) // S + 1 == -(-(n + 1) // S)
+                assert 0 <= t <= b <= t + 1 and 0 <= l <= r <= l + 1
+    assert T.same_padding(112, 112, 3, 2) == (0, 1, 0, 1)
+    assert T.same_padding(112, 112, 5, 2) == (1, 2, 1, 2)
+    assert T.same_padding(14, 14, 5, 1) == (2, 2, 2, 2)
+    with pytest.raises(ValueError, match="top, bottom, left, right"):
+        T.dwconv(FakeCuda((1, 8, 8, 64)), FakeCuda((3, 3, 64)), (1, 1, 1))
+
+
+def test_padding_same_convs_are_converted():
+    import tdc_torch
+    nn = torch.nn
+    model = nn.Sequential(nn.Conv2d(64, 64, 5, padding="same", groups=64),
+                          nn.Conv2d(64, 64, 3, padding="same", groups=64, bias=False))
+    assert tdc_torch.convert_depthwise_convs(model) == 2
+    assert model[0].padding == 2 and model[1].padding == 1
+    m = tdc_torch.DepthwiseConv2d(64, 3, 2, padding="same", device="cpu")
+    assert m.padding == "same" and "padding=same" in repr(m)

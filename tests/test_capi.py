@@ -775,3 +775,24 @@ def test_plain_weight_gradient_units_cover_every_dy_row_once(N, P, Cc, K):
                 seen.add((n, pr))
     assert len(seen) == N * P
     assert pl["chunks"] * pl["cpc"] == Cc // 2
+
+
+def test_per_side_padding_argument_errors(lib):
+    p = C.c_void_p
+    def fwd(K=5, stride=2, C_=72, pads=(0, 1, 0, 1), H=16, act=0, ns=0, N=2, x=16, f=None):
+        f = f or lib.tdc_dwconv_fwd_asym
+        return f(p(x), p(16), None, None, p(16), i64(N), i64(H), i64(16), i64(C_), i64(K),
+                 i64(stride), *[i64(v) for v in pads], i64(act), i64(ns), None)
+    for f in (lib.tdc_dwconv_fwd_asym, lib.tdc_dwconv_fwd_asym_bf16):
+        assert fwd(K=4, f=f) == CODES["TDC_ERR_FILTER_SHAPE"]
+        assert fwd(stride=3, f=f) == CODES["TDC_ERR_STRIDE"]
+        assert fwd(C_=12, f=f) == CODES["TDC_ERR_CHANNELS"]
+        assert fwd(pads=(0, -1, 0, 0), f=f) == CODES["TDC_ERR_PAD"]
+        assert fwd(pads=(0, 0, -1, 0), ns=2, f=f) == CODES["TDC_ERR_PAD"]
+        assert fwd(act=5, f=f) == CODES["TDC_ERR_ACT"]
+        assert fwd(ns=1, f=f) == CODES["TDC_ERR_N_STAGE"]
+        assert fwd(K=7, H=4, pads=(1, 1, 3, 3), f=f) == CODES["TDC_ERR_BAD_SHAPE"]  # 4 + 2 < 7
+        assert fwd(x=24, f=f) == CODES["TDC_ERR_ALIGNMENT"]
+        assert fwd(N=0, f=f) == CODES["TDC_OK"]
+        if not torch.cuda.is_available():
+            assert fwd(f=f) == CODES["TDC_ERR_NO_DEVICE"]

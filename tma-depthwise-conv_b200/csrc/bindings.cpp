@@ -230,6 +230,51 @@ torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Te
   return y;
 }
 
+// dwconv_k with each side's padding given (top, bottom, left, right).
+torch::Tensor dwconv_k_asym(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
+                            std::optional<torch::Tensor> residual, int64_t stride,
+                            int64_t pad_top, int64_t pad_bottom, int64_t pad_left,
+                            int64_t pad_right, int64_t act, int64_t n_stage) {
+  const bool bf16 = check_common_16(x, w, "x");
+  const int64_t K = w.size(0);
+  TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7), "w must be [K,K,C] with K in {3, 5, 7}");
+  TORCH_CHECK(w.size(2) == x.size(3), "channel mismatch");
+  TORCH_CHECK(x.size(3) % 8 == 0, "C must be a multiple of 8");
+  TORCH_CHECK(stride == 1 || stride == 2, "stride must be 1 or 2, got ", stride);
+  TORCH_CHECK(pad_top >= 0 && pad_bottom >= 0 && pad_left >= 0 && pad_right >= 0,
+              "pads must be non-negative");
+  TORCH_CHECK(n_stage == 0 || (n_stage >= 2 && n_stage <= 4),
+              "n_stage must be one of {2, 3, 4} (or 0: chosen from the shape), got ", n_stage);
+  TORCH_CHECK(x.size(1) + pad_top + pad_bottom >= K && x.size(2) + pad_left + pad_right >= K,
+              "input too small for a ", K, "x", K, " kernel with these pads");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t P = (x.size(1) + pad_top + pad_bottom - K) / stride + 1;
+  const int64_t Q = (x.size(2) + pad_left + pad_right - K) / stride + 1;
+  auto y = torch::empty({x.size(0), P, Q, x.size(3)}, x.options());
+  const void* bptr = nullptr;
+  const void* rptr = nullptr;
+  if (bias.has_value()) {
+    const auto& b = *bias;
+    TORCH_CHECK(b.is_cuda() && b.device() == x.device() && b.scalar_type() == x.scalar_type() &&
+                    b.is_contiguous() && b.dim() == 1 && b.size(0) == x.size(3),
+                "bias must be a contiguous [C] tensor of x's dtype on x's device");
+    bptr = b.data_ptr();
+  }
+  if (residual.has_value()) {
+    const auto& r = *residual;
+    TORCH_CHECK(r.is_cuda() && r.device() == x.device() && r.scalar_type() == x.scalar_type() &&
+                    r.is_contiguous() && r.sizes() == y.sizes(),
+                "residual must be a contiguous [N,P,Q,C] tensor of x's dtype on x's device");
+    rptr = r.data_ptr();
+  }
+  auto* fwd = bf16 ? &tdc_dwconv_fwd_asym_bf16 : &tdc_dwconv_fwd_asym;
+  check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
+                   x.size(2), x.size(3), K, stride, pad_top, pad_bottom, pad_left, pad_right, act,
+                   n_stage, stream_of(x)),
+               "dwconv_k_asym");
+  return y;
+}
+
 // The plain K x K forward (no TMA): same checks and epilogue as dwconv_k,
 // band_rows (0 = from the shape) in place of n_stage.
 torch::Tensor dwconv_plain(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
@@ -510,6 +555,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "K x K (3, 5, 7) depthwise forward, stride 1 or 2, optional fused epilogue",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
         py::arg("pad"), py::arg("act"), py::arg("n_stage"));
+  m.def("dwconv_k_asym", &tma_dwconv::dwconv_k_asym,
+        "K x K depthwise forward with each side's padding (top, bottom, left, right)",
+        py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
+        py::arg("pad_top"), py::arg("pad_bottom"), py::arg("pad_left"), py::arg("pad_right"),
+        py::arg("act"), py::arg("n_stage"));
   m.def("dwconv_plain", &tma_dwconv::dwconv_plain,
         "plain (no TMA) K x K depthwise forward, the same result as dwconv_k",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),

@@ -324,6 +324,14 @@ struct Epilogue {
   bool flip_taps = false;  // data gradient: taps w[2-r][2-s], pad may be negative
 };
 
+// Padding on each side of the image (forward entries with asymmetric
+// padding); the kernels take the top and left sides as row / column offsets,
+// and the bottom and right sides only set the output size (rows and columns
+// past the image read as zero).
+struct Pad4 {
+  int64_t top, bottom, left, right;
+};
+
 int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
               int64_t R, int64_t S, int64_t pad, int64_t n_stage, unsigned long long* stall,
               bool probe, int64_t withhold, int64_t timeout_ns, void* stream,
@@ -359,7 +367,7 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.y = static_cast<__half*>(y);
   prm.stall = stall;
   prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
-  prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad);
+  prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad); prm.pad_w = int32_t(pad);
   prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
   prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
   prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
@@ -472,16 +480,17 @@ WsPlan make_geom_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int S, 
 
 int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
              int64_t K, int64_t S, int64_t pad, int64_t n_stage, const Epilogue& epi,
-             void* stream, int dt = kF16) {
+             void* stream, int dt = kF16, const Pad4* p4 = nullptr) {
+  const Pad4 pd = p4 ? *p4 : Pad4{pad, pad, pad, pad};
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (S != 1 && S != 2) return TDC_ERR_STRIDE;
   if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
   if (C % 8 != 0) return TDC_ERR_CHANNELS;
-  if (pad < 0) return TDC_ERR_PAD;
-  if (pad > (1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (pd.top < 0 || pd.bottom < 0 || pd.left < 0 || pd.right < 0) return TDC_ERR_PAD;
+  if (std::max({pd.top, pd.bottom, pd.left, pd.right}) > (1 << 28)) return TDC_ERR_TOO_LARGE;
   if (n_stage < 2 || n_stage > 4) return TDC_ERR_N_STAGE;
-  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
-  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  if (H + pd.top + pd.bottom < K || W + pd.left + pd.right < K) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = (H + pd.top + pd.bottom - K) / S + 1, Q = (W + pd.left + pd.right - K) / S + 1;
   if (N == 0 || C == 0) return TDC_OK;
   if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
@@ -517,7 +526,7 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   prm.w = static_cast<const __half*>(w);
   prm.y = static_cast<__half*>(y);
   prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
-  prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pad);
+  prm.P = int32_t(P); prm.Q = int32_t(Q); prm.pad = int32_t(pd.top); prm.pad_w = int32_t(pd.left);
   prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
   prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
   prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
@@ -571,15 +580,18 @@ int64_t plain_band_rows(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t K, i
 
 int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
               int64_t K, int64_t S, int64_t pad, int64_t band_rows, const Epilogue& epi,
-              void* stream, int dt) {
+              void* stream, int dt, const Pad4* p4 = nullptr) {
+  const Pad4 pd = p4 ? *p4 : Pad4{pad, pad, pad, pad};
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (S != 1 && S != 2) return TDC_ERR_STRIDE;
   if (N < 0 || H < 1 || W < 1 || C < 0 || band_rows < 0) return TDC_ERR_BAD_SHAPE;
   if (C % 8 != 0) return TDC_ERR_CHANNELS;
-  if (pad < 0 && !epi.flip_taps) return TDC_ERR_PAD;
-  if (pad > (1 << 28) || pad < -(1 << 28)) return TDC_ERR_TOO_LARGE;
-  if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
-  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  if (!epi.flip_taps && (pd.top < 0 || pd.bottom < 0 || pd.left < 0 || pd.right < 0))
+    return TDC_ERR_PAD;
+  for (int64_t v : {pd.top, pd.bottom, pd.left, pd.right})
+    if (v > (1 << 28) || v < -(1 << 28)) return TDC_ERR_TOO_LARGE;
+  if (H + pd.top + pd.bottom < K || W + pd.left + pd.right < K) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = (H + pd.top + pd.bottom - K) / S + 1, Q = (W + pd.left + pd.right - K) / S + 1;
   if (N == 0 || C == 0) return TDC_OK;
   if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
@@ -588,7 +600,8 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   // 32-bit row / column arithmetic in the kernel (S * p0 - pad, S * q - pad + s)
   // and a 32-bit thread index.
   const int64_t i32 = 0x7fffffffll;
-  if (N > i32 || C > i32 || H + 2 * std::abs(pad) > i32 || W + 2 * std::abs(pad) > i32)
+  if (N > i32 || C > i32 || H + std::abs(pd.top) + std::abs(pd.bottom) > i32 ||
+      W + std::abs(pd.left) + std::abs(pd.right) > i32)
     return TDC_ERR_TOO_LARGE;
   if (N * Q > i32 || N * Q * (C / 2) > i32) return TDC_ERR_TOO_LARGE;
   if (H * W > i32 || H * W * (C / 2) > i32) return TDC_ERR_TOO_LARGE;  // 32-bit image offsets
@@ -617,7 +630,8 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.chunks = int32_t(cpairs >> chunk_log2);
   prm.bands = int32_t(bands);
   prm.band_rows = int32_t(rows);
-  prm.pad = int32_t(pad);
+  prm.pad = int32_t(pd.top);
+  prm.pad_w = int32_t(pd.left);
   prm.act = epi.act;
   prm.flip_taps = epi.flip_taps ? 1 : 0;
   const bool with_epilogue =
@@ -1370,17 +1384,22 @@ int default_fwd_stages(int64_t K, int64_t S) {
 // at stride 2 on 7-column outputs or layers under 64 MB, while larger
 // stride-2 layers with wider outputs stay on the ws kernel (28 x 28 x 192 at
 // batch 256: 20.2 vs 26.1 us).
-bool prefer_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
-                  int64_t pad) {
+bool prefer_plain_pads(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                       const Pad4& pd) {
   if (K != 3 && K != 5 && K != 7) return false;
   if ((S != 1 && S != 2) || C <= 0 || C % 8 != 0 || N <= 0) return false;
-  if (H + 2 * pad < K || W + 2 * pad < K) return false;
-  const int64_t P = (H + 2 * pad - K) / S + 1, Q = (W + 2 * pad - K) / S + 1;
+  if (H + pd.top + pd.bottom < K || W + pd.left + pd.right < K) return false;
+  const int64_t P = (H + pd.top + pd.bottom - K) / S + 1, Q = (W + pd.left + pd.right - K) / S + 1;
   const double fill_c = double(C) / double(64 * ((C + 63) / 64));
   const double fill_q = double(Q) / double(32 * ((Q + 31) / 32));
   if (fill_c * fill_q >= 0.5) return false;
   const double bytes = 2.0 * double(N) * double(C) * (double(H) * double(W) + double(P) * double(Q));
   return S == 1 || fill_q <= 0.25 || bytes < 64e6;
+}
+
+bool prefer_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                  int64_t pad) {
+  return prefer_plain_pads(N, H, W, C, K, S, Pad4{pad, pad, pad, pad});
 }
 
 // Whether the weight gradient with n_stage = 0 runs the plain kernel: narrow
@@ -1446,6 +1465,49 @@ TDC_API int tdc_dwconv_fwd_bf16(const void* x, const void* w, const void* bias,
                                 int64_t n_stage, void* stream) {
   return fwd_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad, act, n_stage,
                    stream);
+}
+
+// Forward with each side's padding given: the top / left sides are the
+// kernels' row / column offsets, the bottom / right sides set P and Q.  The
+// 3x3 stride-1 fp16 case runs the K x K kernel family (the same arithmetic).
+static int fwd_asym_entry(int dt, const void* x, const void* w, const void* bias,
+                          const void* residual, void* y, int64_t N, int64_t H, int64_t W,
+                          int64_t C, int64_t K, int64_t stride, int64_t pad_top,
+                          int64_t pad_bottom, int64_t pad_left, int64_t pad_right, int64_t act,
+                          int64_t n_stage, void* stream) {
+  if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
+  const Pad4 pd{pad_top, pad_bottom, pad_left, pad_right};
+  Epilogue epi;
+  epi.fused = true;
+  epi.bias = bias;
+  epi.residual = residual;
+  epi.act = int(act);
+  if (n_stage == 0) {  // automatic: the kernel and ring depth follow the shape
+    if (pad_top >= 0 && pad_bottom >= 0 && pad_left >= 0 && pad_right >= 0 &&
+        prefer_plain_pads(N, H, W, C, K, stride, pd))
+      return fwd_plain(x, w, y, N, H, W, C, K, stride, pad_top, 0, epi, stream, dt, &pd);
+    n_stage = default_fwd_stages(K, stride);
+  }
+  return fwd_geom(x, w, y, N, H, W, C, K, stride, pad_top, n_stage, epi, stream, dt, &pd);
+}
+
+TDC_API int tdc_dwconv_fwd_asym(const void* x, const void* w, const void* bias,
+                                const void* residual, void* y, int64_t N, int64_t H, int64_t W,
+                                int64_t C, int64_t K, int64_t stride, int64_t pad_top,
+                                int64_t pad_bottom, int64_t pad_left, int64_t pad_right,
+                                int64_t act, int64_t n_stage, void* stream) {
+  return fwd_asym_entry(kF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad_top,
+                        pad_bottom, pad_left, pad_right, act, n_stage, stream);
+}
+
+TDC_API int tdc_dwconv_fwd_asym_bf16(const void* x, const void* w, const void* bias,
+                                     const void* residual, void* y, int64_t N, int64_t H,
+                                     int64_t W, int64_t C, int64_t K, int64_t stride,
+                                     int64_t pad_top, int64_t pad_bottom, int64_t pad_left,
+                                     int64_t pad_right, int64_t act, int64_t n_stage,
+                                     void* stream) {
+  return fwd_asym_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad_top,
+                        pad_bottom, pad_left, pad_right, act, n_stage, stream);
 }
 
 static int plain_entry(int dt, const void* x, const void* w, const void* bias,

@@ -179,6 +179,7 @@ struct WsParams {
   int32_t act;                // kModeEpilogue only: TDC_ACT_*
   int32_t flip_taps;          // kModeGeneral / kModeEpilogue: use w[2-r][2-s] (data gradient)
   int32_t H, W, C, P, Q, pad;
+  int32_t pad_w;  // column offset (the left padding); pad is the row offset (top)
   int32_t qstrips, cblocks, stage_rows;
   int32_t tail_bands, tail_band_rows;
   int64_t full_units;   // strips handed out whole (a multiple of gridDim.x)
@@ -423,7 +424,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
       const int rows_in = S * (sg.rows - 1) + K;
       const int nst = (rows_in + p.stage_rows - 1) / p.stage_rows;
       const int32_t c0 = sg.cb * kBlockC;
-      const int32_t w0 = S * sg.qs * kStripQ - p.pad;
+      const int32_t w0 = S * sg.qs * kStripQ - p.pad_w;
       const int32_t h0 = S * sg.p0 - p.pad;
       for (int t = 0; t < nst; ++t) {
         const uint32_t eb = smem_addr(&empty_bar[stage]);

@@ -45,7 +45,9 @@ struct PlainParams {
   int32_t chunk_log2;        // log2 of the channel pairs per chunk (2 or 3)
   int32_t chunks;            // cpairs >> chunk_log2
   int32_t bands, band_rows;
-  int32_t pad;               // may be negative (a crop) for the flipped data gradient
+  int32_t pad;               // row offset (top padding); may be negative (a crop) for the
+                             // flipped data gradient
+  int32_t pad_w;             // column offset (left padding), likewise
   int32_t act;
   int32_t flip_taps;         // taps w[K-1-r][K-1-s] (data gradient of the stride-1 forward)
 };
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
   const int q0 = qg * QT;
   const int n_valid = min(QT, p.Q - q0);  // output columns of this thread
   const int h0 = S * p0 - p.pad;          // input row of band row 0
-  const int w0 = S * q0 - p.pad;          // input column of input j = 0
+  const int w0 = S * q0 - p.pad_w;        // input column of input j = 0
 
   uint32_t wt[K * K];
 #pragma unroll

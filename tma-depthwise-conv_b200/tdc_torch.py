@@ -16,9 +16,12 @@ an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
 * ``DepthwiseConv2d`` — a module with ``nn.Conv2d(C, C, K, stride, padding,
   groups=C, bias=...)``'s parameters and NCHW interface.  A channels-last NCHW
   tensor is NHWC in memory, so it runs on the kernels without a copy.
-  ``DepthwiseConv3x3`` is its 3x3 stride-1 form.
+  ``DepthwiseConv3x3`` is its 3x3 stride-1 form.  ``padding="same"`` is
+  TensorFlow's rule at any stride (ceil(H / stride) outputs, the odd row and
+  column at the bottom / right), run by the kernels' per-side padding in
+  inference and as explicit zero padding when a gradient is needed.
 * ``convert_depthwise_convs(model)`` — swaps every eligible ``nn.Conv2d``
-  (depthwise, dilation 1, symmetric integer padding, zeros padding mode,
+  (depthwise, dilation 1, symmetric integer padding or ``padding='same'``, zeros padding mode,
   C % 8 == 0; 3x3 / 5x5 / 7x7 at stride 1 or 2) for a ``DepthwiseConv2d``
   sharing its parameters.
 * ``fuse_depthwise_bn_act(model)`` — for inference: a depthwise convolution
@@ -307,7 +310,7 @@ class DepthwiseConv2d(nn.Module):
     """
 
     def __init__(self, channels: int, kernel_size: int = 3, stride: int = 1,
-                 padding: Optional[int] = None, bias: bool = True, device=None,
+                 padding=None, bias: bool = True, device=None,
                  dtype=torch.float16, activation: str = "none"):
         super().__init__()
         if (kernel_size, stride) not in GEOMETRIES:
@@ -319,7 +322,10 @@ class DepthwiseConv2d(nn.Module):
         self.channels = channels
         self.kernel_size = int(kernel_size)
         self.stride = int(stride)
-        self.padding = kernel_size // 2 if padding is None else int(padding)
+        # an int (the same on every side), or "same": TensorFlow's / PyTorch's
+        # "same" padding, ceil(H / stride) output rows, computed per input
+        self.padding = (kernel_size // 2 if padding is None else
+                        "same" if padding == "same" else int(padding))
         self.weight = nn.Parameter(torch.empty(channels, 1, kernel_size, kernel_size,
                                                device=device, dtype=dtype))
         self.bias = nn.Parameter(torch.empty(channels, device=device, dtype=dtype)) if bias else None
@@ -335,7 +341,7 @@ class DepthwiseConv2d(nn.Module):
         m.channels = conv.in_channels
         m.kernel_size = int(conv.kernel_size[0])
         m.stride = int(conv.stride[0])
-        m.padding = int(conv.padding[0])
+        m.padding = _conv2d_pad(conv)
         m.weight = conv.weight
         m.bias = conv.bias
         m.activation = "none"
@@ -343,16 +349,25 @@ class DepthwiseConv2d(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float16
-        x = x.to(dt).contiguous(memory_format=torch.channels_last)
         act = self.activation
         needs_grad = torch.is_grad_enabled() and (
             x.requires_grad or self.weight.requires_grad
             or (self.bias is not None and self.bias.requires_grad))
+        pad, pads = self.padding, None
+        if pad == "same":
+            pads = _T.same_padding(x.shape[2], x.shape[3], self.kernel_size, self.stride)
+            if pads[0] == pads[1] == pads[2] == pads[3]:
+                pad, pads = pads[0], None
+            elif needs_grad:
+                # training: explicit zero padding, then the symmetric kernels
+                # (whose gradients cover pad 0)
+                x = torch.nn.functional.pad(x, (pads[2], pads[3], pads[0], pads[1]))
+                pad, pads = 0, None
+        x = x.to(dt).contiguous(memory_format=torch.channels_last)
         if needs_grad and not torch.compiler.is_compiling():
             # training, eager: one autograd node for conv + bias (the
             # activation, if any, runs outside the kernel)
-            y = _DepthwiseConvFunction.apply(x, self.weight, self.bias, self.stride,
-                                             self.padding, dt)
+            y = _DepthwiseConvFunction.apply(x, self.weight, self.bias, self.stride, pad, dt)
             return y if act == "none" else _TORCH_ACTS[act](y)
         x_nhwc = x.permute(0, 2, 3, 1)                                  # contiguous view, no copy
         w_rsc = self.weight.to(dt)[:, 0].permute(1, 2, 0)              # [K,K,C]
@@ -361,10 +376,15 @@ class DepthwiseConv2d(nn.Module):
             # inference: straight to the extension (which checks its arguments),
             # without the custom op's dispatch; the activation runs in the
             # kernel's fused epilogue
-            y = _C.dwconv_k(x_nhwc, w_rsc.contiguous(), None if b is None else b.contiguous(),
-                            None, self.stride, self.padding, _T.ACTIVATIONS[act], 0)
-        else:  # under torch.compile: the custom op, which has fake kernels
-            y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, self.padding)
+            b = None if b is None else b.contiguous()
+            if pads is not None:  # "same" with more padding at the bottom / right
+                y = _C.dwconv_k_asym(x_nhwc, w_rsc.contiguous(), b, None, self.stride, *pads,
+                                     _T.ACTIVATIONS[act], 0)
+            else:
+                y = _C.dwconv_k(x_nhwc, w_rsc.contiguous(), b, None, self.stride, pad,
+                                _T.ACTIVATIONS[act], 0)
+        else:  # under torch.compile (pads already explicit): the custom op, which has fake kernels
+            y = dwconv_op(x_nhwc, w_rsc.contiguous(), b, self.stride, pad)
             if act != "none":  # the autograd formula covers conv + bias
                 y = _TORCH_ACTS[act](y)
         return y.permute(0, 3, 1, 2)                                    # NCHW view, channels-last memory
@@ -381,6 +401,15 @@ class DepthwiseConv3x3(DepthwiseConv2d):
     def __init__(self, channels: int, padding: int = 1, bias: bool = True, device=None,
                  dtype=torch.float16):
         super().__init__(channels, 3, 1, padding, bias, device, dtype)
+
+
+def _conv2d_pad(conv: nn.Conv2d) -> int:
+    """The symmetric padding of an eligible depthwise nn.Conv2d: its integer
+    padding, or K // 2 for ``padding='same'`` (PyTorch allows it at stride 1
+    only, where an odd K pads K // 2 on every side)."""
+    if conv.padding == "same":
+        return int(conv.kernel_size[0]) // 2
+    return int(conv.padding[0])
 
 
 def _plain_conv2d(m: nn.Module) -> bool:
@@ -403,8 +432,9 @@ def _plain_conv2d(m: nn.Module) -> bool:
 def _eligible(m: nn.Module, forward_only: bool) -> bool:
     if not (_plain_conv2d(m) and m.dilation == (1, 1)
             and m.groups == m.in_channels == m.out_channels and m.in_channels % 8 == 0
-            and m.padding_mode == "zeros" and isinstance(m.padding, tuple)
-            and m.padding[0] == m.padding[1]
+            and m.padding_mode == "zeros"
+            and ((isinstance(m.padding, tuple) and m.padding[0] == m.padding[1])
+                 or (m.padding == "same" and m.kernel_size[0] % 2 == 1))
             and m.kernel_size[0] == m.kernel_size[1] and m.stride[0] == m.stride[1]):
         return False
     geometry = (m.kernel_size[0], m.stride[0])
@@ -445,8 +475,8 @@ def _fold_bn(conv: nn.Module, bn: nn.BatchNorm2d, activation: str) -> DepthwiseC
     g = gamma / torch.sqrt(bn.running_var.detach().float() + bn.eps)
     k = conv.kernel_size[0] if isinstance(conv.kernel_size, tuple) else conv.kernel_size
     stride = conv.stride[0] if isinstance(conv.stride, tuple) else conv.stride
-    pad = conv.padding[0] if isinstance(conv.padding, tuple) else conv.padding
-    m = DepthwiseConv2d(c, int(k), int(stride), int(pad), bias=True, device=w.device,
+    pad = conv.padding if isinstance(conv, DepthwiseConv2d) else _conv2d_pad(conv)
+    m = DepthwiseConv2d(c, int(k), int(stride), pad, bias=True, device=w.device,
                         dtype=conv.weight.dtype, activation=activation)
     with torch.no_grad():
         m.weight.copy_(w * g[:, None, None, None])

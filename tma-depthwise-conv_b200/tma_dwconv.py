@@ -211,7 +211,20 @@ def dwconv3x3(x: torch.Tensor, w: torch.Tensor, pad: int = 1,
 DWCONV_STAGES = {(3, 1): 2, (3, 2): 4, (5, 1): 4, (5, 2): 2, (7, 1): 3, (7, 2): 4}
 
 
-def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int = 1,
+def same_padding(H: int, W: int, K: int, stride: int = 1) -> tuple[int, int, int, int]:
+    """TensorFlow's "SAME" padding of an H x W input for a K x K kernel:
+    (top, bottom, left, right) giving ceil(H / stride) x ceil(W / stride)
+    outputs, the odd row / column at the bottom / right."""
+    def split(n):
+        out = -(-n // stride)
+        total = max((out - 1) * stride + K - n, 0)
+        return total // 2, total - total // 2
+    top, bottom = split(int(H))
+    left, right = split(int(W))
+    return top, bottom, left, right
+
+
+def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | tuple | None = None, stride: int = 1,
            bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
            activation: str = "none", n_stage: int | None = None) -> torch.Tensor:
     """K x K depthwise forward, K in {3, 5, 7}, stride 1 or 2 (beyond the reference surface).
@@ -226,6 +239,11 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int
     kernel at ``DWCONV_STAGES[(K, stride)]``.  The result is the same bit for
     bit either way.
 
+    ``pad`` may also be a tuple (top, bottom, left, right) of per-side zero
+    padding (e.g. ``same_padding(H, W, K, stride)``, TensorFlow's "SAME"):
+    the top / left sides shift the taps, P = (H + top + bottom - K) // stride
+    + 1 and Q likewise.
+
     Args:
         x: [N, H, W, C] fp16 or bf16 CUDA, contiguous, C % 8 == 0.   w: [K, K, C], x's dtype.
         bias: [C] or None.   residual: [N, P, Q, C] or None (x's dtype), with
@@ -233,6 +251,12 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int
     """
     if w.dim() == 3 and pad is None:
         pad = int(w.shape[0]) // 2
+    pads = None
+    if isinstance(pad, (tuple, list)):
+        if len(pad) != 4:
+            raise ValueError(f"pad must be an int or (top, bottom, left, right), got {pad!r}")
+        pads = tuple(int(v) for v in pad)
+        pad = min(pads)
     _check(x, w, pad, bf16_ok=True)
     K = int(w.shape[0])
     if K not in (3, 5, 7) or w.shape[1] != K:
@@ -245,8 +269,11 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int
         raise ValueError(f"n_stage must be one of {{2, 3, 4}}, got {n_stage}")
     if activation not in ACTIVATIONS:
         raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
-    return _C.dwconv_k(x, w, bias, residual, int(stride), int(pad), ACTIVATIONS[activation],
-                       0 if n_stage is None else int(n_stage))
+    ns = 0 if n_stage is None else int(n_stage)
+    if pads is not None and not (pads[0] == pads[1] == pads[2] == pads[3]):
+        return _C.dwconv_k_asym(x, w, bias, residual, int(stride), *pads,
+                                ACTIVATIONS[activation], ns)
+    return _C.dwconv_k(x, w, bias, residual, int(stride), int(pad), ACTIVATIONS[activation], ns)
 
 
 def dwconv_plain(x: torch.Tensor, w: torch.Tensor, pad: int | None = None, stride: int = 1,
