@@ -186,6 +186,27 @@ TDC_API int tdc_dwconv_fwd_asym_bf16(const void* x, const void* w, const void* b
                                      int64_t pad_left, int64_t pad_right, int64_t act,
                                      int64_t n_stage, void* stream);
 
+/* Dilated K x K forward (K = 3, 5, 7, stride 1 or 2, dilation >= 1) with
+ * per-side padding:
+ *   y[n,p,q,c] = epilogue(chain_{r,s} x[n, S*p + D*r - pad_top, S*q + D*s - pad_left, c] * w[r,s,c])
+ * P = (H + pad_top + pad_bottom - D*(K-1) - 1)/S + 1, Q likewise; the same
+ * fp32 chain, epilogue and rounding as tdc_dwconv_fwd (atrous depthwise layers,
+ * e.g. DeepLab backbones).  dilation 1 is tdc_dwconv_fwd_asym with n_stage 0;
+ * above 1 a plain kernel computes each output's K*K taps through L1.  No
+ * counterpart in the reference (no dilation). */
+TDC_API int tdc_dwconv_fwd_dilated(const void* x, const void* w, const void* bias,
+                                   const void* residual, void* y,
+                                   int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                   int64_t stride, int64_t dilation, int64_t pad_top,
+                                   int64_t pad_bottom, int64_t pad_left, int64_t pad_right,
+                                   int64_t act, void* stream);
+TDC_API int tdc_dwconv_fwd_dilated_bf16(const void* x, const void* w, const void* bias,
+                                        const void* residual, void* y,
+                                        int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                        int64_t stride, int64_t dilation, int64_t pad_top,
+                                        int64_t pad_bottom, int64_t pad_left, int64_t pad_right,
+                                        int64_t act, void* stream);
+
 /* Plain K x K forward: global loads through L1, no TMA, no shared memory, no
  * pipeline.  A thread owns one channel pair of one output column over a band
  * of band_rows output rows (0 = chosen from the shape: the full height unless

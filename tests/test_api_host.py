@@ -107,7 +107,7 @@ def test_convert_depthwise_convs_eligibility():
         nn.Conv2d(64, 64, 7, padding=3, groups=64),             # converted
         nn.Conv2d(64, 64, 5, stride=2, padding=2, groups=64),   # converted (stride 2)
         nn.Sequential(nn.Conv2d(64, 64, 3, stride=2, padding=1, groups=64)),  # nested: converted
-        nn.Conv2d(64, 64, 3, padding=1, groups=64, dilation=2),  # dilated: never
+        nn.Conv2d(64, 64, 3, padding=1, groups=64, dilation=2),  # dilated: forward_only
         nn.Conv2d(64, 64, 3, padding=1, groups=32),              # not depthwise: never
         nn.Conv2d(12, 12, 3, padding=1, groups=12),              # C % 8 != 0: never
         nn.Conv2d(64, 64, 9, padding=4, groups=64),              # 9x9: never
@@ -117,8 +117,11 @@ def test_convert_depthwise_convs_eligibility():
     assert isinstance(model[0], tdc_torch.DepthwiseConv3x3)
     assert type(model[1]) is tdc_torch.DepthwiseConv2d and model[1].kernel_size == 7
     assert model[2].stride == 2 and model[2].padding == 2 and model[3][0].stride == 2
-    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 0  # nothing left
-    assert all(isinstance(m, nn.Conv2d) for m in list(model)[4:])
+    assert tdc_torch.convert_depthwise_convs(model) == 0  # nothing left for training
+    # inference only: the dilated conv too
+    assert tdc_torch.convert_depthwise_convs(model, forward_only=True) == 1
+    assert type(model[4]) is tdc_torch.DepthwiseConv3x3 and model[4].dilation == 2
+    assert all(isinstance(m, nn.Conv2d) for m in list(model)[5:])
     with pytest.raises(ValueError, match="kernel_size must be 3, 5 or 7"):
         tdc_torch.DepthwiseConv2d(64, 9)
 

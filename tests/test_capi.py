@@ -796,3 +796,25 @@ def test_per_side_padding_argument_errors(lib):
         assert fwd(N=0, f=f) == CODES["TDC_OK"]
         if not torch.cuda.is_available():
             assert fwd(f=f) == CODES["TDC_ERR_NO_DEVICE"]
+
+
+def test_dilated_forward_argument_errors(lib):
+    p = C.c_void_p
+    def fwd(K=3, stride=1, D=2, C_=64, pads=(2, 2, 2, 2), H=16, act=0, N=2, x=16, f=None):
+        f = f or lib.tdc_dwconv_fwd_dilated
+        return f(p(x), p(16), None, None, p(16), i64(N), i64(H), i64(16), i64(C_), i64(K),
+                 i64(stride), i64(D), *[i64(v) for v in pads], i64(act), None)
+    for f in (lib.tdc_dwconv_fwd_dilated, lib.tdc_dwconv_fwd_dilated_bf16):
+        assert fwd(K=4, f=f) == CODES["TDC_ERR_FILTER_SHAPE"]
+        assert fwd(stride=3, f=f) == CODES["TDC_ERR_STRIDE"]
+        assert fwd(D=0, f=f) == CODES["TDC_ERR_BAD_SHAPE"]
+        assert fwd(C_=12, f=f) == CODES["TDC_ERR_CHANNELS"]
+        assert fwd(pads=(-1, 2, 2, 2), f=f) == CODES["TDC_ERR_PAD"]
+        assert fwd(act=5, f=f) == CODES["TDC_ERR_ACT"]
+        assert fwd(K=7, D=3, H=4, pads=(0, 0, 9, 9), f=f) == CODES["TDC_ERR_BAD_SHAPE"]  # 4 < 19
+        assert fwd(x=24, f=f) == CODES["TDC_ERR_ALIGNMENT"]
+        assert fwd(x=0, f=f) == CODES["TDC_ERR_NULL_POINTER"]
+        assert fwd(N=0, f=f) == CODES["TDC_OK"]
+        if not torch.cuda.is_available():
+            assert fwd(f=f) == CODES["TDC_ERR_NO_DEVICE"]
+            assert fwd(D=1, f=f) == CODES["TDC_ERR_NO_DEVICE"]  # dilation 1: the asym path

@@ -1,10 +1,13 @@
 """Per-side zero padding (tdc_dwconv_fwd_asym, `tma_dwconv.dwconv(pad=(top,
-bottom, left, right))`) and TensorFlow-style "same" padding
-(`tma_dwconv.same_padding`, `DepthwiseConv2d(padding="same")`), on the GPU.
+bottom, left, right))`), TensorFlow-style "same" padding
+(`tma_dwconv.same_padding`, `DepthwiseConv2d(padding="same")`) and dilation
+(tdc_dwconv_fwd_dilated, `dwconv(dilation=D)`), on the GPU.
 
 Parity bar: bit for bit with the CPU oracle's K x K forward at pad 0 on the
-input zero-padded by hand (padding only adds exact zero products to the fp32
-chain, which never holds -0, so the two are the same arithmetic).
+input zero-padded by hand, and for dilation D on the K' = D*(K-1)+1 kernel
+with zeros between the taps (padding and the inserted zeros only add exact
+zero products to the fp32 chain, which never holds -0, so these are the same
+arithmetic in the same order).
 """
 import numpy as np
 import pytest
@@ -49,7 +52,7 @@ def test_per_side_padding_matches_oracle(K, S, N, H, W, C):
         for n_stage in (None, T.DWCONV_STAGES[(K, S)]):
             y = T.dwconv(xc, wc, pads, stride=S, bias=bc, activation="relu6", n_stage=n_stage)
             assert np.array_equal(_bits(y), want), (pads, n_stage)
-        y = T._C.dwconv_k_asym(xc, wc, bc, None, S, *pads, T.ACTIVATIONS["relu6"], 0)
+        y = T._C.dwconv_k_pads(xc, wc, bc, None, S, 1, *pads, T.ACTIVATIONS["relu6"], 0)
         assert np.array_equal(_bits(y), want), pads
 
 
@@ -102,3 +105,79 @@ def test_converted_same_padding_conv():
         got = model(x)
     assert model[0].padding == 2
     torch.testing.assert_close(got.float(), want.float(), rtol=2e-3, atol=2e-3)
+
+
+def _dilated(w, D):
+    K, _, C = w.shape
+    Ke = D * (K - 1) + 1
+    wd = np.zeros((Ke, Ke, C), dtype=w.dtype)
+    wd[::D, ::D] = w
+    return wd
+
+
+@pytest.mark.parametrize("K,S", GEOMS)
+@pytest.mark.parametrize("D", [2, 3])
+@pytest.mark.parametrize("N,H,W,C", [(2, 21, 30, 64), (3, 17, 17, 200), (1, 33, 12, 16)])
+def test_dilated_matches_oracle(K, S, D, N, H, W, C):
+    x, w, b = _inputs(N, H, W, C, K, seed=K + S + D + C)
+    Ke = D * (K - 1) + 1
+    for pads in [(Ke // 2,) * 4, (0, 1, 2, 0), T.same_padding(H, W, Ke, S)]:
+        t, bo, l, r = pads
+        if H + t + bo < Ke or W + l + r < Ke:
+            continue
+        xp = np.pad(x.numpy(), ((0, 0), (t, bo), (l, r), (0, 0)))
+        want = oracle.dwconv_k_f16(xp, _dilated(w.numpy(), D), 0, S, bias=b.numpy(),
+                                   activation="silu" if K == 3 else "relu").view(np.uint16)
+        act = "silu" if K == 3 else "relu"
+        y = T.dwconv(x.cuda(), w.cuda(), pads, stride=S, bias=b.cuda(), activation=act,
+                     dilation=D)
+        if act == "silu":  # the kernels' fast exp / divide: within the oracle's silu bound
+            got = y.float().cpu().numpy()
+            ref = want.view(np.float16).astype(np.float32)
+            assert (np.abs(got - ref) <= oracle.silu_tolerance(ref)).all(), pads
+        else:
+            assert np.array_equal(_bits(y), want), pads
+
+
+def test_dilated_bf16():
+    x, w, _ = _inputs(2, 19, 26, 72, 5, seed=9, dtype=torch.bfloat16)
+    xp = np.pad(_bits(x), ((0, 0), (4, 4), (4, 4), (0, 0)))
+    want = oracle.dwconv_k_bf16(xp, _dilated(_bits(w), 2), 0, 1)
+    y = T.dwconv(x.cuda(), w.cuda(), 4, dilation=2)
+    assert y.dtype == torch.bfloat16 and np.array_equal(_bits(y), want)
+
+
+def test_dilated_module_is_inference_only():
+    m = tdc_torch.DepthwiseConv2d(64, 3, 1, dilation=2).cuda()
+    x = torch.randn(1, 64, 9, 9, device="cuda").half().to(memory_format=torch.channels_last)
+    with torch.no_grad():
+        assert m(x).shape == (1, 64, 9, 9)
+    with pytest.raises(RuntimeError, match="not implemented"):
+        m(x.requires_grad_())
+
+
+def test_deeplabv3_mobilenet_end_to_end():
+    """torchvision's DeepLabV3-MobileNetV3-Large (dilated depthwise layers in
+    the last stages) with every depthwise + BatchNorm + activation fused,
+    against the unfused fp16 model."""
+    seg = pytest.importorskip("torchvision.models.segmentation")
+    torch.manual_seed(0)
+    model = seg.deeplabv3_mobilenet_v3_large(weights=None, weights_backbone=None,
+                                             num_classes=21, aux_loss=False)
+    for mod in model.modules():
+        if isinstance(mod, torch.nn.BatchNorm2d):
+            mod.running_mean.uniform_(-0.2, 0.2)
+            mod.running_var.uniform_(0.5, 1.5)
+    model = model.eval().cuda().half().to(memory_format=torch.channels_last)
+    dilated = sum(1 for mod in model.modules() if isinstance(mod, torch.nn.Conv2d)
+                  and mod.groups == mod.in_channels > 1 and mod.dilation[0] > 1)
+    x = torch.randn(2, 3, 224, 224, device="cuda").half().to(memory_format=torch.channels_last)
+    with torch.no_grad():
+        want = model(x)["out"].float()
+        fused = tdc_torch.fuse_depthwise_bn_act(model)
+        got = model(x)["out"].float()
+    assert dilated > 0 and fused >= 15
+    assert not any(isinstance(mod, torch.nn.Conv2d) and mod.groups == mod.in_channels > 1
+                   for mod in model.modules())
+    err = (got - want).abs().max().item()
+    assert err <= 2e-2 * want.abs().max().item() + 1e-2, err

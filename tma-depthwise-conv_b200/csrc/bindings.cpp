@@ -230,11 +230,13 @@ torch::Tensor dwconv_k(torch::Tensor x, torch::Tensor w, std::optional<torch::Te
   return y;
 }
 
-// dwconv_k with each side's padding given (top, bottom, left, right).
-torch::Tensor dwconv_k_asym(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
+// dwconv_k with each side's padding given (top, bottom, left, right) and a
+// dilation (1: the sliding-window kernels with n_stage; above 1: the dilated
+// plain kernel, n_stage ignored).
+torch::Tensor dwconv_k_pads(torch::Tensor x, torch::Tensor w, std::optional<torch::Tensor> bias,
                             std::optional<torch::Tensor> residual, int64_t stride,
-                            int64_t pad_top, int64_t pad_bottom, int64_t pad_left,
-                            int64_t pad_right, int64_t act, int64_t n_stage) {
+                            int64_t dilation, int64_t pad_top, int64_t pad_bottom,
+                            int64_t pad_left, int64_t pad_right, int64_t act, int64_t n_stage) {
   const bool bf16 = check_common_16(x, w, "x");
   const int64_t K = w.size(0);
   TORCH_CHECK(w.size(1) == K && (K == 3 || K == 5 || K == 7), "w must be [K,K,C] with K in {3, 5, 7}");
@@ -245,11 +247,14 @@ torch::Tensor dwconv_k_asym(torch::Tensor x, torch::Tensor w, std::optional<torc
               "pads must be non-negative");
   TORCH_CHECK(n_stage == 0 || (n_stage >= 2 && n_stage <= 4),
               "n_stage must be one of {2, 3, 4} (or 0: chosen from the shape), got ", n_stage);
-  TORCH_CHECK(x.size(1) + pad_top + pad_bottom >= K && x.size(2) + pad_left + pad_right >= K,
-              "input too small for a ", K, "x", K, " kernel with these pads");
+  TORCH_CHECK(dilation >= 1, "dilation must be >= 1, got ", dilation);
+  const int64_t Ke = dilation * (K - 1) + 1;
+  TORCH_CHECK(x.size(1) + pad_top + pad_bottom >= Ke && x.size(2) + pad_left + pad_right >= Ke,
+              "input too small for a ", K, "x", K, " kernel (dilation ", dilation,
+              ") with these pads");
   const c10::cuda::CUDAGuard guard(x.device());
-  const int64_t P = (x.size(1) + pad_top + pad_bottom - K) / stride + 1;
-  const int64_t Q = (x.size(2) + pad_left + pad_right - K) / stride + 1;
+  const int64_t P = (x.size(1) + pad_top + pad_bottom - Ke) / stride + 1;
+  const int64_t Q = (x.size(2) + pad_left + pad_right - Ke) / stride + 1;
   auto y = torch::empty({x.size(0), P, Q, x.size(3)}, x.options());
   const void* bptr = nullptr;
   const void* rptr = nullptr;
@@ -267,11 +272,19 @@ torch::Tensor dwconv_k_asym(torch::Tensor x, torch::Tensor w, std::optional<torc
                 "residual must be a contiguous [N,P,Q,C] tensor of x's dtype on x's device");
     rptr = r.data_ptr();
   }
-  auto* fwd = bf16 ? &tdc_dwconv_fwd_asym_bf16 : &tdc_dwconv_fwd_asym;
-  check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
-                   x.size(2), x.size(3), K, stride, pad_top, pad_bottom, pad_left, pad_right, act,
-                   n_stage, stream_of(x)),
-               "dwconv_k_asym");
+  if (dilation == 1) {
+    auto* fwd = bf16 ? &tdc_dwconv_fwd_asym_bf16 : &tdc_dwconv_fwd_asym;
+    check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
+                     x.size(2), x.size(3), K, stride, pad_top, pad_bottom, pad_left, pad_right,
+                     act, n_stage, stream_of(x)),
+                 "dwconv_k_pads");
+  } else {
+    auto* fwd = bf16 ? &tdc_dwconv_fwd_dilated_bf16 : &tdc_dwconv_fwd_dilated;
+    check_status(fwd(x.data_ptr(), w.data_ptr(), bptr, rptr, y.data_ptr(), x.size(0), x.size(1),
+                     x.size(2), x.size(3), K, stride, dilation, pad_top, pad_bottom, pad_left,
+                     pad_right, act, stream_of(x)),
+                 "dwconv_k_pads");
+  }
   return y;
 }
 
@@ -555,11 +568,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "K x K (3, 5, 7) depthwise forward, stride 1 or 2, optional fused epilogue",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
         py::arg("pad"), py::arg("act"), py::arg("n_stage"));
-  m.def("dwconv_k_asym", &tma_dwconv::dwconv_k_asym,
-        "K x K depthwise forward with each side's padding (top, bottom, left, right)",
+  m.def("dwconv_k_pads", &tma_dwconv::dwconv_k_pads,
+        "K x K depthwise forward with each side's padding (top, bottom, left, right) and a "
+        "dilation",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),
-        py::arg("pad_top"), py::arg("pad_bottom"), py::arg("pad_left"), py::arg("pad_right"),
-        py::arg("act"), py::arg("n_stage"));
+        py::arg("dilation"), py::arg("pad_top"), py::arg("pad_bottom"), py::arg("pad_left"),
+        py::arg("pad_right"), py::arg("act"), py::arg("n_stage"));
   m.def("dwconv_plain", &tma_dwconv::dwconv_plain,
         "plain (no TMA) K x K depthwise forward, the same result as dwconv_k",
         py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("stride"),

@@ -642,6 +642,86 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
+// Dilated forward (tdc_plain.cuh): one kernel per (element type, K, epilogue).
+using DilatedLaunchFn = cudaError_t (*)(const tdc::PlainParams&, int32_t, int32_t, int64_t,
+                                        cudaStream_t);
+
+template <int K, class E, bool EPI>
+cudaError_t dilated_launch_t(const tdc::PlainParams& prm, int32_t S, int32_t D, int64_t grid,
+                             cudaStream_t st) {
+  return launch_pdl_block(&tdc::dwconv_dilated_kernel<K, E, EPI>, grid,
+                          unsigned(tdc::kPlainThreads), 0, st, prm, S, D);
+}
+
+#define TDC_DIL_K(E, K) {dilated_launch_t<K, E, false>, dilated_launch_t<K, E, true>}
+#define TDC_DIL_TABLE(E) {TDC_DIL_K(E, 3), TDC_DIL_K(E, 5), TDC_DIL_K(E, 7)}
+// [element type][K index: 3, 5, 7][epilogue]
+const DilatedLaunchFn kDilatedLaunch[2][3][2] = {TDC_DIL_TABLE(tdc::F16), TDC_DIL_TABLE(tdc::BF16)};
+#undef TDC_DIL_TABLE
+#undef TDC_DIL_K
+
+int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
+                int64_t C, int64_t K, int64_t S, int64_t D, const Pad4& pd, const Epilogue& epi,
+                void* stream, int dt) {
+  if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
+  if (S != 1 && S != 2) return TDC_ERR_STRIDE;
+  if (D < 1) return TDC_ERR_BAD_SHAPE;
+  if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return TDC_ERR_CHANNELS;
+  if (pd.top < 0 || pd.bottom < 0 || pd.left < 0 || pd.right < 0) return TDC_ERR_PAD;
+  const int64_t i32 = 0x7fffffffll;
+  if (D > (1 << 24) || std::max({pd.top, pd.bottom, pd.left, pd.right}) > (1 << 28) ||
+      N > i32 || C > i32 || H > i32 || W > i32)
+    return TDC_ERR_TOO_LARGE;
+  const int64_t Ke = D * (K - 1) + 1;  // the dilated kernel's extent
+  if (H + pd.top + pd.bottom < Ke || W + pd.left + pd.right < Ke) return TDC_ERR_BAD_SHAPE;
+  const int64_t P = (H + pd.top + pd.bottom - Ke) / S + 1, Q = (W + pd.left + pd.right - Ke) / S + 1;
+  // 32-bit row / column arithmetic in the kernel (S * p + D * r - pad)
+  if (S * P + D * K + pd.top > i32 || S * Q + D * K + pd.left > i32) return TDC_ERR_TOO_LARGE;
+  if (N == 0 || C == 0) return TDC_OK;
+  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
+      (epi.residual && !aligned16(epi.residual)))
+    return TDC_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  int rc = current_device(&dev, nullptr);
+  if (rc != TDC_OK) return rc;
+  const int64_t cpairs = C / 2;
+  const int chunk_log2 = cpairs % 8 == 0 ? 3 : 2;
+  const int64_t qgroups = (Q + tdc::kDilatedCols - 1) / tdc::kDilatedCols;
+  if (N * qgroups > i32 || N * qgroups * cpairs > i32) return TDC_ERR_TOO_LARGE;
+  const int64_t per_band = std::max<int64_t>(1, N * qgroups * cpairs);
+  const int64_t bands0 = std::min<int64_t>(
+      P, std::max<int64_t>(1, (384 * std::max<int64_t>(1, dev->sms) + per_band - 1) / per_band));
+  const int64_t rows = (P + bands0 - 1) / bands0;
+  const int64_t bands = (P + rows - 1) / rows;
+  const int64_t total = N * qgroups * cpairs * bands;
+  if (total > 0xffffffffll - tdc::kPlainThreads) return TDC_ERR_TOO_LARGE;
+  tdc::PlainParams prm{};
+  prm.x = static_cast<const uint32_t*>(x);
+  prm.w = static_cast<const uint32_t*>(w);
+  prm.bias = static_cast<const uint32_t*>(epi.bias);
+  prm.residual = static_cast<const uint32_t*>(epi.residual);
+  prm.y = static_cast<uint32_t*>(y);
+  prm.total = uint32_t(total);
+  prm.H = int32_t(H); prm.W = int32_t(W); prm.P = int32_t(P); prm.Q = int32_t(Q);
+  prm.qgroups = int32_t(qgroups);
+  prm.cpairs = int32_t(cpairs);
+  prm.chunk_log2 = chunk_log2;
+  prm.chunks = int32_t(cpairs >> chunk_log2);
+  prm.bands = int32_t(bands);
+  prm.band_rows = int32_t(rows);
+  prm.pad = int32_t(pd.top);
+  prm.pad_w = int32_t(pd.left);
+  prm.act = epi.act;
+  const bool with_epilogue =
+      epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
+  const cudaError_t e = kDilatedLaunch[dt][K / 2 - 1][with_epilogue ? 1 : 0](
+      prm, int32_t(S), int32_t(D), (total + tdc::kPlainThreads - 1) / tdc::kPlainThreads,
+      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
 // Plain weight gradient (tdc_plain.cuh): bands of dy rows chosen for about
 // 1024 threads per SM counting the K tap rows, the units of one channel
 // chunk summed per CTA, one workspace slice per unit group.
@@ -1508,6 +1588,44 @@ TDC_API int tdc_dwconv_fwd_asym_bf16(const void* x, const void* w, const void* b
                                      void* stream) {
   return fwd_asym_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, pad_top,
                         pad_bottom, pad_left, pad_right, act, n_stage, stream);
+}
+
+static int fwd_dilated_entry(int dt, const void* x, const void* w, const void* bias,
+                             const void* residual, void* y, int64_t N, int64_t H, int64_t W,
+                             int64_t C, int64_t K, int64_t stride, int64_t dilation,
+                             int64_t pad_top, int64_t pad_bottom, int64_t pad_left,
+                             int64_t pad_right, int64_t act, void* stream) {
+  if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
+  if (dilation == 1)  // the sliding-window kernels, chosen by shape
+    return fwd_asym_entry(dt, x, w, bias, residual, y, N, H, W, C, K, stride, pad_top,
+                          pad_bottom, pad_left, pad_right, act, 0, stream);
+  Epilogue epi;
+  epi.fused = true;
+  epi.bias = bias;
+  epi.residual = residual;
+  epi.act = int(act);
+  return fwd_dilated(x, w, y, N, H, W, C, K, stride, dilation,
+                     Pad4{pad_top, pad_bottom, pad_left, pad_right}, epi, stream, dt);
+}
+
+TDC_API int tdc_dwconv_fwd_dilated(const void* x, const void* w, const void* bias,
+                                   const void* residual, void* y, int64_t N, int64_t H,
+                                   int64_t W, int64_t C, int64_t K, int64_t stride,
+                                   int64_t dilation, int64_t pad_top, int64_t pad_bottom,
+                                   int64_t pad_left, int64_t pad_right, int64_t act,
+                                   void* stream) {
+  return fwd_dilated_entry(kF16, x, w, bias, residual, y, N, H, W, C, K, stride, dilation,
+                           pad_top, pad_bottom, pad_left, pad_right, act, stream);
+}
+
+TDC_API int tdc_dwconv_fwd_dilated_bf16(const void* x, const void* w, const void* bias,
+                                        const void* residual, void* y, int64_t N, int64_t H,
+                                        int64_t W, int64_t C, int64_t K, int64_t stride,
+                                        int64_t dilation, int64_t pad_top, int64_t pad_bottom,
+                                        int64_t pad_left, int64_t pad_right, int64_t act,
+                                        void* stream) {
+  return fwd_dilated_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, dilation,
+                           pad_top, pad_bottom, pad_left, pad_right, act, stream);
 }
 
 static int plain_entry(int dt, const void* x, const void* w, const void* bias,

@@ -172,6 +172,94 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
 }
 
 // ============================================================================
+// Dilated forward (K = 3, 5, 7, stride 1 or 2, dilation D >= 1, per-side
+// padding): y[n,p,q,c] = epilogue(chain_{r,s} x[n, S*p + D*r - pad,
+// S*q + D*s - pad_w, c] * w[r,s,c]).  A dilation known only at run time
+// leaves no compile-time window for the sliding scheme above, so a thread
+// computes kDilatedCols output columns of one channel pair row by row, each
+// output's K*K taps loaded through L1 (the K*K weights in registers); per
+// output the fp32 chain runs in (r, s) order from +0 with the plain kernel's
+// epilogue and rounding, so the result is the same arithmetic as the oracle's
+// on the zero-inflated K' = D*(K-1)+1 kernel.  Threads are dealt as in the
+// plain kernel (PlainParams.qgroups counts groups of kDilatedCols columns).
+// ============================================================================
+constexpr int kDilatedCols = 4;
+
+template <int K, class E, bool EPI>
+__global__ void __launch_bounds__(kPlainThreads) dwconv_dilated_kernel(PlainParams p,
+                                                                       int32_t S, int32_t D) {
+  constexpr int QT = kDilatedCols;
+  griddep_wait();
+  const uint32_t t = blockIdx.x * uint32_t(kPlainThreads) + threadIdx.x;
+  if (t >= p.total) return;
+  const uint32_t cmask = (1u << p.chunk_log2) - 1u;
+  uint32_t r_ = t >> p.chunk_log2;
+  const int qg = int(r_ % uint32_t(p.qgroups));   r_ /= uint32_t(p.qgroups);
+  const int chunk = int(r_ % uint32_t(p.chunks)); r_ /= uint32_t(p.chunks);
+  const int band = int(r_ % uint32_t(p.bands));
+  const int n = int(r_ / uint32_t(p.bands));
+  const int cp = (chunk << p.chunk_log2) + int(t & cmask);
+  const int p0 = band * p.band_rows;
+  const int rows = min(p.band_rows, p.P - p0);
+  const int q0 = qg * QT;
+  const int n_valid = min(QT, p.Q - q0);
+
+  uint32_t wt[K * K];
+#pragma unroll
+  for (int k = 0; k < K * K; ++k) wt[k] = __ldg(p.w + int64_t(k) * p.cpairs + cp);
+  float b0 = 0.f, b1 = 0.f;
+  if constexpr (EPI) {
+    if (p.bias != nullptr) unpack2<E>(__ldg(p.bias + cp), b0, b1);
+  }
+  // Input column of output column m, tap s: S*(q0 + m) - pad_w + D*s.
+  int col0[QT];
+#pragma unroll
+  for (int m = 0; m < QT; ++m) col0[m] = S * (q0 + m) - p.pad_w;
+  const uint32_t* xn = p.x + int64_t(n) * p.H * p.W * p.cpairs + cp;
+  const int64_t y_row = int64_t(p.Q) * p.cpairs;
+  const int64_t y_off = (int64_t(n) * p.P + p0) * y_row + int64_t(q0) * p.cpairs + cp;
+
+  for (int o = 0; o < rows; ++o) {
+    float acc[QT][2];
+#pragma unroll
+    for (int m = 0; m < QT; ++m) { acc[m][0] = 0.f; acc[m][1] = 0.f; }
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+      const int h = S * (p0 + o) + D * r - p.pad;
+      if (unsigned(h) >= unsigned(p.H)) continue;  // a row of zero products
+      const uint32_t* xr = xn + int64_t(h) * p.W * p.cpairs;
+#pragma unroll
+      for (int s = 0; s < K; ++s) {
+#pragma unroll
+        for (int m = 0; m < QT; ++m) {
+          const int col = col0[m] + D * s;
+          const uint32_t v = unsigned(col) < unsigned(p.W) ? __ldg(xr + int64_t(col) * p.cpairs) : 0u;
+          fma2<E>(v, wt[r * K + s], acc[m][0], acc[m][1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < QT; ++m) {
+      if (m >= n_valid) continue;
+      float a0 = acc[m][0], a1 = acc[m][1];
+      const int64_t off = y_off + int64_t(o) * y_row + int64_t(m) * p.cpairs;
+      if constexpr (EPI) {
+        if (p.bias != nullptr) { a0 += b0; a1 += b1; }
+        a0 = apply_act(a0, p.act);
+        a1 = apply_act(a1, p.act);
+        if (p.residual != nullptr) {
+          float r0, r1;
+          unpack2<E>(__ldg(p.residual + off), r0, r1);
+          a0 += r0;
+          a1 += r1;
+        }
+      }
+      p.y[off] = pack2_rn<E>(a0, a1);
+    }
+  }
+}
+
+// ============================================================================
 // Plain weight gradient (K = 3, 5, 7, stride 1 or 2) for the same small
 // shapes:  dw[r,s,c] = sum_{n,p,q} x[n, S*p+r-pad, S*q+s-pad, c] * dy[n,p,q,c].
 //

@@ -21,7 +21,8 @@ an ``nn.Conv2d(groups=C)`` stand-in for channels-last models.
   column at the bottom / right), run by the kernels' per-side padding in
   inference and as explicit zero padding when a gradient is needed.
 * ``convert_depthwise_convs(model)`` — swaps every eligible ``nn.Conv2d``
-  (depthwise, dilation 1, symmetric integer padding or ``padding='same'``, zeros padding mode,
+  (depthwise, dilation 1 — any dilation with ``forward_only=True`` —, symmetric
+  integer padding or ``padding='same'``, zeros padding mode,
   C % 8 == 0; 3x3 / 5x5 / 7x7 at stride 1 or 2) for a ``DepthwiseConv2d``
   sharing its parameters.
 * ``fuse_depthwise_bn_act(model)`` — for inference: a depthwise convolution
@@ -311,20 +312,23 @@ class DepthwiseConv2d(nn.Module):
 
     def __init__(self, channels: int, kernel_size: int = 3, stride: int = 1,
                  padding=None, bias: bool = True, device=None,
-                 dtype=torch.float16, activation: str = "none"):
+                 dtype=torch.float16, activation: str = "none", dilation: int = 1):
         super().__init__()
         if (kernel_size, stride) not in GEOMETRIES:
             raise ValueError(f"kernel_size must be 3, 5 or 7 and stride 1 or 2, got "
                              f"{kernel_size}, {stride}")
         if activation not in _TORCH_ACTS:
             raise ValueError(f"activation must be one of {sorted(_TORCH_ACTS)}, got {activation!r}")
+        if int(dilation) < 1:
+            raise ValueError(f"dilation must be >= 1, got {dilation}")
         self.activation = activation
+        self.dilation = int(dilation)  # > 1: inference only (no gradient kernels)
         self.channels = channels
         self.kernel_size = int(kernel_size)
         self.stride = int(stride)
         # an int (the same on every side), or "same": TensorFlow's / PyTorch's
         # "same" padding, ceil(H / stride) output rows, computed per input
-        self.padding = (kernel_size // 2 if padding is None else
+        self.padding = (self.dilation * (kernel_size - 1) // 2 if padding is None else
                         "same" if padding == "same" else int(padding))
         self.weight = nn.Parameter(torch.empty(channels, 1, kernel_size, kernel_size,
                                                device=device, dtype=dtype))
@@ -342,6 +346,7 @@ class DepthwiseConv2d(nn.Module):
         m.kernel_size = int(conv.kernel_size[0])
         m.stride = int(conv.stride[0])
         m.padding = _conv2d_pad(conv)
+        m.dilation = int(conv.dilation[0])
         m.weight = conv.weight
         m.bias = conv.bias
         m.activation = "none"
@@ -353,9 +358,15 @@ class DepthwiseConv2d(nn.Module):
         needs_grad = torch.is_grad_enabled() and (
             x.requires_grad or self.weight.requires_grad
             or (self.bias is not None and self.bias.requires_grad))
+        dil = getattr(self, "dilation", 1)
+        if dil > 1 and needs_grad:
+            raise RuntimeError("DepthwiseConv2d: gradients of dilated depthwise convolutions are "
+                               "not implemented; run it without gradients (inference), e.g. "
+                               "under torch.no_grad()")
         pad, pads = self.padding, None
         if pad == "same":
-            pads = _T.same_padding(x.shape[2], x.shape[3], self.kernel_size, self.stride)
+            pads = _T.same_padding(x.shape[2], x.shape[3], dil * (self.kernel_size - 1) + 1,
+                                   self.stride)
             if pads[0] == pads[1] == pads[2] == pads[3]:
                 pad, pads = pads[0], None
             elif needs_grad:
@@ -377,8 +388,9 @@ class DepthwiseConv2d(nn.Module):
             # without the custom op's dispatch; the activation runs in the
             # kernel's fused epilogue
             b = None if b is None else b.contiguous()
-            if pads is not None:  # "same" with more padding at the bottom / right
-                y = _C.dwconv_k_asym(x_nhwc, w_rsc.contiguous(), b, None, self.stride, *pads,
+            if pads is not None or dil > 1:  # per-side padding or dilated taps
+                pads = pads if pads is not None else (pad,) * 4
+                y = _C.dwconv_k_pads(x_nhwc, w_rsc.contiguous(), b, None, self.stride, dil, *pads,
                                      _T.ACTIVATIONS[act], 0)
             else:
                 y = _C.dwconv_k(x_nhwc, w_rsc.contiguous(), b, None, self.stride, pad,
@@ -391,8 +403,10 @@ class DepthwiseConv2d(nn.Module):
 
     def extra_repr(self) -> str:
         act = "" if self.activation == "none" else f", activation={self.activation}"
+        dil = getattr(self, "dilation", 1)
+        dil = "" if dil == 1 else f", dilation={dil}"
         return (f"{self.channels}, kernel_size={self.kernel_size}, stride={self.stride}, "
-                f"padding={self.padding}, bias={self.bias is not None}{act}")
+                f"padding={self.padding}{dil}, bias={self.bias is not None}{act}")
 
 
 class DepthwiseConv3x3(DepthwiseConv2d):
@@ -408,7 +422,7 @@ def _conv2d_pad(conv: nn.Conv2d) -> int:
     padding, or K // 2 for ``padding='same'`` (PyTorch allows it at stride 1
     only, where an odd K pads K // 2 on every side)."""
     if conv.padding == "same":
-        return int(conv.kernel_size[0]) // 2
+        return int(conv.dilation[0]) * (int(conv.kernel_size[0]) - 1) // 2
     return int(conv.padding[0])
 
 
@@ -430,7 +444,8 @@ def _plain_conv2d(m: nn.Module) -> bool:
 
 
 def _eligible(m: nn.Module, forward_only: bool) -> bool:
-    if not (_plain_conv2d(m) and m.dilation == (1, 1)
+    if not (_plain_conv2d(m) and m.dilation[0] == m.dilation[1]
+            and (m.dilation[0] == 1 or forward_only)  # dilated: no gradient kernels
             and m.groups == m.in_channels == m.out_channels and m.in_channels % 8 == 0
             and m.padding_mode == "zeros"
             and ((isinstance(m.padding, tuple) and m.padding[0] == m.padding[1])
@@ -445,8 +460,9 @@ def convert_depthwise_convs(model: nn.Module, forward_only: bool = False) -> int
     """Replace eligible depthwise ``nn.Conv2d`` children in place; returns the count.
 
     Every geometry the kernels implement (3x3 / 5x5 / 7x7, stride 1 or 2) has
-    a backward, so ``forward_only`` no longer changes what is converted; it is
-    kept so existing callers keep working.
+    a backward.  ``forward_only=True`` also converts dilated depthwise convs
+    (atrous layers, e.g. DeepLab backbones), which run in inference only:
+    their modules raise if called with a gradient.
     """
     count = 0
     for name, child in list(model.named_children()):
@@ -476,8 +492,9 @@ def _fold_bn(conv: nn.Module, bn: nn.BatchNorm2d, activation: str) -> DepthwiseC
     k = conv.kernel_size[0] if isinstance(conv.kernel_size, tuple) else conv.kernel_size
     stride = conv.stride[0] if isinstance(conv.stride, tuple) else conv.stride
     pad = conv.padding if isinstance(conv, DepthwiseConv2d) else _conv2d_pad(conv)
+    d = conv.dilation[0] if isinstance(conv.dilation, tuple) else getattr(conv, "dilation", 1)
     m = DepthwiseConv2d(c, int(k), int(stride), pad, bias=True, device=w.device,
-                        dtype=conv.weight.dtype, activation=activation)
+                        dtype=conv.weight.dtype, activation=activation, dilation=int(d))
     with torch.no_grad():
         m.weight.copy_(w * g[:, None, None, None])
         m.bias.copy_((b - bn.running_mean.detach().float()) * g + beta)

@@ -226,7 +226,8 @@ def same_padding(H: int, W: int, K: int, stride: int = 1) -> tuple[int, int, int
 
 def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | tuple | None = None, stride: int = 1,
            bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-           activation: str = "none", n_stage: int | None = None) -> torch.Tensor:
+           activation: str = "none", n_stage: int | None = None,
+           dilation: int = 1) -> torch.Tensor:
     """K x K depthwise forward, K in {3, 5, 7}, stride 1 or 2 (beyond the reference surface).
 
     ``y[n,p,q,c] = round(epilogue(sum_{r,s} x[n, stride*p+r-pad, stride*q+s-pad, c] * w[r,s,c]))``,
@@ -242,7 +243,10 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | tuple | None = None, str
     ``pad`` may also be a tuple (top, bottom, left, right) of per-side zero
     padding (e.g. ``same_padding(H, W, K, stride)``, TensorFlow's "SAME"):
     the top / left sides shift the taps, P = (H + top + bottom - K) // stride
-    + 1 and Q likewise.
+    + 1 and Q likewise.  ``dilation`` D > 1 spaces the taps D apart (tap (r,
+    s) reads x[n, stride*p + D*r - top, stride*q + D*s - left, c]; K becomes
+    D*(K-1) + 1 in the output size), on a kernel that computes each output's
+    taps directly (``n_stage`` is then ignored); same chain and rounding.
 
     Args:
         x: [N, H, W, C] fp16 or bf16 CUDA, contiguous, C % 8 == 0.   w: [K, K, C], x's dtype.
@@ -270,8 +274,11 @@ def dwconv(x: torch.Tensor, w: torch.Tensor, pad: int | tuple | None = None, str
     if activation not in ACTIVATIONS:
         raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}, got {activation!r}")
     ns = 0 if n_stage is None else int(n_stage)
-    if pads is not None and not (pads[0] == pads[1] == pads[2] == pads[3]):
-        return _C.dwconv_k_asym(x, w, bias, residual, int(stride), *pads,
+    if int(dilation) < 1:
+        raise ValueError(f"dilation must be >= 1, got {dilation}")
+    if int(dilation) > 1 or (pads is not None and not (pads[0] == pads[1] == pads[2] == pads[3])):
+        pads = pads if pads is not None else (int(pad),) * 4
+        return _C.dwconv_k_pads(x, w, bias, residual, int(stride), int(dilation), *pads,
                                 ACTIVATIONS[activation], ns)
     return _C.dwconv_k(x, w, bias, residual, int(stride), int(pad), ACTIVATIONS[activation], ns)
 
