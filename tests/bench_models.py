@@ -4,6 +4,7 @@
     python tests/bench_models.py --layers [--batch 64]
     python tests/bench_models.py --layers-bwd [--batch 64]
     python tests/bench_models.py --train [--batch 64]
+    python tests/bench_models.py --seg [--batch 8] [--size 512]
 
 torchvision MobileNetV2, MobileNetV3-Large and EfficientNet-B0 (random
 weights, random BatchNorm statistics), fp16, channels-last, eval mode.  Per
@@ -31,7 +32,10 @@ depths, and the plain weight gradient.  ``--train`` times a training step
 against ``convert_depthwise_convs``, eager (use a batch of 128 or more so the
 GPU, not the host's launches, sets the time).  Both fp16 models' losses
 and depthwise weight gradients are compared with an fp32 copy of the model
-(relative L2 distance per layer: largest and median).
+(relative L2 distance per layer: largest and median).  ``--seg`` times
+torchvision's DeepLabV3-MobileNetV3-Large (dilated depthwise layers in its
+last stages) stock against ``fuse_depthwise_bn_act`` (CUDA graphs), and each
+of its dilated depthwise layers alone against cuDNN.
 A script, not a test.
 """
 from __future__ import annotations
@@ -242,6 +246,57 @@ def bench_train(batch: int, size: int, iters: int) -> None:
         print(json.dumps(row), flush=True)
 
 
+def bench_seg(batch: int, size: int, iters: int) -> None:
+    import tma_dwconv as T
+    from torchvision.models import segmentation as seg
+    torch.manual_seed(0)
+    base = seg.deeplabv3_mobilenet_v3_large(weights=None, weights_backbone=None,
+                                            num_classes=21, aux_loss=False)
+    randomize_bn(base, 1)
+    base = base.eval().cuda().half().to(memory_format=torch.channels_last)
+    layers = []
+    for m in base.modules():
+        if isinstance(m, torch.nn.Conv2d) and m.groups == m.in_channels > 1 and m.dilation[0] > 1:
+            m.register_forward_hook(lambda mod, inp, out: layers.append(
+                (tuple(inp[0].shape), mod.kernel_size[0], mod.stride[0], mod.dilation[0],
+                 mod.padding[0])))
+    x = torch.randn(batch, 3, size, size, device="cuda").half()
+    x = x.to(memory_format=torch.channels_last)
+    with torch.no_grad():
+        ref = base(x)["out"].float()
+        for m in base.modules():
+            m._forward_hooks.clear()
+        fused = copy.deepcopy(base)
+        n_fused = tdc_torch.fuse_depthwise_bn_act(fused)
+        row = {"model": "deeplabv3_mobilenet_v3_large", "batch": batch, "size": size,
+               "blocks_fused": n_fused,
+               "max_logit_diff": round((fused(x)["out"].float() - ref).abs().max().item(), 4),
+               "logit_scale": round(ref.abs().max().item(), 3)}
+        for name, m in (("cudnn", base), ("fused", fused)):
+            row[f"{name}_ms"] = round(bench_ms(graphed(lambda inp, m=m: m(inp)["out"], x),
+                                               iters=iters), 3)
+        row["speedup"] = round(row["cudnn_ms"] / row["fused_ms"], 3)
+        print(json.dumps(row), flush=True)
+        reps = 20
+        for (n, c, h, w), k, s, d, pad in dict.fromkeys(layers):
+            g = torch.Generator(device="cuda").manual_seed(0)
+            xl = torch.randn(n, h, w, c, device="cuda", generator=g).half()
+            wt = (torch.randn(k, k, c, device="cuda", generator=g) / k).half()
+            w_conv = wt.permute(2, 0, 1).unsqueeze(1).contiguous()
+            xn = xl.permute(0, 3, 1, 2)
+            cud = graph_of(lambda: torch.nn.functional.conv2d(xn, w_conv, None, s, pad, d, c), reps)
+            ours = graph_of(lambda: T.dwconv(xl, wt, pad, stride=s, dilation=d), reps)
+            t_c = bench_ms(cud, iters=iters) / reps * 1e3
+            t_o = bench_ms(ours, iters=iters) / reps * 1e3
+            p = (h + 2 * pad - d * (k - 1) - 1) // s + 1
+            q = (w + 2 * pad - d * (k - 1) - 1) // s + 1
+            nbytes = 2 * n * c * (h * w + p * q)
+            print(json.dumps({"N": n, "H": h, "W": w, "C": c, "K": k, "stride": s, "dilation": d,
+                              "cudnn_us": round(t_c, 2), "ours_us": round(t_o, 2),
+                              "ours_GBps": round(nbytes / t_o / 1e3, 1),
+                              "speedup": round(t_c / t_o, 3)}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=64)
@@ -251,7 +306,12 @@ def main() -> None:
     ap.add_argument("--layers", action="store_true", help="time each depthwise layer alone")
     ap.add_argument("--layers-bwd", action="store_true", help="time each layer's gradients")
     ap.add_argument("--train", action="store_true", help="time a training step per model")
+    ap.add_argument("--seg", action="store_true", help="DeepLabV3-MobileNetV3 (dilated layers)")
     args = ap.parse_args()
+    if args.seg:
+        bench_seg(8 if args.batch == 64 else args.batch, 512 if args.size == 224 else args.size,
+                  args.iters)
+        return
     if args.train:
         bench_train(args.batch, args.size, args.iters)
         return

@@ -676,8 +676,10 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   const int64_t Ke = D * (K - 1) + 1;  // the dilated kernel's extent
   if (H + pd.top + pd.bottom < Ke || W + pd.left + pd.right < Ke) return TDC_ERR_BAD_SHAPE;
   const int64_t P = (H + pd.top + pd.bottom - Ke) / S + 1, Q = (W + pd.left + pd.right - Ke) / S + 1;
-  // 32-bit row / column arithmetic in the kernel (S * p + D * r - pad)
+  // 32-bit row / column arithmetic in the kernel (S * p + D * r - pad) and
+  // 32-bit column offsets in pairs
   if (S * P + D * K + pd.top > i32 || S * Q + D * K + pd.left > i32) return TDC_ERR_TOO_LARGE;
+  if ((S * Q + D * K + pd.left) * (C / 2) > i32) return TDC_ERR_TOO_LARGE;
   if (N == 0 || C == 0) return TDC_OK;
   if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
@@ -690,9 +692,13 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   const int chunk_log2 = cpairs % 8 == 0 ? 3 : 2;
   const int64_t qgroups = (Q + tdc::kDilatedCols - 1) / tdc::kDilatedCols;
   if (N * qgroups > i32 || N * qgroups * cpairs > i32) return TDC_ERR_TOO_LARGE;
+  // Rows per thread: with no sliding window a row shares nothing with the
+  // next but the K*K weights, so bands are cut down to about 8192 threads
+  // per SM (four waves at 64-128 registers); at 384 per SM, 8 x 32 x 32 x 672
+  // 5x5 dilation 2 ran 82 us.
   const int64_t per_band = std::max<int64_t>(1, N * qgroups * cpairs);
   const int64_t bands0 = std::min<int64_t>(
-      P, std::max<int64_t>(1, (384 * std::max<int64_t>(1, dev->sms) + per_band - 1) / per_band));
+      P, std::max<int64_t>(1, (8192 * std::max<int64_t>(1, dev->sms) + per_band - 1) / per_band));
   const int64_t rows = (P + bands0 - 1) / bands0;
   const int64_t bands = (P + rows - 1) / rows;
   const int64_t total = N * qgroups * cpairs * bands;
