@@ -679,7 +679,7 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   // 32-bit row / column arithmetic in the kernel (S * p + D * r - pad) and
   // 32-bit column offsets in pairs
   if (S * P + D * K + pd.top > i32 || S * Q + D * K + pd.left > i32) return TDC_ERR_TOO_LARGE;
-  if ((S * Q + D * K + pd.left) * (C / 2) > i32) return TDC_ERR_TOO_LARGE;
+  if (W * (C / 2) > i32) return TDC_ERR_TOO_LARGE;  // column offsets of loaded taps
   if (N == 0 || C == 0) return TDC_OK;
   if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||

@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_dilated_kernel(PlainPara
     if (p.bias != nullptr) unpack2<E>(__ldg(p.bias + cp), b0, b1);
   }
   // Input column of output column m, tap s: S*(q0 + m) - pad_w + D*s; its
-  // offset in pairs (32-bit: the host checks the range) and whether it lies
+  // offset in pairs (32-bit: the host checks W * C / 2 < 2^31) and whether it lies
   // inside the image, computed once (the per-load arithmetic was ~15
   // instructions a tap before).
   static_assert(K * QT <= 32, "column mask");
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_dilated_kernel(PlainPara
 #pragma unroll
     for (int m = 0; m < QT; ++m) {
       const int col = S * (q0 + m) - p.pad_w + D * s;
-      coff[s][m] = col * p.cpairs;
+      coff[s][m] = int32_t(int64_t(col) * p.cpairs);  // used only when 0 <= col < W
       colmask |= (unsigned(col) < unsigned(p.W) ? 1u : 0u) << (s * QT + m);
     }
   }
