@@ -254,6 +254,33 @@ def dwconv_k_f16_numpy(x: np.ndarray, w: np.ndarray, pad: int, stride: int = 1) 
     return acc.astype(np.float16)
 
 
+def dwconv_dilated_f16_numpy(x: np.ndarray, w: np.ndarray, pads, stride: int = 1,
+                             dilation: int = 1) -> np.ndarray:
+    """numpy restatement of the dilated forward with per-side padding (small
+    sizes), written directly rather than through a zero-inflated kernel:
+    y[n,p,q,c] = fp16_rne(chain_{r,s} x[n, S*p + D*r - top, S*q + D*s - left, c]
+    * w[r,s,c]) from +0 in (r, s) order, products exact in float32, with
+    pads = (top, bottom, left, right) and P = (H + top + bottom - D*(K-1) - 1)
+    // S + 1 (the formula of tdc_dwconv_fwd_dilated)."""
+    x = np.asarray(x, dtype=np.float16)
+    w = np.asarray(w, dtype=np.float16)
+    N, H, W, C = x.shape
+    K = w.shape[0]
+    top, bottom, left, right = (int(v) for v in pads)
+    S, D = int(stride), int(dilation)
+    Ke = D * (K - 1) + 1
+    P = (H + top + bottom - Ke) // S + 1
+    Q = (W + left + right - Ke) // S + 1
+    xp = np.zeros((N, H + top + bottom + S, W + left + right + S, C), dtype=np.float32)
+    xp[:, top:top + H, left:left + W, :] = x.astype(np.float32)
+    wf = w.astype(np.float32)
+    acc = np.zeros((N, P, Q, C), dtype=np.float32)
+    for r in range(K):
+        for s in range(K):
+            acc = acc + xp[:, D * r:D * r + S * P:S, D * s:D * s + S * Q:S, :] * wf[r, s]
+    return acc.astype(np.float16)
+
+
 def dwconv_ex_f16_numpy(x, w, pad, bias=None, residual=None, activation="none"):
     """numpy restatement of the general forward (small sizes)."""
     N, H, W, C = x.shape

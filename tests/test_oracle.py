@@ -200,3 +200,34 @@ def test_weight_gradient_f64_matches_autograd(K, stride):
     y.backward(torch.from_numpy(dy.astype(np.float64)).permute(0, 3, 1, 2))
     dw = oracle.dwconv_bwd_weight_f64(x, dy, pad, K, stride=stride)
     np.testing.assert_allclose(dw, wt.grad[:, 0].permute(1, 2, 0).numpy(), atol=1e-9)
+
+
+@pytest.mark.parametrize("K", [3, 5, 7])
+@pytest.mark.parametrize("S", [1, 2])
+@pytest.mark.parametrize("D", [1, 2, 3])
+def test_dilation_and_side_pads_equal_the_inflated_kernel(K, S, D):
+    """The GPU tests hold per-side padding and dilation to the C oracle run
+    at pad 0 on the input padded by hand with the K x K taps spread over a
+    D*(K-1)+1 kernel of zeros.  Here that construction is checked, bit for
+    bit, against a direct restatement of the dilated, per-side-padded chain
+    (oracle.dwconv_dilated_f16_numpy), so the zeros it adds are shown to
+    change nothing."""
+    rng = np.random.default_rng(K * 100 + S * 10 + D)
+    Ke = D * (K - 1) + 1
+    for (N, H, W, C) in [(2, 13, 17, 16), (1, 9, 22, 8)]:
+        x = rng.standard_normal((N, H, W, C)).astype(np.float16)
+        w = (rng.standard_normal((K, K, C)) / K).astype(np.float16)
+        for pads in [(Ke // 2,) * 4, (0, 1, 0, 1), (2, 0, 1, 3)]:
+            t, b, l, r = pads
+            if H + t + b < Ke or W + l + r < Ke:
+                continue
+            direct = oracle.dwconv_dilated_f16_numpy(x, w, pads, S, D)
+            wd = np.zeros((Ke, Ke, C), dtype=np.float16)
+            wd[::D, ::D] = w
+            xp = np.pad(x, ((0, 0), (t, b), (l, r), (0, 0)))
+            inflated = oracle.dwconv_k_f16(xp, wd, 0, S)
+            assert direct.shape == inflated.shape
+            assert np.array_equal(direct.view(np.uint16), inflated.view(np.uint16)), pads
+            if D == 1 and t == b == l == r:
+                assert np.array_equal(direct.view(np.uint16),
+                                      oracle.dwconv_k_f16_numpy(x, w, t, S).view(np.uint16))
