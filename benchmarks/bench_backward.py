@@ -1,6 +1,6 @@
 """Backward of the depthwise K x K (stride 1 or 2) vs cuDNN, on one GPU.
 
-    python tests/bench_backward.py [--images 64] [--K 3] [--stride 1] [--n-stage 2]
+    python benchmarks/bench_backward.py [--images 64] [--K 3] [--stride 1] [--n-stage 2]
                                    [--wgrad-n-stage S] [--dtype fp16|bf16]
 
 Headline shape (N x 224 x 336 x 256 fp16 input, pad K // 2; dy is

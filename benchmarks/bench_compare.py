@@ -2,13 +2,13 @@
 and cuDNN, on the reference benchmark's shapes (tests/bench.py:32-39 of
 haowen-han/tma-depthwise-conv), on one GPU.
 
-    python tests/bench_compare.py [--out table.md]
+    python benchmarks/bench_compare.py [--out table.md]
 
 Method as the reference's tests/bench.py:18-29 (CUDA events around 100
 back-to-back calls after 10 warm-up calls), with seeded inputs
 (x ~ randn, w ~ randn*0.1, pad 1).  cuDNN is timed on a pre-permuted NCHW copy
 (the reference's method) and on the channels-last view of the NHWC input.
-The reference's kernels come from oracle/_ref (built by oracle/build_ref.py);
+The reference's kernels come from baseline/_ref (built by oracle/build_ref.py);
 if that build is absent their columns are left empty.  A script, not a test:
 it is the comparison table the reference's benchmark produces, without the
 plot.
@@ -41,7 +41,7 @@ SHAPES = [
 
 
 def load_reference():
-    paths = glob.glob(os.path.join(REPO, "oracle", "_ref", "_tma_dwconv_ref_C*.so"))
+    paths = glob.glob(os.path.join(REPO, "baseline", "_ref", "_tma_dwconv_ref_C*.so"))
     if not paths:
         return None
     spec = importlib.util.spec_from_file_location("_tma_dwconv_ref_C", paths[0])

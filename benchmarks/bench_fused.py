@@ -1,6 +1,6 @@
 """Fused epilogue vs the same work as separate passes, on one GPU.
 
-    python tests/bench_fused.py [--images 64]
+    python benchmarks/bench_fused.py [--images 64]
 
 Headline shape (N x 224 x 336 x 256, pad 1, n_stage 2).  Times per call
 (CUDA events, 10 warm-up + 50 calls) of:

@@ -1,6 +1,6 @@
 """K x K taps and stride 2 (`tma_dwconv.dwconv`) vs cuDNN, on one GPU.
 
-    python tests/bench_kxk.py [--images 64] [--n-stage N] [--only K,S] [--iters 20] [--no-cudnn]
+    python benchmarks/bench_kxk.py [--images 64] [--n-stage N] [--only K,S] [--iters 20] [--no-cudnn]
                               [--dtype fp16|bf16]
 
 Input of the headline shape (N x 224 x 336 x 256 fp16), pad K // 2, for K in

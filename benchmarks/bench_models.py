@@ -1,10 +1,10 @@
 """Whole-model inference with the depthwise layers on these kernels, on one GPU.
 
-    python tests/bench_models.py [--batch 64] [--size 224] [--iters 20] [--graphs]
-    python tests/bench_models.py --layers [--batch 64]
-    python tests/bench_models.py --layers-bwd [--batch 64]
-    python tests/bench_models.py --train [--batch 64]
-    python tests/bench_models.py --seg [--batch 8] [--size 512]
+    python benchmarks/bench_models.py [--batch 64] [--size 224] [--iters 20] [--graphs]
+    python benchmarks/bench_models.py --layers [--batch 64]
+    python benchmarks/bench_models.py --layers-bwd [--batch 64]
+    python benchmarks/bench_models.py --train [--batch 64]
+    python benchmarks/bench_models.py --seg [--batch 8] [--size 512]
 
 torchvision MobileNetV2, MobileNetV3-Large and EfficientNet-B0 (random
 weights, random BatchNorm statistics), fp16, channels-last, eval mode.  Per

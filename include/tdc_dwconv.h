@@ -53,7 +53,7 @@ extern "C" {
 #define TDC_ERR_TOO_LARGE        -8  /* a dimension exceeds what the TMA descriptor encodes  */
 #define TDC_ERR_CUDA             -9  /* a CUDA runtime call failed (see tdc_last_cuda_error) */
 #define TDC_ERR_TMA_ENCODE      -10  /* cuTensorMapEncodeTiled rejected the descriptor       */
-#define TDC_ERR_DEVICE_TIMEOUT  -11  /* a kernel gave up waiting on a pipeline barrier       */
+#define TDC_ERR_DEVICE_TIMEOUT  -11  /* an earlier launch gave up waiting on its pipeline  */
 #define TDC_ERR_NO_DEVICE       -12  /* no usable sm_100 device is current                   */
 #define TDC_ERR_ACT             -13  /* unknown activation code (tdc_dwconv3x3_fwd)          */
 #define TDC_ERR_WORKSPACE       -14  /* workspace too small (tdc_dwconv3x3_bwd_weight)       */
@@ -261,7 +261,7 @@ TDC_API int tdc_dwconv_bwd_weight_uses_plain(int64_t N, int64_t H, int64_t W, in
                                              int64_t K, int64_t stride, int64_t pad);
 
 /* Launch plan tdc_dwconv_fwd would use (same layout as tdc_ws_plan's
- * plan[0..7]; pure host arithmetic).  For K >= 5 at stride 1 and 7x7 at
+ * plan[0..8]; pure host arithmetic).  For K >= 5 at stride 1 and 7x7 at
  * stride 2 the kernel holds the K input rows of one output row at once, and
  * stage_rows satisfies (n_stage - 1) * stage_rows >= K - 1.  The strip is
  * stride*31 + K input columns wide.  No counterpart in the reference. */
@@ -308,6 +308,8 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw,
  *   - Every GPU that loads the library holds the 16 MiB until the process exits.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     A lookup that fails returns TDC_ERR_CUDA and is tried again by the
+ *     next call; a successful one is kept for the process.
  *   - All calls on a device share the array and it keeps the last call's
  *     contents (each call clears the part it uses); calls that overlap on the
  *     GPU, e.g. on two streams, race and give wrong results.
@@ -419,12 +421,17 @@ TDC_API int tdc_ws_occupancy(int64_t n_stage, int64_t kind, int64_t* ctas_per_sm
 
 /* Launch plan the ws kernel would use on a device with `sms` SMs and
  * `ctas_per_sm` resident CTAs (pure host arithmetic, no CUDA call):
- * plan[0..7] = {stage_rows, qstrips, cblocks, strips, full_units,
- * tail_band_rows, grid, dynamic smem bytes}: strips below full_units are
- * dealt whole, round-robin; the rest are cut into bands of tail_band_rows
- * rows (the last band may be shorter) and dealt the same way, band-major.  No counterpart in the reference (whose grid is fixed
- * at (ceil(P/8), C/64, N), csrc/kernel_tma_ws.cu:25-31); exposed so the
- * planner can be checked without a GPU. */
+ * plan[0..8] = {stage_rows, qstrips, cblocks, strips, full_units,
+ * tail_band_rows, grid, dynamic smem bytes, tail_chunk_rows}: strips below
+ * full_units are dealt whole, round-robin.  With tail_chunk_rows = 0 the rest
+ * are cut into bands of tail_band_rows rows (the last band may be shorter)
+ * and dealt the same way, band-major.  With tail_chunk_rows = L > 0 the rest
+ * form (strips - full_units) / cblocks pixel strips whose rows, one pixel
+ * strip after the other, are cut into chunks of L rows: CTA g takes channel
+ * block g % cblocks of chunk g / cblocks (grid is then a multiple of
+ * cblocks).  `plan` holds 9 values.  No counterpart in the reference (whose
+ * grid is fixed at (ceil(P/8), C/64, N), csrc/kernel_tma_ws.cu:25-31);
+ * exposed so the planner can be checked without a GPU. */
 TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
                         int64_t n_stage, int64_t sms, int64_t ctas_per_sm, int64_t* plan);
 
@@ -447,7 +454,19 @@ TDC_API int tdc_dwconv_ws_probe(const void* x, const void* w, void* y,
  * Every mbarrier wait in the ws kernels is bounded.  A wait that exceeds the
  * limit records a TDC_DEVICE_* code in a per-device status word, tells the
  * other warps of its CTA to stop, waits (bounded) for the CTA's own TMA copies
- * still in flight, and returns.  The CUDA context stays usable. */
+ * still in flight, and returns.  The CUDA context stays usable, but that
+ * launch's output is incomplete.
+ *
+ * The first such failure on a device is also written through to pinned host
+ * memory that the GPU maps (one page for the process, created by the first
+ * call that launches a pipelined kernel; tdc_dwconv3x3_bwd_weight_noalloc
+ * never creates it).  Every later entry point that launches work reads it
+ * on entry, without synchronising, and returns TDC_ERR_DEVICE_TIMEOUT before
+ * launching anything while a failure is recorded, until tdc_device_status
+ * (clear != 0) resets it.  It sees the failures of launches that have
+ * finished by the time of the call; a failure of a launch still running is
+ * reported by the first call after it finishes.  (The reference spins on its
+ * barriers without a bound, csrc/kernel_tma_ws.cuh:167,199.) */
 #define TDC_DEVICE_OK               0
 #define TDC_DEVICE_FULL_TIMEOUT     1  /* consumer waited too long for a filled stage */
 #define TDC_DEVICE_EMPTY_TIMEOUT    2  /* producer waited too long for a free stage   */
@@ -456,9 +475,11 @@ TDC_API int tdc_dwconv_ws_probe(const void* x, const void* w, void* y,
 /* Wait limit used by subsequent launches from this process (default 2 s). */
 TDC_API int tdc_set_wait_timeout_ns(int64_t ns);
 
-/* Reads (and if clear != 0, resets) the status word of the CURRENT device.
- * Synchronises the device.  info[0..3] (may be NULL) receives
- * {code, block, stage, load index} of the first failure recorded. */
+/* Reads (and if clear != 0, resets) the status word of the CURRENT device
+ * and its host copy.  Synchronises the device.  info[0..3] (may be NULL)
+ * receives {code, block, stage, load index} of the first failure recorded;
+ * returns TDC_ERR_DEVICE_TIMEOUT when there is one (with clear != 0, later
+ * calls run again). */
 TDC_API int tdc_device_status(int clear, int64_t* info);
 
 /* ws launch in which the producer withholds load number `withhold_load`

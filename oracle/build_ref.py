@@ -17,22 +17,35 @@ is not recorded.  The CUTLASS 4.5.0 header tree shipped inside the installed
 flashinfer wheel is used instead; the reference uses CuTe only for the TMA
 descriptor and mbarrier wrappers, not for arithmetic.
 
-Usage:  python3 oracle/build_ref.py [--reference DIR] [--cutlass DIR] [-j N]
-Writes only into oracle/_ref/.  Runs in this container (nvcc cross-compiles
-for sm_100a); the result is loaded by the GPU tests on a B200.
+Besides the extension it stages, unchanged, the reference's own test files
+``tests/test_dwconv.py``, ``tests/test_ws_time.py`` and ``tests/__init__.py``
+into ``oracle/_ref/tests/`` (git-ignored, like the extension), so that a GPU
+test can run them against this repository's ``tma_dwconv`` on a machine that
+has no reference checkout; and it copies the built extension to
+``baseline/_ref/``, where ``bench.py`` loads it to time the reference's own ws
+kernel beside this repository's (the same binary; ``oracle/_ref`` serves the
+parity tests).
+
+Usage:  TDC_REFERENCE_DIR=<reference checkout> python3 oracle/build_ref.py [--cutlass DIR] [-j N]
+        (or --reference DIR).  Without either, nothing is built.
+Writes only into oracle/_ref/ and baseline/_ref/.  nvcc cross-compiles for
+sm_100a, so no GPU is needed; the result is loaded by the GPU tests on a B200.
 """
 from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
 import os
+import shutil
 import subprocess
 import sys
 import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
+BASELINE_OUT = os.path.join(os.path.dirname(HERE), "baseline", "_ref")
 MODULE = "_tma_dwconv_ref_C"
+REF_TESTS = ["tests/__init__.py", "tests/test_dwconv.py", "tests/test_ws_time.py"]
 
 
 def _default_cutlass() -> str | None:
@@ -49,15 +62,20 @@ def _default_cutlass() -> str | None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TDC_REFERENCE_DIR"))
     ap.add_argument("--cutlass", default=os.environ.get("CUTLASS_DIR") or _default_cutlass())
     ap.add_argument("-j", type=int, default=3)
     args = ap.parse_args()
     ref = args.reference
+    if not ref:
+        print("no reference checkout given (TDC_REFERENCE_DIR or --reference); nothing built",
+              file=sys.stderr)
+        return 0
     srcs = ["csrc/bindings.cpp", "csrc/kernel_v0_naive_float4.cu", "csrc/kernel_tma_ws.cu"]
     if not all(os.path.exists(os.path.join(ref, s)) for s in srcs):
         print(f"reference sources not found under {ref}; nothing built", file=sys.stderr)
         return 0
+    _stage_tests(ref)
     if not args.cutlass:
         print("no CUTLASS header tree found; reference not built", file=sys.stderr)
         return 1
@@ -69,6 +87,7 @@ def main() -> int:
     target = os.path.join(OUT, MODULE + suffix)
     newest_src = max(os.path.getmtime(os.path.join(ref, s)) for s in srcs)
     if os.path.exists(target) and os.path.getmtime(target) >= newest_src:
+        _copy_to_baseline(target)
         print(f"up to date: {target}")
         return 0
 
@@ -113,8 +132,26 @@ def main() -> int:
         return 1
     for o in objs:
         os.remove(o)
+    _copy_to_baseline(target)
     print(f"built {target}")
     return 0
+
+
+def _stage_tests(ref: str) -> None:
+    """Copy the reference's own test files, unchanged, into oracle/_ref/tests/."""
+    dst_dir = os.path.join(OUT, "tests")
+    os.makedirs(dst_dir, exist_ok=True)
+    for rel in REF_TESTS:
+        src = os.path.join(ref, rel)
+        if os.path.exists(src):
+            shutil.copyfile(src, os.path.join(dst_dir, os.path.basename(rel)))
+
+
+def _copy_to_baseline(target: str) -> None:
+    os.makedirs(BASELINE_OUT, exist_ok=True)
+    dst = os.path.join(BASELINE_OUT, os.path.basename(target))
+    if not os.path.exists(dst) or os.path.getmtime(dst) < os.path.getmtime(target):
+        shutil.copyfile(target, dst)
 
 
 if __name__ == "__main__":

@@ -150,32 +150,50 @@ def test_probe_and_status_argument_errors(lib):
     assert lib.tdc_ws_consumer_warps() == 4
 
 
+PLAN_KEYS = ["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid", "smem",
+             "tail_chunk_rows"]
+
+
 def _plan(lib, N, H, W, Cc, pad, ns, sms=148, occ=4):
-    out = (i64 * 8)()
+    out = (i64 * 9)()
     rc = lib.tdc_ws_plan(i64(N), i64(H), i64(W), i64(Cc), i64(pad), i64(ns), i64(sms), i64(occ), out)
     assert rc == 0
-    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
-                     "smem"], list(out)))
+    return dict(zip(PLAN_KEYS, list(out)))
 
 
 def segments(pl, P, g):
     """(strip, first row, end row) of every segment CTA g processes, restating
     the kernel's SegmentIter: whole strips round-robin, then the remaining
-    strips in bands, band-major, round-robin."""
+    strips in bands, band-major, round-robin; or, with tail_chunk_rows = L,
+    channel block g % cblocks of rows [k*L, (k+1)*L) (k = g // cblocks) of
+    the tail's pixel strips' rows taken one pixel strip after the other."""
     out = []
     tail = pl["strips"] - pl["full_units"]
     hb = pl["tail_band_rows"]
     bands = -(-P // hb)
+    L = pl.get("tail_chunk_rows", 0)
     k = g
+    while k < pl["full_units"]:
+        out.append((k, 0, P))
+        k += pl["grid"]
+    if L > 0:
+        cb = pl["cblocks"]
+        assert pl["grid"] % cb == 0 and tail % cb == 0
+        total = tail // cb * P
+        row = min(g // cb * L, total)
+        end = min(row + L, total)
+        while row < end:
+            ps, first = divmod(row, P)
+            last = min(P, first + end - row)
+            out.append((pl["full_units"] + ps * cb + g % cb, first, last))
+            row += last - first
+        return out
     while True:
-        if k < pl["full_units"]:
-            out.append((k, 0, P))
-        else:
-            t = k - pl["full_units"]
-            if t >= tail * bands:
-                break
-            band = t // tail
-            out.append((pl["full_units"] + t % tail, band * hb, min(P, band * hb + hb)))
+        t = k - pl["full_units"]
+        if t >= tail * bands:
+            break
+        band = t // tail
+        out.append((pl["full_units"] + t % tail, band * hb, min(P, band * hb + hb)))
         k += pl["grid"]
     return out
 
@@ -212,12 +230,11 @@ def test_plan_covers_every_output_once(lib, N, H, W, Cc, pad, ns):
 
 
 def _fwd_plan(lib, N, H, W, Cc, K, S, pad, ns, sms=148, occ=3):
-    out = (i64 * 8)()
+    out = (i64 * 9)()
     rc = lib.tdc_dwconv_fwd_plan(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(S), i64(pad), i64(ns),
                                  i64(sms), i64(occ), out)
     assert rc == 0
-    return dict(zip(["stage_rows", "qstrips", "cblocks", "strips", "full_units", "tail_band_rows", "grid",
-                     "smem"], list(out)))
+    return dict(zip(PLAN_KEYS, list(out)))
 
 
 def direct_scheme(K, S):

@@ -3,9 +3,10 @@
 Every mbarrier wait in the ws kernel is bounded.  Here the producer withholds
 one load, so the full barrier of that stage is never completed (a flag that
 nothing sets): the consumers' wait runs out after a short limit, the kernel
-records TDC_DEVICE_FULL_TIMEOUT in the per-device status word, the producer
-drains the copies it did issue, and every CTA returns.  The test then checks
-that the CUDA context still runs a correct launch.
+records TDC_DEVICE_FULL_TIMEOUT in the per-device status word (and its copy
+in mapped host memory), the producer drains the copies it did issue, and
+every CTA returns.  The tests then check that later calls report the failure
+until it is cleared, and that the CUDA context still runs a correct launch.
 """
 import pytest
 import torch
@@ -36,6 +37,30 @@ def test_withheld_load_times_out_and_context_survives(n_stage):
     assert code == FULL_TIMEOUT, (code, block, stage, load)
     assert stage == 1 % n_stage
     # the context is intact: a normal launch completes and is exact
+    y = T.dwconv_ws(x, w, 1, n_stage)
+    assert T.device_status(clear=True)[0] == 0
+    ref = oracle.dwconv_f16(x.cpu().numpy(), w.cpu().numpy(), 1)
+    assert (y.cpu().numpy().view("u2") == ref.view("u2")).all()
+
+
+@pytest.mark.parametrize("n_stage", [2, 3])
+def test_next_call_reports_an_earlier_timeout(n_stage):
+    # The failed launch's record reaches the host through mapped memory: once
+    # that launch has finished, every later call fails before launching
+    # anything (no synchronisation on the call path) until the record is
+    # cleared; then calls run again, exactly.
+    x, w = _inputs()
+    T.device_status(clear=True)
+    T._C.dwconv_ws_withhold(x, w, 1, n_stage, 1, 50_000_000)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="gave up waiting"):
+        T.dwconv_ws(x, w, 1, n_stage)
+    with pytest.raises(RuntimeError, match="gave up waiting"):
+        T.dwconv3x3(x, w, 1, n_stage=n_stage)
+    with pytest.raises(RuntimeError, match="gave up waiting"):
+        T.dwconv(x, w, 1, stride=2)
+    code, block, stage, load = T.device_status(clear=True)
+    assert code == FULL_TIMEOUT, (code, block, stage, load)
     y = T.dwconv_ws(x, w, 1, n_stage)
     assert T.device_status(clear=True)[0] == 0
     ref = oracle.dwconv_f16(x.cpu().numpy(), w.cpu().numpy(), 1)

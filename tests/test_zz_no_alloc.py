@@ -60,7 +60,11 @@ def _noalloc(lib, x, dy, dw, pad, n_stage):
                                                 i64(n_stage), _stream())
 
 
-@pytest.mark.parametrize("N,H,W,C,pad", [(4, 56, 56, 256, 1), (2, 19, 45, 72, 2), (1, 30, 33, 640, 1)])
+# (8, 56, 56, 1024): 144 * C bytes per CTA leave the 16 MiB room for 113 CTAs,
+# fewer than the plan wants, so the entry point re-plans on a smaller grid
+# (another tail split and number of partial sums than the workspace entry).
+@pytest.mark.parametrize("N,H,W,C,pad", [(4, 56, 56, 256, 1), (2, 19, 45, 72, 2), (1, 30, 33, 640, 1),
+                                         (8, 56, 56, 1024, 1)])
 def test_two_calls_match_the_workspace_entry_point(lib, N, H, W, C, pad):
     g = torch.Generator(device="cuda").manual_seed(N * 1000 + C)
     x = (torch.rand(N, H, W, C, device="cuda", generator=g) * 2 - 1).half()
@@ -87,11 +91,21 @@ def test_allocates_no_device_memory(lib):
     dw = torch.empty(3, 3, 128, dtype=torch.float32, device="cuda")
     assert _noalloc(lib, x, dy, dw, 1, 2) == 0  # set-up (if not done yet) and first launch
     torch.cuda.synchronize()
-    free_before = torch.cuda.mem_get_info()[0]
-    for _ in range(3):
-        assert _noalloc(lib, x, dy, dw, 1, 2) == 0
-    torch.cuda.synchronize()
-    assert torch.cuda.mem_get_info()[0] == free_before
+
+    def free_after_three_calls():
+        before_dev, before_torch = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
+        for _ in range(3):
+            assert _noalloc(lib, x, dy, dw, 1, 2) == 0
+        torch.cuda.synchronize()
+        assert torch.cuda.memory_allocated() == before_torch
+        return before_dev, torch.cuda.mem_get_info()[0]
+
+    # The device-wide figure also moves with other processes on the GPU: one
+    # differing reading is taken again before it counts.
+    before, after = free_after_three_calls()
+    if after != before:
+        before, after = free_after_three_calls()
+    assert after == before
 
 
 def test_rejects_channels_beyond_the_scratch(lib):

@@ -82,8 +82,56 @@ cudaError_t prepare_ws(int* occ) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
 }
 
-// Returns TDC_OK and fills *info for the current device, or an error.
-int current_device(DeviceInfo** info, int* dev_out) {
+// Failure records of the kernels' bounded waits, written through by the GPU
+// to mapped pinned host memory: 4 ints per device (code, block, stage, load)
+// in one page, allocated by the first call that launches a pipelined kernel
+// (never by tdc_dwconv3x3_bwd_weight_noalloc, which allocates nothing).
+// With unified addressing the host pointer is also the device address.
+std::mutex g_status_page_mutex;
+std::atomic<int*> g_status_page{nullptr};
+
+// This device's slot of the page (creating the page when allow_alloc), or
+// null.  The allocation may come during a stream capture of the calling
+// thread: the thread's capture mode is relaxed around it, and a failure
+// leaves the page to a later call.
+int* status_slot(int dev, bool allow_alloc) {
+  int* page = g_status_page.load(std::memory_order_acquire);
+  if (page == nullptr && allow_alloc) {
+    std::lock_guard<std::mutex> lock(g_status_page_mutex);
+    page = g_status_page.load(std::memory_order_acquire);
+    if (page == nullptr) {
+      cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+      cudaThreadExchangeStreamCaptureMode(&mode);
+      void* mem = nullptr;
+      const cudaError_t e = cudaHostAlloc(&mem, sizeof(int) * 4 * kMaxDevices,
+                                          cudaHostAllocMapped | cudaHostAllocPortable);
+      cudaThreadExchangeStreamCaptureMode(&mode);
+      if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+      }
+      std::memset(mem, 0, sizeof(int) * 4 * kMaxDevices);
+      page = static_cast<int*>(mem);
+      g_status_page.store(page, std::memory_order_release);
+    }
+  }
+  return page == nullptr ? nullptr : page + 4 * dev;
+}
+
+// The slot of the calling thread's current device (see status_slot).
+int* current_status_slot(bool allow_alloc) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  return status_slot(dev, allow_alloc);
+}
+
+// Returns TDC_OK and fills *info for the current device, or an error.  With
+// check_failures, a failure a kernel recorded on this device (an earlier
+// launch that gave up waiting on its pipeline) fails the call with
+// TDC_ERR_DEVICE_TIMEOUT until tdc_device_status clears it; the record is
+// read from mapped host memory, without synchronising, so it covers the
+// launches that have finished by the time of the call.
+int current_device(DeviceInfo** info, int* dev_out, bool check_failures = true) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver
@@ -143,6 +191,10 @@ int current_device(DeviceInfo** info, int* dev_out) {
   if (d.status != TDC_OK) return d.status;
   *info = &d;
   if (dev_out) *dev_out = dev;
+  if (check_failures) {
+    const volatile int* slot = status_slot(dev, false);
+    if (slot != nullptr && slot[0] != 0) return TDC_ERR_DEVICE_TIMEOUT;
+  }
   return TDC_OK;
 }
 
@@ -177,6 +229,7 @@ struct WsPlan {
   int stage_rows, qstrips, cblocks, tail_bands, tail_band_rows;
   int64_t strips, full_units, tail_strips, grid;
   size_t smem;
+  int tail_chunk_rows;  // > 0: the tail is cut into chunks (SegmentIter), else bands
 };
 
 // Ring capacity in input rows per CTA, split evenly over the n_stage stages
@@ -193,13 +246,33 @@ int stage_rows_for(int64_t n_stage) { return std::max<int>(1, kRingRows / int(n_
 constexpr int kWgradRingRows = 8;
 int wgrad_stage_rows(int64_t n_stage) { return std::max<int>(1, kWgradRingRows / int(n_stage)); }
 
+// Rows the busiest CTA streams (halo rows included) when the tail's
+// (tail_strips / cblocks) * P pixel-strip rows are cut into chunks of L rows,
+// one chunk per cblocks CTAs; 0 when no chunk fits the grid.
+int64_t chunk_tail_cost(int64_t tail_strips, int64_t cblocks, int64_t P, int64_t grid, int64_t L) {
+  const int64_t total = (tail_strips / cblocks) * P;
+  const int64_t chunks = grid / cblocks;
+  if (L < 1 || chunks < 1 || (total + L - 1) / L > chunks) return 0;
+  int64_t worst = 0;
+  for (int64_t a = 0; a < total; a += L) {
+    const int64_t b = std::min(total, a + L);
+    const int64_t segments = (b - 1) / P - a / P + 1;
+    worst = std::max(worst, (b - a) + 2 * segments);
+  }
+  return worst;
+}
+
 // Persistent grid of SMs x resident CTAs.  Whole strips are dealt
 // round-robin while every CTA can take one: full_units =
 // (ceil(strips/grid) - 1) * grid.  The remaining tail_strips strips are cut
 // into bands; the band count minimises the rows the busiest CTA streams in
-// the last wave, (tail units per CTA) x (band rows + 2 halo rows).
+// the last wave, (tail units per CTA) x (band rows + 2 halo rows).  With
+// `chunk_tail` (forward kernels) the tail may instead be cut into chunks of
+// consecutive rows (SegmentIter), when that lets the busiest CTA stream fewer
+// rows: e.g. 16 x 112 x 224 x 128 on 444 CTAs, 224 strips of 112 rows: bands
+// of 16 rows leave the busiest CTA 4 bands = 72 rows, chunks of 57 rows 61.
 WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
-                 int64_t ctas_per_sm) {
+                 int64_t ctas_per_sm, bool chunk_tail = false) {
   WsPlan pl{};
   pl.stage_rows = stage_rows_for(n_stage);
   pl.qstrips = int((Q + tdc::kStripQ - 1) / tdc::kStripQ);
@@ -225,6 +298,16 @@ WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, in
   }
   pl.tail_band_rows = int(best_rows);
   pl.tail_bands = int((P + best_rows - 1) / best_rows);
+  pl.tail_chunk_rows = 0;
+  if (chunk_tail && pl.grid % pl.cblocks == 0) {
+    const int64_t total = (pl.tail_strips / pl.cblocks) * P;
+    const int64_t chunks = pl.grid / pl.cblocks;
+    const int64_t L = std::max<int64_t>(kMinRowsPerCta, (total + chunks - 1) / chunks);
+    const int64_t cost = chunk_tail_cost(pl.tail_strips, pl.cblocks, P, pl.grid, L);
+    // (the kernel counts the tail's rows in 32 bits)
+    if (cost > 0 && cost < best_cost && total + L + pl.grid < (int64_t(1) << 31))
+      pl.tail_chunk_rows = int(L);
+  }
   pl.smem = size_t(n_stage) * pl.stage_rows * tdc::kRowBytes + 128;
   return pl;
 }
@@ -358,11 +441,12 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
       epi.fused && (epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE);
   const int kind = !epi.fused ? (probe ? 1 : 0) : (with_epilogue ? 3 : 2);
   const int occ = std::max(1, dev->ws_occupancy[n_stage - 2][kind]);
-  const WsPlan pl = make_plan(N, P, Q, C, n_stage, dev->sms, occ);
+  const WsPlan pl = make_plan(N, P, Q, C, n_stage, dev->sms, occ, true);
   alignas(64) CUtensorMap map;
   rc = encode_x_map(&map, x, N, H, W, C, pl.stage_rows);
   if (rc != TDC_OK) return rc;
   tdc::WsParams prm{};
+  prm.status_host = current_status_slot(true);
   prm.w = static_cast<const __half*>(w);
   prm.y = static_cast<__half*>(y);
   prm.stall = stall;
@@ -371,6 +455,7 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
   prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
   prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
+  prm.tail_chunk_rows = pl.tail_chunk_rows;
   prm.timeout_ns = uint64_t(timeout_ns > 0 ? timeout_ns : g_timeout_ns.load());
   prm.withhold = withhold;
   prm.bias = static_cast<const __half*>(epi.bias);
@@ -472,7 +557,7 @@ int geom_stage_rows(int K, int S, int64_t n_stage) {
 
 WsPlan make_geom_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int S, int64_t n_stage,
                       int64_t sms, int64_t ctas_per_sm) {
-  WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm, true);
   pl.stage_rows = geom_stage_rows(K, S, n_stage);
   pl.smem = size_t(n_stage) * pl.stage_rows * strip_in_cols(K, S) * tdc::kBlockC * 2 + 128;
   return pl;
@@ -523,6 +608,7 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   rc = encode_nhwc_map(&map, x, N, H, W, C, strip_in_cols(int(K), int(S)), stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WsParams prm{};
+  prm.status_host = current_status_slot(true);
   prm.w = static_cast<const __half*>(w);
   prm.y = static_cast<__half*>(y);
   prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
@@ -530,6 +616,7 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
   prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
   prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
   prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
+  prm.tail_chunk_rows = pl.tail_chunk_rows;
   prm.timeout_ns = uint64_t(g_timeout_ns.load());
   prm.withhold = -1;
   prm.bias = static_cast<const __half*>(epi.bias);
@@ -1114,6 +1201,7 @@ int dgrad_s2(const void* dy, const void* w, void* dx, int64_t N, int64_t H, int6
   rc = encode_nhwc_map(&map, dy, N, P, Q, C, dgrad_s2_dy_cols(int(K)), pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::DgradS2Params g{};
+  g.status_host = current_status_slot(true);
   g.w = static_cast<const __half*>(w);
   g.dx = static_cast<__half*>(dx);
   g.H = int32_t(H); g.W = int32_t(W); g.C = int32_t(C);
@@ -1245,6 +1333,7 @@ int wgrad_s2(const void* x, const void* dy, float* dw, int64_t N, int64_t H, int
   rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
+  g.status_host = current_status_slot(true);
   g.partial = static_cast<float*>(workspace);
   g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
   g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
@@ -1322,7 +1411,7 @@ TDC_API const char* tdc_strerror(int code) {
     case TDC_ERR_TOO_LARGE: return "problem exceeds the TMA descriptor / 32-bit field limits";
     case TDC_ERR_CUDA: return "a CUDA runtime call failed";
     case TDC_ERR_TMA_ENCODE: return "cuTensorMapEncodeTiled failed";
-    case TDC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on a pipeline barrier";
+    case TDC_ERR_DEVICE_TIMEOUT: return "an earlier launch on this device gave up waiting on a pipeline barrier and left its output incomplete; tdc_device_status(1, info) (tma_dwconv.device_status) reports and clears the record";
     case TDC_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
     case TDC_ERR_WORKSPACE: return "workspace smaller than tdc_dwconv3x3_bwd_weight_workspace reports";
     case TDC_ERR_SCRATCH_LIMIT: return "C too large for the 16 MiB static scratch of tdc_dwconv3x3_bwd_weight_noalloc (C <= 116508)";
@@ -1814,6 +1903,7 @@ static int bwd_weight_entry(int dt, const void* x, const void* dy, float* dw, in
   rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
+  g.status_host = current_status_slot(true);
   g.partial = static_cast<float*>(workspace);
   g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
   g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
@@ -1981,6 +2071,7 @@ static int wgrad3x3(int dt, const void* x, const void* dy, float* dw, int64_t N,
   rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows, dt);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
+  g.status_host = current_status_slot(true);
   g.partial = static_cast<float*>(workspace);
   g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
   g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
@@ -2025,10 +2116,12 @@ TDC_API int tdc_dwconv3x3_bwd_weight(const void* x, const void* dy, float* dw, i
 constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // per device, held until exit
 static __device__ __align__(256) float g_tdc_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
+// The scratch's device address per device, looked up on the first call that
+// succeeds in doing so (a failed lookup is not cached: the next call tries
+// again).
 struct NoAllocScratch {
-  std::once_flag once;
-  float* ptr = nullptr;
-  int status = TDC_ERR_CUDA;
+  std::mutex m;
+  std::atomic<float*> ptr{nullptr};
 };
 NoAllocScratch g_noalloc[kMaxDevices];
 
@@ -2057,18 +2150,21 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
   NoAllocScratch& sc = g_noalloc[dev];
-  std::call_once(sc.once, [&sc]() {
-    void* p = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&p, g_tdc_noalloc_scratch);
-    if (err == cudaSuccess && p != nullptr) {
-      sc.ptr = static_cast<float*>(p);
-      sc.status = TDC_OK;
-    } else {
-      t_last_cuda_error = int(err);
-      sc.status = TDC_ERR_CUDA;
+  float* scratch = sc.ptr.load(std::memory_order_acquire);
+  if (scratch == nullptr) {
+    std::lock_guard<std::mutex> lock(sc.m);
+    scratch = sc.ptr.load(std::memory_order_acquire);
+    if (scratch == nullptr) {
+      void* p = nullptr;
+      const cudaError_t err = cudaGetSymbolAddress(&p, g_tdc_noalloc_scratch);
+      if (err != cudaSuccess || p == nullptr) {
+        t_last_cuda_error = int(err);
+        return TDC_ERR_CUDA;
+      }
+      scratch = static_cast<float*>(p);
+      sc.ptr.store(scratch, std::memory_order_release);
     }
-  });
-  if (sc.status != TDC_OK) return sc.status;
+  }
 
   alignas(64) CUtensorMap xmap, dymap;
   rc = encode_x_map(&xmap, x, N, H, W, C, pl.stage_rows);
@@ -2076,7 +2172,8 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
   rc = encode_dy_map(&dymap, dy, N, P, Q, C, pl.stage_rows);
   if (rc != TDC_OK) return rc;
   tdc::WgradParams g{};
-  g.partial = sc.ptr;  // every CTA zeroes its own part before accumulating
+  g.status_host = current_status_slot(false);  // never allocates the page
+  g.partial = scratch;  // every CTA zeroes its own part before accumulating
   g.C = int32_t(C); g.P = int32_t(P); g.Q = int32_t(Q); g.pad = int32_t(pad);
   g.qstrips = pl.qstrips; g.cblocks = pl.cblocks; g.stage_rows = pl.stage_rows;
   g.tail_bands = pl.tail_bands; g.tail_band_rows = pl.tail_band_rows;
@@ -2092,7 +2189,7 @@ TDC_API int tdc_dwconv3x3_bwd_weight_noalloc(const void* x, const void* dy, floa
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   const int n = int(9 * C);
-  e = tdc::launch_wgrad_reduce(sc.ptr, dw, int32_t(pl.grid * tdc::kConsumerWarps), n, st);
+  e = tdc::launch_wgrad_reduce(scratch, dw, int32_t(pl.grid * tdc::kConsumerWarps), n, st);
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
@@ -2145,7 +2242,8 @@ TDC_API int tdc_set_wait_timeout_ns(int64_t ns) {
 
 TDC_API int tdc_device_status(int clear, int64_t* info) {
   DeviceInfo* dev = nullptr;
-  int rc = current_device(&dev, nullptr);
+  int devi = -1;
+  int rc = current_device(&dev, &devi, false);
   if (rc != TDC_OK) return rc;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_fail(e);
@@ -2156,6 +2254,9 @@ TDC_API int tdc_device_status(int clear, int64_t* info) {
     const int z[4] = {0, 0, 0, 0};
     e = cudaMemcpyToSymbol(tdc::g_tdc_status, z, sizeof(z));
     if (e != cudaSuccess) return cuda_fail(e);
+    volatile int* slot = status_slot(devi, false);
+    if (slot != nullptr)
+      for (int i = 0; i < 4; ++i) slot[i] = 0;
   }
   if (info)
     for (int i = 0; i < 4; ++i) info[i] = h[i];
@@ -2180,7 +2281,7 @@ TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
   if (sms < 1 || ctas_per_sm < 1) return TDC_ERR_BAD_SHAPE;
   const int64_t P = H + 2 * pad - 2, Q = W + 2 * pad - 2;
   if (P < 1 || Q < 1) return TDC_ERR_BAD_SHAPE;
-  const WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm);
+  const WsPlan pl = make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm, true);
   plan[0] = pl.stage_rows;
   plan[1] = pl.qstrips;
   plan[2] = pl.cblocks;
@@ -2189,6 +2290,7 @@ TDC_API int tdc_ws_plan(int64_t N, int64_t H, int64_t W, int64_t C, int64_t pad,
   plan[5] = pl.tail_band_rows;
   plan[6] = pl.grid;
   plan[7] = int64_t(pl.smem);
+  plan[8] = pl.tail_chunk_rows;
   return TDC_OK;
 }
 
@@ -2206,7 +2308,7 @@ TDC_API int tdc_dwconv_fwd_plan(int64_t N, int64_t H, int64_t W, int64_t C, int6
   if (H + 2 * pad < K || W + 2 * pad < K) return TDC_ERR_BAD_SHAPE;
   const int64_t P = (H + 2 * pad - K) / stride + 1, Q = (W + 2 * pad - K) / stride + 1;
   const WsPlan pl = (K == 3 && stride == 1)
-                        ? make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm)
+                        ? make_plan(N, P, Q, C, n_stage, sms, ctas_per_sm, true)
                         : make_geom_plan(N, P, Q, C, int(K), int(stride), n_stage, sms, ctas_per_sm);
   plan[0] = pl.stage_rows;
   plan[1] = pl.qstrips;
@@ -2216,6 +2318,7 @@ TDC_API int tdc_dwconv_fwd_plan(int64_t N, int64_t H, int64_t W, int64_t C, int6
   plan[5] = pl.tail_band_rows;
   plan[6] = pl.grid;
   plan[7] = int64_t(pl.smem);
+  plan[8] = pl.tail_chunk_rows;
   return TDC_OK;
 }
 

@@ -72,6 +72,7 @@ struct DgradS2Params {
   int32_t tail_bands, tail_band_rows;
   int64_t full_units, tail_strips;
   uint64_t timeout_ns;
+  int* status_host;  // this device's failure slot in mapped host memory, or null
 };
 
 // The forward's segment enumeration over dx's [N,H,W,C] strips.
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
         if (!mbar_wait_bounded(smem_addr(&empty_bar[stage]), phase ^ 1u, &abort_flag, true,
                                g.timeout_ns)) {
           if (!abort_flag) {
-            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load);
+            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load, g.status_host);
             abort_flag = 1;
           }
           ok = false;
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
       if (!(armed & (1u << s))) continue;
       if (!mbar_wait_bounded(smem_addr(&full_bar[s]), (armed_parity >> s) & 1u, &abort_flag,
                              false, g.timeout_ns))
-        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load);
+        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load, g.status_host);
     }
     return;
   }
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(kWsThreads, (dgrad_s2_min_blocks(K)))
                                            true, g.timeout_ns);
         if (__any_sync(0xffffffffu, !got)) {
           if (lane == 0 && !abort_flag) {
-            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1);
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1, g.status_host);
             abort_flag = 1;
           }
           failed = true;

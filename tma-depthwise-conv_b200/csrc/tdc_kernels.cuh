@@ -144,23 +144,26 @@ __global__ void __launch_bounds__(256) dwconv_v0_kernel(const uint4* __restrict_
 // horizontal neighbours (sharing their halo columns through L2).
 // The grid is persistent.  CTA g first takes whole strips g, g + grid, ...
 // below `full_units` = (ceil(strips/grid) - 1) * grid.  The last
-// `tail_strips` strips are cut into `tail_bands` bands of `tail_band_rows`
-// rows and these tail units, ordered (band, strip), are dealt round-robin
-// the same way, so the last wave is as even as the band height allows while
-// CTAs running at the same moment still work on neighbouring strips at the
-// same rows.
+// `tail_strips` strips are cut either into `tail_bands` bands of
+// `tail_band_rows` rows, these tail units, ordered (band, strip), dealt
+// round-robin the same way, or into chunks of consecutive rows
+// (`tail_chunk_rows`, see SegmentIter), whichever leaves the busiest CTA
+// fewer rows to stream; either way CTAs running at the same moment work on
+// neighbouring strips at the same rows.
 // Per segment the producer (warp 0, one thread) streams input rows
 // [p0 - pad, p0 - pad + rows + 2) as TMA boxes of (64 ch, 34 cols,
 // stage_rows rows, 1 image) into an NS-deep shared-memory ring; box
 // coordinates outside the image are zero-filled by the TMA unit, which
-// implements the padding.  Four consumer warps each own 8 output columns; a
-// lane owns one channel pair (a warp covers the 64 channels = 128 B of one
-// column, so every shared-memory read is conflict-free).  Each input row is
-// read from shared memory once per lane and FMA'd into three rows of
-// accumulators (the rows it is tap r = 0, 1, 2 of): a sliding window down
-// the segment, so the vertical halo is never re-read.  After a row the
-// oldest accumulator row is complete; it is rounded to fp16 and stored with
-// 128-byte-per-warp coalesced stores.
+// implements the padding.  Four consumer warps each own 8 output columns.
+// At 3x3 stride 1 a lane owns one 16-byte vector of 8 channels of two
+// adjacent columns (ws_consumers_vec3x3: 16-byte shared-memory reads and
+// 16-byte global stores); in the other geometries a lane owns one channel
+// pair of all 8 columns (ws_consumers_pairs).  Either way every
+// shared-memory read is conflict-free and each input row is read from shared
+// memory once per lane and FMA'd into the accumulators of every output row it
+// is a tap row of: a sliding window down the segment, so the vertical halo is
+// never re-read.  A finished output row is rounded and stored with full
+// 128-byte lines.
 // ============================================================================
 constexpr int kBlockC = 64;                        // channels per strip (128 B)
 constexpr int kColsPerWarp = 8;                    // output columns per consumer warp
@@ -183,20 +186,38 @@ struct WsParams {
   int32_t qstrips, cblocks, stage_rows;
   int32_t tail_bands, tail_band_rows;
   int64_t full_units;   // strips handed out whole (a multiple of gridDim.x)
-  int64_t tail_strips;  // strips handed out as bands
+  int64_t tail_strips;  // strips handed out as bands or chunks
   uint64_t timeout_ns;
+  int* status_host;     // this device's failure slot in mapped host memory, or null
   int64_t withhold;     // load index the producer withholds (-1: none)
+  // > 0: the tail is cut into chunks of this many rows instead of bands (see
+  // SegmentIter); requires gridDim.x % cblocks == 0.
+  int32_t tail_chunk_rows;
 };
 
 // Per-device failure record written by the bounded waits:
-// {code, block, stage, load index}.
+// {code, block, stage, load index}.  The first failure on the device (until
+// the host clears it) is also written through to `host`, the device's slot
+// in a page of mapped pinned host memory, code last: the library reads that
+// slot at the start of every later call, without synchronising, and fails
+// the call while a failure is recorded.  `host` is null when the page does
+// not exist (the allocation-free entry point never creates it).
 __device__ int g_tdc_status[4];
 
-__device__ __forceinline__ void record_failure(int code, int block, int stage, int64_t load) {
+__device__ __forceinline__ void record_failure(int code, int block, int stage, int64_t load,
+                                               int* host) {
   if (atomicCAS(&g_tdc_status[0], 0, code) == 0) {
     g_tdc_status[1] = block;
     g_tdc_status[2] = stage;
     g_tdc_status[3] = int(load);
+    if (host != nullptr) {
+      volatile int* h = host;
+      h[1] = block;
+      h[2] = stage;
+      h[3] = int(load);
+      __threadfence_system();
+      h[0] = code;
+    }
   }
 }
 
@@ -207,9 +228,21 @@ struct Segment {
 
 // Enumerates the segments of one CTA; the producer and every consumer warp
 // run their own copy and see the same sequence.
+//
+// Tail by chunks (tail_chunk_rows = L > 0).  The tail strips form
+// tail_strips / cblocks pixel strips (the cblocks channel blocks of one
+// image's column strip); their rows, pixel strip after pixel strip, make one
+// sequence of (tail_strips / cblocks) * P rows.  CTA g of the grid takes
+// channel block g % cblocks of rows [k*L, (k+1)*L) of that sequence, k =
+// g / cblocks: one or a few segments (one per pixel strip the chunk
+// touches).  The cblocks CTAs of a chunk stream the same rows of the same
+// pixels at the same time, as the channel-block-fastest strip order does for
+// whole strips, and every CTA streams at most L rows plus two halo rows per
+// segment, however the tail's rows divide by the grid.
 struct SegmentIter {
   int64_t next;  // next work item: whole strips first, then tail units
   int64_t grid;
+  int row = -1;  // chunk tail: next row of this CTA's chunk (-1: not started)
 
   __device__ SegmentIter(int64_t g, int64_t grid_) : next(g), grid(grid_) {}
 
@@ -220,6 +253,21 @@ struct SegmentIter {
       strip = next;
       first = 0;
       last = p.P;
+      next += grid;
+    } else if (p.tail_chunk_rows > 0) {
+      // next stays at full_units + blockIdx.x; the host keeps the tail's rows
+      // below 2^31.
+      const int g = int(next - p.full_units);
+      const int chunk = g / p.cblocks;
+      const int total = int((p.tail_strips / p.cblocks) * p.P);
+      const int end = chunk < int(grid) / p.cblocks ? min((chunk + 1) * p.tail_chunk_rows, total) : 0;
+      if (row < 0) row = min(chunk * p.tail_chunk_rows, end);
+      if (row >= end) return false;
+      const int ps = row / p.P;  // pixel strip of the tail
+      first = row - ps * p.P;
+      last = min(p.P, first + (end - row));
+      row += last - first;
+      strip = p.full_units + int64_t(ps) * p.cblocks + g % p.cblocks;
     } else {
       const int64_t t = next - p.full_units;
       if (t >= p.tail_strips * p.tail_bands) return false;
@@ -227,8 +275,8 @@ struct SegmentIter {
       strip = p.full_units + t % p.tail_strips;
       first = band * p.tail_band_rows;
       last = min(p.P, first + p.tail_band_rows);
+      next += grid;
     }
-    next += grid;
     s.cb = int(strip % p.cblocks);
     const int64_t r = strip / p.cblocks;
     s.qs = int(r % p.qstrips);
@@ -356,15 +404,237 @@ __device__ __forceinline__ void feed_row(const uint32_t (&xr)[Geom<K, S>::kWarpI
   }
 }
 
-// Resident CTAs per SM the kernel is compiled for (bounds its registers).
-#ifndef TDC_MIN_BLOCKS
-#define TDC_MIN_BLOCKS 1
-#endif
-
-template <int MODE>
-__host__ __device__ constexpr int ws_min_blocks() {
-  return MODE == kModeWs ? TDC_MIN_BLOCKS : 3;
+// 16 fp32 values of 8 channels c .. c+7 (a 16-byte vector of fp16 or bf16
+// elements): acc[2k], acc[2k+1] += x.(word k) * w.(word k).
+template <class E>
+__device__ __forceinline__ void fma_vec8(const uint4& x, const uint4& w, float* a) {
+  fma2<E>(x.x, w.x, a[0], a[1]);
+  fma2<E>(x.y, w.y, a[2], a[3]);
+  fma2<E>(x.z, w.z, a[4], a[5]);
+  fma2<E>(x.w, w.w, a[6], a[7]);
 }
+
+template <class E>
+__device__ __forceinline__ uint4 pack_vec8(const float* a) {
+  return make_uint4(pack2_rn<E>(a[0], a[1]), pack2_rn<E>(a[2], a[3]), pack2_rn<E>(a[4], a[5]),
+                    pack2_rn<E>(a[6], a[7]));
+}
+
+// Consumer warps of the 3x3 stride-1 kernel, with 16-byte lanes.
+//
+// Lane l of consumer warp cw owns the 8 channels c0 + 8*(l % 8) .. + 7 (one
+// 16-byte vector) of two adjacent output columns, q_first + 2*(l / 8) and the
+// next, q_first being the first of the warp's 8 columns.  Per input row the
+// lane reads the four input columns those outputs need as 16-byte vectors (a
+// warp instruction reads four 128-byte column blocks of the ring row:
+// conflict-free) and FMAs them into the three output rows the input row is tap
+// row r = 2, 1, 0 of: 3 rotating sets x 2 columns x 8 channels of fp32
+// accumulators, a sliding window down the segment, so vertical halo rows are
+// never re-read.  A finished output row is rounded and stored with one
+// 16-byte store per column (a warp instruction writes four full 128-byte
+// lines).  Each output's chain is (r, s) lexicographic from +0, the same as
+// every other kernel here.
+template <int NS, bool PROBE, int MODE, class E>
+__device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uint8_t* ring_ptr,
+                                                    uint32_t stage_bytes, uint64_t* full_bar,
+                                                    uint64_t* empty_bar, volatile int* abort_flag,
+                                                    int cw, int lane, uint64_t t_start) {
+  constexpr int kVecPerCol = kBlockC * 2 / 16;  // 16-byte vectors per column of a ring row
+  const int vl = lane & 7;                      // this lane's vector of the channel block
+  const int cp = lane >> 3;                     // this lane's column pair of the warp's 8
+  uint64_t stall_cycles = 0;
+  uint32_t stage = 0, phase = 0;
+  SegmentIter it(blockIdx.x, gridDim.x);
+  Segment sg;
+  int last_cb = -1;
+  uint4 wt[9];
+  float acc[3][16];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc[a][k] = 0.f;
+  bool failed = false;
+  while (!failed && it.next_segment(p, sg)) {
+    const int rows_in = sg.rows + 2;
+    const int c0 = sg.cb * kBlockC;
+    const int cl = c0 + 8 * vl;  // this lane's first channel
+    const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
+    const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
+    // This lane's 8 channels exist (always on the ws path, C % 64 == 0; else
+    // C % 8 == 0, so a vector is wholly inside C or wholly outside).
+    const bool chan_ok = MODE == kModeWs || cl < p.C;
+    if (sg.cb != last_cb) {
+#pragma unroll
+      for (int k = 0; k < 9; ++k) {
+        const int src = (MODE != kModeWs && p.flip_taps) ? 8 - k : k;
+        wt[k] = chan_ok ? __ldg(reinterpret_cast<const uint4*>(p.w + int64_t(src) * p.C + cl))
+                        : make_uint4(0u, 0u, 0u, 0u);
+      }
+      last_cb = sg.cb;
+    }
+    const int64_t y_off = ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first + 2 * cp) * p.C + cl;
+    const int64_t y_row_stride = int64_t(p.Q) * p.C;
+    const bool st0 = chan_ok && 2 * cp < n_valid;
+    const bool st1 = chan_ok && 2 * cp + 1 < n_valid;
+
+    // Finishes output row o of the segment from the accumulators a[0..15]
+    // (column 2*cp at a[0..7], the next at a[8..15]) and stores it.
+    auto store_row = [&](int o, float* a) {
+      if constexpr (MODE == kModeEpilogue) {
+        if (p.bias != nullptr && chan_ok) {
+          // Reloaded per row (an L1 hit) rather than held in 8 registers.
+          const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + cl));
+          const uint32_t b4[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float b0, b1;
+            unpack2<E>(b4[k], b0, b1);
+            a[2 * k] += b0;
+            a[2 * k + 1] += b1;
+            a[8 + 2 * k] += b0;
+            a[8 + 2 * k + 1] += b1;
+          }
+        }
+        switch (p.act) {
+          case TDC_ACT_RELU:
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a[k] = apply_act(a[k], TDC_ACT_RELU);
+            break;
+          case TDC_ACT_RELU6:
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a[k] = apply_act(a[k], TDC_ACT_RELU6);
+            break;
+          case TDC_ACT_SILU:
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a[k] = apply_act(a[k], TDC_ACT_SILU);
+            break;
+          case TDC_ACT_HARDSWISH:
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a[k] = apply_act(a[k], TDC_ACT_HARDSWISH);
+            break;
+          default:
+            break;
+        }
+        if (p.residual != nullptr) {
+          // Loaded here, after the FMAs, rather than held through them (the
+          // preloaded version spilled at the 136-register limit).
+          const __half* rp = p.residual + y_off + int64_t(o) * y_row_stride;
+          const uint4 res[2] = {
+              st0 ? __ldg(reinterpret_cast<const uint4*>(rp)) : make_uint4(0u, 0u, 0u, 0u),
+              st1 ? __ldg(reinterpret_cast<const uint4*>(rp + p.C)) : make_uint4(0u, 0u, 0u, 0u)};
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const uint32_t w4[4] = {res[m].x, res[m].y, res[m].z, res[m].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float r0, r1;
+              unpack2<E>(w4[k], r0, r1);
+              a[8 * m + 2 * k] += r0;
+              a[8 * m + 2 * k + 1] += r1;
+            }
+          }
+        }
+      }
+      __half* dst = p.y + y_off + int64_t(o) * y_row_stride;
+      if (st0) *reinterpret_cast<uint4*>(dst) = pack_vec8<E>(a);
+      if (st1) *reinterpret_cast<uint4*>(dst + p.C) = pack_vec8<E>(a + 8);
+    };
+
+    int lr = 0;  // row within the current stage
+    const uint8_t* sbuf = ring_ptr;
+
+    // One input row i (= U mod 3): acquire its stage, feed it, store the
+    // output row it completes (i - 2), release the stage after its last row.
+    auto step = [&](int i, auto u_tag) {
+      constexpr int U = decltype(u_tag)::value;
+      if (lr == 0) {
+        [[maybe_unused]] uint64_t t0 = 0;
+        if constexpr (PROBE) t0 = clock64();
+        const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, abort_flag, true,
+                                           p.timeout_ns);
+        // Keep the warp uniform: one lane giving up makes the whole warp give up.
+        if (__any_sync(0xffffffffu, !got)) {
+          if (lane == 0 && !*abort_flag) {
+            record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1, p.status_host);
+            *abort_flag = 1;
+          }
+          failed = true;
+          return;
+        }
+        if constexpr (PROBE) stall_cycles += clock64() - t0;
+        sbuf = ring_ptr + stage * stage_bytes;
+      }
+      if (n_valid > 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+                               sbuf + lr * kRowBytes + (cw * kColsPerWarp + 2 * cp) * (kBlockC * 2)) +
+                           vl;
+        uint4 xr[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xr[j] = src[j * kVecPerCol];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int s = 0; s < 3; ++s) {
+            const int m = j - s;  // output column (of the lane's two) input column j is tap s of
+            if (m < 0 || m > 1) continue;
+#pragma unroll
+            for (int r = 0; r < 3; ++r) {
+              float* a = acc[(U - r + 3) % 3] + 8 * m;  // the output row i - r
+              if (r == 0 && s == 0) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a[k] = 0.f;
+              }
+              fma_vec8<E>(xr[j], wt[r * 3 + s], a);
+            }
+          }
+        if (i >= 2) store_row(i - 2, acc[(U + 1) % 3]);
+      }
+      if (++lr == p.stage_rows || i == rows_in - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&empty_bar[stage]));
+        lr = 0;
+        if (++stage == NS) { stage = 0; phase ^= 1u; }
+      }
+    };
+
+    for (int i0 = 0; i0 < rows_in; i0 += 3) {
+      bool stop = false;
+      unroll_steps<3>([&](auto u_tag) {
+        constexpr int U = decltype(u_tag)::value;
+        if (stop) return;
+        const int i = i0 + U;
+        if (i >= rows_in) { stop = true; return; }
+        step(i, u_tag);
+        if (failed) stop = true;
+      });
+      if (stop) break;
+    }
+  }
+  if constexpr (PROBE) {
+    if (lane == 0) {
+      unsigned long long* row = p.stall + 4ull * blockIdx.x;
+      atomicAdd(row + 1, (unsigned long long)stall_cycles);
+      atomicAdd(row + 3, (unsigned long long)(clock64() - t_start));
+    }
+  } else {
+    (void)t_start;
+  }
+}
+
+// Registers per thread of the ws kernels, so that 3 CTAs of 160 threads
+// share an SM's 64 K registers: 136 for the 3x3 stride-1 vector consumers
+// (__launch_bounds__(160, 3) lets ptxas use only 128, at which they spill),
+// 128 for the other geometries.
+template <int K, int S>
+__host__ __device__ constexpr int ws_max_regs() {
+  return K == 3 && S == 1 ? 136 : 128;
+}
+
+template <int NS, bool PROBE, int MODE, int K, int S, class E>
+__device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint8_t* ring_ptr,
+                                                   uint32_t stage_bytes, uint64_t* full_bar,
+                                                   uint64_t* empty_bar, volatile int* abort_flag,
+                                                   int cw, int lane, uint64_t t_start);
 
 // MODE (kMode*): kModeGeneral lets the last 64-channel block be partial (TMA
 // zero-fills the missing channels; their lanes neither read taps nor store)
@@ -372,7 +642,7 @@ __host__ __device__ constexpr int ws_min_blocks() {
 // epilogue.  kModeWs is the ws call of the reference surface (3x3, stride 1).
 // E (F16 / BF16) is the element type; the ws surface is fp16 only.
 template <int NS, bool PROBE, int MODE = kModeWs, int K = 3, int S = 1, class E = F16>
-__global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
+__global__ void __maxnreg__((ws_max_regs<K, S>()))
     dwconv_ws_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
   using G = Geom<K, S>;
   static_assert(MODE != kModeWs || (K == 3 && S == 1), "the ws surface is 3x3, stride 1");
@@ -432,7 +702,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
         if constexpr (PROBE) t0 = clock64();
         if (!mbar_wait_bounded(eb, phase ^ 1u, &abort_flag, true, p.timeout_ns)) {
           if (!abort_flag) {
-            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load);
+            record_failure(TDC_DEVICE_EMPTY_TIMEOUT, blockIdx.x, stage, load, p.status_host);
             abort_flag = 1;
           }
           ok = false;
@@ -457,7 +727,7 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
       if (!(armed & (1u << s))) continue;
       if (!mbar_wait_bounded(smem_addr(&full_bar[s]), (armed_parity >> s) & 1u, &abort_flag,
                              false, p.timeout_ns)) {
-        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load);
+        record_failure(TDC_DEVICE_DRAIN_TIMEOUT, blockIdx.x, s, load, p.status_host);
       }
     }
     if constexpr (PROBE) {
@@ -469,7 +739,25 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
   }
 
   // ------------------------------ consumers ------------------------------
-  const int cw = warp - 1;
+  if constexpr (K == 3 && S == 1) {
+    ws_consumers_vec3x3<NS, PROBE, MODE, E>(p, ring_ptr, stage_bytes, full_bar, empty_bar,
+                                            &abort_flag, warp - 1, lane, t_start);
+    return;
+  } else {
+    ws_consumers_pairs<NS, PROBE, MODE, K, S, E>(p, ring_ptr, stage_bytes, full_bar, empty_bar,
+                                                 &abort_flag, warp - 1, lane, t_start);
+  }
+}
+
+// Consumer warps of the other geometries (3x3 stride 2, 5x5, 7x7): lane =
+// channel pair, warp = 8 output columns; sliding window or direct scheme per
+// Geom<K, S>::kDirect.
+template <int NS, bool PROBE, int MODE, int K, int S, class E>
+__device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint8_t* ring_ptr,
+                                                   uint32_t stage_bytes, uint64_t* full_bar,
+                                                   uint64_t* empty_bar, volatile int* abort_flag,
+                                                   int cw, int lane, uint64_t t_start) {
+  using G = Geom<K, S>;
   uint64_t stall_cycles = 0;
   uint32_t stage = 0, phase = 0;
   SegmentIter it(blockIdx.x, gridDim.x);
@@ -597,11 +885,11 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
           [[maybe_unused]] uint64_t t0 = 0;
           if constexpr (PROBE) t0 = clock64();
           const bool got = mbar_wait_bounded(smem_addr(&full_bar[acq_slot]), acq_phase,
-                                             &abort_flag, true, p.timeout_ns);
+                                             abort_flag, true, p.timeout_ns);
           if (__any_sync(0xffffffffu, !got)) {
-            if (lane == 0 && !abort_flag) {
-              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1);
-              abort_flag = 1;
+            if (lane == 0 && !*abort_flag) {
+              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, acq_slot, -1, p.status_host);
+              *abort_flag = 1;
             }
             failed = true;
             break;
@@ -681,13 +969,13 @@ __global__ void __launch_bounds__(kWsThreads, (ws_min_blocks<MODE>()))
         if (lr == 0) {
           [[maybe_unused]] uint64_t t0 = 0;
           if constexpr (PROBE) t0 = clock64();
-          const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, &abort_flag,
+          const bool got = mbar_wait_bounded(smem_addr(&full_bar[stage]), phase, abort_flag,
                                              true, p.timeout_ns);
           // Keep the warp uniform: one lane giving up makes the whole warp give up.
           if (__any_sync(0xffffffffu, !got)) {
-            if (lane == 0 && !abort_flag) {
-              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1);
-              abort_flag = 1;
+            if (lane == 0 && !*abort_flag) {
+              record_failure(TDC_DEVICE_FULL_TIMEOUT, blockIdx.x, stage, -1, p.status_host);
+              *abort_flag = 1;
             }
             failed = true;
             return;
