@@ -167,6 +167,24 @@ def _cuda_time(fn, steps: int, stream) -> float:
     return start.elapsed_time(end)
 
 
+def _live_copy_gbs(dev) -> float:
+    """This GPU's copy bandwidth now, the method of the measured peak: torch
+    copy_ of 1 Gi bf16 elements, read + write bytes, best of 10, CUDA events."""
+    a = torch.empty(1 << 30, dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(a)
+    best = float("inf")
+    for _ in range(11):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        b.copy_(a)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    torch.cuda.empty_cache()
+    return 2 * (1 << 30) * 2 / (best * 1e-3) / 1e9
+
+
 def _host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -462,6 +480,7 @@ def run_tdc(args, wl) -> None:
     local_ms = ms / args.steps
     achieved = my_bytes / (local_ms * 1e-3) / 1e9
     traffic, traffic_src = _traffic_per_call(wl.name, n)
+    live = _live_copy_gbs(dev)  # after the timed region
 
     line = {
         "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
@@ -478,7 +497,8 @@ def run_tdc(args, wl) -> None:
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": None if traffic is None else round(traffic),
                      "traffic_source": traffic_src,
-                     "algorithmic_bytes": my_bytes, "kernel": "dwconv_ws_kernel"},
+                     "algorithmic_bytes": my_bytes, "kernel": "dwconv_ws_kernel",
+                     "live_copy_gbs": round(live, 1), "frac_of_live_copy": round(achieved / live, 4)},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }

@@ -271,8 +271,8 @@ int64_t chunk_tail_cost(int64_t tail_strips, int64_t cblocks, int64_t P, int64_t
 // consecutive rows (SegmentIter), when that lets the busiest CTA stream fewer
 // rows: e.g. 16 x 112 x 224 x 128 on 444 CTAs, 224 strips of 112 rows: bands
 // of 16 rows leave the busiest CTA 4 bands = 72 rows, chunks of 57 rows 61.
-WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
-                 int64_t ctas_per_sm, bool chunk_tail = false) {
+WsPlan compute_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
+                    int64_t ctas_per_sm, bool chunk_tail) {
   WsPlan pl{};
   pl.stage_rows = stage_rows_for(n_stage);
   pl.qstrips = int((Q + tdc::kStripQ - 1) / tdc::kStripQ);
@@ -304,11 +304,57 @@ WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, in
     const int64_t chunks = pl.grid / pl.cblocks;
     const int64_t L = std::max<int64_t>(kMinRowsPerCta, (total + chunks - 1) / chunks);
     const int64_t cost = chunk_tail_cost(pl.tail_strips, pl.cblocks, P, pl.grid, L);
-    // (the kernel counts the tail's rows in 32 bits)
-    if (cost > 0 && cost < best_cost && total + L + pl.grid < (int64_t(1) << 31))
+    // Chunks cost DRAM re-reads bands do not: the two halo columns a strip
+    // shares with each column-strip neighbour are read from L2 by both while
+    // both run the same rows at the same time; chunks run neighbours' rows
+    // at different times, so those columns come from DRAM twice (+8 % reads
+    // at 8 x 224 x 336 x 256, ncu).  So chunks are taken only when they leave
+    // the busiest CTA at least 1/16 fewer rows.  (The kernel counts the
+    // tail's rows in 32 bits.)
+    if (cost > 0 && cost + cost / 16 < best_cost && total + L + pl.grid < (int64_t(1) << 31))
       pl.tail_chunk_rows = int(L);
   }
   pl.smem = size_t(n_stage) * pl.stage_rows * tdc::kRowBytes + 128;
+  return pl;
+}
+
+// A few recent results of a pure host computation, per host thread: the
+// launch plan (a few microseconds of integer work) and the TMA descriptor
+// are the same for every call on the same shapes and pointers, and on small
+// problems they would otherwise be a visible part of the call.  Keys hold
+// every input, so an entry is never stale.
+template <class Key, class Value, int kEntries>
+struct RecentCache {
+  Key keys[kEntries];
+  Value values[kEntries];
+  bool used[kEntries] = {};
+  int next = 0;
+  const Value* find(const Key& k) const {
+    for (int i = 0; i < kEntries; ++i)
+      if (used[i] && std::memcmp(&keys[i], &k, sizeof(Key)) == 0) return &values[i];
+    return nullptr;
+  }
+  void put(const Key& k, const Value& v) {
+    keys[next] = k;
+    values[next] = v;
+    used[next] = true;
+    next = (next + 1) % kEntries;
+  }
+};
+
+struct PlanKey {
+  int64_t N, P, Q, C, n_stage, sms, ctas_per_sm, chunk_tail;
+};
+
+WsPlan make_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int64_t n_stage, int64_t sms,
+                 int64_t ctas_per_sm, bool chunk_tail = false) {
+  thread_local RecentCache<PlanKey, WsPlan, 8> cache;
+  PlanKey k;
+  std::memset(&k, 0, sizeof(k));
+  k = PlanKey{N, P, Q, C, n_stage, sms, ctas_per_sm, chunk_tail ? 1 : 0};
+  if (const WsPlan* hit = cache.find(k)) return *hit;
+  const WsPlan pl = compute_plan(N, P, Q, C, n_stage, sms, ctas_per_sm, chunk_tail);
+  cache.put(k, pl);
   return pl;
 }
 
@@ -328,8 +374,38 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // box (64 ch, box_cols columns, box_rows rows, 1 image); out-of-bounds
 // elements read 0.  Stores the CUresult of a failed encode for
 // tdc_last_cuda_error.
+struct MapKey {
+  const void* t;
+  int64_t N, H, W, C, box_cols, box_rows, dt;
+};
+struct alignas(64) MapValue {
+  CUtensorMap map;
+};
+
+int encode_nhwc_map_uncached(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W,
+                             int64_t C, int box_cols, int box_rows, int dt);
+
 int encode_nhwc_map(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W, int64_t C,
                     int box_cols, int box_rows, int dt = kF16) {
+  thread_local RecentCache<MapKey, MapValue, 8> cache;
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k = MapKey{t, N, H, W, C, box_cols, box_rows, dt};
+  if (const MapValue* hit = cache.find(k)) {
+    *map = hit->map;
+    return TDC_OK;
+  }
+  const int rc = encode_nhwc_map_uncached(map, t, N, H, W, C, box_cols, box_rows, dt);
+  if (rc == TDC_OK) {
+    MapValue v;
+    v.map = *map;
+    cache.put(k, v);
+  }
+  return rc;
+}
+
+int encode_nhwc_map_uncached(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W,
+                             int64_t C, int box_cols, int box_rows, int dt) {
   auto fn = get_encode_fn();
   if (!fn) return TDC_ERR_TMA_ENCODE;
   const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
