@@ -423,7 +423,32 @@ def _comparisons(args, ref_ext, x, w, pad, C, stream, dev, iters: int) -> dict:
     return {k: round(v, 2) for k, v in out.items()}
 
 
-def _time_workload(T, wl, n0, n1, dev, stream, n_stage, iters, warmup, rotate: int = 1):
+def _graph_us(fn, iters: int, stream) -> float | None:
+    """µs per call of `iters` calls of fn captured in one CUDA graph and
+    replayed: the device time of back-to-back calls without the host's launch
+    path (Python, binding, C ABI, launch), which small problems can fall below."""
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        us = _cuda_time(g.replay, 5, stream) / 5 * 1e3 / iters
+        del g
+        return us
+    except Exception:  # reported only
+        return None
+
+
+def _time_workload(T, wl, n0, n1, dev, stream, n_stage, iters, warmup, rotate: int = 1,
+                   graph: bool = False):
     """µs per call of dwconv_ws on images [n0, n1) of wl (max over ranks), the
     output of the last call, and the inputs.  `rotate` > 1 cycles through that
     many input/output copies (L2-cold inputs for workloads smaller than L2)."""
@@ -442,6 +467,8 @@ def _time_workload(T, wl, n0, n1, dev, stream, n_stage, iters, warmup, rotate: i
         f()
     us = tdc_dist.max_over_ranks(_cuda_time(f, iters, stream), dev) / iters * 1e3
     y = ys[(k[0] - 1) % rotate]
+    if graph:
+        return us, x, w, y, _graph_us(f, iters, stream)
     return us, x, w, y
 
 
@@ -563,11 +590,16 @@ def run_tdc(args, wl) -> None:
         per = {}
         for name in PER_CONFIG:
             pwl = WORKLOADS[name]
-            us, xp, wp, yp = _time_workload(T, pwl, 0, pwl.N, dev, stream, args.n_stage, 100, 10)
+            small = pwl.bytes_per_call() < 1e9
+            timed = _time_workload(T, pwl, 0, pwl.N, dev, stream, args.n_stage, 100, 10, graph=small)
+            us, xp, wp, yp = timed[:4]
             nbytes = pwl.bytes_per_call()
             ent = {"us_per_call": round(us, 2), "value": round(nbytes / (us * 1e-6) / 1e9, 2),
                    "unit": "GB/s", "frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4),
                    "method": "10 warm-up + 100 back-to-back calls (reference tests/bench.py:18-29)"}
+            if small and timed[4] is not None:
+                ent["us_per_call_graph"] = round(timed[4], 2)
+                ent["graph"] = "the same 100 calls captured in one CUDA graph and replayed (device time)"
             if nbytes * 2 < 126e6:
                 ent["l2"] = "hot: the same buffers every call (inputs and outputs fit in L2)"
                 us_r, _, _, _ = _time_workload(T, pwl, 0, pwl.N, dev, stream, args.n_stage, 100, 10,

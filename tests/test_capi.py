@@ -675,6 +675,59 @@ def test_plain_threads_cover_every_output_once(K, N, P, Q, Cc, band_rows):
     assert len(seen) == N * P * Q * (Cc // 2)
 
 
+def dilated_threads(N, P, Q, Cc, K, D, band_rows):
+    """Restates dwconv_plain_kernel's thread decomposition with dilation D
+    (PlainParams dil / phases): (pair, column group, chunk, band, phase,
+    image); a thread of phase (pa, pb) owns output rows pa + D*(p0 + o) and
+    columns pb + D*(q0 + m).  Yields (n, pa, pb, p0, rows, q0, n_valid, cp)
+    for the threads that have work."""
+    cpairs = Cc // 2
+    clog = 3 if cpairs % 8 == 0 else 2
+    chunks = cpairs >> clog
+    QT = plain_cols(K)
+    Pp, Qp = -(-P // D), -(-Q // D)
+    qgroups = -(-Qp // QT)
+    bands = -(-Pp // band_rows)
+    total = N * D * D * bands * chunks * qgroups * (1 << clog)
+    for t in range(total):
+        r = t >> clog
+        qg = r % qgroups; r //= qgroups
+        chunk = r % chunks; r //= chunks
+        band = r % bands; r //= bands
+        ph, n = r % (D * D), r // (D * D)
+        pa, pb = divmod(ph, D)
+        cp = (chunk << clog) + (t & ((1 << clog) - 1))
+        p0, q0 = band * band_rows, qg * QT
+        rows = min(band_rows, -(-(P - pa) // D) - p0)
+        n_valid = min(QT, -(-(Q - pb) // D) - q0)
+        if rows <= 0 or n_valid <= 0:
+            continue
+        yield n, pa, pb, p0, rows, q0, n_valid, cp
+
+
+@pytest.mark.parametrize("K,S", [(3, 1), (5, 1), (5, 2), (7, 2)])
+@pytest.mark.parametrize("D", [1, 2, 3, 4])
+@pytest.mark.parametrize("N,P,Q,Cc,band_rows", [(2, 7, 9, 16, 2), (1, 10, 5, 24, 3), (1, 3, 17, 8, 4)])
+def test_dilated_threads_cover_every_output_once(K, S, D, N, P, Q, Cc, band_rows):
+    pad = 2
+    seen = set()
+    for n, pa, pb, p0, rows, q0, n_valid, cp in dilated_threads(N, P, Q, Cc, K, D, band_rows):
+        h0 = S * (pa + D * p0) - pad
+        w0 = S * (pb + D * q0) - pad
+        for o in range(rows):
+            p_ = pa + D * (p0 + o)
+            for r in range(K):  # window row S*o + r of the thread reads input row h0 + D*(S*o + r)
+                assert h0 + D * (S * o + r) == S * p_ + D * r - pad
+            for m in range(n_valid):
+                q_ = pb + D * (q0 + m)
+                for s_ in range(K):
+                    assert w0 + D * (S * m + s_) == S * q_ + D * s_ - pad
+                key = (n, p_, q_, cp)
+                assert 0 <= p_ < P and 0 <= q_ < Q and key not in seen
+                seen.add(key)
+    assert len(seen) == N * P * Q * (Cc // 2)
+
+
 @pytest.mark.parametrize("K,S", [(3, 1), (3, 2), (5, 1), (5, 2), (7, 1), (7, 2)])
 def test_plain_row_loop_feeds_each_output_its_taps_in_order(K, S):
     """Replays the kernel's row loop (unrolled by L = S * ceil(K/S) rows) for

@@ -797,6 +797,8 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   prm.pad_w = int32_t(pd.left);
   prm.act = epi.act;
   prm.flip_taps = epi.flip_taps ? 1 : 0;
+  prm.dil = 1;
+  prm.phases = 1;
   const bool with_epilogue =
       epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
   const int64_t grid = (total + tdc::kPlainThreads - 1) / tdc::kPlainThreads;
@@ -805,24 +807,8 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 
-// Dilated forward (tdc_plain.cuh): one kernel per (element type, K, epilogue).
-using DilatedLaunchFn = cudaError_t (*)(const tdc::PlainParams&, int32_t, int32_t, int64_t,
-                                        cudaStream_t);
-
-template <int K, class E, bool EPI>
-cudaError_t dilated_launch_t(const tdc::PlainParams& prm, int32_t S, int32_t D, int64_t grid,
-                             cudaStream_t st) {
-  return launch_pdl_block(&tdc::dwconv_dilated_kernel<K, E, EPI>, grid,
-                          unsigned(tdc::kPlainThreads), 0, st, prm, S, D);
-}
-
-#define TDC_DIL_K(E, K) {dilated_launch_t<K, E, false>, dilated_launch_t<K, E, true>}
-#define TDC_DIL_TABLE(E) {TDC_DIL_K(E, 3), TDC_DIL_K(E, 5), TDC_DIL_K(E, 7)}
-// [element type][K index: 3, 5, 7][epilogue]
-const DilatedLaunchFn kDilatedLaunch[2][3][2] = {TDC_DIL_TABLE(tdc::F16), TDC_DIL_TABLE(tdc::BF16)};
-#undef TDC_DIL_TABLE
-#undef TDC_DIL_K
-
+// Dilated forward: the plain kernel on the D*D phases of the output (see
+// PlainParams::dil).
 int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
                 int64_t C, int64_t K, int64_t S, int64_t D, const Pad4& pd, const Epilogue& epi,
                 void* stream, int dt) {
@@ -839,10 +825,13 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   const int64_t Ke = D * (K - 1) + 1;  // the dilated kernel's extent
   if (H + pd.top + pd.bottom < Ke || W + pd.left + pd.right < Ke) return TDC_ERR_BAD_SHAPE;
   const int64_t P = (H + pd.top + pd.bottom - Ke) / S + 1, Q = (W + pd.left + pd.right - Ke) / S + 1;
-  // 32-bit row / column arithmetic in the kernel (S * p + D * r - pad) and
-  // 32-bit column offsets in pairs
-  if (S * P + D * K + pd.top > i32 || S * Q + D * K + pd.left > i32) return TDC_ERR_TOO_LARGE;
-  if (W * (C / 2) > i32) return TDC_ERR_TOO_LARGE;  // column offsets of loaded taps
+  // 32-bit row / column arithmetic in the kernel: a thread's first input row
+  // S * (phase + D * p0) - pad plus D * (its window rows), likewise columns
+  // with S * plain_cols(K) - S + K window columns.
+  if (S * P + D * (S + K) + pd.top > i32 ||
+      S * Q + D * (S * tdc::plain_cols(int(K)) + K) + pd.left > i32)
+    return TDC_ERR_TOO_LARGE;
+  if (H * W > i32 || H * W * (C / 2) > i32) return TDC_ERR_TOO_LARGE;  // 32-bit image offsets
   if (N == 0 || C == 0) return TDC_OK;
   if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
@@ -853,18 +842,15 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   if (rc != TDC_OK) return rc;
   const int64_t cpairs = C / 2;
   const int chunk_log2 = cpairs % 8 == 0 ? 3 : 2;
-  const int64_t qgroups = (Q + tdc::kDilatedCols - 1) / tdc::kDilatedCols;
-  if (N * qgroups > i32 || N * qgroups * cpairs > i32) return TDC_ERR_TOO_LARGE;
-  // Rows per thread: with no sliding window a row shares nothing with the
-  // next but the K*K weights, so bands are cut down to about 8192 threads
-  // per SM (four waves at 64-128 registers); at 384 per SM, 8 x 32 x 32 x 672
-  // 5x5 dilation 2 ran 82 us.
-  const int64_t per_band = std::max<int64_t>(1, N * qgroups * cpairs);
-  const int64_t bands0 = std::min<int64_t>(
-      P, std::max<int64_t>(1, (8192 * std::max<int64_t>(1, dev->sms) + per_band - 1) / per_band));
-  const int64_t rows = (P + bands0 - 1) / bands0;
-  const int64_t bands = (P + rows - 1) / rows;
-  const int64_t total = N * qgroups * cpairs * bands;
+  // The largest phase: ceil(P / D) rows, ceil(Q / D) columns; D*D phases
+  // per image.
+  const int64_t Pp = (P + D - 1) / D, Qp = (Q + D - 1) / D;
+  const int64_t qgroups = (Qp + tdc::plain_cols(int(K)) - 1) / tdc::plain_cols(int(K));
+  if (N * D * D > i32 || N * D * D * qgroups > i32 || N * D * D * qgroups * cpairs > i32)
+    return TDC_ERR_TOO_LARGE;
+  const int64_t rows = plain_band_rows(N * D * D, Pp, Qp, C, K, dev->sms);
+  const int64_t bands = (Pp + rows - 1) / rows;
+  const int64_t total = N * D * D * qgroups * cpairs * bands;
   if (total > 0xffffffffll - tdc::kPlainThreads) return TDC_ERR_TOO_LARGE;
   tdc::PlainParams prm{};
   prm.x = static_cast<const uint32_t*>(x);
@@ -883,11 +869,12 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   prm.pad = int32_t(pd.top);
   prm.pad_w = int32_t(pd.left);
   prm.act = epi.act;
+  prm.dil = int32_t(D);
+  prm.phases = int32_t(D * D);
   const bool with_epilogue =
       epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
-  const cudaError_t e = kDilatedLaunch[dt][K / 2 - 1][with_epilogue ? 1 : 0](
-      prm, int32_t(S), int32_t(D), (total + tdc::kPlainThreads - 1) / tdc::kPlainThreads,
-      static_cast<cudaStream_t>(stream));
+  const cudaError_t e = kPlainLaunch[dt][K / 2 - 1][S - 1][with_epilogue ? 1 : 0](
+      prm, (total + tdc::kPlainThreads - 1) / tdc::kPlainThreads, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TDC_OK : cuda_fail(e);
 }
 

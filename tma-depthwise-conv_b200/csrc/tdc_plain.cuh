@@ -20,6 +20,15 @@
 // order, the fused epilogue t = acc (+ bias) -> act -> (+ residual), one
 // rounding.  The result is therefore bit-identical to the ws kernels and the
 // oracle.
+//
+// Dilation (PlainParams::dil = D > 1, the atrous layers of segmentation
+// backbones) runs on the same kernel: output rows and columns are split into
+// the D*D phases (p mod D, q mod D); within a phase the outputs D apart read
+// inputs D apart, i.e. an undilated problem on the D-strided sub-lattice of
+// x, so a thread owns outputs D apart and its window steps D rows and columns
+// at a time.  Each input element is then loaded once per thread window, as at
+// D = 1, instead of once per tap (K*K loads per output, the first dilated
+// kernel's scheme).
 #pragma once
 
 #include "tdc_kernels.cuh"
@@ -50,6 +59,15 @@ struct PlainParams {
   int32_t pad_w;             // column offset (left padding), likewise
   int32_t act;
   int32_t flip_taps;         // taps w[K-1-r][K-1-s] (data gradient of the stride-1 forward)
+  // Dilation D (>= 1; 0 reads as 1): tap (r, s) of output (p, q) reads input
+  // (S*p + D*r - pad, S*q + D*s - pad_w).  The outputs split into D*D phases
+  // (p mod D, q mod D); on each, the outputs D apart read inputs D apart, an
+  // undilated K x K stride-S problem on the D-strided sub-lattice of x, so a
+  // thread's outputs are D apart and its sliding window steps D rows and
+  // columns at a time.  bands / qgroups count the largest phase's
+  // ceil(P/D) rows and ceil(Q/D) columns; phases = D*D threads' worth of them.
+  int32_t dil;
+  int32_t phases;
 };
 
 template <int K, int S, class E, bool EPI>
@@ -66,16 +84,21 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
   uint32_t r_ = t >> p.chunk_log2;
   const int qg = int(r_ % uint32_t(p.qgroups));   r_ /= uint32_t(p.qgroups);
   const int chunk = int(r_ % uint32_t(p.chunks)); r_ /= uint32_t(p.chunks);
-  const int band = int(r_ % uint32_t(p.bands));
-  const int n = int(r_ / uint32_t(p.bands));
+  const int band = int(r_ % uint32_t(p.bands));   r_ /= uint32_t(p.bands);
+  const int D = p.dil > 1 ? p.dil : 1;
+  const uint32_t phases = p.phases > 1 ? uint32_t(p.phases) : 1u;
+  const int ph = int(r_ % phases);
+  const int n = int(r_ / phases);
+  const int pa = ph / D, pb = ph - pa * D;  // this thread's output row / column phase
   const int cp = (chunk << p.chunk_log2) + int(t & cmask);
-  const int p0 = band * p.band_rows;
-  const int rows = min(p.band_rows, p.P - p0);
+  const int p0 = band * p.band_rows;      // in rows of the phase
+  const int rows = min(p.band_rows, (p.P - pa + D - 1) / D - p0);
+  const int q0 = qg * QT;                 // in columns of the phase
+  const int n_valid = min(QT, (p.Q - pb + D - 1) / D - q0);  // output columns of this thread
+  if (rows <= 0 || n_valid <= 0) return;  // a phase smaller than the largest (D > 1 only)
   const int n_in = S * (rows - 1) + K;
-  const int q0 = qg * QT;
-  const int n_valid = min(QT, p.Q - q0);  // output columns of this thread
-  const int h0 = S * p0 - p.pad;          // input row of band row 0
-  const int w0 = S * q0 - p.pad_w;        // input column of input j = 0
+  const int h0 = S * (pa + D * p0) - p.pad;    // input row of band row 0
+  const int w0 = S * (pb + D * q0) - p.pad_w;  // input column of input j = 0
 
   uint32_t wt[K * K];
 #pragma unroll
@@ -85,26 +108,29 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
   if constexpr (EPI) {
     if (p.bias != nullptr) unpack2<E>(__ldg(p.bias + cp), b0, b1);
   }
-  uint32_t col_ok = 0;  // bit j: input column w0 + j is inside the image
+  uint32_t col_ok = 0;  // bit j: input column w0 + D*j is inside the image
 #pragma unroll
-  for (int j = 0; j < NI; ++j) col_ok |= (unsigned(w0 + j) < unsigned(p.W) ? 1u : 0u) << j;
+  for (int j = 0; j < NI; ++j) col_ok |= (unsigned(w0 + D * j) < unsigned(p.W) ? 1u : 0u) << j;
 
   // Offsets within one image are 32-bit (the host checks H * W * C / 2 < 2^31).
   const uint32_t* xn = p.x + int64_t(n) * p.H * p.W * p.cpairs + cp;
-  const int64_t y_row = int64_t(p.Q) * p.cpairs;
-  const int64_t y_off = (int64_t(n) * p.P + p0) * y_row + int64_t(q0) * p.cpairs + cp;
+  const uint32_t x_col = uint32_t(D * p.cpairs);           // between this thread's input columns
+  const int64_t y_col = int64_t(D) * p.cpairs;             // ... and output columns
+  const int64_t y_row = int64_t(D) * p.Q * p.cpairs;       // ... and output rows
+  const int64_t y_off = (int64_t(n) * p.P + pa + int64_t(D) * p0) * p.Q * p.cpairs +
+                        (pb + int64_t(D) * q0) * p.cpairs + cp;
 
   // The NI pairs of band input row i (zero outside the image).  The row test
   // is the same for every thread of a band; a column's offset is the
-  // previous one plus C / 2.
+  // previous one plus D * C / 2.
   auto load_row = [&](int i, uint32_t (&v)[NI]) {
-    const int h = h0 + i;
+    const int h = h0 + D * i;
     if (unsigned(h) < unsigned(p.H)) {
       uint32_t off = uint32_t((h * p.W + w0) * p.cpairs);  // wraps below 0; used only when inside
 #pragma unroll
       for (int j = 0; j < NI; ++j) {
         v[j] = ((col_ok >> j) & 1u) ? __ldg(xn + off) : 0u;
-        off += uint32_t(p.cpairs);
+        off += x_col;
       }
     } else {
 #pragma unroll
@@ -117,7 +143,7 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
     for (int m = 0; m < QT; ++m) {
       if (m >= n_valid) continue;
       float a0 = a[m][0], a1 = a[m][1];
-      const int64_t off = y_off + int64_t(o) * y_row + int64_t(m) * p.cpairs;
+      const int64_t off = y_off + int64_t(o) * y_row + int64_t(m) * y_col;
       if constexpr (EPI) {
         if (p.bias != nullptr) { a0 += b0; a1 += b1; }
         a0 = apply_act(a0, p.act);
@@ -168,105 +194,6 @@ __global__ void __launch_bounds__(kPlainThreads) dwconv_plain_kernel(PlainParams
     unroll_steps<L>([&](auto u_tag) {
       if (i0 + decltype(u_tag)::value < n_in) step(i0, u_tag);
     });
-  }
-}
-
-// ============================================================================
-// Dilated forward (K = 3, 5, 7, stride 1 or 2, dilation D >= 1, per-side
-// padding): y[n,p,q,c] = epilogue(chain_{r,s} x[n, S*p + D*r - pad,
-// S*q + D*s - pad_w, c] * w[r,s,c]).  A dilation known only at run time
-// leaves no compile-time window for the sliding scheme above, so a thread
-// computes kDilatedCols output columns of one channel pair row by row, each
-// output's K*K taps loaded through L1 (the K*K weights in registers); per
-// output the fp32 chain runs in (r, s) order from +0 with the plain kernel's
-// epilogue and rounding, so the result is the same arithmetic as the oracle's
-// on the zero-inflated K' = D*(K-1)+1 kernel.  Threads are dealt as in the
-// plain kernel (PlainParams.qgroups counts groups of kDilatedCols columns).
-// ============================================================================
-constexpr int kDilatedCols = 4;
-
-template <int K, class E, bool EPI>
-__global__ void __launch_bounds__(kPlainThreads) dwconv_dilated_kernel(PlainParams p,
-                                                                       int32_t S, int32_t D) {
-  constexpr int QT = kDilatedCols;
-  griddep_wait();
-  const uint32_t t = blockIdx.x * uint32_t(kPlainThreads) + threadIdx.x;
-  if (t >= p.total) return;
-  const uint32_t cmask = (1u << p.chunk_log2) - 1u;
-  uint32_t r_ = t >> p.chunk_log2;
-  const int qg = int(r_ % uint32_t(p.qgroups));   r_ /= uint32_t(p.qgroups);
-  const int chunk = int(r_ % uint32_t(p.chunks)); r_ /= uint32_t(p.chunks);
-  const int band = int(r_ % uint32_t(p.bands));
-  const int n = int(r_ / uint32_t(p.bands));
-  const int cp = (chunk << p.chunk_log2) + int(t & cmask);
-  const int p0 = band * p.band_rows;
-  const int rows = min(p.band_rows, p.P - p0);
-  const int q0 = qg * QT;
-  const int n_valid = min(QT, p.Q - q0);
-
-  uint32_t wt[K * K];
-#pragma unroll
-  for (int k = 0; k < K * K; ++k) wt[k] = __ldg(p.w + int64_t(k) * p.cpairs + cp);
-  float b0 = 0.f, b1 = 0.f;
-  if constexpr (EPI) {
-    if (p.bias != nullptr) unpack2<E>(__ldg(p.bias + cp), b0, b1);
-  }
-  // Input column of output column m, tap s: S*(q0 + m) - pad_w + D*s; its
-  // offset in pairs (32-bit: the host checks W * C / 2 < 2^31) and whether it lies
-  // inside the image, computed once (the per-load arithmetic was ~15
-  // instructions a tap before).
-  static_assert(K * QT <= 32, "column mask");
-  int32_t coff[K][QT];
-  uint32_t colmask = 0;
-#pragma unroll
-  for (int s = 0; s < K; ++s) {
-#pragma unroll
-    for (int m = 0; m < QT; ++m) {
-      const int col = S * (q0 + m) - p.pad_w + D * s;
-      coff[s][m] = int32_t(int64_t(col) * p.cpairs);  // used only when 0 <= col < W
-      colmask |= (unsigned(col) < unsigned(p.W) ? 1u : 0u) << (s * QT + m);
-    }
-  }
-  const uint32_t* xn = p.x + int64_t(n) * p.H * p.W * p.cpairs + cp;
-  const int64_t y_row = int64_t(p.Q) * p.cpairs;
-  const int64_t y_off = (int64_t(n) * p.P + p0) * y_row + int64_t(q0) * p.cpairs + cp;
-
-  for (int o = 0; o < rows; ++o) {
-    float acc[QT][2];
-#pragma unroll
-    for (int m = 0; m < QT; ++m) { acc[m][0] = 0.f; acc[m][1] = 0.f; }
-#pragma unroll
-    for (int r = 0; r < K; ++r) {
-      const int h = S * (p0 + o) + D * r - p.pad;
-      if (unsigned(h) >= unsigned(p.H)) continue;  // a row of zero products
-      const uint32_t* xr = xn + int64_t(h) * p.W * p.cpairs;
-#pragma unroll
-      for (int s = 0; s < K; ++s) {
-#pragma unroll
-        for (int m = 0; m < QT; ++m) {
-          const uint32_t v = ((colmask >> (s * QT + m)) & 1u) ? __ldg(xr + coff[s][m]) : 0u;
-          fma2<E>(v, wt[r * K + s], acc[m][0], acc[m][1]);
-        }
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < QT; ++m) {
-      if (m >= n_valid) continue;
-      float a0 = acc[m][0], a1 = acc[m][1];
-      const int64_t off = y_off + int64_t(o) * y_row + int64_t(m) * p.cpairs;
-      if constexpr (EPI) {
-        if (p.bias != nullptr) { a0 += b0; a1 += b1; }
-        a0 = apply_act(a0, p.act);
-        a1 = apply_act(a1, p.act);
-        if (p.residual != nullptr) {
-          float r0, r1;
-          unpack2<E>(__ldg(p.residual + off), r0, r1);
-          a0 += r0;
-          a1 += r1;
-        }
-      }
-      p.y[off] = pack2_rn<E>(a0, a1);
-    }
   }
 }
 

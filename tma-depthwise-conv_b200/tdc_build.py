@@ -51,12 +51,21 @@ def _deps(*names: str) -> list[str]:
     return [os.path.join(CSRC, n) for n in names] + hdrs + [os.path.join(INCLUDE, "tdc_dwconv.h")]
 
 
+def _tmp(path: str) -> str:
+    """A temporary name beside `path`: a binary is written there and renamed
+    into place, so no reader ever sees a partly written file."""
+    d, f = os.path.split(path)
+    return os.path.join(d, f".{f}.{os.getpid()}.tmp")
+
+
 def build_lib(force: bool = False) -> str:
     deps = _deps("tdc_capi.cu")
     if force or _stale(LIB, deps):
         nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+        tmp = _tmp(LIB)
         out = _run([nvcc, *NVCC_FLAGS, "-shared", f"-I{INCLUDE}", f"-I{CSRC}",
-                    os.path.join(CSRC, "tdc_capi.cu"), "-o", LIB])
+                    os.path.join(CSRC, "tdc_capi.cu"), "-o", tmp])
+        os.replace(tmp, LIB)
         with open(os.path.join(HERE, "libtdc_sm100.ptxas.txt"), "w") as f:
             f.write("\n".join(l for l in out.splitlines() if "ptxas" in l or "spill" in l) + "\n")
     return LIB
@@ -72,12 +81,13 @@ def build_ext(force: bool = False) -> str:
         cmd = ["g++", "-shared", "-fPIC", "-O2", "-std=c++17",
                "-DTORCH_EXTENSION_NAME=_tma_dwconv_C", "-DTORCH_API_INCLUDE_EXTENSION_H",
                f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
-               *[f"-I{i}" for i in incs], os.path.join(CSRC, "bindings.cpp"), "-o", EXT,
+               *[f"-I{i}" for i in incs], os.path.join(CSRC, "bindings.cpp"), "-o", _tmp(EXT),
                f"-L{HERE}", "-ltdc_sm100", "-Wl,-rpath,$ORIGIN",
                *[f"-L{d}" for d in libdirs],
                "-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python", "-lc10_cuda", "-ltorch_cuda",
                "-lcudart"]
         _run(cmd)
+        os.replace(_tmp(EXT), EXT)
     return EXT
 
 
