@@ -447,8 +447,22 @@ def _graph_us(fn, iters: int, stream) -> float | None:
         return None
 
 
+def _device_warmup(fn, seconds: float) -> int:
+    """Calls fn for `seconds` (synchronising every 4 calls); returns the count.
+    In a fresh process, or after a fifth of a second idle, the GPU runs the
+    first ~0.1 s of calls 5-10 % slower than the calls after them."""
+    t_end = time.perf_counter() + seconds
+    calls = 0
+    while time.perf_counter() < t_end:
+        for _ in range(4):
+            fn()
+        calls += 4
+        torch.cuda.synchronize()
+    return calls
+
+
 def _time_workload(T, wl, n0, n1, dev, stream, n_stage, iters, warmup, rotate: int = 1,
-                   graph: bool = False):
+                   graph: bool = False, device_warmup: float = 0.0):
     """µs per call of dwconv_ws on images [n0, n1) of wl (max over ranks), the
     output of the last call, and the inputs.  `rotate` > 1 cycles through that
     many input/output copies (L2-cold inputs for workloads smaller than L2)."""
@@ -463,6 +477,7 @@ def _time_workload(T, wl, n0, n1, dev, stream, n_stage, iters, warmup, rotate: i
         T.dwconv_ws_out(xs[i], w, ys[i], wl.pad, n_stage)
         k[0] += 1
 
+    _device_warmup(f, device_warmup)
     for _ in range(warmup):
         f()
     us = tdc_dist.max_over_ranks(_cuda_time(f, iters, stream), dev) / iters * 1e3
@@ -499,13 +514,7 @@ def run_tdc(args, wl) -> None:
     # 5-10 % slower than the calls after them (880 vs 790-820 µs per call,
     # measured call by call; the GPU's clocks ramp under sustained load), so
     # the timed steps follow `--device-warmup` seconds of the same calls.
-    t_end = time.perf_counter() + args.device_warmup
-    warm_calls = 0
-    while time.perf_counter() < t_end:
-        for _ in range(4):
-            step()
-        warm_calls += 4
-        torch.cuda.synchronize()
+    warm_calls = _device_warmup(step, args.device_warmup)
     for _ in range(max(args.warmup, 3)):
         y = step()
     torch.cuda.synchronize()
@@ -576,7 +585,8 @@ def run_tdc(args, wl) -> None:
         # other multi-GPU workloads
         if not weak_headline:
             us_w, xw, ww, yw = _time_workload(T, wl, rank * wl.N, (rank + 1) * wl.N, dev, stream,
-                                              args.n_stage, iters=10, warmup=3)
+                                              args.n_stage, iters=10, warmup=3,
+                                              device_warmup=args.device_warmup)
             tot = tdc_dist.sum_over_ranks(float(wl.bytes_per_call(wl.N)), dev)
             line["weak"] = {"images_per_rank": wl.N, "us_per_call": round(us_w, 2),
                             "value": round(tot / (us_w * 1e-6) / 1e9, 2), "unit": "GB/s"}
@@ -587,7 +597,8 @@ def run_tdc(args, wl) -> None:
             swl = WORKLOADS[name]
             s0, s1 = shard_range(swl.N, world, rank)
             iters = 100 if swl.bytes_per_call() < 1e9 else 30
-            us, xs, wsw, ys = _time_workload(T, swl, s0, s1, dev, stream, args.n_stage, iters, 10)
+            us, xs, wsw, ys = _time_workload(T, swl, s0, s1, dev, stream, args.n_stage, iters, 10,
+                                             device_warmup=args.device_warmup)
             ok = True
             if s1 > s0 and not args.no_cpu:
                 _, ok = _cpu_baseline_leg(swl, xs[-1:].cpu(), wsw.cpu(), ys[-1:], timed=False)
@@ -607,7 +618,8 @@ def run_tdc(args, wl) -> None:
         for name in PER_CONFIG:
             pwl = WORKLOADS[name]
             small = pwl.bytes_per_call() < 1e9
-            timed = _time_workload(T, pwl, 0, pwl.N, dev, stream, args.n_stage, 100, 10, graph=small)
+            timed = _time_workload(T, pwl, 0, pwl.N, dev, stream, args.n_stage, 100, 10, graph=small,
+                                   device_warmup=args.device_warmup)
             us, xp, wp, yp = timed[:4]
             nbytes = pwl.bytes_per_call()
             ent = {"us_per_call": round(us, 2), "value": round(nbytes / (us * 1e-6) / 1e9, 2),
@@ -619,7 +631,7 @@ def run_tdc(args, wl) -> None:
             if nbytes * 2 < 126e6:
                 ent["l2"] = "hot: the same buffers every call (inputs and outputs fit in L2)"
                 us_r, _, _, _ = _time_workload(T, pwl, 0, pwl.N, dev, stream, args.n_stage, 100, 10,
-                                               rotate=8)
+                                               rotate=8, device_warmup=args.device_warmup)
                 ent["us_per_call_l2_cold"] = round(us_r, 2)
                 ent["l2_cold"] = "8 rotating input/output sets (205 MB > L2)"
             else:
