@@ -232,15 +232,21 @@ struct WsPlan {
   int tail_chunk_rows;  // > 0: the tail is cut into chunks (SegmentIter), else bands
 };
 
-// Ring capacity in input rows per CTA, split evenly over the n_stage stages
-// (12 rows = 52 KB, so three CTAs of ~120 registers fit an SM with room to
-// spare).
+// Ring capacity in input rows per CTA, split evenly over the n_stage stages:
+// 12 rows (52 KB) of 3x3 stride-1 rows for the K x K geometries
+// (geom_stage_rows), 10 rows (43.5 KB) for 3x3 stride 1 itself.  At 3x3
+// stride 1 the 444 CTAs' stages in flight (up to 2 x 26 KB each with 6-row
+// stages) oversubscribe the memory system when the SMs run at full clock:
+// measured in alternating bursts on 64 x 224 x 336 x 256, 5-row stages take
+// 0.945 of the time of 6-row stages at 1965 MHz and 0.997 under the power
+// cap (1.6-1.8 GHz); 4-row stages 0.880 and 1.028.
 constexpr int kRingRows = 12;
+constexpr int kRingRows3x3 = 10;
 // A CTA is not given fewer output rows than this (each segment streams two
 // halo rows).
 constexpr int64_t kMinRowsPerCta = 8;
 
-int stage_rows_for(int64_t n_stage) { return std::max<int>(1, kRingRows / int(n_stage)); }
+int stage_rows_for(int64_t n_stage) { return std::max<int>(1, kRingRows3x3 / int(n_stage)); }
 
 // The weight-gradient ring carries x and dy rows (8448 B per row): 8 rows.
 constexpr int kWgradRingRows = 8;
@@ -616,6 +622,7 @@ int strip_in_cols(int K, int S) { return S * (tdc::kStripQ - 1) + K; }
 // stage leaves the producer room to run ahead (measured on the 7x7 and 5x5
 // kernels at 64 x 224 x 336 x 256: 3-8 % faster than the minimum).
 int geom_stage_rows(int K, int S, int64_t n_stage) {
+  if (K == 3 && S == 1) return stage_rows_for(n_stage);  // the ws kernel's ring
   const int ns = int(n_stage);
   const int row_bytes = strip_in_cols(K, S) * tdc::kBlockC * 2;
   const int ring_rows = std::max<int>(ns, (kRingRows * tdc::kRowBytes) / row_bytes);
