@@ -25,6 +25,9 @@
  * Return value: TDC_OK (0) or a negative TDC_ERR_* code.  Argument errors are
  * detected on the host before any CUDA call is made.  An empty output
  * (N, C, P or Q == 0) is a successful no-op and may come with NULL pointers.
+ * TDC_ERR_DEVICE_TIMEOUT from a call that launches work reports an EARLIER
+ * launch on the device that gave up on a pipeline wait (see "pipeline-wait
+ * failure detection" below); nothing was launched.
  */
 #ifndef TDC_DWCONV_H_
 #define TDC_DWCONV_H_
