@@ -79,8 +79,9 @@ TDC_API int tdc_last_cuda_error(void);
 TDC_API int tdc_output_hw(int64_t H, int64_t W, int64_t R, int64_t S, int64_t pad,
                           int64_t* P, int64_t* Q);
 
-/* Plain (non-TMA) kernel: direct 16-byte global loads, 8 channels per thread.
- * Requires C % 8 == 0.
+/* Plain (non-TMA) kernel: global loads through L1, no shared memory; a
+ * thread slides 8 output columns of one channel pair down a band of rows
+ * (the kernel of tdc_dwconv_fwd_plain).  Requires C % 8 == 0.
  * Replaces tma_dwconv::dwconv_v0 (csrc/bindings.cpp:6,
  * csrc/kernel_v0_naive_float4.cu:78-118), with y supplied by the caller. */
 TDC_API int tdc_dwconv_v0(const void* x, const void* w, void* y,

@@ -542,40 +542,6 @@ def test_bf16_entry_points_validate_like_fp16(lib):
                                                         i64(1), i64(2), C.byref(b)) == CODES["TDC_ERR_NO_DEVICE"]
 
 
-def v0_band_rows(N, P, Q, Cc, sms=148):
-    """Restates tdc_dwconv_v0's band height: up to 16 output rows per thread,
-    halved while the threads would not fill sms * 1024."""
-    band = min(16, P)
-    per_band = N * Q * (Cc // 8)
-    while band > 1 and per_band * (-(-P // band)) < sms * 1024:
-        band = (band + 1) // 2
-    return band
-
-
-@pytest.mark.parametrize("N,H,W,Cc,pad", SHAPES)
-def test_v0_bands_store_every_output_row_once(N, H, W, Cc, pad):
-    P = H + 2 * pad - 2
-    if P < 1:
-        return
-    band = v0_band_rows(N, P, W + 2 * pad - 2, Cc)
-    assert 1 <= band <= 16
-    stored = []
-    for b in range(-(-P // band)):
-        p0 = b * band
-        rows = min(band, P - p0)
-        # the kernel's loop: input row i of the band is tap row r of output i - r;
-        # output o is stored after its last tap row (r = 2)
-        for i in range(rows + 2):
-            for r in range(3):
-                o = i - r
-                if 0 <= o < rows and r == 2:
-                    stored.append(p0 + o)
-                # accumulator set of output o at input row i: (i mod 3 - r) mod 3 == o mod 3
-                if 0 <= o < rows:
-                    assert ((i % 3) - r) % 3 == o % 3
-    assert sorted(stored) == list(range(P))
-
-
 def test_plain_forward_argument_errors(lib):
     p = C.c_void_p
     def fwd(K=5, stride=2, C_=72, pad=2, H=16, act=0, band=0, N=2, x=16, f=None):

@@ -147,6 +147,23 @@ def test_v0_small_channel_counts(C):
     _assert_bits_equal(T.dwconv_v0(x, w, 1), oracle.dwconv_f16(x.cpu().numpy(), w.cpu().numpy(), 1))
 
 
+def test_v0_image_beyond_32bit_offsets():
+    # One image of 2^32 elements (8.6 GB): past the plain kernel's 32-bit
+    # offsets within an image, dwconv_v0 runs the general ring kernel; it
+    # must equal dwconv_ws (64-bit output offsets) bit for bit.
+    N, H, W, C = 1, 4096, 4096, 256
+    assert H * W * C // 2 > 2 ** 31 - 1
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.empty(N, H, W, C, device="cuda", dtype=torch.float16).uniform_(-1, 1, generator=g)
+    w = (torch.rand(3, 3, C, device="cuda", generator=g) * 2 / 3 - 1 / 3).half()
+    a = T.dwconv_v0(x, w, 1)
+    b = T.dwconv_ws(x, w, 1, 2)
+    del x
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    del a, b
+    torch.cuda.empty_cache()
+
+
 def test_empty_output_and_batch():
     x, w = _inputs(2, 2, 2, 64)
     assert T.dwconv_ws(x, w, pad=0).shape == (2, 0, 0, 64)

@@ -1510,24 +1510,20 @@ TDC_API int tdc_dwconv_v0(const void* x, const void* w, void* y, int64_t N, int6
   int rc = validate(x, w, y, N, H, W, C, R, S, pad, 8, &P, &Q, &empty);
   if (rc != TDC_OK) return rc;
   if (empty) return TDC_OK;
-  DeviceInfo* dev = nullptr;
-  rc = current_device(&dev, nullptr);
-  if (rc != TDC_OK) return rc;
-  // Bands of up to 16 output rows (the 2 halo rows re-read per band mostly
-  // hit L2), fewer when that leaves too few threads to fill the GPU.
-  int64_t band_rows = std::min<int64_t>(16, P);
-  const int64_t per_band = N * Q * (C / 8);
-  while (band_rows > 1 && per_band * ((P + band_rows - 1) / band_rows) < int64_t(dev->sms) * 1024)
-    band_rows = (band_rows + 1) / 2;
-  const int64_t bands = (P + band_rows - 1) / band_rows;
-  tdc::V0Params prm{N, H, W, C, P, Q, pad, C / 8, bands, band_rows, per_band * bands};
-  const int threads = 256;
-  const int64_t want = (prm.total + threads - 1) / threads;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(want, int64_t(dev->sms) * 32));
-  tdc::dwconv_v0_kernel<<<dim3(unsigned(blocks)), dim3(threads), 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(x), static_cast<const uint4*>(w), static_cast<uint4*>(y), prm);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+  // The plain kernel (no TMA, no shared memory, loads through L1): a thread
+  // slides 8 output columns of one channel pair down its band of rows.
+  // Measured against this call's first kernel (one 8-channel vector of one
+  // column per thread, 16-byte loads, 16-row bands) on the same B200, same
+  // bits: 64 x 224 x 336 x 256 1240 vs 1766 us, 32 x 224 x 336 x 256 693 vs
+  // 880, 16 x 112 x 224 x 128 62.0 vs 86.0, 8 x 56 x 56 x 256 10.3 vs 14.4.
+  rc = fwd_plain(x, w, y, N, H, W, C, 3, 1, pad, 0, Epilogue(), stream, kF16);
+  if (rc != TDC_ERR_TOO_LARGE) return rc;
+  // One image beyond the plain kernel's 32-bit offsets within an image
+  // (H * W * C / 2 >= 2^31, 8.6 GB of fp16): the general ring kernel, whose
+  // output offsets are 64-bit; the same arithmetic.
+  Epilogue epi;
+  epi.fused = true;
+  return ws_common(x, w, y, N, H, W, C, R, S, pad, 2, nullptr, false, -1, 0, stream, epi);
 }
 
 TDC_API int tdc_dwconv_ws(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,

@@ -34,107 +34,6 @@ __device__ __forceinline__ void unroll_steps(F&& f) {
 }
 
 // ============================================================================
-// Plain kernel (the `dwconv_v0` call): direct 16-byte global loads, no shared
-// memory, no TMA.  A thread owns one 8-channel vector of one output column
-// over a band of `band_rows` output rows and slides down it: each input row
-// of the band (plus the two halo rows) is loaded once, three 16-byte vectors
-// (columns q - pad .. q - pad + 2) issued one row ahead of their use, and fed
-// into the three output rows it is tap row r = 0, 1, 2 of; an output row is
-// rounded and stored (one 16-byte store) once its last tap row is in.
-// Accumulators rotate through three sets, the loop unrolled by three rows so
-// every set index is a compile-time constant.  Consecutive threads take
-// consecutive channel vectors, then columns, so a warp's loads and stores are
-// contiguous in NHWC memory.  Per output the chain is r-major, s-minor from
-// +0, as in the ws kernel.  64-bit index arithmetic; C % 8 == 0.
-// (Measured at 64 x 224 x 336 x 256: one thread per output vector with nine
-// loads, the first version, 2640 us; this kernel 1761 us; with 4-channel
-// vectors and two rows in flight 1973 us.)
-// ============================================================================
-struct V0Params {
-  int64_t N, H, W, C, P, Q, pad;
-  int64_t cvecs;       // C / 8
-  int64_t bands;       // ceil(P / band_rows)
-  int64_t band_rows;
-  int64_t total;       // N * bands * Q * cvecs threads of work
-};
-
-__device__ __forceinline__ void fma8_f16f32(const uint4& x, const uint4& w, float (&a)[8]) {
-  fma2_f16f32(x.x, w.x, a[0], a[1]);
-  fma2_f16f32(x.y, w.y, a[2], a[3]);
-  fma2_f16f32(x.z, w.z, a[4], a[5]);
-  fma2_f16f32(x.w, w.w, a[6], a[7]);
-}
-
-__global__ void __launch_bounds__(256) dwconv_v0_kernel(const uint4* __restrict__ x,
-                                                       const uint4* __restrict__ w,
-                                                       uint4* __restrict__ y, V0Params p) {
-  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < p.total;
-       t += int64_t(gridDim.x) * blockDim.x) {
-    int64_t r_ = t;
-    const int64_t cv = r_ % p.cvecs;  r_ /= p.cvecs;
-    const int64_t q  = r_ % p.Q;      r_ /= p.Q;
-    const int64_t b  = r_ % p.bands;
-    const int64_t n  = r_ / p.bands;
-    const int64_t p0 = b * p.band_rows;
-    const int rows = int(min(p.band_rows, p.P - p0));
-    uint4 wt[9];
-#pragma unroll
-    for (int k = 0; k < 9; ++k) wt[k] = __ldg(&w[k * p.cvecs + cv]);
-    float acc[3][8];
-    const int64_t w0 = q - p.pad;  // input column of tap s = 0
-    const uint4* xn = x + n * p.H * p.W * p.cvecs + cv;
-    uint4* yo = y + ((n * p.P + p0) * p.Q + q) * p.cvecs + cv;
-    const int64_t y_row = p.Q * p.cvecs;
-    // The three 16-byte vectors of input row i of the band (zero outside the image).
-    auto load_row = [&](int i, uint4 (&v)[3]) {
-      const int64_t h = p0 - p.pad + i;
-#pragma unroll
-      for (int s = 0; s < 3; ++s) {
-        const int64_t wi = w0 + s;
-        v[s] = make_uint4(0u, 0u, 0u, 0u);
-        if (h >= 0 && h < p.H && wi >= 0 && wi < p.W) v[s] = __ldg(xn + (h * p.W + wi) * p.cvecs);
-      }
-    };
-    uint4 xv[3], xnext[3];
-    load_row(0, xv);
-    // Input row i of the band (h = p0 - pad + i) is tap row r of output row
-    // i - r; U = i mod 3 fixes the accumulator sets at compile time.  Row
-    // i + 1 is loaded before row i is used, so its latency overlaps the FMAs.
-    auto step = [&](int i, auto u_tag) {
-      constexpr int U = decltype(u_tag)::value;
-      if (i + 1 < rows + 2) load_row(i + 1, xnext);
-#pragma unroll
-      for (int r = 0; r < 3; ++r) {
-        const int o = i - r;  // output row of the band this row is tap row r of
-        if (o < 0 || o >= rows) continue;
-        float (&a)[8] = acc[(U - r + 3) % 3];
-        if (r == 0) {
-#pragma unroll
-          for (int v = 0; v < 8; ++v) a[v] = 0.f;
-        }
-#pragma unroll
-        for (int s = 0; s < 3; ++s) fma8_f16f32(xv[s], wt[r * 3 + s], a);
-        if (r == 2) {
-          uint4 out;
-          out.x = pack_half2_rn(a[0], a[1]);
-          out.y = pack_half2_rn(a[2], a[3]);
-          out.z = pack_half2_rn(a[4], a[5]);
-          out.w = pack_half2_rn(a[6], a[7]);
-          yo[o * y_row] = out;
-        }
-      }
-#pragma unroll
-      for (int s = 0; s < 3; ++s) xv[s] = xnext[s];
-    };
-    for (int i0 = 0; i0 < rows + 2; i0 += 3) {
-      step(i0, std::integral_constant<int, 0>{});
-      if (i0 + 1 < rows + 2) step(i0 + 1, std::integral_constant<int, 1>{});
-      if (i0 + 2 < rows + 2) step(i0 + 2, std::integral_constant<int, 2>{});
-    }
-  }
-}
-
-// ============================================================================
 // TMA warp-specialised kernel (the `dwconv_ws` / `dwconv_ws_probe` calls).
 //
 // Work decomposition.  A strip is (image n, 32 output columns, 64-channel
