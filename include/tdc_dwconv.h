@@ -195,8 +195,15 @@ TDC_API int tdc_dwconv_fwd_asym_bf16(const void* x, const void* w, const void* b
  *   y[n,p,q,c] = epilogue(chain_{r,s} x[n, S*p + D*r - pad_top, S*q + D*s - pad_left, c] * w[r,s,c])
  * P = (H + pad_top + pad_bottom - D*(K-1) - 1)/S + 1, Q likewise; the same
  * fp32 chain, epilogue and rounding as tdc_dwconv_fwd (atrous depthwise layers,
- * e.g. DeepLab backbones).  dilation 1 is tdc_dwconv_fwd_asym with n_stage 0;
- * above 1 a plain kernel computes each output's K*K taps through L1.  No
+ * e.g. DeepLab backbones).  dilation 1 is tdc_dwconv_fwd_asym with n_stage 0.
+ * Above 1 the outputs split into the D*D phases (p mod D, q mod D); on each,
+ * outputs D apart read inputs D apart: an undilated K x K problem on the
+ * D-strided sub-lattice of x.  The ring (TMA) kernel runs the phases as
+ * extra images, its tensor map loading the sub-lattice with traversal
+ * stride D (while D * (32*S + K - S) <= 256); the plain kernel slides its
+ * window D rows and columns at a time.  The ring kernel runs when the phases
+ * are at least 32 x 32 outputs and the undilated choice of tdc_dwconv_fwd
+ * (n_stage 0) gives them to it (tdc_dwconv_fwd_dilated_uses_plain).  No
  * counterpart in the reference (no dilation). */
 TDC_API int tdc_dwconv_fwd_dilated(const void* x, const void* w, const void* bias,
                                    const void* residual, void* y,
@@ -210,6 +217,26 @@ TDC_API int tdc_dwconv_fwd_dilated_bf16(const void* x, const void* w, const void
                                         int64_t stride, int64_t dilation, int64_t pad_top,
                                         int64_t pad_bottom, int64_t pad_left, int64_t pad_right,
                                         int64_t act, void* stream);
+
+/* tdc_dwconv_fwd_dilated / _bf16 (bf16 != 0) with the kernel named:
+ * kernel 1 = the ring kernel, at the geometry's default ring depth
+ * (TDC_ERR_UNSUPPORTED for dilation 1 or when its tensor map cannot step
+ * `dilation` rows and columns), -1 = the plain kernel, 0 = chosen by shape
+ * (tdc_dwconv_fwd_dilated).  Every kernel gives the same result, bit for
+ * bit.  No counterpart in the reference. */
+TDC_API int tdc_dwconv_fwd_dilated_ex(const void* x, const void* w, const void* bias,
+                                      const void* residual, void* y,
+                                      int64_t N, int64_t H, int64_t W, int64_t C, int64_t K,
+                                      int64_t stride, int64_t dilation, int64_t pad_top,
+                                      int64_t pad_bottom, int64_t pad_left, int64_t pad_right,
+                                      int64_t act, int64_t kernel, int64_t bf16, void* stream);
+
+/* 1 if tdc_dwconv_fwd_dilated runs the plain kernel on this shape, else 0
+ * (pure host arithmetic).  No counterpart in the reference. */
+TDC_API int tdc_dwconv_fwd_dilated_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C,
+                                              int64_t K, int64_t stride, int64_t dilation,
+                                              int64_t pad_top, int64_t pad_bottom,
+                                              int64_t pad_left, int64_t pad_right);
 
 /* Plain K x K forward: global loads through L1, no TMA, no shared memory, no
  * pipeline.  A thread owns one channel pair of one output column over a band

@@ -10,6 +10,7 @@ import ctypes as C
 import os
 import re
 
+import numpy as np
 import pytest
 import torch
 
@@ -290,6 +291,55 @@ def test_kxk_plan_covers_every_output_once(lib, K, S, N, H, W, Cc, pad, ns):
                 assert (strip, r) not in seen
                 seen.add((strip, r))
     assert len(seen) == pl["strips"] * P
+
+
+@pytest.mark.parametrize("K,S,D", [(3, 1, 2), (3, 1, 3), (5, 1, 2), (3, 2, 2), (7, 2, 3), (7, 1, 4)])
+@pytest.mark.parametrize("N,P,Q,Cc", [(2, 41, 70, 64), (1, 29, 37, 200), (12, 96, 160, 256), (3, 7, 5, 8)])
+def test_dilated_ring_segments_cover_every_output_once(lib, K, S, D, N, P, Q, Cc):
+    """The ring kernel's dilated schedule: the plan of the N*D*D phase
+    sub-problems of the largest phase's ceil(P/D) x ceil(Q/D) outputs; a
+    segment of image n' is phase (a, b) = divmod(n' % D^2, D) of image
+    n' // D^2, its rows clipped to that phase's ceil((P - a)/D), its columns
+    to ceil((Q - b)/D); phase output (p', q') is y's (a + D*p', b + D*q').
+    Every output of y, per channel block, is written exactly once."""
+    Pp, Qp = -(-P // D), -(-Q // D)
+    H, W = S * (Pp - 1) + K, S * (Qp - 1) + K  # at pad 0 the sub-problem has Pp x Qp outputs
+    ns = 2 if (K, S) == (3, 1) else 4
+    pl = _fwd_plan(lib, N * D * D, H, W, Cc, K, S, 0, ns)
+    seen = np.zeros((N, P, Q, pl["cblocks"]), dtype=np.int32)
+    for g in range(pl["grid"]):
+        for strip, a, b in segments(pl, Pp, g):
+            cb = strip % pl["cblocks"]
+            qs = strip // pl["cblocks"] % pl["qstrips"]
+            nn = strip // pl["cblocks"] // pl["qstrips"]
+            n, ph = divmod(nn, D * D)
+            pa, pb = divmod(ph, D)
+            last = min(b, -(-(P - pa) // D))
+            qn = -(-(Q - pb) // D)
+            if last <= a:
+                continue  # a segment of a smaller phase left empty: skipped
+            for r in range(a, last):
+                for q in range(qs * 32, min(qs * 32 + 32, qn)):
+                    seen[n, pa + D * r, pb + D * q, cb] += 1
+    assert (seen == 1).all()
+
+
+def test_dilated_kernel_choice(lib):
+    """tdc_dwconv_fwd_dilated_uses_plain: the ring kernel for phases of at
+    least 32 x 32 outputs that the undilated choice gives it, while its map
+    can step D; the plain kernel otherwise."""
+    def plain(N, H, W, Cc, K, S, D):
+        pad = D * (K - 1) // 2
+        return lib.tdc_dwconv_fwd_dilated_uses_plain(i64(N), i64(H), i64(W), i64(Cc), i64(K), i64(S),
+                                                     i64(D), i64(pad), i64(pad), i64(pad), i64(pad))
+    assert plain(32, 128, 128, 256, 3, 1, 2) == 0
+    assert plain(16, 128, 128, 256, 3, 1, 4) == 0
+    assert plain(16, 112, 112, 384, 5, 1, 2) == 0
+    assert plain(8, 64, 64, 256, 3, 1, 2) == 0
+    assert plain(8, 64, 64, 256, 3, 1, 4) == 1     # 16 x 16 phases
+    assert plain(8, 32, 32, 960, 5, 1, 2) == 1     # DeepLab's layer: 16 x 16 phases
+    assert plain(8, 256, 256, 256, 3, 1, 8) == 1   # 34 columns x 8 > the map's 256
+    assert plain(8, 256, 256, 16, 3, 1, 2) == 1    # 16 of a strip's 64 channels
 
 
 def test_kxk_plan_of_3x3_stride_1_is_the_ws_plan(lib):

@@ -378,30 +378,38 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 // 4-D map over an NHWC fp16 tensor viewed as (C, W, H, N), innermost first;
 // box (64 ch, box_cols columns, box_rows rows, 1 image); out-of-bounds
-// elements read 0.  Stores the CUresult of a failed encode for
+// elements read 0.  With dil = D > 1 the columns and rows of the box are D
+// apart (traversal stride D: the map's box spans D * box_cols columns and
+// D * box_rows rows, of which the copy takes every D-th), so shared memory
+// receives the same dense box.  Stores the CUresult of a failed encode for
 // tdc_last_cuda_error.
+// Limits of a tiled tensor map: elements per box dimension and traversal
+// stride.
+constexpr int kMaxTmaBox = 256;
+constexpr int kMaxTmaStride = 8;
+
 struct MapKey {
   const void* t;
-  int64_t N, H, W, C, box_cols, box_rows, dt;
+  int64_t N, H, W, C, box_cols, box_rows, dt, dil;
 };
 struct alignas(64) MapValue {
   CUtensorMap map;
 };
 
 int encode_nhwc_map_uncached(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W,
-                             int64_t C, int box_cols, int box_rows, int dt);
+                             int64_t C, int box_cols, int box_rows, int dt, int dil);
 
 int encode_nhwc_map(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W, int64_t C,
-                    int box_cols, int box_rows, int dt = kF16) {
+                    int box_cols, int box_rows, int dt = kF16, int dil = 1) {
   thread_local RecentCache<MapKey, MapValue, 8> cache;
   MapKey k;
   std::memset(&k, 0, sizeof(k));
-  k = MapKey{t, N, H, W, C, box_cols, box_rows, dt};
+  k = MapKey{t, N, H, W, C, box_cols, box_rows, dt, dil};
   if (const MapValue* hit = cache.find(k)) {
     *map = hit->map;
     return TDC_OK;
   }
-  const int rc = encode_nhwc_map_uncached(map, t, N, H, W, C, box_cols, box_rows, dt);
+  const int rc = encode_nhwc_map_uncached(map, t, N, H, W, C, box_cols, box_rows, dt, dil);
   if (rc == TDC_OK) {
     MapValue v;
     v.map = *map;
@@ -411,14 +419,16 @@ int encode_nhwc_map(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64
 }
 
 int encode_nhwc_map_uncached(CUtensorMap* map, const void* t, int64_t N, int64_t H, int64_t W,
-                             int64_t C, int box_cols, int box_rows, int dt) {
+                             int64_t C, int box_cols, int box_rows, int dt, int dil) {
   auto fn = get_encode_fn();
   if (!fn) return TDC_ERR_TMA_ENCODE;
+  if (dil < 1 || dil > kMaxTmaStride || box_cols * dil > kMaxTmaBox || box_rows * dil > kMaxTmaBox)
+    return TDC_ERR_UNSUPPORTED;
   const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
   const cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(W) * C * 2, cuuint64_t(H) * W * C * 2};
-  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(box_cols), cuuint32_t(box_rows),
-                             1u};
-  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const cuuint32_t box[4] = {cuuint32_t(tdc::kBlockC), cuuint32_t(box_cols * dil),
+                             cuuint32_t(box_rows * dil), 1u};
+  const cuuint32_t estr[4] = {1u, cuuint32_t(dil), cuuint32_t(dil), 1u};
   CUresult r = fn(map, dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   4, const_cast<void*>(t), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -609,8 +619,44 @@ const GeomOccFn kGeomOcc[2][3][2][2][3] = {TDC_GEOM_TABLE(geom_occ_t, tdc::F16),
 #undef TDC_GEOM_MODES
 #undef TDC_GEOM_NS
 
+// Ring depth of the forward per geometry when the caller leaves it to the
+// library (n_stage = 0), measured at 64 x 224 x 336 x 256.
+constexpr int kFwdStages[3][2] = {{2, 4}, {4, 2}, {3, 4}};  // [K: 3, 5, 7][stride - 1]
+constexpr int fwd_stages_of(int K, int S) { return kFwdStages[K / 2 - 1][S - 1]; }
+
+// The dilated instantiations of the general forward (DIL = true), at the
+// geometry's default ring depth.
+template <int MODE, int K, int S, class E>
+cudaError_t dil_launch_t(const CUtensorMap& map, const tdc::WsParams& prm, int64_t grid,
+                         size_t smem, cudaStream_t st) {
+  return launch_pdl(&tdc::dwconv_ws_kernel<fwd_stages_of(K, S), false, MODE, K, S, E, true>, grid,
+                    smem, st, map, prm);
+}
+
+template <int MODE, int K, int S, class E>
+cudaError_t dil_occ_t(int* occ, size_t smem) {
+  auto* k = &tdc::dwconv_ws_kernel<fwd_stages_of(K, S), false, MODE, K, S, E, true>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
+}
+
+#define TDC_DIL_MODES(FN, E, K, S) {FN<tdc::kModeGeneral, K, S, E>, FN<tdc::kModeEpilogue, K, S, E>}
+#define TDC_DIL_TABLE(FN, E)                                              \
+  {{TDC_DIL_MODES(FN, E, 3, 1), TDC_DIL_MODES(FN, E, 3, 2)},               \
+   {TDC_DIL_MODES(FN, E, 5, 1), TDC_DIL_MODES(FN, E, 5, 2)},               \
+   {TDC_DIL_MODES(FN, E, 7, 1), TDC_DIL_MODES(FN, E, 7, 2)}}
+// [element type][K index: 3, 5, 7][stride - 1][mode: general, epilogue]
+const GeomLaunchFn kDilLaunch[2][3][2][2] = {TDC_DIL_TABLE(dil_launch_t, tdc::F16),
+                                             TDC_DIL_TABLE(dil_launch_t, tdc::BF16)};
+const GeomOccFn kDilOcc[2][3][2][2] = {TDC_DIL_TABLE(dil_occ_t, tdc::F16),
+                                       TDC_DIL_TABLE(dil_occ_t, tdc::BF16)};
+#undef TDC_DIL_TABLE
+#undef TDC_DIL_MODES
+
 std::mutex g_geom_mutex;
 int g_geom_occ[kMaxDevices][2][3][2][2][3] = {};  // 0 = not queried yet
+int g_dil_occ[kMaxDevices][2][3][2][2] = {};      // 0 = not queried yet
 
 int strip_in_cols(int K, int S) { return S * (tdc::kStripQ - 1) + K; }
 
@@ -646,6 +692,23 @@ WsPlan make_geom_plan(int64_t N, int64_t P, int64_t Q, int64_t C, int K, int S, 
   return pl;
 }
 
+// Resident CTAs per SM of the general forward kernel (queried once per
+// device and instantiation).
+int geom_occupancy(int devi, int dt, int K, int S, bool with_epilogue, int64_t n_stage, int* occ) {
+  const int ki = K / 2 - 1, si = S - 1, mi = with_epilogue ? 1 : 0, ni = int(n_stage - 2);
+  const size_t smem = make_geom_plan(1, 1, 1, 8, K, S, n_stage, 1, 1).smem;
+  std::lock_guard<std::mutex> lock(g_geom_mutex);
+  int v = g_geom_occ[devi][dt][ki][si][mi][ni];
+  if (v == 0) {
+    const cudaError_t e = kGeomOcc[dt][ki][si][mi][ni](&v, smem);
+    if (e != cudaSuccess) return cuda_fail(e);
+    v = std::max(1, v);
+    g_geom_occ[devi][dt][ki][si][mi][ni] = v;
+  }
+  *occ = v;
+  return TDC_OK;
+}
+
 int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W, int64_t C,
              int64_t K, int64_t S, int64_t pad, int64_t n_stage, const Epilogue& epi,
              void* stream, int dt = kF16, const Pad4* p4 = nullptr) {
@@ -674,18 +737,9 @@ int fwd_geom(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_
       epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
   const int ki = int(K / 2 - 1), si = int(S - 1), mi = with_epilogue ? 1 : 0, ni = int(n_stage - 2);
   const int stage_rows = geom_stage_rows(int(K), int(S), n_stage);
-  const size_t smem = make_geom_plan(1, 1, 1, 8, int(K), int(S), n_stage, 1, 1).smem;
-  int occ;
-  {
-    std::lock_guard<std::mutex> lock(g_geom_mutex);
-    occ = g_geom_occ[devi][dt][ki][si][mi][ni];
-    if (occ == 0) {
-      const cudaError_t e = kGeomOcc[dt][ki][si][mi][ni](&occ, smem);
-      if (e != cudaSuccess) return cuda_fail(e);
-      occ = std::max(1, occ);
-      g_geom_occ[devi][dt][ki][si][mi][ni] = occ;
-    }
-  }
+  int occ = 0;
+  rc = geom_occupancy(devi, dt, int(K), int(S), with_epilogue, n_stage, &occ);
+  if (rc != TDC_OK) return rc;
   const WsPlan pl = make_geom_plan(N, P, Q, C, int(K), int(S), n_stage, dev->sms, occ);
   alignas(64) CUtensorMap map;
   rc = encode_nhwc_map(&map, x, N, H, W, C, strip_in_cols(int(K), int(S)), stage_rows, dt);
@@ -816,15 +870,151 @@ int fwd_plain(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
 
 // Dilated forward: the plain kernel on the D*D phases of the output (see
 // PlainParams::dil).
+// Ring depth of the ws forward per geometry when the caller leaves it to the
+// library (n_stage = 0), measured at 64 x 224 x 336 x 256.
+int default_fwd_stages(int64_t K, int64_t S) {
+  return (K == 3 || K == 5 || K == 7) && (S == 1 || S == 2) ? fwd_stages_of(int(K), int(S)) : 2;
+}
+
+// Whether the plain kernel beats the ws kernel on this shape.  The ws kernel
+// works in strips of 32 output columns x 64 channels; fill_c and fill_q are
+// the fractions of a strip's lanes and columns that hold real outputs.  From
+// both kernels timed on the 28 depthwise layers of MobileNetV2 / V3-Large /
+// EfficientNet-B0 at batch 64 and 256: with fill_c * fill_q >= 0.5 the ws
+// kernel wins or ties everywhere; below it the plain kernel wins at stride 1
+// (e.g. 14 x 14 x 576: 10.3 vs 12.8 us, 112 x 112 x 16: 18.2 vs 44.4 us) and
+// at stride 2 on 7-column outputs or layers under 64 MB, while larger
+// stride-2 layers with wider outputs stay on the ws kernel (28 x 28 x 192 at
+// batch 256: 20.2 vs 26.1 us).
+bool prefer_plain_pq(int64_t Q, int64_t C, int64_t S, double bytes) {
+  const double fill_c = double(C) / double(64 * ((C + 63) / 64));
+  const double fill_q = double(Q) / double(32 * ((Q + 31) / 32));
+  if (fill_c * fill_q >= 0.5) return false;
+  return S == 1 || fill_q <= 0.25 || bytes < 64e6;
+}
+
+bool prefer_plain_pads(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                       const Pad4& pd) {
+  if (K != 3 && K != 5 && K != 7) return false;
+  if ((S != 1 && S != 2) || C <= 0 || C % 8 != 0 || N <= 0) return false;
+  if (H + pd.top + pd.bottom < K || W + pd.left + pd.right < K) return false;
+  const int64_t P = (H + pd.top + pd.bottom - K) / S + 1, Q = (W + pd.left + pd.right - K) / S + 1;
+  const double bytes = 2.0 * double(N) * double(C) * (double(H) * double(W) + double(P) * double(Q));
+  return prefer_plain_pq(Q, C, S, bytes);
+}
+
+bool prefer_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                  int64_t pad) {
+  return prefer_plain_pads(N, H, W, C, K, S, Pad4{pad, pad, pad, pad});
+}
+
+// Whether the ring kernel's tensor map can step D rows and columns: the box
+// spans D * (input columns of a strip) columns and D * stage_rows rows (the
+// dilated ring runs at the geometry's default depth).
+bool dilated_ring_fits(int64_t K, int64_t S, int64_t D) {
+  return D >= 1 && D <= kMaxTmaStride && strip_in_cols(int(K), int(S)) * D <= kMaxTmaBox &&
+         geom_stage_rows(int(K), int(S), default_fwd_stages(K, S)) * D <= kMaxTmaBox;
+}
+
+// Whether the dilated forward with n_stage = 0 runs the plain kernel.  The
+// ring kernel takes the phase sub-problems (ceil(P/D) x ceil(Q/D) outputs
+// each) where its map can step D, the undilated choice would give them the
+// ring kernel, and both sides are at least 32: on smaller phases its
+// strips are short and the plain kernel wins.  Measured on one B200 (us,
+// plain / ring; CUDA graphs): 32 x 128 x 128 x 256 3x3 D2 154.6 / 102.1,
+// 16 x 112 x 112 x 384 5x5 D2 160.2 / 120.3, 16 x 128 x 128 x 256 3x3 D4
+// 81.2 / 55.4, 8 x 64 x 64 x 256 3x3 D2 11.5 / 10.3; phases under 32:
+// 8 x 64 x 64 x 256 D4 11.4 / 18.4, 8 x 128 x 128 x 128 D6 21.3 / 22.5,
+// 8 x 32 x 32 x 960 5x5 D2 20.7 / 23.7, 32 x 64 x 64 x 512 stride 2 D2
+// 31.1 / 32.7.
+bool dilated_prefers_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
+                           int64_t D, int64_t P, int64_t Q) {
+  const int64_t Pp = (P + D - 1) / D, Qp = (Q + D - 1) / D;
+  const double bytes = 2.0 * double(N) * double(C) * (double(H) * double(W) + double(P) * double(Q));
+  return !dilated_ring_fits(K, S, D) || std::min(Pp, Qp) < 32 ||
+         prefer_plain_pq(Qp, C, S, bytes);
+}
+
+// Dilated forward on the ring kernel: the N*D*D phase sub-problems (each
+// an undilated K x K stride-S problem on the D-strided sub-lattice of x,
+// loaded with traversal stride D) are scheduled as N*D*D images of the
+// largest phase's ceil(P/D) x ceil(Q/D) outputs; the kernel maps a phase's
+// output (p', q') to y's (pa + D*p', pb + D*q').  Arguments are checked by
+// fwd_dilated.
+int fwd_dilated_ring(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
+                     int64_t C, int64_t K, int64_t S, int64_t D, int64_t P, int64_t Q,
+                     const Pad4& pd, const Epilogue& epi, void* stream, int dt) {
+  if (D < 2 || !dilated_ring_fits(K, S, D)) return TDC_ERR_UNSUPPORTED;
+  const int64_t n_stage = default_fwd_stages(K, S);
+  const int64_t Pp = (P + D - 1) / D, Qp = (Q + D - 1) / D;
+  const int stage_rows = geom_stage_rows(int(K), int(S), n_stage);
+  const int in_cols = strip_in_cols(int(K), int(S));
+  // 32-bit tensor-map coordinates (row S*pa - pad + D*S*p0 + D*t*stage_rows,
+  // column S*pb - pad_w + D*S*32*qs, plus the box) and column step D*C.
+  const int64_t i32 = 0x7fffffffll;
+  if (N * D * D > i32 || D * C > i32 ||
+      D * S * (2 * Pp + 2) + D * (K + 2 * stage_rows) + pd.top > i32 ||
+      D * S * (Qp + tdc::kStripQ + 1) + D * in_cols + pd.left > i32)
+    return TDC_ERR_TOO_LARGE;
+  int rc = check_ws_limits(N, H, W, C, P, Q);
+  if (rc != TDC_OK) return rc;
+  DeviceInfo* dev = nullptr;
+  int devi = -1;
+  rc = current_device(&dev, &devi);
+  if (rc != TDC_OK) return rc;
+  const bool with_epilogue =
+      epi.bias != nullptr || epi.residual != nullptr || epi.act != TDC_ACT_NONE;
+  const int ki = int(K / 2 - 1), si = int(S - 1), mi = with_epilogue ? 1 : 0;
+  const WsPlan pl1 = make_geom_plan(1, 1, 1, 8, int(K), int(S), n_stage, 1, 1);
+  int occ;
+  {
+    std::lock_guard<std::mutex> lock(g_geom_mutex);
+    occ = g_dil_occ[devi][dt][ki][si][mi];
+    if (occ == 0) {
+      const cudaError_t e = kDilOcc[dt][ki][si][mi](&occ, pl1.smem);
+      if (e != cudaSuccess) return cuda_fail(e);
+      occ = std::max(1, occ);
+      g_dil_occ[devi][dt][ki][si][mi] = occ;
+    }
+  }
+  const WsPlan pl = make_geom_plan(N * D * D, Pp, Qp, C, int(K), int(S), n_stage, dev->sms, occ);
+  alignas(64) CUtensorMap map;
+  rc = encode_nhwc_map(&map, x, N, H, W, C, in_cols, stage_rows, dt, int(D));
+  if (rc != TDC_OK) return rc;
+  tdc::WsParams prm{};
+  prm.status_host = current_status_slot(true);
+  prm.w = static_cast<const __half*>(w);
+  prm.y = static_cast<__half*>(y);
+  prm.H = int32_t(H); prm.W = int32_t(W); prm.C = int32_t(C);
+  prm.P = int32_t(Pp); prm.Q = int32_t(Qp); prm.pad = int32_t(pd.top); prm.pad_w = int32_t(pd.left);
+  prm.dil = int32_t(D); prm.yP = int32_t(P); prm.yQ = int32_t(Q);
+  prm.qstrips = pl.qstrips; prm.cblocks = pl.cblocks; prm.stage_rows = pl.stage_rows;
+  prm.tail_bands = pl.tail_bands; prm.tail_band_rows = pl.tail_band_rows;
+  prm.full_units = pl.full_units; prm.tail_strips = pl.tail_strips;
+  prm.tail_chunk_rows = pl.tail_chunk_rows;
+  prm.timeout_ns = uint64_t(g_timeout_ns.load());
+  prm.withhold = -1;
+  prm.bias = static_cast<const __half*>(epi.bias);
+  prm.residual = static_cast<const __half*>(epi.residual);
+  prm.act = epi.act;
+  const cudaError_t e =
+      kDilLaunch[dt][ki][si][mi](map, prm, pl.grid, pl.smem, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TDC_OK : cuda_fail(e);
+}
+
+// Dilated forward.  kernel = 1: the ring kernel (TDC_ERR_UNSUPPORTED when
+// its tensor map cannot step D, or D = 1); -1: the plain kernel; 0: chosen
+// by shape (dilated_prefers_plain).
 int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int64_t W,
                 int64_t C, int64_t K, int64_t S, int64_t D, const Pad4& pd, const Epilogue& epi,
-                void* stream, int dt) {
+                int64_t kernel, void* stream, int dt) {
   if (K != 3 && K != 5 && K != 7) return TDC_ERR_FILTER_SHAPE;
   if (S != 1 && S != 2) return TDC_ERR_STRIDE;
   if (D < 1) return TDC_ERR_BAD_SHAPE;
   if (N < 0 || H < 1 || W < 1 || C < 0) return TDC_ERR_BAD_SHAPE;
   if (C % 8 != 0) return TDC_ERR_CHANNELS;
   if (pd.top < 0 || pd.bottom < 0 || pd.left < 0 || pd.right < 0) return TDC_ERR_PAD;
+  if (kernel < -1 || kernel > 1) return TDC_ERR_UNSUPPORTED;
   const int64_t i32 = 0x7fffffffll;
   if (D > (1 << 24) || std::max({pd.top, pd.bottom, pd.left, pd.right}) > (1 << 28) ||
       N > i32 || C > i32 || H > i32 || W > i32)
@@ -832,18 +1022,20 @@ int fwd_dilated(const void* x, const void* w, void* y, int64_t N, int64_t H, int
   const int64_t Ke = D * (K - 1) + 1;  // the dilated kernel's extent
   if (H + pd.top + pd.bottom < Ke || W + pd.left + pd.right < Ke) return TDC_ERR_BAD_SHAPE;
   const int64_t P = (H + pd.top + pd.bottom - Ke) / S + 1, Q = (W + pd.left + pd.right - Ke) / S + 1;
-  // 32-bit row / column arithmetic in the kernel: a thread's first input row
+  if (N == 0 || C == 0) return TDC_OK;
+  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
+      (epi.residual && !aligned16(epi.residual)))
+    return TDC_ERR_ALIGNMENT;
+  if (kernel == 0) kernel = dilated_prefers_plain(N, H, W, C, K, S, D, P, Q) ? -1 : 1;
+  if (kernel == 1) return fwd_dilated_ring(x, w, y, N, H, W, C, K, S, D, P, Q, pd, epi, stream, dt);
+  // 32-bit row / column arithmetic in the plain kernel: a thread's first input row
   // S * (phase + D * p0) - pad plus D * (its window rows), likewise columns
   // with S * plain_cols(K) - S + K window columns.
   if (S * P + D * (S + K) + pd.top > i32 ||
       S * Q + D * (S * tdc::plain_cols(int(K)) + K) + pd.left > i32)
     return TDC_ERR_TOO_LARGE;
   if (H * W > i32 || H * W * (C / 2) > i32) return TDC_ERR_TOO_LARGE;  // 32-bit image offsets
-  if (N == 0 || C == 0) return TDC_OK;
-  if (!x || !w || !y) return TDC_ERR_NULL_POINTER;
-  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (epi.bias && !aligned16(epi.bias)) ||
-      (epi.residual && !aligned16(epi.residual)))
-    return TDC_ERR_ALIGNMENT;
   DeviceInfo* dev = nullptr;
   int rc = current_device(&dev, nullptr);
   if (rc != TDC_OK) return rc;
@@ -1608,41 +1800,6 @@ TDC_API int tdc_dwconv3x3_fwd(const void* x, const void* w, const void* bias,
   return ws_common(x, w, y, N, H, W, C, 3, 3, pad, n_stage, nullptr, false, -1, 0, stream, epi);
 }
 
-// Ring depth of the ws forward per geometry when the caller leaves it to the
-// library (n_stage = 0), measured at 64 x 224 x 336 x 256.
-int default_fwd_stages(int64_t K, int64_t S) {
-  static const int kStages[3][2] = {{2, 4}, {4, 2}, {3, 4}};  // [K: 3, 5, 7][stride - 1]
-  return (K == 3 || K == 5 || K == 7) && (S == 1 || S == 2) ? kStages[K / 2 - 1][S - 1] : 2;
-}
-
-// Whether the plain kernel beats the ws kernel on this shape.  The ws kernel
-// works in strips of 32 output columns x 64 channels; fill_c and fill_q are
-// the fractions of a strip's lanes and columns that hold real outputs.  From
-// both kernels timed on the 28 depthwise layers of MobileNetV2 / V3-Large /
-// EfficientNet-B0 at batch 64 and 256: with fill_c * fill_q >= 0.5 the ws
-// kernel wins or ties everywhere; below it the plain kernel wins at stride 1
-// (e.g. 14 x 14 x 576: 10.3 vs 12.8 us, 112 x 112 x 16: 18.2 vs 44.4 us) and
-// at stride 2 on 7-column outputs or layers under 64 MB, while larger
-// stride-2 layers with wider outputs stay on the ws kernel (28 x 28 x 192 at
-// batch 256: 20.2 vs 26.1 us).
-bool prefer_plain_pads(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
-                       const Pad4& pd) {
-  if (K != 3 && K != 5 && K != 7) return false;
-  if ((S != 1 && S != 2) || C <= 0 || C % 8 != 0 || N <= 0) return false;
-  if (H + pd.top + pd.bottom < K || W + pd.left + pd.right < K) return false;
-  const int64_t P = (H + pd.top + pd.bottom - K) / S + 1, Q = (W + pd.left + pd.right - K) / S + 1;
-  const double fill_c = double(C) / double(64 * ((C + 63) / 64));
-  const double fill_q = double(Q) / double(32 * ((Q + 31) / 32));
-  if (fill_c * fill_q >= 0.5) return false;
-  const double bytes = 2.0 * double(N) * double(C) * (double(H) * double(W) + double(P) * double(Q));
-  return S == 1 || fill_q <= 0.25 || bytes < 64e6;
-}
-
-bool prefer_plain(int64_t N, int64_t H, int64_t W, int64_t C, int64_t K, int64_t S,
-                  int64_t pad) {
-  return prefer_plain_pads(N, H, W, C, K, S, Pad4{pad, pad, pad, pad});
-}
-
 // Whether the weight gradient with n_stage = 0 runs the plain kernel: narrow
 // outputs (Q <= 16, half a ws strip or less) or at most 16 channels.  A plain
 // thread walks the whole output width, so wide images with more channels stay
@@ -1755,9 +1912,9 @@ static int fwd_dilated_entry(int dt, const void* x, const void* w, const void* b
                              const void* residual, void* y, int64_t N, int64_t H, int64_t W,
                              int64_t C, int64_t K, int64_t stride, int64_t dilation,
                              int64_t pad_top, int64_t pad_bottom, int64_t pad_left,
-                             int64_t pad_right, int64_t act, void* stream) {
+                             int64_t pad_right, int64_t act, int64_t kernel, void* stream) {
   if (act < TDC_ACT_NONE || act > TDC_ACT_HARDSWISH) return TDC_ERR_ACT;
-  if (dilation == 1)  // the sliding-window kernels, chosen by shape
+  if (dilation == 1 && kernel == 0)  // the undilated forward, chosen by shape
     return fwd_asym_entry(dt, x, w, bias, residual, y, N, H, W, C, K, stride, pad_top,
                           pad_bottom, pad_left, pad_right, act, 0, stream);
   Epilogue epi;
@@ -1766,7 +1923,7 @@ static int fwd_dilated_entry(int dt, const void* x, const void* w, const void* b
   epi.residual = residual;
   epi.act = int(act);
   return fwd_dilated(x, w, y, N, H, W, C, K, stride, dilation,
-                     Pad4{pad_top, pad_bottom, pad_left, pad_right}, epi, stream, dt);
+                     Pad4{pad_top, pad_bottom, pad_left, pad_right}, epi, kernel, stream, dt);
 }
 
 TDC_API int tdc_dwconv_fwd_dilated(const void* x, const void* w, const void* bias,
@@ -1776,7 +1933,7 @@ TDC_API int tdc_dwconv_fwd_dilated(const void* x, const void* w, const void* bia
                                    int64_t pad_left, int64_t pad_right, int64_t act,
                                    void* stream) {
   return fwd_dilated_entry(kF16, x, w, bias, residual, y, N, H, W, C, K, stride, dilation,
-                           pad_top, pad_bottom, pad_left, pad_right, act, stream);
+                           pad_top, pad_bottom, pad_left, pad_right, act, 0, stream);
 }
 
 TDC_API int tdc_dwconv_fwd_dilated_bf16(const void* x, const void* w, const void* bias,
@@ -1786,7 +1943,35 @@ TDC_API int tdc_dwconv_fwd_dilated_bf16(const void* x, const void* w, const void
                                         int64_t pad_left, int64_t pad_right, int64_t act,
                                         void* stream) {
   return fwd_dilated_entry(kBF16, x, w, bias, residual, y, N, H, W, C, K, stride, dilation,
-                           pad_top, pad_bottom, pad_left, pad_right, act, stream);
+                           pad_top, pad_bottom, pad_left, pad_right, act, 0, stream);
+}
+
+TDC_API int tdc_dwconv_fwd_dilated_ex(const void* x, const void* w, const void* bias,
+                                      const void* residual, void* y, int64_t N, int64_t H,
+                                      int64_t W, int64_t C, int64_t K, int64_t stride,
+                                      int64_t dilation, int64_t pad_top, int64_t pad_bottom,
+                                      int64_t pad_left, int64_t pad_right, int64_t act,
+                                      int64_t kernel, int64_t bf16, void* stream) {
+  return fwd_dilated_entry(bf16 ? kBF16 : kF16, x, w, bias, residual, y, N, H, W, C, K, stride,
+                           dilation, pad_top, pad_bottom, pad_left, pad_right, act, kernel,
+                           stream);
+}
+
+TDC_API int tdc_dwconv_fwd_dilated_uses_plain(int64_t N, int64_t H, int64_t W, int64_t C,
+                                              int64_t K, int64_t stride, int64_t dilation,
+                                              int64_t pad_top, int64_t pad_bottom,
+                                              int64_t pad_left, int64_t pad_right) {
+  const Pad4 pd{pad_top, pad_bottom, pad_left, pad_right};
+  if (dilation == 1) return prefer_plain_pads(N, H, W, C, K, stride, pd) ? 1 : 0;
+  if (K != 3 && K != 5 && K != 7) return 0;
+  if ((stride != 1 && stride != 2) || dilation < 1 || dilation > (1 << 24) || N <= 0 || C <= 0 ||
+      C % 8 != 0)
+    return 0;
+  const int64_t Ke = dilation * (K - 1) + 1;
+  if (H + pad_top + pad_bottom < Ke || W + pad_left + pad_right < Ke) return 0;
+  const int64_t P = (H + pad_top + pad_bottom - Ke) / stride + 1;
+  const int64_t Q = (W + pad_left + pad_right - Ke) / stride + 1;
+  return dilated_prefers_plain(N, H, W, C, K, stride, dilation, P, Q) ? 1 : 0;
 }
 
 static int plain_entry(int dt, const void* x, const void* w, const void* bias,

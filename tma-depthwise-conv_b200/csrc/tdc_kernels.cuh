@@ -92,6 +92,18 @@ struct WsParams {
   // > 0: the tail is cut into chunks of this many rows instead of bands (see
   // SegmentIter); requires gridDim.x % cblocks == 0.
   int32_t tail_chunk_rows;
+  // Dilation D (forward; read only by the kernels instantiated with DIL,
+  // which the host launches with D > 1 only).  With
+  // D > 1, tap (r, s) of output (p, q) reads input (S*p + D*r - pad,
+  // S*q + D*s - pad_w).  The outputs split into the D*D phases (p mod D,
+  // q mod D); on phase (a, b) the outputs D apart read inputs D apart, an
+  // undilated problem on the D-strided sub-lattice of x, which the tensor
+  // map loads with traversal stride D.  The kernel then runs the undilated
+  // schedule over N*D*D "images" (image n, phase a*D + b) of P x Q = the
+  // largest phase's ceil(yP/D) x ceil(yQ/D) outputs, yP x yQ being y's rows
+  // and columns.
+  int32_t dil;
+  int32_t yP, yQ;
 };
 
 // Per-device failure record written by the bounded waits:
@@ -120,9 +132,11 @@ __device__ __forceinline__ void record_failure(int code, int block, int stage, i
   }
 }
 
-// A run of output rows [p0, p0 + rows) of one strip.
+// A run of output rows [p0, p0 + rows) of one strip; with dilation, of
+// phase (pa, pb) of image n.
 struct Segment {
   int n, qs, cb, p0, rows;
+  int pa, pb;
 };
 
 // Enumerates the segments of one CTA; the producer and every consumer warp
@@ -138,6 +152,10 @@ struct Segment {
 // pixels at the same time, as the channel-block-fastest strip order does for
 // whole strips, and every CTA streams at most L rows plus two halo rows per
 // segment, however the tail's rows divide by the grid.
+//
+// Dilation (p.dil = D > 1): strips run over N*D*D images of the largest
+// phase's size; a phase with fewer rows clips its segments, and segments
+// left empty are skipped.
 struct SegmentIter {
   int64_t next;  // next work item: whole strips first, then tail units
   int64_t grid;
@@ -145,7 +163,27 @@ struct SegmentIter {
 
   __device__ SegmentIter(int64_t g, int64_t grid_) : next(g), grid(grid_) {}
 
+  // kDilated: the dilated instantiations (p.dil > 1).
+  template <bool kDilated = false>
   __device__ bool next_segment(const WsParams& p, Segment& s) {
+    for (;;) {
+      if (!next_unit(p, s)) return false;
+      if (!kDilated) {
+        s.pa = 0;
+        s.pb = 0;
+        return true;
+      }
+      const int D = p.dil;
+      const int ph = s.n % (D * D);
+      s.n /= D * D;
+      s.pa = ph / D;
+      s.pb = ph - s.pa * D;
+      s.rows = min(s.rows, (p.yP - s.pa + D - 1) / D - s.p0);
+      if (s.rows > 0) return true;
+    }
+  }
+
+  __device__ bool next_unit(const WsParams& p, Segment& s) {
     int64_t strip;
     int first, last;
     if (next < p.full_units) {
@@ -333,7 +371,7 @@ __device__ __forceinline__ uint4 pack_vec8(const float* a) {
 // 16-byte store per column (a warp instruction writes four full 128-byte
 // lines).  Each output's chain is (r, s) lexicographic from +0, the same as
 // every other kernel here.
-template <int NS, bool PROBE, int MODE, class E>
+template <int NS, bool PROBE, int MODE, class E, bool DIL>
 __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uint8_t* ring_ptr,
                                                     uint32_t stage_bytes, uint64_t* full_bar,
                                                     uint64_t* empty_bar, volatile int* abort_flag,
@@ -353,12 +391,16 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
 #pragma unroll
     for (int k = 0; k < 16; ++k) acc[a][k] = 0.f;
   bool failed = false;
-  while (!failed && it.next_segment(p, sg)) {
+  while (!failed && it.next_segment<DIL>(p, sg)) {
     const int rows_in = sg.rows + 2;
     const int c0 = sg.cb * kBlockC;
     const int cl = c0 + 8 * vl;  // this lane's first channel
     const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
-    const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
+    // Dilation D (DIL only): this phase has ceil((yQ - pb) / D) output
+    // columns.
+    const int D = DIL ? p.dil : 1;
+    const int qn = DIL ? (p.yQ - sg.pb + D - 1) / D : p.Q;
+    const int n_valid = min(kColsPerWarp, qn - q_first);  // <= 0: warp idle
     // This lane's 8 channels exist (always on the ws path, C % 64 == 0; else
     // C % 8 == 0, so a vector is wholly inside C or wholly outside).
     const bool chan_ok = MODE == kModeWs || cl < p.C;
@@ -371,8 +413,15 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
       }
       last_cb = sg.cb;
     }
-    const int64_t y_off = ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first + 2 * cp) * p.C + cl;
-    const int64_t y_row_stride = int64_t(p.Q) * p.C;
+    // Output (p0 + o, q) of the segment is y's row pa + D*(p0 + o), column
+    // pb + D*q.  The column step D*C (< 2^31, checked by the host) is
+    // recomputed from the parameters where it is used.
+    const int64_t y_off =
+        DIL ? ((int64_t(sg.n) * p.yP + sg.pa + int64_t(D) * sg.p0) * p.yQ + sg.pb +
+               int64_t(D) * (q_first + 2 * cp)) * p.C + cl
+            : ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first + 2 * cp) * p.C + cl;
+    const int64_t y_row_stride = DIL ? int64_t(D) * p.yQ * p.C : int64_t(p.Q) * p.C;
+    auto y_col = [&]() { return DIL ? p.dil * p.C : p.C; };
     const bool st0 = chan_ok && 2 * cp < n_valid;
     const bool st1 = chan_ok && 2 * cp + 1 < n_valid;
 
@@ -420,7 +469,7 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
           const __half* rp = p.residual + y_off + int64_t(o) * y_row_stride;
           const uint4 res[2] = {
               st0 ? __ldg(reinterpret_cast<const uint4*>(rp)) : make_uint4(0u, 0u, 0u, 0u),
-              st1 ? __ldg(reinterpret_cast<const uint4*>(rp + p.C)) : make_uint4(0u, 0u, 0u, 0u)};
+              st1 ? __ldg(reinterpret_cast<const uint4*>(rp + y_col())) : make_uint4(0u, 0u, 0u, 0u)};
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
             const uint32_t w4[4] = {res[m].x, res[m].y, res[m].z, res[m].w};
@@ -436,7 +485,7 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
       }
       __half* dst = p.y + y_off + int64_t(o) * y_row_stride;
       if (st0) *reinterpret_cast<uint4*>(dst) = pack_vec8<E>(a);
-      if (st1) *reinterpret_cast<uint4*>(dst + p.C) = pack_vec8<E>(a + 8);
+      if (st1) *reinterpret_cast<uint4*>(dst + y_col()) = pack_vec8<E>(a + 8);
     };
 
     int lr = 0;  // row within the current stage
@@ -529,7 +578,7 @@ __host__ __device__ constexpr int ws_max_regs() {
   return K == 3 && S == 1 ? 136 : 128;
 }
 
-template <int NS, bool PROBE, int MODE, int K, int S, class E>
+template <int NS, bool PROBE, int MODE, int K, int S, class E, bool DIL>
 __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint8_t* ring_ptr,
                                                    uint32_t stage_bytes, uint64_t* full_bar,
                                                    uint64_t* empty_bar, volatile int* abort_flag,
@@ -540,12 +589,13 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
 // and can flip the taps (the data gradient); kModeEpilogue adds the fused
 // epilogue.  kModeWs is the ws call of the reference surface (3x3, stride 1).
 // E (F16 / BF16) is the element type; the ws surface is fp16 only.
-template <int NS, bool PROBE, int MODE = kModeWs, int K = 3, int S = 1, class E = F16>
+template <int NS, bool PROBE, int MODE = kModeWs, int K = 3, int S = 1, class E = F16, bool DIL = false>
 __global__ void __maxnreg__((ws_max_regs<K, S>()))
     dwconv_ws_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ WsParams p) {
   using G = Geom<K, S>;
   static_assert(MODE != kModeWs || (K == 3 && S == 1), "the ws surface is 3x3, stride 1");
   static_assert(MODE != kModeWs || std::is_same_v<E, F16>, "the ws surface is fp16");
+  static_assert(!DIL || (MODE != kModeWs && !PROBE), "dilation: general forward modes only");
   __shared__ __align__(8) uint64_t full_bar[NS];
   __shared__ __align__(8) uint64_t empty_bar[NS];
   __shared__ volatile int abort_flag;
@@ -589,12 +639,15 @@ __global__ void __maxnreg__((ws_max_regs<K, S>()))
     bool ok = true;
     SegmentIter it(blockIdx.x, gridDim.x);
     Segment sg;
-    while (ok && it.next_segment(p, sg)) {
+    while (ok && it.next_segment<DIL>(p, sg)) {
       const int rows_in = S * (sg.rows - 1) + K;
       const int nst = (rows_in + p.stage_rows - 1) / p.stage_rows;
       const int32_t c0 = sg.cb * kBlockC;
-      const int32_t w0 = S * sg.qs * kStripQ - p.pad_w;
-      const int32_t h0 = S * sg.p0 - p.pad;
+      // First input column and row of the segment; a stage of the ring
+      // holds stage_rows rows, D apart (D = 1 without dilation).
+      const int32_t D = DIL ? p.dil : 1;
+      const int32_t w0 = S * sg.pb - p.pad_w + D * S * sg.qs * kStripQ;
+      const int32_t h0 = S * sg.pa - p.pad + D * S * sg.p0;
       for (int t = 0; t < nst; ++t) {
         const uint32_t eb = smem_addr(&empty_bar[stage]);
         [[maybe_unused]] uint64_t t0 = 0;
@@ -611,7 +664,7 @@ __global__ void __maxnreg__((ws_max_regs<K, S>()))
         if (load != p.withhold) {
           const uint32_t fb = smem_addr(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, stage_bytes);
-          tma_load_4d(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + t * p.stage_rows, sg.n);
+          tma_load_4d(ring + stage * stage_bytes, &tmap, fb, c0, w0, h0 + D * t * p.stage_rows, sg.n);
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
         } else {
@@ -639,11 +692,11 @@ __global__ void __maxnreg__((ws_max_regs<K, S>()))
 
   // ------------------------------ consumers ------------------------------
   if constexpr (K == 3 && S == 1) {
-    ws_consumers_vec3x3<NS, PROBE, MODE, E>(p, ring_ptr, stage_bytes, full_bar, empty_bar,
+    ws_consumers_vec3x3<NS, PROBE, MODE, E, DIL>(p, ring_ptr, stage_bytes, full_bar, empty_bar,
                                             &abort_flag, warp - 1, lane, t_start);
     return;
   } else {
-    ws_consumers_pairs<NS, PROBE, MODE, K, S, E>(p, ring_ptr, stage_bytes, full_bar, empty_bar,
+    ws_consumers_pairs<NS, PROBE, MODE, K, S, E, DIL>(p, ring_ptr, stage_bytes, full_bar, empty_bar,
                                                  &abort_flag, warp - 1, lane, t_start);
   }
 }
@@ -651,7 +704,7 @@ __global__ void __maxnreg__((ws_max_regs<K, S>()))
 // Consumer warps of the other geometries (3x3 stride 2, 5x5, 7x7): lane =
 // channel pair, warp = 8 output columns; sliding window or direct scheme per
 // Geom<K, S>::kDirect.
-template <int NS, bool PROBE, int MODE, int K, int S, class E>
+template <int NS, bool PROBE, int MODE, int K, int S, class E, bool DIL>
 __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint8_t* ring_ptr,
                                                    uint32_t stage_bytes, uint64_t* full_bar,
                                                    uint64_t* empty_bar, volatile int* abort_flag,
@@ -667,11 +720,15 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
   // (running counters, no division per pass).
   int acq_slot = 0, rel_slot = 0, seg_slot = 0;
   uint32_t acq_phase = 0;
-  while (it.next_segment(p, sg)) {
+  while (it.next_segment<DIL>(p, sg)) {
     const int rows_in = S * (sg.rows - 1) + K;
     const int c0 = sg.cb * kBlockC;
     const int q_first = sg.qs * kStripQ + cw * kColsPerWarp;
-    const int n_valid = min(kColsPerWarp, p.Q - q_first);  // <= 0: warp idle
+    // Dilation D (DIL only): this phase has ceil((yQ - pb) / D) output
+    // columns.
+    const int D = DIL ? p.dil : 1;
+    const int qn = DIL ? (p.yQ - sg.pb + D - 1) / D : p.Q;
+    const int n_valid = min(kColsPerWarp, qn - q_first);  // <= 0: warp idle
     // This lane's channel pair exists (always on the ws path, C % 64 == 0).
     const bool chan_ok = MODE == kModeWs || c0 + 2 * lane < p.C;
     if (sg.cb != last_cb) {
@@ -689,8 +746,15 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
         unpack2<E>(*reinterpret_cast<const uint32_t*>(p.bias + c0 + 2 * lane), bias0, bias1);
       }
     }
-    __half* yrow = p.y + ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first) * p.C + c0 + 2 * lane;
-    const int64_t y_row_stride = int64_t(p.Q) * p.C;
+    // Output (p0 + o, q) of the segment is y's row pa + D*(p0 + o), column
+    // pb + D*q.  The column step D*C (< 2^31, checked by the host) is
+    // recomputed from the parameters where it is used.
+    __half* yrow =
+        p.y + c0 + 2 * lane +
+        (DIL ? ((int64_t(sg.n) * p.yP + sg.pa + int64_t(D) * sg.p0) * p.yQ + sg.pb + int64_t(D) * q_first) * p.C
+             : ((int64_t(sg.n) * p.P + sg.p0) * p.Q + q_first) * p.C);
+    const int64_t y_row_stride = DIL ? int64_t(D) * p.yQ * p.C : int64_t(p.Q) * p.C;
+    auto y_col = [&]() { return DIL ? p.dil * p.C : p.C; };
 
     bool failed = false;
 
@@ -703,7 +767,7 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
           const __half* rrow = p.residual + ((yrow - p.y) + int64_t(o) * y_row_stride);
 #pragma unroll
           for (int m = 0; m < kColsPerWarp; ++m)
-            res[m] = m < n_valid ? __ldg(reinterpret_cast<const uint32_t*>(rrow + int64_t(m) * p.C))
+            res[m] = m < n_valid ? __ldg(reinterpret_cast<const uint32_t*>(rrow + int64_t(m) * y_col()))
                                  : 0u;
         }
       }
@@ -755,7 +819,7 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
 #pragma unroll
       for (int m = 0; m < kColsPerWarp; ++m)
         if (m < n_valid)
-          *reinterpret_cast<uint32_t*>(dst + int64_t(m) * p.C) =
+          *reinterpret_cast<uint32_t*>(dst + int64_t(m) * y_col()) =
               pack2_rn<E>(fin.v[2 * m], fin.v[2 * m + 1]);
     };
 
