@@ -569,13 +569,14 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
   }
 }
 
-// Registers per thread of the ws kernels, so that 3 CTAs of 160 threads
-// share an SM's 64 K registers: 136 for the 3x3 stride-1 vector consumers
-// (__launch_bounds__(160, 3) lets ptxas use only 128, at which they spill),
-// 128 for the other geometries.
+// Registers per thread of the ws kernels: 128, so that 3 CTAs of 160 threads
+// are resident per SM.  At 136 only 2 fit (ncu: occupancy limit by
+// registers 2 blocks, 136 allocated per thread), which cost the 3x3 kernel
+// with an epilogue a third of its rate; at 128 it spills a few words
+// instead.
 template <int K, int S>
 __host__ __device__ constexpr int ws_max_regs() {
-  return K == 3 && S == 1 ? 136 : 128;
+  return 128;
 }
 
 template <int NS, bool PROBE, int MODE, int K, int S, class E, bool DIL>
