@@ -82,6 +82,18 @@ cudaError_t prepare_ws(int* occ) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, k, tdc::kWsThreads, smem);
 }
 
+template <int NS>
+cudaError_t prepare_ws_act() {
+  int occ = 0;
+  cudaError_t e = cudaSuccess;
+  if (e == cudaSuccess) e = prepare_ws<NS, false, tdc::kModeEpilogueAct + TDC_ACT_NONE>(&occ);
+  if (e == cudaSuccess) e = prepare_ws<NS, false, tdc::kModeEpilogueAct + TDC_ACT_RELU>(&occ);
+  if (e == cudaSuccess) e = prepare_ws<NS, false, tdc::kModeEpilogueAct + TDC_ACT_RELU6>(&occ);
+  if (e == cudaSuccess) e = prepare_ws<NS, false, tdc::kModeEpilogueAct + TDC_ACT_SILU>(&occ);
+  if (e == cudaSuccess) e = prepare_ws<NS, false, tdc::kModeEpilogueAct + TDC_ACT_HARDSWISH>(&occ);
+  return e;
+}
+
 // Failure records of the kernels' bounded waits, written through by the GPU
 // to mapped pinned host memory: 4 ints per device (code, block, stage, load)
 // in one page, allocated by the first call that launches a pipelined kernel
@@ -175,6 +187,10 @@ int current_device(DeviceInfo** info, int* dev_out, bool check_failures = true) 
     if (e2 == cudaSuccess) e2 = prepare_ws<2, false, tdc::kModeEpilogue>(&d.ws_occupancy[0][3]);
     if (e2 == cudaSuccess) e2 = prepare_ws<3, false, tdc::kModeEpilogue>(&d.ws_occupancy[1][3]);
     if (e2 == cudaSuccess) e2 = prepare_ws<4, false, tdc::kModeEpilogue>(&d.ws_occupancy[2][3]);
+    // The compile-time-activation epilogue kernels run at the plan of kind 3.
+    if (e2 == cudaSuccess) e2 = prepare_ws_act<2>();
+    if (e2 == cudaSuccess) e2 = prepare_ws_act<3>();
+    if (e2 == cudaSuccess) e2 = prepare_ws_act<4>();
     if (e2 == cudaSuccess) e2 = prepare_wgrad<2, tdc::F16>(&d.wgrad_occupancy[kF16][0]);
     if (e2 == cudaSuccess) e2 = prepare_wgrad<3, tdc::F16>(&d.wgrad_occupancy[kF16][1]);
     if (e2 == cudaSuccess) e2 = prepare_wgrad<4, tdc::F16>(&d.wgrad_occupancy[kF16][2]);
@@ -491,6 +507,20 @@ cudaError_t launch_ws_t(const CUtensorMap& map, const tdc::WsParams& prm, const 
   return launch_pdl(&tdc::dwconv_ws_kernel<NS, PROBE, MODE>, pl.grid, pl.smem, st, map, prm);
 }
 
+// The epilogue kernel with prm.act fixed at compile time.
+template <int NS>
+cudaError_t launch_ws_epi(const CUtensorMap& map, const tdc::WsParams& prm, const WsPlan& pl,
+                          cudaStream_t st) {
+  switch (prm.act) {
+    case TDC_ACT_RELU: return launch_ws_t<NS, false, tdc::kModeEpilogueAct + TDC_ACT_RELU>(map, prm, pl, st);
+    case TDC_ACT_RELU6: return launch_ws_t<NS, false, tdc::kModeEpilogueAct + TDC_ACT_RELU6>(map, prm, pl, st);
+    case TDC_ACT_SILU: return launch_ws_t<NS, false, tdc::kModeEpilogueAct + TDC_ACT_SILU>(map, prm, pl, st);
+    case TDC_ACT_HARDSWISH:
+      return launch_ws_t<NS, false, tdc::kModeEpilogueAct + TDC_ACT_HARDSWISH>(map, prm, pl, st);
+    default: return launch_ws_t<NS, false, tdc::kModeEpilogueAct + TDC_ACT_NONE>(map, prm, pl, st);
+  }
+}
+
 struct Epilogue {
   bool fused = false;
   const void* bias = nullptr;
@@ -558,9 +588,9 @@ int ws_common(const void* x, const void* w, void* y, int64_t N, int64_t H, int64
   cudaError_t e;
   if (with_epilogue) {
     switch (n_stage) {
-      case 2: e = launch_ws_t<2, false, tdc::kModeEpilogue>(map, prm, pl, st); break;
-      case 3: e = launch_ws_t<3, false, tdc::kModeEpilogue>(map, prm, pl, st); break;
-      default: e = launch_ws_t<4, false, tdc::kModeEpilogue>(map, prm, pl, st); break;
+      case 2: e = launch_ws_epi<2>(map, prm, pl, st); break;
+      case 3: e = launch_ws_epi<3>(map, prm, pl, st); break;
+      default: e = launch_ws_epi<4>(map, prm, pl, st); break;
     }
     return e == cudaSuccess ? TDC_OK : cuda_fail(e);
   }

@@ -253,6 +253,13 @@ __device__ __forceinline__ float apply_act(float t, int act) {
 constexpr int kModeWs = 0;        // the reference surface: C % 64, plain output
 constexpr int kModeGeneral = 1;   // C % 8 (partial last channel block), optional flipped taps
 constexpr int kModeEpilogue = 2;  // kModeGeneral + bias / activation / residual
+// kModeEpilogueAct + TDC_ACT_*: kModeEpilogue with the activation fixed at
+// compile time (the 3x3 stride-1 fp16 forward), so the per-row epilogue
+// carries no dispatch on it.
+constexpr int kModeEpilogueAct = 16;
+__host__ __device__ constexpr bool epilogue_mode(int mode) {
+  return mode == kModeEpilogue || mode >= kModeEpilogueAct;
+}
 
 __host__ __device__ constexpr int pmod(int a, int b) { return ((a % b) + b) % b; }
 
@@ -428,7 +435,7 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
     // Finishes output row o of the segment from the accumulators a[0..15]
     // (column 2*cp at a[0..7], the next at a[8..15]) and stores it.
     auto store_row = [&](int o, float* a) {
-      if constexpr (MODE == kModeEpilogue) {
+      if constexpr (epilogue_mode(MODE)) {
         if (p.bias != nullptr && chan_ok) {
           // Reloaded per row (an L1 hit) rather than held in 8 registers.
           const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + cl));
@@ -443,7 +450,7 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
             a[8 + 2 * k + 1] += b1;
           }
         }
-        switch (p.act) {
+        switch (MODE >= kModeEpilogueAct ? MODE - kModeEpilogueAct : p.act) {
           case TDC_ACT_RELU:
 #pragma unroll
             for (int k = 0; k < 16; ++k) a[k] = apply_act(a[k], TDC_ACT_RELU);
@@ -742,7 +749,7 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
       last_cb = sg.cb;
     }
     float bias0 = 0.f, bias1 = 0.f;
-    if constexpr (MODE == kModeEpilogue) {
+    if constexpr (epilogue_mode(MODE)) {
       if (p.bias != nullptr && chan_ok) {
         unpack2<E>(*reinterpret_cast<const uint32_t*>(p.bias + c0 + 2 * lane), bias0, bias1);
       }
@@ -763,7 +770,7 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
     // before the FMAs that finish the row so its latency overlaps them.
     // The branch depends on kernel parameters only (warp-uniform).
     auto load_res = [&](int o, uint32_t (&res)[kColsPerWarp]) {
-      if constexpr (MODE == kModeEpilogue) {
+      if constexpr (epilogue_mode(MODE)) {
         if (p.residual != nullptr && chan_ok) {
           const __half* rrow = p.residual + ((yrow - p.y) + int64_t(o) * y_row_stride);
 #pragma unroll
@@ -776,7 +783,7 @@ __device__ __forceinline__ void ws_consumers_pairs(const WsParams& p, const uint
 
     // Stores output row o of the segment from accumulator set `fin`.
     auto store_row = [&](int o, RowAcc& fin, const uint32_t (&res)[kColsPerWarp]) {
-      if constexpr (MODE == kModeEpilogue) {
+      if constexpr (epilogue_mode(MODE)) {
         if (!chan_ok) return;
         float* t = fin.v;  // dead after this store: the set restarts from +0
         if (p.bias != nullptr) {
