@@ -5,7 +5,12 @@
 Headline shape (N x 224 x 336 x 256, pad 1, n_stage 2).  Times per call
 (CUDA events, 10 warm-up + 50 calls) of:
   conv                 dwconv_ws alone
+  fused bias           dwconv3x3(bias)
+  fused relu           dwconv3x3(activation="relu")
   fused bias+relu      dwconv3x3(bias, "relu")
+  fused bias+relu6     dwconv3x3(bias, "relu6")
+  fused bias+silu      dwconv3x3(bias, "silu")
+  fused residual       dwconv3x3(residual=r)
   fused bias+silu+res  dwconv3x3(bias, "silu", residual)
   unfused              dwconv_ws, then y + bias, silu, + residual as torch ops
 Prints one JSON line per variant: µs, algorithmic GB/s (x + y + residual +
@@ -59,7 +64,12 @@ def main() -> None:
 
     rows = [
         ("conv", lambda: T.dwconv_ws(x, w, 1, 2), 2 * io),
+        ("fused bias", lambda: T.dwconv3x3(x, w, 1, bias=b), 2 * io),
+        ("fused relu", lambda: T.dwconv3x3(x, w, 1, activation="relu"), 2 * io),
         ("fused bias+relu", lambda: T.dwconv3x3(x, w, 1, bias=b, activation="relu"), 2 * io),
+        ("fused bias+relu6", lambda: T.dwconv3x3(x, w, 1, bias=b, activation="relu6"), 2 * io),
+        ("fused bias+silu", lambda: T.dwconv3x3(x, w, 1, bias=b, activation="silu"), 2 * io),
+        ("fused residual", lambda: T.dwconv3x3(x, w, 1, residual=r), 3 * io),
         ("fused bias+silu+res", lambda: T.dwconv3x3(x, w, 1, bias=b, residual=r, activation="silu"),
          3 * io),
         ("unfused bias+silu+res", unfused, 3 * io),
