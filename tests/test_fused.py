@@ -89,3 +89,20 @@ def test_argument_errors():
         T.dwconv3x3(xd, wd, 1, bias=b[:32].cuda())
     with pytest.raises(RuntimeError, match="residual must be"):
         T.dwconv3x3(xd, wd, 1, residual=xd[:, :4].contiguous())
+
+
+@pytest.mark.parametrize("activation", ["none", "relu", "relu6", "silu", "hardswish"])
+@pytest.mark.parametrize("n_stage", [2, 3, 4])
+def test_every_activation_kernel_and_ring_depth(activation, n_stage):
+    """The 3x3 stride-1 fp16 epilogue has one kernel per activation and ring
+    depth: each against the oracle, with a bias and with a bias + residual."""
+    N, H, W, C, pad = 2, 29, 41, 72, 1
+    x, w, b = _inputs(N, H, W, C, seed=11 + n_stage)
+    r = torch.randn(N, H, W, C, generator=torch.Generator().manual_seed(13)).half()
+    for res in (None, r):
+        y = T.dwconv3x3(x.cuda(), w.cuda(), pad, bias=b.cuda(),
+                        residual=None if res is None else res.cuda(), activation=activation,
+                        n_stage=n_stage)
+        want = oracle.dwconv_ex_f16(x.numpy(), w.numpy(), pad, b.numpy(),
+                                    None if res is None else res.numpy(), activation)
+        _check(y, want, activation, None if res is None else res.numpy())

@@ -438,16 +438,14 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
       if constexpr (epilogue_mode(MODE)) {
         if (p.bias != nullptr && chan_ok) {
           // Reloaded per row (an L1 hit) rather than held in 8 registers.
+          // t += b as fma(b, 1, t) on the packed 16-bit values: b * 1 is
+          // exact, so this is the fp32 add, with no conversion instruction.
           const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + cl));
           const uint32_t b4[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            float b0, b1;
-            unpack2<E>(b4[k], b0, b1);
-            a[2 * k] += b0;
-            a[2 * k + 1] += b1;
-            a[8 + 2 * k] += b0;
-            a[8 + 2 * k + 1] += b1;
+            fma2<E>(b4[k], ones2<E>(), a[2 * k], a[2 * k + 1]);
+            fma2<E>(b4[k], ones2<E>(), a[8 + 2 * k], a[8 + 2 * k + 1]);
           }
         }
         switch (MODE >= kModeEpilogueAct ? MODE - kModeEpilogueAct : p.act) {
@@ -472,7 +470,8 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
         }
         if (p.residual != nullptr) {
           // Loaded here, after the FMAs, rather than held through them (the
-          // preloaded version spilled at the 136-register limit).
+          // preloaded version spilled at the register limit); added as
+          // fma(r, 1, t), like the bias.
           const __half* rp = p.residual + y_off + int64_t(o) * y_row_stride;
           const uint4 res[2] = {
               st0 ? __ldg(reinterpret_cast<const uint4*>(rp)) : make_uint4(0u, 0u, 0u, 0u),
@@ -481,12 +480,7 @@ __device__ __forceinline__ void ws_consumers_vec3x3(const WsParams& p, const uin
           for (int m = 0; m < 2; ++m) {
             const uint32_t w4[4] = {res[m].x, res[m].y, res[m].z, res[m].w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              float r0, r1;
-              unpack2<E>(w4[k], r0, r1);
-              a[8 * m + 2 * k] += r0;
-              a[8 * m + 2 * k + 1] += r1;
-            }
+            for (int k = 0; k < 4; ++k) fma2<E>(w4[k], ones2<E>(), a[8 * m + 2 * k], a[8 * m + 2 * k + 1]);
           }
         }
       }

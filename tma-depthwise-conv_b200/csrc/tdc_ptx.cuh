@@ -138,6 +138,14 @@ __device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
 struct F16 {};
 struct BF16 {};
 
+// Two packed 16-bit ones (the w operand of fma2 that adds x to acc exactly).
+template <class E>
+__host__ __device__ constexpr uint32_t ones2();
+template <>
+__host__ __device__ constexpr uint32_t ones2<F16>() { return 0x3C003C00u; }
+template <>
+__host__ __device__ constexpr uint32_t ones2<BF16>() { return 0x3F803F80u; }
+
 // acc{0,1} += x.{lo,hi} * w.{lo,hi}: fma.rn.f32.f16 / fma.rn.f32.bf16.
 template <class E>
 __device__ __forceinline__ void fma2(uint32_t x2, uint32_t w2, float& acc0, float& acc1);
