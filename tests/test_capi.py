@@ -294,7 +294,8 @@ def test_kxk_plan_covers_every_output_once(lib, K, S, N, H, W, Cc, pad, ns):
 
 
 @pytest.mark.parametrize("K,S,D", [(3, 1, 2), (3, 1, 3), (5, 1, 2), (3, 2, 2), (7, 2, 3), (7, 1, 4)])
-@pytest.mark.parametrize("N,P,Q,Cc", [(2, 41, 70, 64), (1, 29, 37, 200), (12, 96, 160, 256), (3, 7, 5, 8)])
+@pytest.mark.parametrize("N,P,Q,Cc", [(2, 41, 70, 64), (1, 29, 37, 200), (12, 96, 160, 256), (3, 7, 5, 8),
+                                      (2, 2, 3, 64), (1, 1, 1, 8)])
 def test_dilated_ring_segments_cover_every_output_once(lib, K, S, D, N, P, Q, Cc):
     """The ring kernel's dilated schedule: the plan of the N*D*D phase
     sub-problems of the largest phase's ceil(P/D) x ceil(Q/D) outputs; a

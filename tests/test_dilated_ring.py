@@ -111,6 +111,19 @@ def test_ring_largest_steps(lib, K, S, D):
     assert np.array_equal(_bits(y), want)
 
 
+@pytest.mark.parametrize("K,S,D,H,W", [(3, 1, 3, 8, 9), (3, 1, 4, 9, 9), (5, 2, 2, 10, 13), (3, 2, 3, 8, 8)])
+def test_ring_phases_without_outputs(lib, K, S, D, H, W):
+    """Outputs fewer than D in a direction: some phases have no rows or no
+    columns, and their segments are skipped by the producer and the
+    consumers alike."""
+    x, w, b = _inputs(3, H, W, 96, K, seed=H * W + D)
+    pads = (0, 0, 0, 0)
+    want = _want(x, w, pads, S, D, bias=b.numpy(), activation="relu6")
+    rc, y = _run(lib, x.cuda(), w.cuda(), pads, S, D, 1, bias=b.cuda(), act="relu6")
+    assert rc == 0 and y.shape[1] * y.shape[2] > 0
+    assert np.array_equal(_bits(y), want)
+
+
 def test_ring_rejects_steps_beyond_the_map(lib):
     x = torch.zeros(1, 40, 300, 64, dtype=torch.float16, device="cuda")
     w = torch.zeros(3, 3, 64, dtype=torch.float16, device="cuda")
