@@ -905,3 +905,27 @@ def test_dilated_forward_argument_errors(lib):
         if not torch.cuda.is_available():
             assert fwd(f=f) == CODES["TDC_ERR_NO_DEVICE"]
             assert fwd(D=1, f=f) == CODES["TDC_ERR_NO_DEVICE"]  # dilation 1: the asym path
+
+
+
+def test_dilated_forward_named_kernel_argument_errors(lib):
+    """tdc_dwconv_fwd_dilated_ex: the same checks, an unknown kernel
+    (TDC_ERR_UNSUPPORTED), and without a device the ring and plain kernels
+    both reach the device check."""
+    p = C.c_void_p
+    def ex(kernel=1, D=2, act=0, bf16=0, K=3, C_=64, x=16, N=2):
+        return lib.tdc_dwconv_fwd_dilated_ex(p(x), p(16), None, None, p(16), i64(N), i64(16), i64(16),
+                                             i64(C_), i64(K), i64(1), i64(D), *[i64(D)] * 4, i64(act),
+                                             i64(kernel), i64(bf16), None)
+    for bf16 in (0, 1):
+        assert ex(kernel=2, bf16=bf16) == CODES["TDC_ERR_UNSUPPORTED"]
+        assert ex(kernel=-2, bf16=bf16) == CODES["TDC_ERR_UNSUPPORTED"]
+        assert ex(act=7, bf16=bf16) == CODES["TDC_ERR_ACT"]
+        assert ex(K=9, bf16=bf16) == CODES["TDC_ERR_FILTER_SHAPE"]
+        assert ex(C_=20, bf16=bf16) == CODES["TDC_ERR_CHANNELS"]
+        assert ex(x=8, bf16=bf16) == CODES["TDC_ERR_ALIGNMENT"]
+        assert ex(N=0, bf16=bf16) == CODES["TDC_OK"]
+        if not torch.cuda.is_available():
+            for kernel in (-1, 0, 1):
+                assert ex(kernel=kernel, bf16=bf16) == CODES["TDC_ERR_NO_DEVICE"]
+            assert ex(kernel=-1, D=1, bf16=bf16) == CODES["TDC_ERR_NO_DEVICE"]  # plain, undilated
